@@ -1,0 +1,612 @@
+// api.cu -- the C ABI (include/apt_moe.h): handle, weights, workspace, and the
+// ESRouter / ESExperts entry points.
+//
+// Reference interface each entry point replaces (paths within the reference):
+//   apt_moe_route          ESRouter::routeTopK       aptransformer/ESRouter.mm:14-32
+//   apt_moe_route_weights  ESRouter::routeWeights    aptransformer/ESRouter.mm:34-40
+//   apt_moe_experts        ESExperts::sparseForward  aptransformer/ESExperts.mm:44-60
+//   apt_moe_experts_dense  ESExperts::forward        aptransformer/ESExperts.mm:28-42
+//   apt_moe_forward        MoE section of ESDecoderLayer::forward, ESDecoderLayer.mm:67-75
+//   apt_moe_load_*         ESRouter / ESExperts ctors, esMakeExperts (ESWeightLoader.mm:145-154)
+//   apt_moe_config_from_json  ESModelConfig::fromConfigJSON MoE keys (ESModelConfig.mm:46-49)
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+
+#include "../../include/apt_moe.h"
+#include "moe_internal.h"
+
+using namespace apt;
+
+struct apt_moe_handle {
+    apt_moe_config cfg{};
+    std::string err;
+    int launches = 0;
+    int gemv_max_tokens = 64;
+
+    // per-stage CUDA-event timing (apt_moe_set_timing / apt_moe_stage_times)
+    bool timing = false;
+    cudaEvent_t ev[APT_STAGE_COUNT][2] = {};
+    bool ev_used[APT_STAGE_COUNT] = {};
+
+    // router
+    uint16_t *proj = nullptr, *scale = nullptr, *pes = nullptr;
+    // experts, bf16 (kept when quantised from bf16 so the dense path works)
+    uint16_t *gu = nullptr, *dn = nullptr;
+    // experts, affine quantised
+    uint32_t *gu_q = nullptr, *dn_q = nullptr;
+    uint16_t *gu_s = nullptr, *gu_b = nullptr, *dn_s = nullptr, *dn_b = nullptr;
+    int qbits = 0, qgs = 64;
+
+    // workspace
+    int Tm = 0, Pcap = 0;
+    float *scores = nullptr;
+    int32_t *idx_i = nullptr;
+    uint16_t *w_i = nullptr;
+    int32_t *counts = nullptr, *offsets = nullptr, *perm = nullptr, *inv = nullptr;
+    int32_t *active = nullptr, *n_active = nullptr, *errflag = nullptr;
+    uint16_t *xp = nullptr, *yp = nullptr, *op = nullptr;
+    uint16_t *Wd = nullptr;     // dense routing matrix [Tm,E]
+    int32_t *idx2 = nullptr;    // dense pair lists [Pcap]
+    uint16_t *w2 = nullptr;
+    uint16_t *xin = nullptr, *xout = nullptr;  // host-API staging [Tm,H]
+
+    Dispatch disp() const { return Dispatch{counts, offsets, perm, inv, active, n_active}; }
+};
+
+namespace {
+
+apt_status fail(apt_moe_handle *h, apt_status code, const char *fmt, ...) {
+    if (h) {
+        char buf[512];
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(buf, sizeof buf, fmt, ap);
+        va_end(ap);
+        h->err = buf;
+    }
+    return code;
+}
+
+#define CUDA_TRY(h, expr)                                                                    \
+    do {                                                                                     \
+        cudaError_t e_ = (expr);                                                             \
+        if (e_ != cudaSuccess)                                                               \
+            return fail((h), APT_ERR_CUDA, "%s: %s (%s:%d)", #expr, cudaGetErrorString(e_),  \
+                        __FILE__, __LINE__);                                                 \
+    } while (0)
+
+template <class T>
+cudaError_t dalloc(T **p, size_t n) {
+    return cudaMalloc(reinterpret_cast<void **>(p), n * sizeof(T) + 256);
+}
+
+void dfree(void *p) {
+    if (p) cudaFree(p);
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+apt_status copy_in(apt_moe_handle *h, void *dst, const void *src, size_t bytes, int on_device) {
+    CUDA_TRY(h, cudaMemcpy(dst, src, bytes, on_device ? cudaMemcpyDeviceToDevice
+                                                      : cudaMemcpyHostToDevice));
+    return APT_OK;
+}
+
+ExpertWeights weights_for(const apt_moe_handle *h, bool quant) {
+    ExpertWeights w{};
+    w.gu = h->gu;
+    w.dn = h->dn;
+    if (quant) {
+        w.gu_q = h->gu_q;
+        w.dn_q = h->dn_q;
+        w.gu_s = h->gu_s;
+        w.gu_b = h->gu_b;
+        w.dn_s = h->dn_s;
+        w.dn_b = h->dn_b;
+        w.bits = h->qbits;
+        w.gs = h->qgs;
+    }
+    return w;
+}
+
+struct StageScope {
+    apt_moe_handle *h;
+    int id;
+    cudaStream_t s;
+    StageScope(apt_moe_handle *h_, int id_, cudaStream_t s_) : h(h_), id(id_), s(s_) {
+        if (h->timing) cudaEventRecord(h->ev[id][0], s);
+    }
+    ~StageScope() {
+        if (h->timing) {
+            cudaEventRecord(h->ev[id][1], s);
+            h->ev_used[id] = true;
+        }
+    }
+};
+
+// Run one launch inside a timed stage scope.
+#define STAGE(h, id, s, expr)                    \
+    do {                                         \
+        StageScope sc_((h), (id), (s));          \
+        CUDA_TRY((h), (expr));                   \
+    } while (0)
+
+void begin_call(apt_moe_handle *h) {
+    h->launches = 0;
+    for (int i = 0; i < APT_STAGE_COUNT; ++i) h->ev_used[i] = false;
+}
+
+// ---- tiny config.json reader (MoE keys only)
+
+const char *find_key(const char *begin, const char *end, const char *key) {
+    std::string pat = std::string("\"") + key + "\"";
+    const char *p = begin;
+    while (p < end) {
+        const char *q = strstr(p, pat.c_str());
+        if (!q || q >= end) return nullptr;
+        const char *c = q + pat.size();
+        while (c < end && (*c == ' ' || *c == '\t' || *c == '\n' || *c == '\r')) ++c;
+        if (c < end && *c == ':') {
+            ++c;
+            while (c < end && (*c == ' ' || *c == '\t' || *c == '\n' || *c == '\r')) ++c;
+            return c;
+        }
+        p = q + 1;
+    }
+    return nullptr;
+}
+
+bool read_num(const char *b, const char *e, const char *key, double *out) {
+    const char *v = find_key(b, e, key);
+    if (!v) return false;
+    if (!strncmp(v, "true", 4)) { *out = 1; return true; }
+    if (!strncmp(v, "false", 5)) { *out = 0; return true; }
+    if (!strncmp(v, "null", 4)) return false;
+    char *endp = nullptr;
+    double d = strtod(v, &endp);
+    if (endp == v) return false;
+    *out = d;
+    return true;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ config
+
+extern "C" apt_status apt_moe_config_from_json(const char *json, apt_moe_config *cfg) {
+    if (!json || !cfg) return APT_ERR_INVALID;
+    memset(cfg, 0, sizeof *cfg);
+    cfg->rms_norm_eps = 1e-6f;
+    cfg->quant_group_size = 64;
+    cfg->max_tokens = 8192;
+    const char *b = json, *e = json + strlen(json);
+    // prefer the text_config object when present (multimodal Gemma-4 configs)
+    const char *tc = find_key(b, e, "text_config");
+    if (tc && *tc == '{') {
+        int depth = 0;
+        const char *p = tc;
+        for (; p < e; ++p) {
+            if (*p == '{') ++depth;
+            else if (*p == '}' && --depth == 0) break;
+        }
+        b = tc;
+        e = p;
+    }
+    double v;
+    if (read_num(b, e, "hidden_size", &v)) cfg->hidden_size = (int)v;
+    if (read_num(b, e, "num_experts", &v)) cfg->num_experts = (int)v;
+    if (read_num(b, e, "top_k_experts", &v)) cfg->top_k_experts = (int)v;
+    if (read_num(b, e, "moe_intermediate_size", &v)) cfg->moe_intermediate_size = (int)v;
+    if (read_num(b, e, "rms_norm_eps", &v)) cfg->rms_norm_eps = (float)v;
+    if (read_num(b, e, "enable_moe_block", &v)) cfg->enable_moe_block = v != 0.0;
+    return APT_OK;
+}
+
+extern "C" const char *apt_moe_version(void) { return "apt_moe 0.1 (sm_100a)"; }
+
+// ------------------------------------------------------------------ lifecycle
+
+extern "C" apt_status apt_moe_create(const apt_moe_config *cfg, apt_moe_handle **out) {
+    if (!cfg || !out) return APT_ERR_INVALID;
+    *out = nullptr;
+    const int H = cfg->hidden_size, E = cfg->num_experts, K = cfg->top_k_experts,
+              I = cfg->moe_intermediate_size;
+    if (H <= 0 || E <= 0 || K <= 0 || I <= 0 || cfg->max_tokens <= 0) return APT_ERR_INVALID;
+    if (H % 64 || I % 64 || E > 256 || K > 32 || K > E) return APT_ERR_UNSUPPORTED;
+    if (cfg->quant_bits && !((cfg->quant_bits == 4 || cfg->quant_bits == 8) &&
+                             cfg->quant_group_size == 64))
+        return APT_ERR_UNSUPPORTED;
+    apt_moe_handle *h = new apt_moe_handle();
+    h->cfg = *cfg;
+    if (cfg->max_tokens > (1 << 24) / K) {
+        delete h;
+        return APT_ERR_UNSUPPORTED;
+    }
+    DeviceGuard g(cfg->device);
+    h->Tm = cfg->max_tokens;
+    h->Pcap = h->Tm * K;
+    cudaError_t e1 = cudaSuccess;
+#define ALLOC(p, n) if (e1 == cudaSuccess) e1 = dalloc(&h->p, (size_t)(n))
+    ALLOC(scores, (size_t)h->Tm * E);
+    ALLOC(idx_i, h->Pcap);
+    ALLOC(w_i, h->Pcap);
+    ALLOC(counts, E);
+    ALLOC(offsets, E + 1);
+    ALLOC(perm, h->Pcap);
+    ALLOC(inv, h->Pcap);
+    ALLOC(active, E);
+    ALLOC(n_active, 1);
+    ALLOC(errflag, 4);
+    ALLOC(xp, (size_t)h->Pcap * H);
+    ALLOC(yp, (size_t)h->Pcap * I);
+    ALLOC(op, (size_t)h->Pcap * H);
+    ALLOC(Wd, (size_t)h->Tm * E);
+    ALLOC(idx2, h->Pcap);
+    ALLOC(w2, h->Pcap);
+    ALLOC(xin, (size_t)h->Tm * H);
+    ALLOC(xout, (size_t)h->Tm * H);
+#undef ALLOC
+    if (e1 == cudaSuccess) e1 = router_init();
+    if (e1 == cudaSuccess) e1 = gemv_init();
+    if (e1 == cudaSuccess) e1 = gemm_init();
+    if (e1 == cudaSuccess) e1 = cudaMemset(h->errflag, 0, 16);
+    for (int i = 0; i < APT_STAGE_COUNT && e1 == cudaSuccess; ++i)
+        for (int j = 0; j < 2 && e1 == cudaSuccess; ++j) e1 = cudaEventCreate(&h->ev[i][j]);
+    if (e1 != cudaSuccess) {
+        apt_moe_destroy(h);
+        return APT_ERR_CUDA;
+    }
+    *out = h;
+    return APT_OK;
+}
+
+extern "C" apt_status apt_moe_destroy(apt_moe_handle *h) {
+    if (!h) return APT_OK;
+    DeviceGuard g(h->cfg.device);
+    void *ptrs[] = {h->proj, h->scale, h->pes, h->gu, h->dn, h->gu_q, h->dn_q, h->gu_s, h->gu_b,
+                    h->dn_s, h->dn_b, h->scores, h->idx_i, h->w_i, h->counts, h->offsets,
+                    h->perm, h->inv, h->active, h->n_active, h->errflag, h->xp, h->yp, h->op,
+                    h->Wd, h->idx2, h->w2, h->xin, h->xout};
+    for (void *p : ptrs) dfree(p);
+    for (int i = 0; i < APT_STAGE_COUNT; ++i)
+        for (int j = 0; j < 2; ++j)
+            if (h->ev[i][j]) cudaEventDestroy(h->ev[i][j]);
+    delete h;
+    return APT_OK;
+}
+
+extern "C" const char *apt_moe_last_error(const apt_moe_handle *h) {
+    return h ? h->err.c_str() : "null handle";
+}
+
+extern "C" apt_status apt_moe_set_gemv_max_tokens(apt_moe_handle *h, int t) {
+    if (!h) return APT_ERR_INVALID;
+    h->gemv_max_tokens = t;
+    return APT_OK;
+}
+
+extern "C" apt_status apt_moe_set_timing(apt_moe_handle *h, int enable) {
+    if (!h) return APT_ERR_INVALID;
+    h->timing = enable != 0;
+    return APT_OK;
+}
+
+extern "C" apt_status apt_moe_stage_times(apt_moe_handle *h, float *ms) {
+    if (!h || !ms) return APT_ERR_INVALID;
+    DeviceGuard g(h->cfg.device);
+    for (int i = 0; i < APT_STAGE_COUNT; ++i) {
+        ms[i] = -1.f;
+        if (!h->ev_used[i]) continue;
+        CUDA_TRY(h, cudaEventSynchronize(h->ev[i][1]));
+        CUDA_TRY(h, cudaEventElapsedTime(&ms[i], h->ev[i][0], h->ev[i][1]));
+    }
+    return APT_OK;
+}
+
+extern "C" int apt_moe_last_launches(const apt_moe_handle *h) { return h ? h->launches : -1; }
+
+extern "C" apt_status apt_moe_last_counts(apt_moe_handle *h, int32_t *counts_host) {
+    if (!h || !counts_host) return APT_ERR_INVALID;
+    DeviceGuard g(h->cfg.device);
+    CUDA_TRY(h, cudaDeviceSynchronize());
+    CUDA_TRY(h, cudaMemcpy(counts_host, h->counts, sizeof(int32_t) * h->cfg.num_experts,
+                           cudaMemcpyDeviceToHost));
+    return APT_OK;
+}
+
+extern "C" apt_status apt_moe_sync(apt_moe_handle *h) {
+    if (!h) return APT_ERR_INVALID;
+    DeviceGuard g(h->cfg.device);
+    CUDA_TRY(h, cudaDeviceSynchronize());
+    int32_t ef[4] = {0, 0, 0, 0};
+    CUDA_TRY(h, cudaMemcpy(ef, h->errflag, sizeof ef, cudaMemcpyDeviceToHost));
+    if (ef[0]) {
+        cudaMemset(h->errflag, 0, sizeof ef);
+        return fail(h, APT_ERR_TIMEOUT, "device wait gave up (code %d, at %d)", ef[0], ef[1]);
+    }
+    return APT_OK;
+}
+
+// ------------------------------------------------------------------ weights
+
+extern "C" apt_status apt_moe_load_router(apt_moe_handle *h, const uint16_t *proj,
+                                          const uint16_t *scale, const uint16_t *pes,
+                                          int on_device) {
+    if (!h || !proj || !scale || !pes) return fail(h, APT_ERR_INVALID, "null router weight");
+    DeviceGuard g(h->cfg.device);
+    const int H = h->cfg.hidden_size, E = h->cfg.num_experts;
+    if (!h->proj) {
+        CUDA_TRY(h, dalloc(&h->proj, (size_t)E * H));
+        CUDA_TRY(h, dalloc(&h->scale, (size_t)H));
+        CUDA_TRY(h, dalloc(&h->pes, (size_t)E));
+    }
+    apt_status st;
+    if ((st = copy_in(h, h->proj, proj, sizeof(uint16_t) * E * H, on_device))) return st;
+    if ((st = copy_in(h, h->scale, scale, sizeof(uint16_t) * H, on_device))) return st;
+    if ((st = copy_in(h, h->pes, pes, sizeof(uint16_t) * E, on_device))) return st;
+    return APT_OK;
+}
+
+extern "C" apt_status apt_moe_load_experts_bf16(apt_moe_handle *h, const uint16_t *gate_up,
+                                                const uint16_t *down, int on_device) {
+    if (!h || !gate_up || !down) return fail(h, APT_ERR_INVALID, "null expert weight");
+    DeviceGuard g(h->cfg.device);
+    const size_t H = h->cfg.hidden_size, E = h->cfg.num_experts, I = h->cfg.moe_intermediate_size;
+    if (!h->gu) {
+        CUDA_TRY(h, dalloc(&h->gu, E * 2 * I * H));
+        CUDA_TRY(h, dalloc(&h->dn, E * H * I));
+    }
+    apt_status st;
+    if ((st = copy_in(h, h->gu, gate_up, sizeof(uint16_t) * E * 2 * I * H, on_device))) return st;
+    if ((st = copy_in(h, h->dn, down, sizeof(uint16_t) * E * H * I, on_device))) return st;
+    if (h->cfg.quant_bits) {
+        // ESExperts ctor with quantBits > 0 (ESExperts.mm:13-18): quantise at load,
+        // keep bf16 for the dense path.
+        const int bits = h->cfg.quant_bits, gs = h->cfg.quant_group_size;
+        if (!h->gu_q) {
+            CUDA_TRY(h, dalloc(&h->gu_q, E * 2 * I * H * bits / 32));
+            CUDA_TRY(h, dalloc(&h->dn_q, E * H * I * bits / 32));
+            CUDA_TRY(h, dalloc(&h->gu_s, E * 2 * I * H / gs));
+            CUDA_TRY(h, dalloc(&h->gu_b, E * 2 * I * H / gs));
+            CUDA_TRY(h, dalloc(&h->dn_s, E * H * I / gs));
+            CUDA_TRY(h, dalloc(&h->dn_b, E * H * I / gs));
+        }
+        CUDA_TRY(h, launch_quantize_affine(h->gu, (int64_t)E * 2 * I, (int)H, gs, bits, h->gu_q,
+                                           h->gu_s, h->gu_b, 0));
+        CUDA_TRY(h, launch_quantize_affine(h->dn, (int64_t)E * H, (int)I, gs, bits, h->dn_q,
+                                           h->dn_s, h->dn_b, 0));
+        CUDA_TRY(h, cudaDeviceSynchronize());
+        h->qbits = bits;
+        h->qgs = gs;
+    }
+    return APT_OK;
+}
+
+extern "C" apt_status apt_moe_load_experts_quant(apt_moe_handle *h, const uint32_t *gu_q,
+                                                 const uint16_t *gu_s, const uint16_t *gu_b,
+                                                 const uint32_t *dn_q, const uint16_t *dn_s,
+                                                 const uint16_t *dn_b, int bits, int gs,
+                                                 int on_device) {
+    if (!h || !gu_q || !gu_s || !gu_b || !dn_q || !dn_s || !dn_b)
+        return fail(h, APT_ERR_INVALID, "null quantised expert weight");
+    if (!((bits == 4 || bits == 8) && gs == 64))
+        return fail(h, APT_ERR_UNSUPPORTED, "bits=%d group=%d (need bits 4|8, group 64)", bits, gs);
+    DeviceGuard g(h->cfg.device);
+    const size_t H = h->cfg.hidden_size, E = h->cfg.num_experts, I = h->cfg.moe_intermediate_size;
+    dfree(h->gu_q); dfree(h->dn_q); dfree(h->gu_s); dfree(h->gu_b); dfree(h->dn_s); dfree(h->dn_b);
+    h->gu_q = h->dn_q = nullptr;
+    h->gu_s = h->gu_b = h->dn_s = h->dn_b = nullptr;
+    CUDA_TRY(h, dalloc(&h->gu_q, E * 2 * I * H * bits / 32));
+    CUDA_TRY(h, dalloc(&h->dn_q, E * H * I * bits / 32));
+    CUDA_TRY(h, dalloc(&h->gu_s, E * 2 * I * H / gs));
+    CUDA_TRY(h, dalloc(&h->gu_b, E * 2 * I * H / gs));
+    CUDA_TRY(h, dalloc(&h->dn_s, E * H * I / gs));
+    CUDA_TRY(h, dalloc(&h->dn_b, E * H * I / gs));
+    apt_status st;
+    if ((st = copy_in(h, h->gu_q, gu_q, 4 * E * 2 * I * H * bits / 32, on_device))) return st;
+    if ((st = copy_in(h, h->dn_q, dn_q, 4 * E * H * I * bits / 32, on_device))) return st;
+    if ((st = copy_in(h, h->gu_s, gu_s, 2 * E * 2 * I * H / gs, on_device))) return st;
+    if ((st = copy_in(h, h->gu_b, gu_b, 2 * E * 2 * I * H / gs, on_device))) return st;
+    if ((st = copy_in(h, h->dn_s, dn_s, 2 * E * H * I / gs, on_device))) return st;
+    if ((st = copy_in(h, h->dn_b, dn_b, 2 * E * H * I / gs, on_device))) return st;
+    // a bundle carries no bf16 experts (ESExperts.mm:21-26): dense path unavailable
+    dfree(h->gu);
+    dfree(h->dn);
+    h->gu = h->dn = nullptr;
+    h->qbits = bits;
+    h->qgs = gs;
+    return APT_OK;
+}
+
+// ------------------------------------------------------------------ compute
+
+namespace {
+
+apt_status check_T(apt_moe_handle *h, int T) {
+    if (T < 0 || T > h->Tm)
+        return fail(h, APT_ERR_INVALID, "T=%d outside [0, max_tokens=%d]", T, h->Tm);
+    return APT_OK;
+}
+
+// Grouped experts over an already-dispatched pair list, then the combine.
+// idx/w: [T, Kp] pair lists (Kp = K for sparse, E for dense).
+apt_status run_experts(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
+                       const uint16_t *w, int T, int Kp, bool quant, uint16_t *out,
+                       cudaStream_t s) {
+    const int H = h->cfg.hidden_size, E = h->cfg.num_experts, I = h->cfg.moe_intermediate_size;
+    const int P = T * Kp;
+    Dispatch d = h->disp();
+    STAGE(h, APT_STAGE_DISPATCH, s, launch_dispatch(idx, P, E, d, s, &h->launches));
+    ExpertWeights ew = weights_for(h, quant);
+    const int max_rows = T;  // an expert appears at most once per token
+    const bool gemm = !quant && T > h->gemv_max_tokens && gemm_supported(H, I);
+    if (gemm) {
+        const int rows_cap = P < h->Pcap ? P : h->Pcap;
+        STAGE(h, APT_STAGE_GATHER, s, launch_gather_rows(x, H, Kp, E, d, rows_cap, h->xp, s, &h->launches));
+        STAGE(h, APT_STAGE_GATE_UP, s, launch_gemm_gateup(h->xp, d, ew, rows_cap, H, I, E, h->yp, h->errflag, s,
+                                       &h->launches));
+        STAGE(h, APT_STAGE_DOWN, s, launch_gemm_down(h->yp, d, ew, rows_cap, H, I, E, h->op, h->errflag, s,
+                                     &h->launches));
+    } else {
+        STAGE(h, APT_STAGE_GATE_UP, s, launch_gemv_gateup(x, Kp, d, ew, H, I, E, max_rows, h->yp, s, &h->launches));
+        STAGE(h, APT_STAGE_DOWN, s, launch_gemv_down(h->yp, d, ew, H, I, E, max_rows, h->op, s, &h->launches));
+    }
+    STAGE(h, APT_STAGE_COMBINE, s, launch_combine(h->op, idx, w, d, T, Kp, H, out, s, &h->launches));
+    return APT_OK;
+}
+
+apt_status experts_sparse(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
+                          const uint16_t *w, int T, uint16_t *out, cudaStream_t s,
+                          bool counts_ready) {
+    const int E = h->cfg.num_experts, K = h->cfg.top_k_experts;
+    const bool quant = h->qbits > 0;
+    if (!quant && !h->gu) return fail(h, APT_ERR_STATE, "expert weights not loaded");
+    if (quant && !h->gu_q) return fail(h, APT_ERR_STATE, "quantised expert weights not loaded");
+    if (!counts_ready) {
+        CUDA_TRY(h, cudaMemsetAsync(h->counts, 0, sizeof(int32_t) * E, s));
+        STAGE(h, APT_STAGE_DISPATCH_COUNT, s, launch_count(idx, T * K, E, h->counts, s, &h->launches));
+    }
+    return run_experts(h, x, idx, w, T, K, quant, out, s);
+}
+
+apt_status experts_dense(apt_moe_handle *h, const uint16_t *x, const uint16_t *W, int T,
+                         uint16_t *out, cudaStream_t s) {
+    const int H = h->cfg.hidden_size, E = h->cfg.num_experts;
+    if (!h->gu)
+        return fail(h, APT_ERR_STATE,
+                    "dense expert path needs bf16 experts (unavailable from a quantised bundle)");
+    // chunks small enough that even a fully dense W fits the pair workspace
+    const int chunk = h->Pcap / E > 0 ? h->Pcap / E : 1;
+    for (int t0 = 0; t0 < T; t0 += chunk) {
+        const int tc = T - t0 < chunk ? T - t0 : chunk;
+        CUDA_TRY(h, cudaMemsetAsync(h->counts, 0, sizeof(int32_t) * E, s));
+        STAGE(h, APT_STAGE_DISPATCH_COUNT, s, launch_dense_to_pairs(W + (size_t)t0 * E, tc, E, h->idx2, h->w2, h->counts, s,
+                                          &h->launches));
+        apt_status st = run_experts(h, x + (size_t)t0 * H, h->idx2, h->w2, tc, E, false,
+                                    out + (size_t)t0 * H, s);
+        if (st) return st;
+    }
+    return APT_OK;
+}
+
+}  // namespace
+
+extern "C" apt_status apt_moe_route(apt_moe_handle *h, const uint16_t *x, int T, int32_t *idx,
+                                    uint16_t *w, void *stream) {
+    if (!h) return APT_ERR_INVALID;
+    if (check_T(h, T)) return APT_ERR_INVALID;
+    if (!h->proj) return fail(h, APT_ERR_STATE, "router weights not loaded");
+    if (T == 0) return APT_OK;
+    if (!x || !idx || !w) return fail(h, APT_ERR_INVALID, "null pointer");
+    DeviceGuard g(h->cfg.device);
+    cudaStream_t s = (cudaStream_t)stream;
+    begin_call(h);
+    const int H = h->cfg.hidden_size, E = h->cfg.num_experts, K = h->cfg.top_k_experts;
+    STAGE(h, APT_STAGE_ROUTER_SCORES, s, launch_router_scores(x, h->proj, h->scale, T, H, E, h->cfg.rms_norm_eps,
+                                     h->scores, s, &h->launches));
+    STAGE(h, APT_STAGE_ROUTER_SELECT, s, launch_router_select(h->scores, h->pes, T, E, K, idx, w, nullptr, s,
+                                     &h->launches));
+    return APT_OK;
+}
+
+extern "C" apt_status apt_moe_route_weights(apt_moe_handle *h, const uint16_t *x, int T,
+                                            uint16_t *W, void *stream) {
+    if (!h) return APT_ERR_INVALID;
+    if (check_T(h, T)) return APT_ERR_INVALID;
+    if (T == 0) return APT_OK;
+    if (!W) return fail(h, APT_ERR_INVALID, "null pointer");
+    apt_status st = apt_moe_route(h, x, T, h->idx_i, h->w_i, stream);
+    if (st) return st;
+    DeviceGuard g(h->cfg.device);
+    STAGE(h, APT_STAGE_ROUTER_SELECT, (cudaStream_t)stream, launch_scatter_dense(h->idx_i, h->w_i, T, h->cfg.num_experts,
+                                     h->cfg.top_k_experts, W, (cudaStream_t)stream,
+                                     &h->launches));
+    return APT_OK;
+}
+
+extern "C" apt_status apt_moe_experts(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
+                                      const uint16_t *w, int T, uint16_t *out, void *stream) {
+    if (!h) return APT_ERR_INVALID;
+    if (check_T(h, T)) return APT_ERR_INVALID;
+    if (T == 0) return APT_OK;
+    if (!x || !idx || !w || !out) return fail(h, APT_ERR_INVALID, "null pointer");
+    DeviceGuard g(h->cfg.device);
+    begin_call(h);
+    return experts_sparse(h, x, idx, w, T, out, (cudaStream_t)stream, false);
+}
+
+extern "C" apt_status apt_moe_experts_dense(apt_moe_handle *h, const uint16_t *x,
+                                            const uint16_t *W, int T, uint16_t *out,
+                                            void *stream) {
+    if (!h) return APT_ERR_INVALID;
+    if (check_T(h, T)) return APT_ERR_INVALID;
+    if (T == 0) return APT_OK;
+    if (!x || !W || !out) return fail(h, APT_ERR_INVALID, "null pointer");
+    DeviceGuard g(h->cfg.device);
+    begin_call(h);
+    return experts_dense(h, x, W, T, out, (cudaStream_t)stream);
+}
+
+extern "C" apt_status apt_moe_forward(apt_moe_handle *h, const uint16_t *x_router,
+                                      const uint16_t *x_experts, int T, uint16_t *out,
+                                      int32_t *idx_out, uint16_t *w_out, void *stream) {
+    if (!h) return APT_ERR_INVALID;
+    if (check_T(h, T)) return APT_ERR_INVALID;
+    if (T == 0) return APT_OK;
+    if (!x_router || !out) return fail(h, APT_ERR_INVALID, "null pointer");
+    if (!x_experts) x_experts = x_router;
+    if (!h->proj) return fail(h, APT_ERR_STATE, "router weights not loaded");
+    DeviceGuard g(h->cfg.device);
+    cudaStream_t s = (cudaStream_t)stream;
+    begin_call(h);
+    const int H = h->cfg.hidden_size, E = h->cfg.num_experts, K = h->cfg.top_k_experts;
+    int32_t *idx = idx_out ? idx_out : h->idx_i;
+    uint16_t *w = w_out ? w_out : h->w_i;
+    STAGE(h, APT_STAGE_ROUTER_SCORES, s, launch_router_scores(x_router, h->proj, h->scale, T, H, E, h->cfg.rms_norm_eps,
+                                     h->scores, s, &h->launches));
+    if (h->cfg.moe_sparse) {
+        CUDA_TRY(h, cudaMemsetAsync(h->counts, 0, sizeof(int32_t) * E, s));
+        STAGE(h, APT_STAGE_ROUTER_SELECT, s, launch_router_select(h->scores, h->pes, T, E, K, idx, w, h->counts, s,
+                                         &h->launches));
+        return experts_sparse(h, x_experts, idx, w, T, out, s, true);
+    }
+    // dense (reference default): routeWeights then ESExperts::forward
+    STAGE(h, APT_STAGE_ROUTER_SELECT, s, launch_router_select(h->scores, h->pes, T, E, K, idx, w, nullptr, s,
+                                     &h->launches));
+    STAGE(h, APT_STAGE_ROUTER_SELECT, s, launch_scatter_dense(idx, w, T, E, K, h->Wd, s, &h->launches));
+    return experts_dense(h, x_experts, h->Wd, T, out, s);
+}
+
+extern "C" apt_status apt_moe_forward_host(apt_moe_handle *h, const uint16_t *x_host, int T,
+                                           uint16_t *out_host, void *stream) {
+    if (!h) return APT_ERR_INVALID;
+    if (check_T(h, T)) return APT_ERR_INVALID;
+    if (T == 0) return APT_OK;
+    if (!x_host || !out_host) return fail(h, APT_ERR_INVALID, "null pointer");
+    DeviceGuard g(h->cfg.device);
+    cudaStream_t s = (cudaStream_t)stream;
+    const size_t bytes = sizeof(uint16_t) * (size_t)T * h->cfg.hidden_size;
+    CUDA_TRY(h, cudaMemcpyAsync(h->xin, x_host, bytes, cudaMemcpyHostToDevice, s));
+    apt_status st = apt_moe_forward(h, h->xin, h->xin, T, h->xout, nullptr, nullptr, stream);
+    if (st) return st;
+    CUDA_TRY(h, cudaMemcpyAsync(out_host, h->xout, bytes, cudaMemcpyDeviceToHost, s));
+    CUDA_TRY(h, cudaStreamSynchronize(s));
+    return APT_OK;
+}

@@ -1,0 +1,74 @@
+// common.cuh -- shared device helpers for the MoE block kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace apt {
+
+// ---------------------------------------------------------------- bf16 bits
+
+__device__ __forceinline__ float bf_lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+__device__ __forceinline__ float bf2f(uint16_t b) { return __uint_as_float(((uint32_t)b) << 16); }
+
+// Round-to-nearest-even f32 -> bf16 (the hardware conversion; NaN preserved).
+__device__ __forceinline__ uint16_t f2bf(float f) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+__device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
+__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
+    return (uint32_t)f2bf(lo) | ((uint32_t)f2bf(hi) << 16);
+}
+
+// Unpack 8 bf16 held in a uint4 into f32.
+__device__ __forceinline__ void unpack8(const uint4 &v, float *f) {
+    f[0] = bf_lo(v.x); f[1] = bf_hi(v.x);
+    f[2] = bf_lo(v.y); f[3] = bf_hi(v.y);
+    f[4] = bf_lo(v.z); f[5] = bf_hi(v.z);
+    f[6] = bf_lo(v.w); f[7] = bf_hi(v.w);
+}
+
+// Streaming 16-byte global load that does not allocate in L1 (weights are
+// read once per launch).
+__device__ __forceinline__ uint4 ldg_stream(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+// ---------------------------------------------------------------- gelu
+
+// gelu_pytorch_tanh in f32 with the reference op order (aptransformer/ESOps.h:29-37):
+//   x3 = (x*x)*x; inner = c0*(x + c1*x3); y = (0.5*x)*(1 + tanh(inner)).
+// Contraction into FMAs is disabled so every step rounds like the reference.
+__device__ __forceinline__ float gelu_tanh_f32(float x) {
+    float x3 = __fmul_rn(__fmul_rn(x, x), x);
+    float inner = __fmul_rn(0.7978845608028654f, __fadd_rn(x, __fmul_rn(0.044715f, x3)));
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+// y = bf16( bf16(gelu(g)) * u ) for bf16-valued g and u (ESExperts.mm:53-54).
+__device__ __forceinline__ float geglu_bf16(float g_bf, float u_bf) {
+    float ge = rbf(gelu_tanh_f32(g_bf));
+    return rbf(__fmul_rn(ge, u_bf));
+}
+
+// ---------------------------------------------------------------- warp helpers
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+}  // namespace apt

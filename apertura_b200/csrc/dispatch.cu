@@ -1,0 +1,187 @@
+// dispatch.cu -- token dispatch and weighted combine for the MoE block.
+//
+// The reference gathers weights per (token, k) inside mx::gather_mm
+// (aptransformer/ESExperts.mm:50-57) and never groups tokens by expert.  Here
+// the pairs are grouped once per call so every expert's weights stream from
+// HBM once for all of its tokens:
+//   counts   per-expert histogram (fused into the router's select kernel)
+//   offsets  exclusive scan of counts
+//   perm     sorted row -> pair id, stable in pair order (deterministic)
+//   inv      pair id -> sorted row
+// The combine restates ESExperts.mm:58-59 (sum over k of w * out): each
+// product is rounded to bf16, accumulated in f32 in k order, rounded once.
+#include "common.cuh"
+#include "moe_internal.h"
+
+namespace apt {
+
+namespace {
+
+__global__ void count_kernel(const int32_t *__restrict__ idx, int P, int E,
+                             int32_t *__restrict__ counts) {
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < P; p += gridDim.x * blockDim.x) {
+        const int e = idx[p];
+        if (e >= 0 && e < E) atomicAdd(counts + e, 1);
+    }
+}
+
+constexpr int kDispThreads = 256;
+constexpr int kDispPer = 4;  // pairs per thread per sweep
+
+// One CTA per expert.  Every CTA derives its own offset and its rank among the
+// active experts from the 128 counts, then sweeps the pair list in order and
+// places its matches with a ballot/prefix scan, so positions are stable.
+__global__ void __launch_bounds__(kDispThreads)
+dispatch_kernel(const int32_t *__restrict__ idx, int P, int E, const int32_t *__restrict__ counts,
+                int32_t *__restrict__ offsets, int32_t *__restrict__ perm,
+                int32_t *__restrict__ inv, int32_t *__restrict__ active,
+                int32_t *__restrict__ n_active) {
+    __shared__ int s_off, s_act;
+    __shared__ int warp_tot[kDispThreads / 32];
+    const int e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) {
+        s_off = 0;
+        s_act = 0;
+    }
+    __syncthreads();
+    int my_off = 0, my_act = 0;
+    for (int j = tid; j < e; j += kDispThreads) {
+        const int c = counts[j];
+        my_off += c;
+        my_act += c > 0;
+    }
+    atomicAdd(&s_off, my_off);
+    atomicAdd(&s_act, my_act);
+    __syncthreads();
+    const int off = s_off, cnt = counts[e];
+    if (tid == 0) {
+        offsets[e] = off;
+        if (cnt > 0) active[s_act] = e;
+        if (e == E - 1) {
+            offsets[E] = off + cnt;
+            *n_active = s_act + (cnt > 0);
+        }
+    }
+    if (cnt == 0) return;
+    int running = 0;
+    for (int base = 0; base < P && running < cnt; base += kDispThreads * kDispPer) {
+        const int p0 = base + tid * kDispPer;
+        int m[kDispPer];
+        int nm = 0;
+#pragma unroll
+        for (int j = 0; j < kDispPer; ++j) {
+            m[j] = (p0 + j < P) && (idx[p0 + j] == e);
+            nm += m[j];
+        }
+        // exclusive prefix of nm over the block
+        int incl = nm;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        if (lane == 31) warp_tot[warp] = incl;
+        __syncthreads();
+        int wbase = 0, total = 0;
+#pragma unroll
+        for (int w = 0; w < kDispThreads / 32; ++w) {
+            const int v = warp_tot[w];
+            wbase += (w < warp) ? v : 0;
+            total += v;
+        }
+        int pos = off + running + wbase + incl - nm;
+#pragma unroll
+        for (int j = 0; j < kDispPer; ++j) {
+            if (m[j]) {
+                perm[pos] = p0 + j;
+                inv[p0 + j] = pos;
+                ++pos;
+            }
+        }
+        running += total;
+        __syncthreads();
+    }
+}
+
+// One warp per sorted row: xp[row] = x[perm[row] / K].
+__global__ void gather_rows_kernel(const uint16_t *__restrict__ x, int H, int K,
+                                   const int32_t *__restrict__ perm,
+                                   const int32_t *__restrict__ offsets, int E, int max_rows,
+                                   uint16_t *__restrict__ xp) {
+    const int rows = offsets[E];
+    const int lane = threadIdx.x & 31;
+    for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows && row < max_rows;
+         row += (gridDim.x * blockDim.x) >> 5) {
+        const int t = perm[row] / K;
+        const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)t * H);
+        uint4 *dst = reinterpret_cast<uint4 *>(xp + (size_t)row * H);
+        for (int v = lane; v < H / 8; v += 32) dst[v] = src[v];
+    }
+}
+
+// One CTA per token; each thread owns 8 consecutive hidden elements.
+__global__ void combine_kernel(const uint16_t *__restrict__ op, const int32_t *__restrict__ idx,
+                               const uint16_t *__restrict__ w, const int32_t *__restrict__ inv,
+                               int T, int K, int H, uint16_t *__restrict__ out) {
+    const int t = blockIdx.x;
+    for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int k = 0; k < K; ++k) {
+            const int p = t * K + k;
+            if (idx[p] < 0) continue;
+            const float wk = bf2f(w[p]);
+            const uint4 o = *reinterpret_cast<const uint4 *>(op + (size_t)inv[p] * H + v * 8);
+            float f[8];
+            unpack8(o, f);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(acc[j], rbf(__fmul_rn(wk, f[j])));
+        }
+        uint4 r;
+        r.x = pack_bf2(acc[0], acc[1]);
+        r.y = pack_bf2(acc[2], acc[3]);
+        r.z = pack_bf2(acc[4], acc[5]);
+        r.w = pack_bf2(acc[6], acc[7]);
+        *reinterpret_cast<uint4 *>(out + (size_t)t * H + v * 8) = r;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_count(const int32_t *idx, int P, int E, int32_t *counts, cudaStream_t s,
+                         int *launches) {
+    const int blocks = min(1024, (P + 255) / 256);
+    count_kernel<<<blocks > 0 ? blocks : 1, 256, 0, s>>>(idx, P, E, counts);
+    if (launches) ++*launches;
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dispatch(const int32_t *idx, int P, int E, const Dispatch &d, cudaStream_t s,
+                            int *launches) {
+    dispatch_kernel<<<E, kDispThreads, 0, s>>>(idx, P, E, d.counts, d.offsets, d.perm, d.inv,
+                                               d.active, d.n_active);
+    if (launches) ++*launches;
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gather_rows(const uint16_t *x, int H, int K, int E, const Dispatch &d,
+                               int max_rows, uint16_t *xp, cudaStream_t s, int *launches) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int blocks = min(sms * 8, (max_rows + 7) / 8);
+    gather_rows_kernel<<<blocks > 0 ? blocks : 1, 256, 0, s>>>(x, H, K, d.perm, d.offsets, E,
+                                                                 max_rows, xp);
+    if (launches) ++*launches;
+    return cudaGetLastError();
+}
+
+cudaError_t launch_combine(const uint16_t *op, const int32_t *idx, const uint16_t *w,
+                           const Dispatch &d, int T, int K, int H, uint16_t *out, cudaStream_t s,
+                           int *launches) {
+    const int threads = min(512, ((H / 8 + 31) / 32) * 32);
+    combine_kernel<<<T, threads, 0, s>>>(op, idx, w, d.inv, T, K, H, out);
+    if (launches) ++*launches;
+    return cudaGetLastError();
+}
+
+}  // namespace apt

@@ -1,0 +1,82 @@
+// moe_internal.h -- kernel launchers shared between the .cu files of libapt_moe.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace apt {
+
+// Routing / dispatch state of one call, all device pointers.
+struct Dispatch {
+    int32_t *counts;    // [E]   tokens routed to each expert
+    int32_t *offsets;   // [E+1] exclusive scan of counts (offsets[E] = rows)
+    int32_t *perm;      // [P]   sorted row -> pair id (t*K + k)
+    int32_t *inv;       // [P]   pair id -> sorted row
+    int32_t *active;    // [E]   experts with counts > 0, ascending
+    int32_t *n_active;  // [1]
+};
+
+// Per-device one-time kernel attribute set-up (called with the device current).
+cudaError_t router_init();
+cudaError_t gemv_init();
+cudaError_t gemm_init();
+
+// ---- router (router.cu)
+// scores [T,E] f32 = (((x*rsqrt(mean(x^2)+eps))*scale)*H^-1/2) . proj^T
+cudaError_t launch_router_scores(const uint16_t *x, const uint16_t *proj, const uint16_t *scale,
+                                 int T, int H, int E, float eps, float *scores,
+                                 cudaStream_t s, int *launches);
+// softmax + top-K + renorm + per-expert scale; optional per-expert counts
+cudaError_t launch_router_select(const float *scores, const uint16_t *pes, int T, int E, int K,
+                                 int32_t *idx, uint16_t *w, int32_t *counts, cudaStream_t s,
+                                 int *launches);
+// dense routeWeights scatter: W [T,E] = 0 except W[t, idx[t,k]] = w[t,k]
+cudaError_t launch_scatter_dense(const int32_t *idx, const uint16_t *w, int T, int E, int K,
+                                 uint16_t *W, cudaStream_t s, int *launches);
+// dense W [T,E] -> pair lists idx2/w2 [T,E] (nonzero experts in index order, rest -1)
+cudaError_t launch_dense_to_pairs(const uint16_t *W, int T, int E, int32_t *idx2, uint16_t *w2,
+                                  int32_t *counts, cudaStream_t s, int *launches);
+
+// ---- dispatch (dispatch.cu)
+cudaError_t launch_count(const int32_t *idx, int P, int E, int32_t *counts, cudaStream_t s,
+                         int *launches);
+cudaError_t launch_dispatch(const int32_t *idx, int P, int E, const Dispatch &d, cudaStream_t s,
+                            int *launches);
+// xp[row] = x[perm[row] / K] for row < offsets[E]
+cudaError_t launch_gather_rows(const uint16_t *x, int H, int K, int E, const Dispatch &d,
+                               int max_rows, uint16_t *xp, cudaStream_t s, int *launches);
+// out[t] = bf16( sum_k f32(bf16(w[t,k] * op[inv[t*K+k]])) )
+cudaError_t launch_combine(const uint16_t *op, const int32_t *idx, const uint16_t *w,
+                           const Dispatch &d, int T, int K, int H, uint16_t *out,
+                           cudaStream_t s, int *launches);
+
+// ---- decode GEMV (gemv.cu).  Weight formats: bits == 0 -> bf16, else affine.
+struct ExpertWeights {
+    const uint16_t *gu, *dn;                // bf16 [E,2I,H], [E,H,I]
+    const uint32_t *gu_q, *dn_q;            // packed
+    const uint16_t *gu_s, *gu_b, *dn_s, *dn_b;
+    int bits, gs;
+};
+// max_rows_per_expert bounds counts[e] for this call (T for top-k routing).
+cudaError_t launch_gemv_gateup(const uint16_t *x, int K, const Dispatch &d, const ExpertWeights &w,
+                               int H, int I, int E, int max_rows_per_expert, uint16_t *yp,
+                               cudaStream_t s, int *launches);
+cudaError_t launch_gemv_down(const uint16_t *yp, const Dispatch &d, const ExpertWeights &w, int H,
+                             int I, int E, int max_rows_per_expert, uint16_t *op, cudaStream_t s,
+                             int *launches);
+
+// ---- prefill grouped GEMM (gemm_sm100.cu), bf16 tcgen05 tiles
+struct GemmPlan;  // opaque, owns tensor maps
+bool gemm_supported(int H, int I);
+cudaError_t launch_gemm_gateup(const uint16_t *xp, const Dispatch &d, const ExpertWeights &w,
+                               int rows_cap, int H, int I, int E, uint16_t *yp, int32_t *err,
+                               cudaStream_t s, int *launches);
+cudaError_t launch_gemm_down(const uint16_t *yp, const Dispatch &d, const ExpertWeights &w,
+                             int rows_cap, int H, int I, int E, uint16_t *op, int32_t *err,
+                             cudaStream_t s, int *launches);
+
+// ---- quantisation (quant.cu)
+cudaError_t launch_quantize_affine(const uint16_t *w, int64_t rows, int cols, int gs, int bits,
+                                   uint32_t *q, uint16_t *sc, uint16_t *bi, cudaStream_t s);
+
+}  // namespace apt

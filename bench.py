@@ -1,0 +1,414 @@
+"""Benchmark of the B200 Gemma-4 MoE block (ESRouter + ESExperts).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--no-prefill] [--no-cpu-baseline]
+
+Workload (the decode sweep): one step is one
+MoE-block forward at each T in {1, 4, 16, 64} on the Gemma-4-26B block shape
+(H=2816, E=128, top-8, I=704, bf16), seeded synthetic inputs, uniform-ish
+routing.  value = tokens/s over the whole job (85 tokens per step per GPU).
+L2 is flushed (256 MiB write) before every timed forward and the flush is
+outside the timed events.  The prefill config (T=8192, Zipf(1.1) routing) is
+reported as an extra object.
+
+``--impl reference`` times the CPU oracle (the C restatement of the
+reference's mx:: op sequence; MLX itself is not installed) on the host cores
+for the same workload.  Under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MoE-block tokens/s (decode T=1..64, prefill T=8192); % of HBM / TC roofline"
+SWEEP = (1, 4, 16, 64)
+H, E, K, I = 2816, 128, 8, 704
+EXPERT_BYTES = (2 * I * H + H * I) * 2          # 11,894,784 B per touched expert
+GATEUP_BYTES = 2 * I * H * 2                    # gate_up part of it
+ROUTER_BYTES = E * H * 2                        # 720,896 B
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return dict(hbm=d["hbm_gbs"], tc=d["bf16_tflops"], tc_sust=d["bf16_tflops_sustained"],
+                    src="measured")
+    return dict(hbm=6650.0, tc=1590.0, tc_sust=1400.0, src="fallback")
+
+
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons sampled every 200 ms in the background."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------- helpers
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def n_unique(idx):
+    import torch
+    return int(torch.unique(idx).numel())
+
+
+def oracle_sweep_inputs(d_by_T, gate_up, down):
+    """CPU copies (numpy bf16 bits) for the oracle."""
+    from apertura_b200.synthetic import to_numpy_bits as nb
+    xs = {T: nb(d["x"]) for T, d in d_by_T.items()}
+    d0 = next(iter(d_by_T.values()))
+    return dict(xs=xs, proj=nb(d0["proj"]), scale=nb(d0["scale"]), pes=nb(d0["pes"]),
+                gate_up=nb(gate_up), down=nb(down))
+
+
+def time_oracle_sweep(o, budget_s=12.0, max_passes=50):
+    """Oracle (route + sparse experts) over the sweep until `budget_s` elapses.
+    Returns (tokens/s, passes, seconds, threads)."""
+    from oracle import oracle as O
+    O.build()
+    passes, t0 = 0, time.perf_counter()
+    while True:
+        for T, x in o["xs"].items():
+            idx, w = O.route_topk(x, o["proj"], o["scale"], o["pes"], K)
+            O.experts_sparse(x, o["gate_up"], o["down"], idx, w)
+        passes += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or passes >= max_passes:
+            break
+    return passes * sum(SWEEP) / el, passes, el, O.num_threads()
+
+
+def make_sweep_inputs(dev, seed=0):
+    from apertura_b200.synthetic import block_inputs, expert_bank
+    gate_up, down = expert_bank(E, H, I, seed, dev)
+    # one router and 85 distinct tokens, split over the sweep's T values
+    d = block_inputs(sum(SWEEP), seed=seed, device=dev, with_experts=False)
+    d_by_T, t0 = {}, 0
+    for T in SWEEP:
+        d_by_T[T] = dict(d, x=d["x"][t0:t0 + T].contiguous(), T=T)
+        t0 += T
+    return d_by_T, gate_up, down
+
+
+# --------------------------------------------------------------------- reference arm
+
+def run_reference(args):
+    world, rank, local = dist_env()
+    if rank != 0:
+        return 0
+    import torch
+    dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
+    d_by_T, gate_up, down = make_sweep_inputs(dev)
+    o = oracle_sweep_inputs(d_by_T, gate_up, down)
+    from oracle import oracle as O
+    O.build()
+    # warm-up passes (untimed), then K timed sweep passes, each its own step
+    for _ in range(max(args.warmup, 0)):
+        x = o["xs"][1]
+        idx, w = O.route_topk(x, o["proj"], o["scale"], o["pes"], K)
+        O.experts_sparse(x, o["gate_up"], o["down"], idx, w)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for T, x in o["xs"].items():
+            idx, w = O.route_topk(x, o["proj"], o["scale"], o["pes"], K)
+            O.experts_sparse(x, o["gate_up"], o["down"], idx, w)
+    el = time.perf_counter() - t0
+    tps = args.steps * sum(SWEEP) / el
+    sample = (f"{args.steps} passes of the decode sweep T in {SWEEP} (route + sparse experts), "
+              f"C restatement of ESRouter.mm/ESExperts.mm with OpenMP (MLX not installed)")
+    line = {
+        "metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": "decode sweep T in {1,4,16,64}, Gemma-4-26B MoE block "
+                               "(H=2816,E=128,K=8,I=704), bf16, uniform routing, CPU"},
+        "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": O.num_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------- our arm
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import apertura_b200 as A
+    from apertura_b200 import build as B
+
+    world, rank, local = dist_env()
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B.build()
+    peaks = load_peaks()
+
+    d_by_T, gate_up, down = make_sweep_inputs(dev, seed=rank)
+    d0 = d_by_T[SWEEP[0]]
+    cfg = A.ESModelConfig(moe_sparse=True, max_tokens=8192 if args.prefill else max(SWEEP),
+                          device=local)
+    blk = A.MoEBlock(cfg, d0["proj"], d0["scale"], d0["pes"], gate_up, down)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def forward_T(T):
+        return blk.forward(d_by_T[T]["x"])
+
+    # routing stats per T (U = distinct experts touched)
+    U = {}
+    for T in SWEEP:
+        _, tk = blk.forward(d_by_T[T]["x"], return_routing=True)
+        U[T] = n_unique(tk.idx)
+    launches_per_step = 0
+    for T in SWEEP:
+        forward_T(T)
+        launches_per_step += blk.handle.last_launches()
+    for _ in range(args.warmup):
+        for T in SWEEP:
+            forward_T(T)
+    torch.cuda.synchronize()
+
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps * len(SWEEP))]
+    per_T_ms = {T: 0.0 for T in SWEEP}
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        i = 0
+        for _ in range(args.steps):
+            for T in SWEEP:
+                flush.zero_()                       # evict L2 (outside the events)
+                a, b = evs[i]
+                a.record(stream)
+                forward_T(T)
+                b.record(stream)
+                i += 1
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+    i = 0
+    total_ms = 0.0
+    for _ in range(args.steps):
+        for T in SWEEP:
+            ms = evs[i][0].elapsed_time(evs[i][1])
+            per_T_ms[T] += ms / args.steps
+            total_ms += ms
+            i += 1
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    value = world * sum(SWEEP) / (ms_per_step / 1e3)
+
+    # per-stage times (separate untimed-for-value pass with stage events on)
+    blk.handle.set_timing(True)
+    stage = {T: {} for T in SWEEP}
+    reps = 5
+    for _ in range(reps):
+        for T in SWEEP:
+            flush.zero_()
+            forward_T(T)
+            for k, v in blk.handle.stage_times().items():
+                stage[T][k] = stage[T].get(k, 0.0) + v / reps
+    blk.handle.set_timing(False)
+
+    # roofline of the dominant kernel (gate_up GEMV) over the sweep
+    gu_bytes = sum(U[T] * GATEUP_BYTES + T * H * 2 + T * K * I * 2 for T in SWEEP)
+    gu_ms = sum(stage[T].get("gate_up", 0.0) for T in SWEEP)
+    achieved = gu_bytes / (gu_ms / 1e3) / 1e9
+    block_bytes = {T: U[T] * EXPERT_BYTES + ROUTER_BYTES + T * H * 2 * 2 + T * K * 6
+                   for T in SWEEP}
+    sweep_detail = {
+        str(T): {"ms": per_T_ms[T], "tokens_per_s": T / (per_T_ms[T] / 1e3), "U": U[T],
+                 "block_GBps": block_bytes[T] / (per_T_ms[T] / 1e3) / 1e9,
+                 "block_hbm_frac": block_bytes[T] / (per_T_ms[T] / 1e3) / 1e9 / peaks["hbm"],
+                 "stages_ms": stage[T]}
+        for T in SWEEP}
+
+    # e2e through the C ABI with host buffers (pinned), copies inside the events
+    xh = {T: d_by_T[T]["x"].cpu().pin_memory() for T in SWEEP}
+    oh = {T: torch.empty(T, H, dtype=torch.bfloat16).pin_memory() for T in SWEEP}
+    for T in SWEEP:
+        blk.forward_host(xh[T], oh[T])
+    e2e_ms = 0.0
+    for _ in range(args.steps):
+        for T in SWEEP:
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            blk.forward_host(xh[T], oh[T])
+            b.record(stream)
+            b.synchronize()
+            e2e_ms += a.elapsed_time(b)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {"value": world * sum(SWEEP) * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+           "h2d_bytes_per_step": sum(SWEEP) * H * 2, "d2h_bytes_per_step": sum(SWEEP) * H * 2}
+
+    prefill = run_prefill(blk, dev, peaks, flush) if args.prefill else None
+
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_baseline:
+        o = oracle_sweep_inputs(d_by_T, gate_up, down)
+        tps, passes, el, thr = time_oracle_sweep(o)
+        cpu = {"value": tps, "unit": "tokens/s", "cores": thr, "kind": "port",
+               "sample": f"{passes} passes of the decode sweep T in {SWEEP} ({el:.1f} s), C "
+                         f"restatement of ESRouter.mm/ESExperts.mm, OpenMP"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": "decode sweep T in {1,4,16,64}, Gemma-4-26B MoE block "
+                                   "(H=2816,E=128,K=8,I=704), bf16, uniform routing",
+                       "l2": "flushed before every timed forward (256 MiB write, untimed)",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "roofline": {"bound": "hbm", "kernel": "gemv_gateup", "achieved": achieved,
+                         "peak": peaks["hbm"], "unit": "GB/s", "frac": achieved / peaks["hbm"],
+                         "peak_source": peaks["src"], "traffic": args.traffic},
+            "sweep": sweep_detail,
+            "e2e": e2e,
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks.summary(),
+        }
+        if prefill:
+            line["prefill"] = prefill
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def run_prefill(blk, dev, peaks, flush, T=8192, steps=3):
+    """T=8192 with Zipf(1.1) routing; tensor-pipe roofline."""
+    import torch
+    from apertura_b200.synthetic import block_inputs
+    d = block_inputs(T, seed=1, device=dev, routing="zipf", with_experts=False)
+    # router weights of the Zipf config go into the same handle
+    from apertura_b200.moe import ESRouter
+    ESRouter(d["proj"], d["scale"], d["pes"], E, K, H, handle=blk.handle)
+    out = blk.forward(d["x"])
+    torch.cuda.synchronize()
+    ms = 0.0
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        blk.forward(d["x"])
+        b.record(stream)
+        b.synchronize()
+        ms += a.elapsed_time(b) / steps
+    blk.handle.set_timing(True)
+    blk.forward(d["x"])
+    st = blk.handle.stage_times()
+    blk.handle.set_timing(False)
+    flops = 2.0 * T * K * (2 * I * H + I * H)
+    gemm_ms = st.get("gate_up", 0.0) + st.get("down", 0.0)
+    counts = blk.handle.last_counts()
+    return {"T": T, "ms": ms, "tokens_per_s": T / (ms / 1e3),
+            "block_tflops": flops / (ms / 1e3) / 1e12,
+            "block_tc_frac": flops / (ms / 1e3) / 1e12 / peaks["tc"],
+            "expert_kernels_tflops": flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None,
+            "stages_ms": st, "max_expert_rows": int(counts.max()),
+            "zipf_top_share": float(d["zipf"]["achieved"].max()), "routing": "zipf s=1.1"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-prefill", dest="prefill", action="store_false")
+    ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--traffic", type=float, default=None,
+                    help="dram bytes per gate_up launch from an ncu capture (reported as is)")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    return run_reference(args) if args.impl == "reference" else run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,204 @@
+/*
+ * apt_moe.h -- C ABI of the B200-native Gemma-4 MoE block (ESRouter + ESExperts).
+ *
+ * Drop-in boundary for the reference's MoE section of ESDecoderLayer::forward
+ * (aptransformer/ESDecoderLayer.mm:67-75).  The reference has no FFI: its
+ * callers use the C++ classes es::ESRouter (aptransformer/ESRouter.h:17-34)
+ * and es::ESExperts (aptransformer/ESExperts.h:17-41).  Each entry point below
+ * replaces one of their members; the mapping is given beside it.
+ *
+ * Conventions
+ *   - Every function returns apt_status (0 = APT_OK) and never throws.  The
+ *     message of the last failure on a handle is apt_moe_last_error(h).
+ *   - bf16 tensors are passed as uint16_t* holding raw bf16 bits, row-major.
+ *   - Pointers marked "device" are CUDA device pointers on the handle's
+ *     device; "host" pointers are ordinary host memory (pinned for speed).
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy stream).  All
+ *     compute entry points are stream-ordered and asynchronous.
+ *   - A handle is not re-entrant: callers serialise calls per handle.
+ *   - Shapes: T tokens, H hidden_size, E num_experts, K top_k_experts,
+ *     I moe_intermediate_size.
+ */
+#ifndef APT_MOE_H
+#define APT_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define APT_API __attribute__((visibility("default")))
+#else
+#define APT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int apt_status;
+enum {
+    APT_OK = 0,
+    APT_ERR_INVALID = 1,      /* bad argument / shape                        */
+    APT_ERR_UNSUPPORTED = 2,  /* unsupported bits / group size / shape       */
+    APT_ERR_CUDA = 3,         /* a CUDA runtime or driver call failed        */
+    APT_ERR_NCCL = 4,         /* an NCCL call failed                         */
+    APT_ERR_TIMEOUT = 5,      /* a bounded device-side wait gave up          */
+    APT_ERR_STATE = 6         /* weights not loaded / wrong call order       */
+};
+
+typedef struct apt_moe_handle apt_moe_handle;
+
+/*
+ * MoE subset of ESModelConfig (aptransformer/ESModelConfig.h:135-157; parsed
+ * from config.json text_config at ESModelConfig.mm:46-49).
+ */
+typedef struct apt_moe_config {
+    int hidden_size;            /* H  (text_config.hidden_size)                */
+    int num_experts;            /* E  (text_config.num_experts)                */
+    int top_k_experts;          /* K  (text_config.top_k_experts)              */
+    int moe_intermediate_size;  /* I  (text_config.moe_intermediate_size)      */
+    float rms_norm_eps;         /* router RMSNorm eps (text_config.rms_norm_eps) */
+    int enable_moe_block;       /* text_config.enable_moe_block                */
+    int moe_sparse;             /* runtime: 1 = top-k gather path, 0 = dense    */
+    int quant_bits;             /* runtime: 0 = bf16 experts, 4 or 8 = affine   */
+    int quant_group_size;       /* runtime: affine group size (64)              */
+    int max_tokens;             /* largest T per call; sizes the workspace      */
+    int device;                 /* CUDA device ordinal                          */
+} apt_moe_config;
+
+/* Fill *cfg from the text of an HF config.json (top level or text_config).
+ * Runtime knobs get the reference defaults: moe_sparse=0, quant_bits=0,
+ * quant_group_size=64; max_tokens=8192, device=0.
+ * Replaces ESModelConfig::fromConfigJSON (ESModelConfig.h:69) for these keys. */
+APT_API apt_status apt_moe_config_from_json(const char *json_text, apt_moe_config *cfg);
+
+/* Create a handle: validates the config, allocates the workspace for
+ * max_tokens on cfg->device.  No weights yet. */
+APT_API apt_status apt_moe_create(const apt_moe_config *cfg, apt_moe_handle **out);
+APT_API apt_status apt_moe_destroy(apt_moe_handle *h);
+APT_API const char *apt_moe_last_error(const apt_moe_handle *h);
+/* Library version string (static). */
+APT_API const char *apt_moe_version(void);
+
+/*
+ * Router weights (ESRouter ctor, ESRouter.mm:8-12): proj [E,H], scale [H],
+ * per_expert_scale [E], bf16.  src_on_device: 0 = host pointers, 1 = device.
+ */
+APT_API apt_status apt_moe_load_router(apt_moe_handle *h, const uint16_t *proj, const uint16_t *scale,
+                               const uint16_t *per_expert_scale, int src_on_device);
+
+/*
+ * bf16 expert weights in HF layout (ESExperts ctor, ESExperts.mm:8-19):
+ * gate_up [E,2I,H] (gate = rows 0..I-1, up = rows I..2I-1), down [E,H,I].
+ * If cfg.quant_bits > 0 the weights are quantised on the device (MLX affine,
+ * group cfg.quant_group_size) exactly as the reference quantises at load.
+ */
+APT_API apt_status apt_moe_load_experts_bf16(apt_moe_handle *h, const uint16_t *gate_up,
+                                     const uint16_t *down, int src_on_device);
+
+/*
+ * Pre-quantised expert weights in MLX affine format (ESExperts bundle ctor,
+ * ESExperts.mm:21-26; esMakeExperts, ESWeightLoader.mm:145-154):
+ *   gate_up: q [E,2I,H*bits/32] u32, scales/biases [E,2I,H/gs] bf16
+ *   down:    q [E,H,I*bits/32]  u32, scales/biases [E,H,I/gs]  bf16
+ * bits in {4,8}; gs = 64.  Values are adopted verbatim.
+ */
+APT_API apt_status apt_moe_load_experts_quant(apt_moe_handle *h, const uint32_t *gu_q,
+                                      const uint16_t *gu_scales, const uint16_t *gu_biases,
+                                      const uint32_t *dn_q, const uint16_t *dn_scales,
+                                      const uint16_t *dn_biases, int bits, int group_size,
+                                      int src_on_device);
+
+/*
+ * ESRouter::routeTopK (ESRouter.mm:14-32).  x [T,H] bf16 (device) ->
+ * idx [T,K] int32 (descending probability), w [T,K] bf16 (device).
+ */
+APT_API apt_status apt_moe_route(apt_moe_handle *h, const uint16_t *x, int T, int32_t *idx,
+                         uint16_t *w, void *stream);
+
+/*
+ * ESRouter::routeWeights (ESRouter.mm:34-40).  x [T,H] (device) ->
+ * W [T,E] bf16 dense (device), zero except at the top-k experts.
+ */
+APT_API apt_status apt_moe_route_weights(apt_moe_handle *h, const uint16_t *x, int T, uint16_t *W,
+                                 void *stream);
+
+/*
+ * ESExperts::sparseForward (ESExperts.mm:44-60).  x [T,H], idx [T,K] int32,
+ * w [T,K] bf16 -> out [T,H] bf16; all device.  idx entries < 0 are skipped.
+ */
+APT_API apt_status apt_moe_experts(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
+                           const uint16_t *w, int T, uint16_t *out, void *stream);
+
+/*
+ * ESExperts::forward (ESExperts.mm:28-42), the dense path: out[t] =
+ * sum_e bf16(W[t,e] * expert_e(x[t])).  W [T,E] bf16 (device).  Experts with
+ * W[t,e] == 0 contribute exactly zero and are not evaluated.
+ */
+APT_API apt_status apt_moe_experts_dense(apt_moe_handle *h, const uint16_t *x, const uint16_t *W,
+                                 int T, uint16_t *out, void *stream);
+
+/*
+ * The MoE section of ESDecoderLayer::forward (ESDecoderLayer.mm:70-73):
+ * router reads x_router (the raw residual x1), experts read x_experts
+ * (pre_ff_ln_2(x1)); pass the same pointer for both in a block harness.
+ * Honours cfg.moe_sparse (sparse vs dense dispatch) and the loaded weight
+ * format.  idx_out / w_out (device, [T,K]) may be NULL.
+ */
+APT_API apt_status apt_moe_forward(apt_moe_handle *h, const uint16_t *x_router,
+                           const uint16_t *x_experts, int T, uint16_t *out, int32_t *idx_out,
+                           uint16_t *w_out, void *stream);
+
+/*
+ * Same as apt_moe_forward with HOST buffers: copies x to the device, runs
+ * the block, copies out back and synchronises the stream.  x_host [T,H],
+ * out_host [T,H] bf16.
+ */
+APT_API apt_status apt_moe_forward_host(apt_moe_handle *h, const uint16_t *x_host, int T,
+                                uint16_t *out_host, void *stream);
+
+/* Synchronise the handle's device and report any pending CUDA error. */
+APT_API apt_status apt_moe_sync(apt_moe_handle *h);
+
+/*
+ * Introspection for tests and the bench: per-expert token counts of the last
+ * dispatch (device -> host copy, synchronous), and kernel launch count of the
+ * last compute call.
+ */
+APT_API apt_status apt_moe_last_counts(apt_moe_handle *h, int32_t *counts_host);
+APT_API int apt_moe_last_launches(const apt_moe_handle *h);
+
+/*
+ * Path selection: the grouped expert kernels run as HBM-streaming GEMV when
+ * T <= gemv_max_tokens and as tcgen05 tensor-core tiles otherwise.
+ * Default 64.  Set to 0 to force the tensor-core path, to a huge value to
+ * force the GEMV path (used by the parity tests).
+ */
+APT_API apt_status apt_moe_set_gemv_max_tokens(apt_moe_handle *h, int t);
+
+/*
+ * Per-stage timing for measurement: when enabled, every compute call records
+ * a CUDA event pair on its stream around each stage's kernel;
+ * apt_moe_stage_times fills ms[APT_STAGE_COUNT] with the last call's
+ * durations (-1 for stages that did not run), synchronising on the events.
+ * A stage that launched several times in one call reports its last launch.
+ */
+enum {
+    APT_STAGE_ROUTER_SCORES = 0,
+    APT_STAGE_ROUTER_SELECT = 1,
+    APT_STAGE_DISPATCH_COUNT = 2,
+    APT_STAGE_DISPATCH = 3,
+    APT_STAGE_GATHER = 4,
+    APT_STAGE_GATE_UP = 5,
+    APT_STAGE_DOWN = 6,
+    APT_STAGE_COMBINE = 7,
+    APT_STAGE_COUNT = 8
+};
+APT_API apt_status apt_moe_set_timing(apt_moe_handle *h, int enable);
+APT_API apt_status apt_moe_stage_times(apt_moe_handle *h, float *ms);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* APT_MOE_H */
