@@ -22,7 +22,7 @@ EXPORTED = [
     "apt_moe_load_experts_quant", "apt_moe_route", "apt_moe_route_weights", "apt_moe_experts",
     "apt_moe_experts_dense", "apt_moe_forward", "apt_moe_forward_host", "apt_moe_sync",
     "apt_moe_last_counts", "apt_moe_last_launches", "apt_moe_set_gemv_max_tokens",
-    "apt_moe_set_timing", "apt_moe_stage_times",
+    "apt_moe_set_timing", "apt_moe_stage_times", "apt_moe_route_noalloc",
 ]
 
 STAGES = ["router_scores", "router_select", "dispatch_count", "dispatch", "gather", "gate_up",
@@ -85,6 +85,7 @@ def lib():
         "apt_moe_set_gemv_max_tokens": ([hp, i32], i32),
         "apt_moe_set_timing": ([hp, i32], i32),
         "apt_moe_stage_times": ([hp, P], i32),
+        "apt_moe_route_noalloc": ([P, i32, P, P, P, i32, i32, i32, f32, P, P, P], i32),
     }
     for name, (argtypes, restype) in sig.items():
         fn = getattr(L, name)

@@ -197,6 +197,33 @@ enum {
 APT_API apt_status apt_moe_set_timing(apt_moe_handle *h, int enable);
 APT_API apt_status apt_moe_stage_times(apt_moe_handle *h, float *ms);
 
+/*
+ * Router without any allocation.  This entry point has no counterpart in the
+ * reference: it exists for callers that may not allocate device memory while
+ * they run -- code between a CUDA-graph-style memory plan and its replay, a
+ * host runtime whose memory pool owns every device byte, or an embedding
+ * (an FFI binding, a plugin) that receives only the buffers its host hands it.
+ * It computes exactly what apt_moe_route computes, with the same kernels, but
+ * takes every weight as a caller pointer and needs no handle.
+ *
+ * All pointers are device pointers: x [T,H] bf16, proj [E,H], scale [H],
+ * per_expert_scale [E] bf16 -> idx [T,K] int32, w [T,K] bf16.
+ * Its only scratch (the [T,E] f32 router scores) lives in a fixed array
+ * compiled into the library, APT_NOALLOC_MAX_SCORES floats (64 KiB) per GPU,
+ * held by every GPU that loads the library until the process exits; calls
+ * with T * num_experts above that limit return APT_ERR_UNSUPPORTED (and print
+ * the limit to stderr).  The first call on each device looks up that array's
+ * device address (no allocation); make that first call outside any stream
+ * capture.  Every call shares the array, so two calls that overlap on the GPU
+ * (different streams, or different host threads) race; serialise them.
+ * Requires hidden_size % 64 == 0, num_experts <= 256, top_k <= min(32, E).
+ */
+#define APT_NOALLOC_MAX_SCORES 16384
+APT_API apt_status apt_moe_route_noalloc(const uint16_t *x, int T, const uint16_t *proj,
+                                         const uint16_t *scale, const uint16_t *per_expert_scale,
+                                         int hidden_size, int num_experts, int top_k, float eps,
+                                         int32_t *idx, uint16_t *w, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
