@@ -47,7 +47,7 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks + throttle reasons sampled every 200 ms in the background."""
+    """nvidia-smi clocks + throttle reasons polled every ~200 ms from a thread."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -55,32 +55,28 @@ class ClockSampler:
 
     def __init__(self, index):
         self.index = index
-        self.proc = None
         self.lines = []
+        self.stop = threading.Event()
+
+    def _poll(self):
+        cmd = ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+               "--format=csv,noheader,nounits"]
+        while not self.stop.is_set():
+            try:
+                r = subprocess.run(cmd, capture_output=True, text=True, timeout=5)
+                self.lines.extend(l.strip() for l in r.stdout.splitlines() if l.strip())
+            except Exception:
+                return
+            self.stop.wait(0.2)
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except Exception:
-            self.proc = None
+        self.t = threading.Thread(target=self._poll, daemon=True)
+        self.t.start()
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self.stop.set()
+        self.t.join(timeout=10)
 
     def summary(self):
         sm, mx, reasons = [], None, set()
