@@ -1,18 +1,354 @@
-// gemm_sm100.cu -- prefill grouped expert GEMM (tcgen05 / TMEM / TMA).  [in progress]
+// gemm_sm100.cu -- prefill grouped expert GEMM on the 5th-generation tensor
+// cores (tcgen05 + TMEM), fed by TMA.
+//
+// Restates the gather_mm path of ESExperts::sparseForward
+// (aptransformer/ESExperts.mm:50-57) for prefill-sized token groups, after
+// the dispatch grouped the (token, k) rows by expert:
+//   gate_up: yp[r, j] = bf16( bf16(gelu(bf16(xp_r . Wg_j))) * bf16(xp_r . Wu_j) )
+//   down:    op[r, h] = bf16( yp_r . Wd_h )
+// with f32 accumulation in TMEM and the GeGLU fused into the epilogue.
+//
+// One persistent CTA per SM walks a static tile list (m-tile of 128 rows of
+// one expert x n-tile of the weights, n fastest) with three warp roles:
+//   warp 0      TMA producer: A (activation rows) and B (weight rows) tiles,
+//               128-byte swizzled, into a STAGES-deep shared-memory ring
+//   warp 1      owns TMEM (512 columns = two accumulators) and issues
+//               tcgen05.mma (M=128, N=BN, K=16) from one thread
+//   warps 2..5  epilogue: tcgen05.ld from TMEM, GeGLU / bf16 rounding,
+//               stores; overlaps the next tile's MMAs (double buffer)
+// For gate_up a B tile is BN2 gate rows followed by the BN2 matching up rows
+// (two TMA boxes), so each accumulator row holds g and u for the same j.
+// Every mbarrier wait is bounded; on expiry the kernel records an error code
+// and leaves through the normal exit (TMEM released).  No cluster multicast.
+#include <cuda.h>
+
 #include "common.cuh"
 #include "moe_internal.h"
+#include "sm100_ptx.cuh"
 
 namespace apt {
 
-cudaError_t gemm_init() { return cudaSuccess; }
-bool gemm_supported(int, int) { return false; }
-cudaError_t launch_gemm_gateup(const uint16_t *, const Dispatch &, const ExpertWeights &, int, int,
-                               int, int, uint16_t *, int32_t *, cudaStream_t, int *) {
-    return cudaErrorNotSupported;
+namespace {
+
+using namespace sm100;
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;                  // one 128-byte swizzle atom of bf16
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 512;
+constexpr int kAccStride = 256;          // TMEM columns between the two accumulators
+constexpr long long kWaitLimit = 4000000000LL;  // cycles (~2 s) before giving up
+constexpr int kMaxExperts = 256;
+
+enum { EPI_GATEUP = 0, EPI_DOWN = 1 };
+
+template <int BN>
+struct Smem {
+    static constexpr int A_BYTES = kBM * kBK * 2;
+    static constexpr int B_BYTES = BN * kBK * 2;
+};
+
+__device__ __forceinline__ void record_error(int32_t *err, int code, int where) {
+    if (atomicCAS(err, 0, code) == 0) err[1] = where;
 }
-cudaError_t launch_gemm_down(const uint16_t *, const Dispatch &, const ExpertWeights &, int, int,
-                             int, int, uint16_t *, int32_t *, cudaStream_t, int *) {
-    return cudaErrorNotSupported;
+
+// Tile t -> (expert, m-tile within expert, n-tile).  mtp = m-tile prefix.
+__device__ __forceinline__ void decode_tile(int t, int NT, const int *mtp, int E, int &e, int &mloc,
+                                            int &nt) {
+    const int mt = t / NT;
+    nt = t - mt * NT;
+    int lo = 0, hi = E - 1;  // first e with mtp[e+1] > mt
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (mtp[mid + 1] > mt) hi = mid;
+        else lo = mid + 1;
+    }
+    e = lo;
+    mloc = mt - mtp[e];
+}
+
+template <int EPI, int BN, int BN2, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const int32_t *__restrict__ counts, const int32_t *__restrict__ offsets, int E,
+                int Kdim, int I, int H, uint16_t *__restrict__ out, int out_ld,
+                int32_t *__restrict__ err) {
+    constexpr int A_BYTES = Smem<BN>::A_BYTES, B_BYTES = Smem<BN>::B_BYTES;
+    constexpr uint32_t IDESC = idesc_bf16_f32(kBM, BN);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                ~uintptr_t(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + STAGES * A_BYTES;
+    uint64_t *full = reinterpret_cast<uint64_t *>(sB + STAGES * B_BYTES);
+    uint64_t *empty = full + STAGES;
+    uint64_t *tfull = empty + STAGES;
+    uint64_t *tempty = tfull + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+    int *mtp = reinterpret_cast<int *>(tmem_slot + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 128);
+        }
+        fence_barrier_init();
+        tma_prefetch(&tmA);
+        tma_prefetch(&tmB);
+    }
+    if (warp == 0 && lane == 0) {
+        int acc = 0;
+        for (int e = 0; e < E; ++e) {
+            mtp[e] = acc;
+            acc += (counts[e] + kBM - 1) / kBM;
+        }
+        mtp[E] = acc;
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    fence_proxy_async();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int NT = (EPI == EPI_GATEUP) ? I / BN2 : H / BN;
+    const int tiles = mtp[E] * NT;
+    const int KB = Kdim / kBK;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int g = 0;
+            for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+                int e, mloc, nt;
+                decode_tile(t, NT, mtp, E, e, mloc, nt);
+                const int row0 = offsets[e] + mloc * kBM;
+                for (int kb = 0; kb < KB; ++kb, ++g) {
+                    const int s = g % STAGES;
+                    const uint32_t ph = (g / STAGES) & 1;
+                    if (!mbar_wait(&empty[s], ph ^ 1, kWaitLimit)) {
+                        record_error(err, 1, t);
+                        goto done;
+                    }
+                    mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
+                    tma_load_2d(sA + s * A_BYTES, &tmA, &full[s], kb * kBK, row0);
+                    if (EPI == EPI_GATEUP) {
+                        const int gate_row = e * 2 * I + nt * BN2;
+                        tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], kb * kBK, gate_row);
+                        tma_load_2d(sB + s * B_BYTES + BN2 * kBK * 2, &tmB, &full[s], kb * kBK,
+                                    gate_row + I);
+                    } else {
+                        tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], kb * kBK, e * H + nt * BN);
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int g = 0, i = 0;
+            for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+                const int buf = i & 1;
+                const uint32_t use = i >> 1;
+                if (!mbar_wait(&tempty[buf], (use & 1) ^ 1, kWaitLimit)) {
+                    record_error(err, 2, t);
+                    goto done;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + buf * kAccStride;
+                for (int kb = 0; kb < KB; ++kb, ++g) {
+                    const int s = g % STAGES;
+                    const uint32_t ph = (g / STAGES) & 1;
+                    if (!mbar_wait(&full[s], ph, kWaitLimit)) {
+                        record_error(err, 3, t);
+                        goto done;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + s * A_BYTES);
+                    const uint32_t b0 = smem_u32(sB + s * B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk)
+                        mma_bf16(d, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32),
+                                 IDESC, (kb | kk) != 0);
+                    mma_commit(&empty[s]);  // frees the stage once these MMAs finish
+                }
+                mma_commit(&tfull[buf]);    // accumulator ready for the epilogue
+            }
+        }
+    } else {
+        const int q = warp & 3;             // TMEM lane quarter this warp may read
+        const int r = q * 32 + lane;        // accumulator row of this thread
+        int i = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+            int e, mloc, nt;
+            decode_tile(t, NT, mtp, E, e, mloc, nt);
+            const int nvalid = counts[e] - mloc * kBM;
+            const int row = offsets[e] + mloc * kBM + r;
+            const int buf = i & 1;
+            const uint32_t use = i >> 1;
+            if (!mbar_wait(&tfull[buf], use & 1, kWaitLimit)) {
+                record_error(err, 4, t);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t taddr = tmem_base + buf * kAccStride + ((uint32_t)(q * 32) << 16);
+            if (EPI == EPI_GATEUP) {
+                uint16_t *dst = out + (size_t)row * out_ld + nt * BN2;
+#pragma unroll 1
+                for (int c = 0; c < BN2 / 8; ++c) {
+                    uint32_t gr[8], ur[8];
+                    tmem_ld8(taddr + c * 8, gr);
+                    tmem_ld8(taddr + BN2 + c * 8, ur);
+                    tmem_ld_wait();
+                    float y[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        y[j] = geglu_bf16(rbf(__uint_as_float(gr[j])), rbf(__uint_as_float(ur[j])));
+                    if (r < nvalid) {
+                        uint4 v;
+                        v.x = pack_bf2(y[0], y[1]);
+                        v.y = pack_bf2(y[2], y[3]);
+                        v.z = pack_bf2(y[4], y[5]);
+                        v.w = pack_bf2(y[6], y[7]);
+                        *reinterpret_cast<uint4 *>(dst + c * 8) = v;
+                    }
+                }
+            } else {
+                uint16_t *dst = out + (size_t)row * out_ld + nt * BN;
+#pragma unroll 1
+                for (int c = 0; c < BN / 8; ++c) {
+                    uint32_t a[8];
+                    tmem_ld8(taddr + c * 8, a);
+                    tmem_ld_wait();
+                    if (r < nvalid) {
+                        uint4 v;
+                        v.x = pack_bf2(__uint_as_float(a[0]), __uint_as_float(a[1]));
+                        v.y = pack_bf2(__uint_as_float(a[2]), __uint_as_float(a[3]));
+                        v.z = pack_bf2(__uint_as_float(a[4]), __uint_as_float(a[5]));
+                        v.w = pack_bf2(__uint_as_float(a[6]), __uint_as_float(a[7]));
+                        *reinterpret_cast<uint4 *>(dst + c * 8) = v;
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[buf]);
+        }
+    }
+done:
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------- host side
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2-D bf16 row-major [rows, inner] tensor, box {64, box_rows}, 128-byte swizzle.
+bool make_map(CUtensorMap *m, const void *base, uint64_t inner, uint64_t rows, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {inner, rows};
+    cuuint64_t strides[1] = {inner * 2};
+    cuuint32_t box[2] = {(cuuint32_t)kBK, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box,
+              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
+
+template <int EPI, int BN, int BN2, int STAGES>
+constexpr size_t smem_bytes() {
+    return 1024 + (size_t)STAGES * (Smem<BN>::A_BYTES + Smem<BN>::B_BYTES) + 8 * (2 * STAGES + 4) +
+           16 + 4 * (kMaxExperts + 1);
+}
+
+template <int EPI, int BN, int BN2, int STAGES>
+cudaError_t set_attr() {
+    return cudaFuncSetAttribute(moe_gemm_kernel<EPI, BN, BN2, STAGES>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)smem_bytes<EPI, BN, BN2, STAGES>());
+}
+
+template <int EPI, int BN, int BN2, int STAGES>
+cudaError_t launch(const CUtensorMap &a, const CUtensorMap &b, const Dispatch &d, int E, int Kdim,
+                   int I, int H, uint16_t *out, int out_ld, int32_t *err, cudaStream_t s) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    moe_gemm_kernel<EPI, BN, BN2, STAGES><<<sms, kThreads, smem_bytes<EPI, BN, BN2, STAGES>(), s>>>(
+        a, b, d.counts, d.offsets, E, Kdim, I, H, out, out_ld, err);
+    return cudaGetLastError();
+}
+
+// gate_up tile: BN2 gate + BN2 up rows; down tile: BN rows of W_down.
+constexpr int kGuStages = 5, kDnStages = 4;
+
+}  // namespace
+
+cudaError_t gemm_init() {
+    cudaError_t e;
+    if ((e = set_attr<EPI_GATEUP, 176, 88, kGuStages>())) return e;
+    if ((e = set_attr<EPI_GATEUP, 128, 64, kGuStages>())) return e;
+    if ((e = set_attr<EPI_DOWN, 256, 0, kDnStages>())) return e;
+    return set_attr<EPI_DOWN, 128, 0, kDnStages>();
+}
+
+bool gemm_supported(int H, int I) {
+    return encode_fn() != nullptr && H % 128 == 0 && (I % 88 == 0 || I % 64 == 0) && I % 64 == 0;
+}
+
+cudaError_t launch_gemm_gateup(const uint16_t *xp, const Dispatch &d, const ExpertWeights &w,
+                               int rows_cap, int H, int I, int E, uint16_t *yp, int32_t *err,
+                               cudaStream_t s, int *launches) {
+    if (E > kMaxExperts) return cudaErrorInvalidValue;
+    const int bn2 = (I % 88 == 0) ? 88 : 64;
+    CUtensorMap a, b;
+    if (!make_map(&a, xp, H, rows_cap, kBM) || !make_map(&b, w.gu, H, (uint64_t)E * 2 * I, bn2))
+        return cudaErrorInvalidValue;
+    cudaError_t e = (bn2 == 88)
+        ? launch<EPI_GATEUP, 176, 88, kGuStages>(a, b, d, E, H, I, H, yp, I, err, s)
+        : launch<EPI_GATEUP, 128, 64, kGuStages>(a, b, d, E, H, I, H, yp, I, err, s);
+    if (launches) ++*launches;
+    return e;
+}
+
+cudaError_t launch_gemm_down(const uint16_t *yp, const Dispatch &d, const ExpertWeights &w,
+                             int rows_cap, int H, int I, int E, uint16_t *op, int32_t *err,
+                             cudaStream_t s, int *launches) {
+    if (E > kMaxExperts) return cudaErrorInvalidValue;
+    const int bn = (H % 256 == 0) ? 256 : 128;
+    CUtensorMap a, b;
+    if (!make_map(&a, yp, I, rows_cap, kBM) || !make_map(&b, w.dn, I, (uint64_t)E * H, bn))
+        return cudaErrorInvalidValue;
+    cudaError_t e = (bn == 256)
+        ? launch<EPI_DOWN, 256, 0, kDnStages>(a, b, d, E, I, I, H, op, H, err, s)
+        : launch<EPI_DOWN, 128, 0, kDnStages>(a, b, d, E, I, I, H, op, H, err, s);
+    if (launches) ++*launches;
+    return e;
 }
 
 }  // namespace apt

@@ -1,0 +1,78 @@
+"""tcgen05 grouped-GEMM path (prefill-sized groups) vs the CPU oracle and vs
+the GEMV path.  The GEMM path is forced with set_gemv_max_tokens(0)."""
+import numpy as np
+import pytest
+import torch
+
+from tests.helpers import bf16_to_f32, block_close
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+import apertura_b200 as A  # noqa: E402
+from apertura_b200.synthetic import block_inputs, to_numpy_bits as _np  # noqa: E402
+
+DEV = torch.device("cuda", 0)
+TIGHT_REL = 2.0 ** -6
+
+
+def _block(d, T):
+    cfg = A.ESModelConfig(hidden_size=d["H"], num_experts=d["E"], top_k_experts=d["K"],
+                          moe_intermediate_size=d["I"], moe_sparse=True, max_tokens=T)
+    return A.MoEBlock(cfg, d["proj"], d["scale"], d["pes"], d["gate_up"], d["down"])
+
+
+def _run(blk, x, gemv_max):
+    blk.handle.set_gemv_max_tokens(gemv_max)
+    out, tk = blk.forward(x, return_routing=True)
+    torch.cuda.synchronize()
+    blk.handle.sync()  # raises if a bounded device wait gave up
+    return out, tk
+
+
+@pytest.mark.parametrize("shape,T", [((256, 32, 8, 128), 100), ((2816, 128, 8, 704), 48),
+                                     ((2816, 128, 8, 704), 300)])
+def test_gemm_vs_oracle(oracle, shape, T):
+    H, E, K, I = shape
+    d = block_inputs(T, seed=60 + T, device=DEV, H=H, E=E, K=K, I=I)
+    blk = _block(d, T)
+    out, tk = _run(blk, d["x"], 0)
+    ref = oracle.experts_sparse(_np(d["x"]), _np(d["gate_up"]), _np(d["down"]),
+                                tk.idx.cpu().numpy(), _np(tk.w))
+    got, refv = bf16_to_f32(_np(out)), bf16_to_f32(ref)
+    ok, ma, cos = block_close(got, refv)
+    assert ok and ma <= TIGHT_REL * np.abs(refv).max(), (ma, cos)
+
+
+def test_gemm_matches_gemv_zipf():
+    """Skewed routing (Zipf 1.1): hot experts span many m-tiles, cold ones one
+    partial tile; both paths must agree to a few bf16 ulps."""
+    T = 2048
+    d = block_inputs(T, seed=3, device=DEV, routing="zipf")
+    blk = _block(d, T)
+    a, tk = _run(blk, d["x"], 0)
+    a = a.clone()
+    b, tk2 = _run(blk, d["x"], 1 << 30)
+    assert torch.equal(tk.idx, tk2.idx)
+    fa, fb = bf16_to_f32(_np(a)), bf16_to_f32(_np(b))
+    ok, ma, cos = block_close(fa, fb)
+    assert ok and ma <= TIGHT_REL * np.abs(fb).max(), (ma, cos)
+    counts = blk.handle.last_counts().numpy()
+    assert counts.max() > 4 * 128  # the hot expert really spans several m-tiles
+
+
+def test_gemm_prefill_sample_vs_oracle(oracle):
+    """BASELINE config 3 shape (T=8192, Zipf): oracle on a sample of tokens."""
+    T = 8192
+    d = block_inputs(T, seed=9, device=DEV, routing="zipf")
+    blk = _block(d, T)
+    out, tk = _run(blk, d["x"], 0)
+    rng = np.random.default_rng(0)
+    rows = np.sort(rng.choice(T, 48, replace=False))
+    ref = oracle.experts_sparse(_np(d["x"][rows]), _np(d["gate_up"]), _np(d["down"]),
+                                tk.idx.cpu().numpy()[rows], _np(tk.w)[rows])
+    got, refv = bf16_to_f32(_np(out))[rows], bf16_to_f32(ref)
+    ok, ma, cos = block_close(got, refv)
+    assert ok and ma <= TIGHT_REL * np.abs(refv).max(), (ma, cos)
