@@ -27,7 +27,8 @@ struct apt_moe_handle {
     apt_moe_config cfg{};
     std::string err;
     int launches = 0;
-    int gemv_max_tokens = 64;
+    int gemv_max_tokens = 8;
+    bool gemv_tma = true;  // TMA-streamed bf16 GEMV (else the register-prefetch GEMV)
 
     // per-stage CUDA-event timing (apt_moe_set_timing / apt_moe_stage_times)
     bool timing = false;
@@ -50,6 +51,7 @@ struct apt_moe_handle {
     uint16_t *w_i = nullptr;
     int32_t *counts = nullptr, *offsets = nullptr, *perm = nullptr, *inv = nullptr;
     int32_t *active = nullptr, *n_active = nullptr, *errflag = nullptr;
+    int32_t *done = nullptr;    // fused decode router's completion counter (self-resetting)
     uint16_t *xp = nullptr, *yp = nullptr, *op = nullptr;
     uint16_t *Wd = nullptr;     // dense routing matrix [Tm,E]
     int32_t *idx2 = nullptr;    // dense pair lists [Pcap]
@@ -254,6 +256,7 @@ extern "C" apt_status apt_moe_create(const apt_moe_config *cfg, apt_moe_handle *
     ALLOC(active, E);
     ALLOC(n_active, 1);
     ALLOC(errflag, 4);
+    ALLOC(done, 1);
     ALLOC(xp, (size_t)h->Pcap * H);
     ALLOC(yp, (size_t)h->Pcap * I);
     ALLOC(op, (size_t)h->Pcap * H);
@@ -266,7 +269,9 @@ extern "C" apt_status apt_moe_create(const apt_moe_config *cfg, apt_moe_handle *
     if (e1 == cudaSuccess) e1 = router_init();
     if (e1 == cudaSuccess) e1 = gemv_init();
     if (e1 == cudaSuccess) e1 = gemm_init();
+    if (e1 == cudaSuccess) e1 = gemv_tma_init();
     if (e1 == cudaSuccess) e1 = cudaMemset(h->errflag, 0, 16);
+    if (e1 == cudaSuccess) e1 = cudaMemset(h->done, 0, 4);
     for (int i = 0; i < APT_STAGE_COUNT && e1 == cudaSuccess; ++i)
         for (int j = 0; j < 2 && e1 == cudaSuccess; ++j) e1 = cudaEventCreate(&h->ev[i][j]);
     if (e1 != cudaSuccess) {
@@ -282,7 +287,7 @@ extern "C" apt_status apt_moe_destroy(apt_moe_handle *h) {
     DeviceGuard g(h->cfg.device);
     void *ptrs[] = {h->proj, h->scale, h->pes, h->gu, h->dn, h->gu_q, h->dn_q, h->gu_s, h->gu_b,
                     h->dn_s, h->dn_b, h->scores, h->idx_i, h->w_i, h->counts, h->offsets,
-                    h->perm, h->inv, h->active, h->n_active, h->errflag, h->xp, h->yp, h->op,
+                    h->perm, h->inv, h->active, h->n_active, h->errflag, h->done, h->xp, h->yp, h->op,
                     h->Wd, h->idx2, h->w2, h->xin, h->xout};
     for (void *p : ptrs) dfree(p);
     for (int i = 0; i < APT_STAGE_COUNT; ++i)
@@ -449,11 +454,12 @@ apt_status check_T(apt_moe_handle *h, int T) {
 // idx/w: [T, Kp] pair lists (Kp = K for sparse, E for dense).
 apt_status run_experts(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
                        const uint16_t *w, int T, int Kp, bool quant, uint16_t *out,
-                       cudaStream_t s) {
+                       cudaStream_t s, bool dispatched = false) {
     const int H = h->cfg.hidden_size, E = h->cfg.num_experts, I = h->cfg.moe_intermediate_size;
     const int P = T * Kp;
     Dispatch d = h->disp();
-    STAGE(h, APT_STAGE_DISPATCH, s, launch_dispatch(idx, P, E, d, s, &h->launches));
+    if (!dispatched)
+        STAGE(h, APT_STAGE_DISPATCH, s, launch_dispatch(idx, P, E, d, s, &h->launches));
     ExpertWeights ew = weights_for(h, quant);
     const int max_rows = T;  // an expert appears at most once per token
     const bool gemm = !quant && T > h->gemv_max_tokens && gemm_supported(H, I);
@@ -464,6 +470,11 @@ apt_status run_experts(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
                                        &h->launches));
         STAGE(h, APT_STAGE_DOWN, s, launch_gemm_down(h->yp, d, ew, rows_cap, H, I, E, h->op, h->errflag, s,
                                      &h->launches));
+    } else if (!quant && h->gemv_tma && gemv_tma_supported(H, I)) {
+        STAGE(h, APT_STAGE_GATE_UP, s, launch_gemv_tma_gateup(x, Kp, d, ew, H, I, E, max_rows, h->yp,
+                                                              h->errflag, s, &h->launches));
+        STAGE(h, APT_STAGE_DOWN, s, launch_gemv_tma_down(h->yp, d, ew, H, I, E, Kp, max_rows, h->op,
+                                                         h->errflag, s, &h->launches));
     } else {
         STAGE(h, APT_STAGE_GATE_UP, s, launch_gemv_gateup(x, Kp, d, ew, H, I, E, max_rows, h->yp, s, &h->launches));
         STAGE(h, APT_STAGE_DOWN, s, launch_gemv_down(h->yp, d, ew, H, I, E, max_rows, h->op, s, &h->launches));
@@ -579,6 +590,17 @@ extern "C" apt_status apt_moe_forward(apt_moe_handle *h, const uint16_t *x_route
     const int H = h->cfg.hidden_size, E = h->cfg.num_experts, K = h->cfg.top_k_experts;
     int32_t *idx = idx_out ? idx_out : h->idx_i;
     uint16_t *w = w_out ? w_out : h->w_i;
+    if (h->cfg.moe_sparse && router_dispatch_fusable(T, H, E, K)) {
+        // decode: router + top-k + dispatch in one launch
+        const bool quant = h->qbits > 0;
+        if (!quant && !h->gu) return fail(h, APT_ERR_STATE, "expert weights not loaded");
+        if (quant && !h->gu_q) return fail(h, APT_ERR_STATE, "quantised expert weights not loaded");
+        STAGE(h, APT_STAGE_ROUTER_SCORES, s,
+              launch_router_dispatch(x_router, h->proj, h->scale, h->pes, T, H, E, K,
+                                     h->cfg.rms_norm_eps, h->scores, idx, w, h->disp(), h->done,
+                                     s, &h->launches));
+        return run_experts(h, x_experts, idx, w, T, K, quant, out, s, true);
+    }
     STAGE(h, APT_STAGE_ROUTER_SCORES, s, launch_router_scores(x_router, h->proj, h->scale, T, H, E, h->cfg.rms_norm_eps,
                                      h->scores, s, &h->launches));
     if (h->cfg.moe_sparse) {

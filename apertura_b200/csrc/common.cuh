@@ -57,6 +57,16 @@ __device__ __forceinline__ float geglu_bf16(float g_bf, float u_bf) {
     return rbf(__fmul_rn(ge, u_bf));
 }
 
+// ---------------------------------------------------------------- PDL
+
+// Programmatic dependent launch: wait until the preceding kernel on the
+// stream has completed and its writes are visible (no-op when this kernel
+// was launched without the attribute), and let the next kernel start early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- warp helpers
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -11,6 +11,7 @@
 // The combine restates ESExperts.mm:58-59 (sum over k of w * out): each
 // product is rounded to bf16, accumulated in f32 in k order, rounded once.
 #include "common.cuh"
+#include "launch_util.h"
 #include "moe_internal.h"
 
 namespace apt {
@@ -39,6 +40,8 @@ dispatch_kernel(const int32_t *__restrict__ idx, int P, int E, const int32_t *__
     __shared__ int s_off, s_act;
     __shared__ int warp_tot[kDispThreads / 32];
     const int e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_trigger();
+    pdl_wait();
     if (tid == 0) {
         s_off = 0;
         s_act = 0;
@@ -108,6 +111,8 @@ __global__ void gather_rows_kernel(const uint16_t *__restrict__ x, int H, int K,
                                    const int32_t *__restrict__ perm,
                                    const int32_t *__restrict__ offsets, int E, int max_rows,
                                    uint16_t *__restrict__ xp) {
+    pdl_trigger();
+    pdl_wait();
     const int rows = offsets[E];
     const int lane = threadIdx.x & 31;
     for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows && row < max_rows;
@@ -119,22 +124,46 @@ __global__ void gather_rows_kernel(const uint16_t *__restrict__ x, int H, int K,
     }
 }
 
-// One CTA per token; each thread owns 8 consecutive hidden elements.
+// One CTA per token; each thread owns 8 consecutive hidden elements.  The
+// token's K (idx, w, inv) triples are read into shared memory first, so the
+// K row loads that follow are independent and all in flight at once.
+constexpr int kMaxK = 256;
+
 __global__ void combine_kernel(const uint16_t *__restrict__ op, const int32_t *__restrict__ idx,
                                const uint16_t *__restrict__ w, const int32_t *__restrict__ inv,
                                int T, int K, int H, uint16_t *__restrict__ out) {
+    __shared__ int s_row[kMaxK];
+    __shared__ float s_w[kMaxK];
     const int t = blockIdx.x;
+    pdl_trigger();
+    pdl_wait();
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        const int p = t * K + k;
+        const bool live = idx[p] >= 0;
+        s_row[k] = live ? inv[p] : -1;
+        s_w[k] = live ? bf2f(w[p]) : 0.f;
+    }
+    __syncthreads();
     for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
         float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        for (int k = 0; k < K; ++k) {
-            const int p = t * K + k;
-            if (idx[p] < 0) continue;
-            const float wk = bf2f(w[p]);
-            const uint4 o = *reinterpret_cast<const uint4 *>(op + (size_t)inv[p] * H + v * 8);
-            float f[8];
-            unpack8(o, f);
+        constexpr int B = 8;  // rows in flight per batch
+        for (int k0 = 0; k0 < K; k0 += B) {
+            uint4 o[B];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(acc[j], rbf(__fmul_rn(wk, f[j])));
+            for (int j = 0; j < B; ++j) {
+                const int row = (k0 + j < K) ? s_row[k0 + j] : -1;
+                if (row >= 0) o[j] = *reinterpret_cast<const uint4 *>(op + (size_t)row * H + v * 8);
+            }
+#pragma unroll
+            for (int j = 0; j < B; ++j) {
+                const int row = (k0 + j < K) ? s_row[k0 + j] : -1;
+                if (row < 0) continue;
+                const float wk = s_w[k0 + j];
+                float f[8];
+                unpack8(o[j], f);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) acc[q] = __fadd_rn(acc[q], rbf(__fmul_rn(wk, f[q])));
+            }
         }
         uint4 r;
         r.x = pack_bf2(acc[0], acc[1]);
@@ -157,31 +186,32 @@ cudaError_t launch_count(const int32_t *idx, int P, int E, int32_t *counts, cuda
 
 cudaError_t launch_dispatch(const int32_t *idx, int P, int E, const Dispatch &d, cudaStream_t s,
                             int *launches) {
-    dispatch_kernel<<<E, kDispThreads, 0, s>>>(idx, P, E, d.counts, d.offsets, d.perm, d.inv,
-                                               d.active, d.n_active);
+    cudaError_t err = launch_ex(dispatch_kernel, dim3(E), dim3(kDispThreads), 0, s, true, idx, P, E,
+                                (const int32_t *)d.counts, d.offsets, d.perm, d.inv, d.active,
+                                d.n_active);
     if (launches) ++*launches;
-    return cudaGetLastError();
+    return err;
 }
 
 cudaError_t launch_gather_rows(const uint16_t *x, int H, int K, int E, const Dispatch &d,
                                int max_rows, uint16_t *xp, cudaStream_t s, int *launches) {
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int sms = num_sms(current_device());
     const int blocks = min(sms * 8, (max_rows + 7) / 8);
-    gather_rows_kernel<<<blocks > 0 ? blocks : 1, 256, 0, s>>>(x, H, K, d.perm, d.offsets, E,
-                                                                 max_rows, xp);
+    cudaError_t err = launch_ex(gather_rows_kernel, dim3(blocks > 0 ? blocks : 1), dim3(256), 0, s,
+                                true, x, H, K, (const int32_t *)d.perm,
+                                (const int32_t *)d.offsets, E, max_rows, xp);
     if (launches) ++*launches;
-    return cudaGetLastError();
+    return err;
 }
 
 cudaError_t launch_combine(const uint16_t *op, const int32_t *idx, const uint16_t *w,
                            const Dispatch &d, int T, int K, int H, uint16_t *out, cudaStream_t s,
                            int *launches) {
     const int threads = min(512, ((H / 8 + 31) / 32) * 32);
-    combine_kernel<<<T, threads, 0, s>>>(op, idx, w, d.inv, T, K, H, out);
+    cudaError_t err = launch_ex(combine_kernel, dim3(T), dim3(threads), 0, s, true, op, idx, w,
+                                (const int32_t *)d.inv, T, K, H, out);
     if (launches) ++*launches;
-    return cudaGetLastError();
+    return err;
 }
 
 }  // namespace apt

@@ -24,6 +24,7 @@
 
 #include "common.cuh"
 #include "moe_internal.h"
+#include "launch_util.h"
 #include "sm100_ptx.cuh"
 
 namespace apt {
@@ -101,6 +102,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         tma_prefetch(&tmA);
         tma_prefetch(&tmB);
     }
+    pdl_wait();  // dispatch / gather / gate_up output this kernel reads is complete
     if (warp == 0 && lane == 0) {
         int acc = 0;
         for (int e = 0; e < E; ++e) {
@@ -117,6 +119,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_trigger();
     const int NT = (EPI == EPI_GATEUP) ? I / BN2 : H / BN;
     const int tiles = mtp[E] * NT;
     const int KB = Kdim / kBK;
@@ -248,36 +251,9 @@ done:
 
 // ---------------------------------------------------------------- host side
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
-                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
-                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    }
-    return fn;
-}
-
 // 2-D bf16 row-major [rows, inner] tensor, box {64, box_rows}, 128-byte swizzle.
 bool make_map(CUtensorMap *m, const void *base, uint64_t inner, uint64_t rows, uint32_t box_rows) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return false;
-    cuuint64_t dims[2] = {inner, rows};
-    cuuint64_t strides[1] = {inner * 2};
-    cuuint32_t box[2] = {(cuuint32_t)kBK, box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box,
-              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
-           CUDA_SUCCESS;
+    return bf16_map_2d(m, base, inner, rows, kBK, box_rows, true);
 }
 
 template <int EPI, int BN, int BN2, int STAGES>
@@ -296,12 +272,10 @@ cudaError_t set_attr() {
 template <int EPI, int BN, int BN2, int STAGES>
 cudaError_t launch(const CUtensorMap &a, const CUtensorMap &b, const Dispatch &d, int E, int Kdim,
                    int I, int H, uint16_t *out, int out_ld, int32_t *err, cudaStream_t s) {
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    moe_gemm_kernel<EPI, BN, BN2, STAGES><<<sms, kThreads, smem_bytes<EPI, BN, BN2, STAGES>(), s>>>(
-        a, b, d.counts, d.offsets, E, Kdim, I, H, out, out_ld, err);
-    return cudaGetLastError();
+    const int sms = num_sms(current_device());
+    return launch_ex(moe_gemm_kernel<EPI, BN, BN2, STAGES>, dim3(sms), dim3(kThreads),
+                     smem_bytes<EPI, BN, BN2, STAGES>(), s, true, a, b, d.counts, d.offsets, E,
+                     Kdim, I, H, out, out_ld, err);
 }
 
 // gate_up tile: BN2 gate + BN2 up rows; down tile: BN rows of W_down.
@@ -318,7 +292,7 @@ cudaError_t gemm_init() {
 }
 
 bool gemm_supported(int H, int I) {
-    return encode_fn() != nullptr && H % 128 == 0 && (I % 88 == 0 || I % 64 == 0) && I % 64 == 0;
+    return encode_tiled_fn() != nullptr && H % 128 == 0 && (I % 88 == 0 || I % 64 == 0) && I % 64 == 0;
 }
 
 cudaError_t launch_gemm_gateup(const uint16_t *xp, const Dispatch &d, const ExpertWeights &w,

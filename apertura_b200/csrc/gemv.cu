@@ -21,6 +21,7 @@
 // processed in chunks of up to 8; the chunk's token count selects a
 // specialised inner loop.
 #include "common.cuh"
+#include "launch_util.h"
 #include "moe_internal.h"
 
 namespace apt {
@@ -241,8 +242,10 @@ __device__ __forceinline__ void gateup_chunk(const GemvArgs &a, int e, int j0, c
     }
 }
 
-template <class F, int RJ, int U>
+template <class F, int RJ, int U, int NTMAX>
 __global__ void __launch_bounds__(kWarps * 32) gemv_gateup(GemvArgs a) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ __align__(16) float xs[];
     __shared__ const uint16_t *src[kTokChunk];
     if ((int)blockIdx.y >= *a.n_active) return;
@@ -258,14 +261,17 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_gateup(GemvArgs a) {
         __syncthreads();
         stage_rows<F::EPL>(xs, src, nt, a.H);
         __syncthreads();
-        if (nt == 1)
+        // only the token counts this launch can see are instantiated, so the
+        // register budget follows the call's T, not the worst case
+        if (nt == 1) {
             gateup_chunk<F, 1, RJ, U>(a, e, j0, xs, c, nt, base + tc);
-        else if (nt == 2)
-            gateup_chunk<F, 2, RJ, U>(a, e, j0, xs, c, nt, base + tc);
-        else if (nt <= 4)
-            gateup_chunk<F, 4, RJ, U2>(a, e, j0, xs, c, nt, base + tc);
-        else
-            gateup_chunk<F, 8, RJ, U2>(a, e, j0, xs, c, nt, base + tc);
+        } else if (nt == 2) {
+            if constexpr (NTMAX >= 2) gateup_chunk<F, 2, RJ, U>(a, e, j0, xs, c, nt, base + tc);
+        } else if (nt <= 4) {
+            if constexpr (NTMAX >= 4) gateup_chunk<F, 4, RJ, U2>(a, e, j0, xs, c, nt, base + tc);
+        } else {
+            if constexpr (NTMAX >= 8) gateup_chunk<F, 8, RJ, U2>(a, e, j0, xs, c, nt, base + tc);
+        }
         __syncthreads();
     }
 }
@@ -293,8 +299,10 @@ __device__ __forceinline__ void down_chunk(const GemvArgs &a, int e, int h0, con
     }
 }
 
-template <class F, int R, int U>
+template <class F, int R, int U, int NTMAX>
 __global__ void __launch_bounds__(kWarps * 32) gemv_down(GemvArgs a) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ __align__(16) float ys[];
     __shared__ const uint16_t *src[kTokChunk];
     if ((int)blockIdx.y >= *a.n_active) return;
@@ -309,28 +317,29 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_down(GemvArgs a) {
         __syncthreads();
         stage_rows<F::EPL>(ys, src, nt, a.I);
         __syncthreads();
-        if (nt == 1)
+        if (nt == 1) {
             down_chunk<F, 1, R, U>(a, e, h0, ys, c, nt, base + tc);
-        else if (nt == 2)
-            down_chunk<F, 2, R, U>(a, e, h0, ys, c, nt, base + tc);
-        else if (nt <= 4)
-            down_chunk<F, 4, R, U2>(a, e, h0, ys, c, nt, base + tc);
-        else
-            down_chunk<F, 8, R, U2>(a, e, h0, ys, c, nt, base + tc);
+        } else if (nt == 2) {
+            if constexpr (NTMAX >= 2) down_chunk<F, 2, R, U>(a, e, h0, ys, c, nt, base + tc);
+        } else if (nt <= 4) {
+            if constexpr (NTMAX >= 4) down_chunk<F, 4, R, U2>(a, e, h0, ys, c, nt, base + tc);
+        } else {
+            if constexpr (NTMAX >= 8) down_chunk<F, 8, R, U2>(a, e, h0, ys, c, nt, base + tc);
+        }
         __syncthreads();
     }
 }
 
 // ---------------------------------------------------------------- launch plumbing
 
-template <class F, int RJ, int U>
+template <class F, int RJ, int U, int NTMAX>
 cudaError_t set_gateup_attr() {
-    return cudaFuncSetAttribute(gemv_gateup<F, RJ, U>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    return cudaFuncSetAttribute(gemv_gateup<F, RJ, U, NTMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 200 * 1024);
 }
-template <class F, int R, int U>
+template <class F, int R, int U, int NTMAX>
 cudaError_t set_down_attr() {
-    return cudaFuncSetAttribute(gemv_down<F, R, U>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    return cudaFuncSetAttribute(gemv_down<F, R, U, NTMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 200 * 1024);
 }
 
@@ -340,20 +349,26 @@ cudaError_t set_down_attr() {
 template <class F>
 cudaError_t init_fmt() {
     cudaError_t e;
-    if ((e = set_gateup_attr<F, 1, 4>())) return e;
-    if ((e = set_gateup_attr<F, 2, 2>())) return e;
-    if ((e = set_down_attr<F, 1, 4>())) return e;
-    return set_down_attr<F, 4, 2>();
+    if ((e = set_gateup_attr<F, 1, 4, 1>())) return e;
+    if ((e = set_gateup_attr<F, 1, 4, 2>())) return e;
+    if ((e = set_gateup_attr<F, 2, 2, 4>())) return e;
+    if ((e = set_gateup_attr<F, 2, 2, 8>())) return e;
+    if ((e = set_down_attr<F, 1, 4, 1>())) return e;
+    if ((e = set_down_attr<F, 1, 4, 2>())) return e;
+    if ((e = set_down_attr<F, 4, 2, 4>())) return e;
+    return set_down_attr<F, 4, 2, 8>();
 }
 
 template <class F>
 void launch_gateup_fmt(const GemvArgs &a, int E, int max_rows, size_t smem, cudaStream_t s) {
     if (max_rows <= 2) {
         dim3 grid(a.I / (kWarps * 4 * 1), E);
-        gemv_gateup<F, 1, 4><<<grid, kWarps * 32, smem, s>>>(a);
+        if (max_rows <= 1) launch_ex(gemv_gateup<F, 1, 4, 1>, grid, dim3(kWarps * 32), smem, s, true, a);
+        else launch_ex(gemv_gateup<F, 1, 4, 2>, grid, dim3(kWarps * 32), smem, s, true, a);
     } else {
         dim3 grid(a.I / (kWarps * 4 * 2), E);
-        gemv_gateup<F, 2, 2><<<grid, kWarps * 32, smem, s>>>(a);
+        if (max_rows <= 4) launch_ex(gemv_gateup<F, 2, 2, 4>, grid, dim3(kWarps * 32), smem, s, true, a);
+        else launch_ex(gemv_gateup<F, 2, 2, 8>, grid, dim3(kWarps * 32), smem, s, true, a);
     }
 }
 
@@ -361,10 +376,12 @@ template <class F>
 void launch_down_fmt(const GemvArgs &a, int E, int max_rows, size_t smem, cudaStream_t s) {
     if (max_rows <= 2) {
         dim3 grid(a.H / (kWarps * 4 * 1), E);
-        gemv_down<F, 1, 4><<<grid, kWarps * 32, smem, s>>>(a);
+        if (max_rows <= 1) launch_ex(gemv_down<F, 1, 4, 1>, grid, dim3(kWarps * 32), smem, s, true, a);
+        else launch_ex(gemv_down<F, 1, 4, 2>, grid, dim3(kWarps * 32), smem, s, true, a);
     } else {
         dim3 grid(a.H / (kWarps * 4 * 4), E);
-        gemv_down<F, 4, 2><<<grid, kWarps * 32, smem, s>>>(a);
+        if (max_rows <= 4) launch_ex(gemv_down<F, 4, 2, 4>, grid, dim3(kWarps * 32), smem, s, true, a);
+        else launch_ex(gemv_down<F, 4, 2, 8>, grid, dim3(kWarps * 32), smem, s, true, a);
     }
 }
 

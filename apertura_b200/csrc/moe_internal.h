@@ -30,6 +30,13 @@ cudaError_t launch_router_scores(const uint16_t *x, const uint16_t *proj, const 
 cudaError_t launch_router_select(const float *scores, const uint16_t *pes, int T, int E, int K,
                                  int32_t *idx, uint16_t *w, int32_t *counts, cudaStream_t s,
                                  int *launches);
+// Decode-sized fused router + dispatch (one launch): writes idx/w and the full
+// Dispatch.  `done` is a zero-initialised device counter the kernel resets.
+bool router_dispatch_fusable(int T, int H, int E, int K);
+cudaError_t launch_router_dispatch(const uint16_t *x, const uint16_t *proj, const uint16_t *scale,
+                                   const uint16_t *pes, int T, int H, int E, int K, float eps,
+                                   float *scores, int32_t *idx, uint16_t *w, const Dispatch &d,
+                                   int32_t *done, cudaStream_t s, int *launches);
 // dense routeWeights scatter: W [T,E] = 0 except W[t, idx[t,k]] = w[t,k]
 cudaError_t launch_scatter_dense(const int32_t *idx, const uint16_t *w, int T, int E, int K,
                                  uint16_t *W, cudaStream_t s, int *launches);
@@ -64,6 +71,16 @@ cudaError_t launch_gemv_gateup(const uint16_t *x, int K, const Dispatch &d, cons
 cudaError_t launch_gemv_down(const uint16_t *yp, const Dispatch &d, const ExpertWeights &w, int H,
                              int I, int E, int max_rows_per_expert, uint16_t *op, cudaStream_t s,
                              int *launches);
+
+// ---- decode GEMV with TMA-streamed bf16 weights (gemv_tma.cu)
+cudaError_t gemv_tma_init();
+bool gemv_tma_supported(int H, int I);
+cudaError_t launch_gemv_tma_gateup(const uint16_t *x, int K, const Dispatch &d,
+                                   const ExpertWeights &w, int H, int I, int E, int max_rows,
+                                   uint16_t *yp, int32_t *err, cudaStream_t s, int *launches);
+cudaError_t launch_gemv_tma_down(const uint16_t *yp, const Dispatch &d, const ExpertWeights &w,
+                                 int H, int I, int E, int max_k, int max_rows, uint16_t *op, int32_t *err,
+                                 cudaStream_t s, int *launches);
 
 // ---- prefill grouped GEMM (gemm_sm100.cu), bf16 tcgen05 tiles
 struct GemmPlan;  // opaque, owns tensor maps

@@ -13,6 +13,7 @@
 // register-tiled f32 kernel for prefill-sized T (proj and x tiles reused from
 // shared memory).  The selection kernel runs one warp per token.
 #include "common.cuh"
+#include "launch_util.h"
 #include "moe_internal.h"
 
 namespace apt {
@@ -21,6 +22,7 @@ namespace {
 
 constexpr int kSmallTok = 8;     // tokens staged per CTA in the decode kernel
 constexpr int kSmallWarps = 4;   // experts per CTA in the decode kernel
+constexpr int kSmallThreads = 256;  // 8 warps: 4 experts x 2 token groups
 
 // r_t = 1/sqrt(mean(x_t^2) + eps) for one token, computed by one warp.
 __device__ __forceinline__ float token_rrms(const uint16_t *xr, int H, float eps, int lane) {
@@ -42,67 +44,107 @@ __device__ __forceinline__ float router_h(float x, float r, float sc, float root
     return __fmul_rn(__fmul_rn(__fmul_rn(x, r), sc), root);
 }
 
-__global__ void __launch_bounds__(kSmallWarps * 32)
-router_scores_small(const uint16_t *__restrict__ x, const uint16_t *__restrict__ proj,
-                    const uint16_t *__restrict__ scale, int T, int H, int E, float eps,
-                    float root, float *__restrict__ scores) {
-    extern __shared__ float hs[];  // [kSmallTok][H]
-    __shared__ float rs[kSmallTok];
+// Scores of experts [blockIdx.x*4, +4) for tokens [blockIdx.y*8, +8).  All
+// global reads the phase needs (the warp's proj row, the scale vector and its
+// tokens' rows) are issued before any is consumed, so the phase costs one
+// memory round trip; h is then staged in shared memory for the dot products.
+constexpr int kMaxVec = 12;  // H <= 12 * 256
+
+__device__ __forceinline__ void scores_small_block(const uint16_t *__restrict__ x,
+                                                   const uint16_t *__restrict__ proj,
+                                                   const uint16_t *__restrict__ scale, int T,
+                                                   int H, int E, float eps, float root,
+                                                   float *__restrict__ scores, float *hs) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int e = blockIdx.x * kSmallWarps + warp;
-    const uint16_t *pr = proj + (size_t)(e < E ? e : 0) * H;
-    for (int t0 = 0; t0 < T; t0 += kSmallTok) {
-        const int nt = min(kSmallTok, T - t0);
-        for (int t = warp; t < nt; t += kSmallWarps)
-            {
-                float r = token_rrms(x + (size_t)(t0 + t) * H, H, eps, lane);
-                if (lane == 0) rs[t] = r;
+    const int e = blockIdx.x * kSmallWarps + (warp & (kSmallWarps - 1));
+    const int tg = warp / kSmallWarps;  // token group of this warp in the dot phase
+    const int t0 = blockIdx.y * kSmallTok;
+    const int nt = min(kSmallTok, T - t0);
+    const int nv = H / 256;
+    uint4 pv[kMaxVec];
+    const uint16_t *pr = proj + (size_t)(e < E ? e : 0) * H + lane * 8;
+#pragma unroll
+    for (int i = 0; i < kMaxVec; ++i)
+        if (i < nv) pv[i] = __ldg(reinterpret_cast<const uint4 *>(pr + i * 256));
+    if (warp < nt) {  // warp w stages token w
+        const uint16_t *xr = x + (size_t)(t0 + warp) * H + lane * 8;
+        uint4 xv[kMaxVec], sv[kMaxVec];
+#pragma unroll
+        for (int i = 0; i < kMaxVec; ++i)
+            if (i < nv) {
+                xv[i] = __ldg(reinterpret_cast<const uint4 *>(xr + i * 256));
+                sv[i] = __ldg(reinterpret_cast<const uint4 *>(scale + i * 256 + lane * 8));
             }
-        __syncthreads();
-        const int vecs = H / 8;
-        for (int v = threadIdx.x; v < nt * vecs; v += blockDim.x) {
-            const int t = v / vecs, i = (v - t * vecs) * 8;
-            uint4 xv = *reinterpret_cast<const uint4 *>(x + (size_t)(t0 + t) * H + i);
-            uint4 sv = *reinterpret_cast<const uint4 *>(scale + i);
-            float xf[8], sf[8];
-            unpack8(xv, xf);
-            unpack8(sv, sf);
-            float *dst = hs + t * H + i;
+        float ss = 0.f;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) dst[j] = router_h(xf[j], rs[t], sf[j], root);
-        }
-        __syncthreads();
-        if (e < E) {
-            float acc[kSmallTok];
+        for (int i = 0; i < kMaxVec; ++i)
+            if (i < nv) {
+                float f[8];
+                unpack8(xv[i], f);
 #pragma unroll
-            for (int t = 0; t < kSmallTok; ++t) acc[t] = 0.f;
-            for (int i = lane * 8; i < H; i += 256) {
+                for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+            }
+        ss = warp_sum(ss);
+        const float r = 1.0f / sqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / (float)H), eps));
+        float *dst = hs + warp * H + lane * 8;
+#pragma unroll
+        for (int i = 0; i < kMaxVec; ++i)
+            if (i < nv) {
+                float f[8], sf[8], hv[8];
+                unpack8(xv[i], f);
+                unpack8(sv[i], sf);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) hv[j] = router_h(f[j], r, sf[j], root);
+                *reinterpret_cast<float4 *>(dst + i * 256) = make_float4(hv[0], hv[1], hv[2], hv[3]);
+                *reinterpret_cast<float4 *>(dst + i * 256 + 4) = make_float4(hv[4], hv[5], hv[6], hv[7]);
+            }
+    }
+    __syncthreads();
+    constexpr int TPW = kSmallTok / (kSmallThreads / 32 / kSmallWarps);  // tokens per warp
+    if (e < E) {
+        float acc[TPW];
+#pragma unroll
+        for (int q = 0; q < TPW; ++q) acc[q] = 0.f;
+#pragma unroll
+        for (int i = 0; i < kMaxVec; ++i)
+            if (i < nv) {
                 float p[8];
-                unpack8(*reinterpret_cast<const uint4 *>(pr + i), p);
+                unpack8(pv[i], p);
 #pragma unroll
-                for (int t = 0; t < kSmallTok; ++t) {
+                for (int q = 0; q < TPW; ++q) {
+                    const int t = tg + q * (kSmallThreads / 32 / kSmallWarps);
                     if (t < nt) {
-                        const float4 a = *reinterpret_cast<const float4 *>(hs + t * H + i);
-                        const float4 b = *reinterpret_cast<const float4 *>(hs + t * H + i + 4);
-                        acc[t] = fmaf(p[0], a.x, acc[t]);
-                        acc[t] = fmaf(p[1], a.y, acc[t]);
-                        acc[t] = fmaf(p[2], a.z, acc[t]);
-                        acc[t] = fmaf(p[3], a.w, acc[t]);
-                        acc[t] = fmaf(p[4], b.x, acc[t]);
-                        acc[t] = fmaf(p[5], b.y, acc[t]);
-                        acc[t] = fmaf(p[6], b.z, acc[t]);
-                        acc[t] = fmaf(p[7], b.w, acc[t]);
+                        const float *hr = hs + t * H + i * 256 + lane * 8;
+                        const float4 a4 = *reinterpret_cast<const float4 *>(hr);
+                        const float4 b4 = *reinterpret_cast<const float4 *>(hr + 4);
+                        float s2 = acc[q];
+                        s2 = fmaf(p[0], a4.x, s2);
+                        s2 = fmaf(p[1], a4.y, s2);
+                        s2 = fmaf(p[2], a4.z, s2);
+                        s2 = fmaf(p[3], a4.w, s2);
+                        s2 = fmaf(p[4], b4.x, s2);
+                        s2 = fmaf(p[5], b4.y, s2);
+                        s2 = fmaf(p[6], b4.z, s2);
+                        s2 = fmaf(p[7], b4.w, s2);
+                        acc[q] = s2;
                     }
                 }
             }
 #pragma unroll
-            for (int t = 0; t < kSmallTok; ++t) {
-                float s = warp_sum(acc[t]);
-                if (lane == 0 && t < nt) scores[(size_t)(t0 + t) * E + e] = s;
-            }
+        for (int q = 0; q < TPW; ++q) {
+            const int t = tg + q * (kSmallThreads / 32 / kSmallWarps);
+            const float v = warp_sum(acc[q]);
+            if (lane == 0 && t < nt) scores[(size_t)(t0 + t) * E + e] = v;
         }
-        __syncthreads();
     }
+}
+
+__global__ void __launch_bounds__(kSmallThreads)
+router_scores_small(const uint16_t *__restrict__ x, const uint16_t *__restrict__ proj,
+                    const uint16_t *__restrict__ scale, int T, int H, int E, float eps,
+                    float root, float *__restrict__ scores) {
+    extern __shared__ float hs[];  // [kSmallTok][H]
+    scores_small_block(x, proj, scale, T, H, E, eps, root, scores, hs);
 }
 
 // Register-tiled f32 GEMM: CTA = 64 tokens x 64 experts, 256 threads, each
@@ -180,20 +222,18 @@ router_scores_tiled(const uint16_t *__restrict__ x, const uint16_t *__restrict__
 
 constexpr int kMaxPerLane = 8;  // E <= 256
 
-// One warp per token: softmax, top-K (descending prob, lower id on ties),
-// renormalise, per-expert scale, bf16.
-__global__ void router_select(const float *__restrict__ scores, const uint16_t *__restrict__ pes,
-                              int T, int E, int K, int32_t *__restrict__ idx,
-                              uint16_t *__restrict__ w, int32_t *__restrict__ counts) {
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (warp >= T) return;
-    const float *sr = scores + (size_t)warp * E;
+// Softmax, top-K (descending prob, lower id on ties), renormalise and
+// per-expert scale for one token, by one warp.  Lanes k < K return the k-th
+// choice in (sel_e, wk); other lanes return sel_e = -1.
+__device__ __forceinline__ void select_token(const float *__restrict__ sr,
+                                             const uint16_t *__restrict__ pes, int E, int K,
+                                             int lane, int &sel_e_out, float &wk_out) {
     float p[kMaxPerLane];
     float m = -INFINITY;
 #pragma unroll
     for (int j = 0; j < kMaxPerLane; ++j) {
         const int e = lane + 32 * j;
-        p[j] = (e < E) ? sr[e] : -INFINITY;
+        p[j] = (e < E) ? __ldcg(sr + e) : -INFINITY;  // written by other CTAs
         m = fmaxf(m, p[j]);
     }
     m = warp_max(m);
@@ -212,11 +252,10 @@ __global__ void router_select(const float *__restrict__ scores, const uint16_t *
     }
     float sum = 0.f;
     float sel_p = 0.f;
-    int sel_e = 0;
+    int sel_e = -1;
     unsigned taken = 0;
     for (int k = 0; k < K; ++k) {
-        // lane-local best among untaken
-        float bp = -2.f;
+        float bp = -2.f;  // lane-local best among untaken
         int be = 0x7fffffff;
 #pragma unroll
         for (int j = 0; j < kMaxPerLane; ++j) {
@@ -242,12 +281,140 @@ __global__ void router_select(const float *__restrict__ scores, const uint16_t *
             sel_e = be;
         }
     }
+    wk_out = 0.f;
+    sel_e_out = -1;
     if (lane < K) {
-        float wk = __fdiv_rn(sel_p, sum);
-        wk = __fmul_rn(wk, bf2f(pes[sel_e]));
-        idx[(size_t)warp * K + lane] = sel_e;
+        wk_out = __fmul_rn(__fdiv_rn(sel_p, sum), bf2f(pes[sel_e]));
+        sel_e_out = sel_e;
+    }
+}
+
+// One warp per token.
+__global__ void router_select(const float *__restrict__ scores, const uint16_t *__restrict__ pes,
+                              int T, int E, int K, int32_t *__restrict__ idx,
+                              uint16_t *__restrict__ w, int32_t *__restrict__ counts) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    pdl_trigger();
+    pdl_wait();
+    if (warp >= T) return;
+    int e;
+    float wk;
+    select_token(scores + (size_t)warp * E, pes, E, K, lane, e, wk);
+    if (lane < K) {
+        idx[(size_t)warp * K + lane] = e;
         w[(size_t)warp * K + lane] = f2bf(wk);
-        if (counts) atomicAdd(counts + sel_e, 1);
+        if (counts) atomicAdd(counts + e, 1);
+    }
+}
+
+// Decode-sized fused routing: the scores of router_scores_small, then the
+// last CTA to finish (threadfence + counter, self-resetting) selects the
+// top-K of every token and builds the whole dispatch -- counts, offsets,
+// active-expert list and the stable sorted order -- in shared memory.
+// Requires T <= 64, T*K <= kFusedMaxPairs, E <= 256.
+constexpr int kFusedMaxPairs = 512;
+
+__global__ void __launch_bounds__(kSmallThreads)
+router_dispatch_small(const uint16_t *__restrict__ x, const uint16_t *__restrict__ proj,
+                      const uint16_t *__restrict__ scale, const uint16_t *__restrict__ pes, int T,
+                      int H, int E, int K, float eps, float root, float *__restrict__ scores,
+                      int32_t *__restrict__ idx, uint16_t *__restrict__ w, Dispatch d,
+                      int32_t *__restrict__ done) {
+    extern __shared__ float hs[];
+    __shared__ int s_last;
+    __shared__ int s_idx[kFusedMaxPairs];
+    __shared__ int s_cnt[256];
+    __shared__ int s_off[257];
+    __shared__ int s_cur[256];
+    pdl_trigger();
+    scores_small_block(x, proj, scale, T, H, E, eps, root, scores, hs);
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int prev = atomicAdd(done, 1);
+        s_last = (prev == (int)(gridDim.x * gridDim.y) - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    constexpr int NW = kSmallThreads / 32;
+    for (int e = tid; e < E; e += blockDim.x) {
+        s_cnt[e] = 0;
+        s_cur[e] = 0;
+    }
+    __syncthreads();
+    for (int t = warp; t < T; t += NW) {
+        int e;
+        float wk;
+        select_token(scores + (size_t)t * E, pes, E, K, lane, e, wk);
+        if (lane < K) {
+            idx[(size_t)t * K + lane] = e;
+            w[(size_t)t * K + lane] = f2bf(wk);
+            s_idx[t * K + lane] = e;
+            atomicAdd(&s_cnt[e], 1);
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {  // exclusive scan of the counts, 8 experts per lane
+        int loc[8], sum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = lane * 8 + j;
+            loc[j] = (e < E) ? s_cnt[e] : 0;
+            sum += loc[j];
+        }
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        int run = incl - sum;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = lane * 8 + j;
+            if (e < E) {
+                s_off[e] = run;
+                d.counts[e] = loc[j];
+                d.offsets[e] = run;
+            }
+            run += loc[j];
+        }
+        if (lane == 31) {
+            s_off[E] = incl;
+            d.offsets[E] = incl;
+        }
+        // active list: experts with nonzero count, ascending
+        int na = 0;
+        for (int e0 = 0; e0 < E; e0 += 32) {
+            const int e = e0 + lane;
+            const bool act = e < E && s_cnt[e] > 0;
+            const unsigned m = __ballot_sync(0xffffffffu, act);
+            if (act) d.active[na + __popc(m & ((1u << lane) - 1u))] = e;
+            na += __popc(m);
+        }
+        if (lane == 0) {
+            *d.n_active = na;
+            *done = 0;  // ready for the next call
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {  // stable positions: pairs in order, 32 at a time
+        const int P = T * K;
+        for (int p0 = 0; p0 < P; p0 += 32) {
+            const int p = p0 + lane;
+            const int e = p < P ? s_idx[p] : -1 - lane;
+            const unsigned m = __match_any_sync(0xffffffffu, e);
+            if (p < P) {
+                const int pos = s_off[e] + s_cur[e] + __popc(m & ((1u << lane) - 1u));
+                d.perm[pos] = p;
+                d.inv[p] = pos;
+            }
+            __syncwarp();
+            if (p < P && (m & ((1u << lane) - 1u)) == 0) s_cur[e] += __popc(m);
+            __syncwarp();
+        }
     }
 }
 
@@ -288,18 +455,39 @@ __global__ void dense_to_pairs(const uint16_t *__restrict__ W, int T, int E,
 }  // namespace
 
 cudaError_t router_init() {
-    return cudaFuncSetAttribute(router_scores_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(router_scores_small,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e) return e;
+    return cudaFuncSetAttribute(router_dispatch_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 200 * 1024);
+}
+
+bool router_dispatch_fusable(int T, int H, int E, int K) {
+    return T >= 1 && T <= 64 && T * K <= kFusedMaxPairs && E <= 256 && H % 256 == 0 &&
+           H <= 256 * kMaxVec;
+}
+
+cudaError_t launch_router_dispatch(const uint16_t *x, const uint16_t *proj, const uint16_t *scale,
+                                   const uint16_t *pes, int T, int H, int E, int K, float eps,
+                                   float *scores, int32_t *idx, uint16_t *w, const Dispatch &d,
+                                   int32_t *done, cudaStream_t s, int *launches) {
+    const float root = (float)(1.0 / sqrt((double)H));
+    const size_t smem = (size_t)(T < kSmallTok ? T : kSmallTok) * H * sizeof(float);
+    dim3 grid((E + kSmallWarps - 1) / kSmallWarps, (T + kSmallTok - 1) / kSmallTok);
+    router_dispatch_small<<<grid, kSmallThreads, smem, s>>>(x, proj, scale, pes, T, H, E, K,
+                                                               eps, root, scores, idx, w, d, done);
+    if (launches) ++*launches;
+    return cudaGetLastError();
 }
 
 cudaError_t launch_router_scores(const uint16_t *x, const uint16_t *proj, const uint16_t *scale,
                                  int T, int H, int E, float eps, float *scores, cudaStream_t s,
                                  int *launches) {
     const float root = (float)(1.0 / sqrt((double)H));
-    if (T <= 64) {
-        const size_t smem = (size_t)kSmallTok * H * sizeof(float);
-        dim3 grid((E + kSmallWarps - 1) / kSmallWarps);
-        router_scores_small<<<grid, kSmallWarps * 32, smem, s>>>(x, proj, scale, T, H, E, eps,
+    if (T <= 64 && H % 256 == 0 && H <= 256 * kMaxVec) {
+        const size_t smem = (size_t)(T < kSmallTok ? T : kSmallTok) * H * sizeof(float);
+        dim3 grid((E + kSmallWarps - 1) / kSmallWarps, (T + kSmallTok - 1) / kSmallTok);
+        router_scores_small<<<grid, kSmallThreads, smem, s>>>(x, proj, scale, T, H, E, eps,
                                                                  root, scores);
     } else {
         dim3 grid((E + kEB - 1) / kEB, (T + kTT - 1) / kTT);
@@ -314,9 +502,10 @@ cudaError_t launch_router_select(const float *scores, const uint16_t *pes, int T
                                  int *launches) {
     const int warps_per_block = 8;
     dim3 grid((T + warps_per_block - 1) / warps_per_block);
-    router_select<<<grid, warps_per_block * 32, 0, s>>>(scores, pes, T, E, K, idx, w, counts);
+    cudaError_t err = launch_ex(router_select, grid, dim3(warps_per_block * 32), 0, s, true,
+                                (const float *)scores, pes, T, E, K, idx, w, counts);
     if (launches) ++*launches;
-    return cudaGetLastError();
+    return err;
 }
 
 cudaError_t launch_scatter_dense(const int32_t *idx, const uint16_t *w, int T, int E, int K,

@@ -7,8 +7,8 @@ Workload (the decode sweep): one step is one
 MoE-block forward at each T in {1, 4, 16, 64} on the Gemma-4-26B block shape
 (H=2816, E=128, top-8, I=704, bf16), seeded synthetic inputs, uniform-ish
 routing.  value = tokens/s over the whole job (85 tokens per step per GPU).
-L2 is flushed (256 MiB write) before every timed forward and the flush is
-outside the timed events.  The prefill config (T=8192, Zipf(1.1) routing) is
+L2 is flushed (a 256 MiB read, which also writes back dirty lines) before
+every timed forward and the flush is outside the timed events.  The prefill config (T=8192, Zipf(1.1) routing) is
 reported as an extra object.
 
 ``--impl reference`` times the CPU oracle (the C restatement of the
@@ -215,7 +215,9 @@ def run_ours(args):
     cfg = A.ESModelConfig(moe_sparse=True, max_tokens=8192 if args.prefill else max(SWEEP),
                           device=local)
     blk = A.MoEBlock(cfg, d0["proj"], d0["scale"], d0["pes"], gate_up, down)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    if args.gemv_max_tokens is not None:
+        blk.handle.set_gemv_max_tokens(args.gemv_max_tokens)
+    flush = torch.ones(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
     def forward_T(T):
@@ -245,7 +247,7 @@ def run_ours(args):
         i = 0
         for _ in range(args.steps):
             for T in SWEEP:
-                flush.zero_()                       # evict L2 (outside the events)
+                flush.sum()                         # evict L2 (outside the events)
                 a, b = evs[i]
                 a.record(stream)
                 forward_T(T)
@@ -276,7 +278,7 @@ def run_ours(args):
     reps = 5
     for _ in range(reps):
         for T in SWEEP:
-            flush.zero_()
+            flush.sum()
             forward_T(T)
             for k, v in blk.handle.stage_times().items():
                 stage[T][k] = stage[T].get(k, 0.0) + v / reps
@@ -303,7 +305,7 @@ def run_ours(args):
     e2e_ms = 0.0
     for _ in range(args.steps):
         for T in SWEEP:
-            flush.zero_()
+            flush.sum()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
             blk.forward_host(xh[T], oh[T])
@@ -335,7 +337,7 @@ def run_ours(args):
             "data": "synthetic",
             "config": {"workload": "decode sweep T in {1,4,16,64}, Gemma-4-26B MoE block "
                                    "(H=2816,E=128,K=8,I=704), bf16, uniform routing",
-                       "l2": "flushed before every timed forward (256 MiB write, untimed)",
+                       "l2": "flushed before every timed forward (256 MiB read, untimed)",
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
             "roofline": {"bound": "hbm", "kernel": "gemv_gateup", "achieved": achieved,
                          "peak": peaks["hbm"], "unit": "GB/s", "frac": achieved / peaks["hbm"],
@@ -368,7 +370,7 @@ def run_prefill(blk, dev, peaks, flush, T=8192, steps=3):
     ms = 0.0
     stream = torch.cuda.current_stream(dev)
     for _ in range(steps):
-        flush.zero_()
+        flush.sum()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
         blk.forward(d["x"])
@@ -390,6 +392,27 @@ def run_prefill(blk, dev, peaks, flush, T=8192, steps=3):
             "zipf_top_share": float(d["zipf"]["achieved"].max()), "routing": "zipf s=1.1"}
 
 
+def run_prefill_only(args):
+    """Prefill config alone at T tokens (the small case the ncu captures use)."""
+    import torch
+    import apertura_b200 as A
+    from apertura_b200 import build as B
+    from apertura_b200.synthetic import expert_bank
+    B.build()
+    dev = torch.device("cuda", 0)
+    gate_up, down = expert_bank(E, H, I, 0, dev)
+    T = args.prefill_only
+    ones_h = torch.ones(H, dtype=torch.bfloat16, device=dev)
+    ones_e = torch.ones(E, dtype=torch.bfloat16, device=dev)
+    proj = torch.zeros(E, H, dtype=torch.bfloat16, device=dev)
+    cfg = A.ESModelConfig(moe_sparse=True, max_tokens=T)
+    blk = A.MoEBlock(cfg, proj, ones_h, ones_e, gate_up, down)
+    flush = torch.ones(256 << 20, dtype=torch.uint8, device=dev)
+    res = run_prefill(blk, dev, load_peaks(), flush, T=T, steps=args.steps)
+    print(json.dumps({"prefill_only": res}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -398,11 +421,17 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-prefill", dest="prefill", action="store_false")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--gemv-max-tokens", type=int, default=None,
+                    help="largest T that uses the GEMV expert kernels (default: library's)")
+    ap.add_argument("--prefill-only", type=int, default=0, metavar="T",
+                    help="only run the prefill config at T tokens (profiling case)")
     ap.add_argument("--traffic", type=float, default=None,
                     help="dram bytes per gate_up launch from an ncu capture (reported as is)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
+    if args.prefill_only:
+        return run_prefill_only(args)
     return run_reference(args) if args.impl == "reference" else run_ours(args)
 
 

@@ -171,7 +171,7 @@ APT_API int apt_moe_last_launches(const apt_moe_handle *h);
 /*
  * Path selection: the grouped expert kernels run as HBM-streaming GEMV when
  * T <= gemv_max_tokens and as tcgen05 tensor-core tiles otherwise.
- * Default 64.  Set to 0 to force the tensor-core path, to a huge value to
+ * Default 8.  Set to 0 to force the tensor-core path, to a huge value to
  * force the GEMV path (used by the parity tests).
  */
 APT_API apt_status apt_moe_set_gemv_max_tokens(apt_moe_handle *h, int t);
