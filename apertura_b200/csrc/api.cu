@@ -52,6 +52,8 @@ struct apt_moe_handle {
     int32_t *counts = nullptr, *offsets = nullptr, *perm = nullptr, *inv = nullptr;
     int32_t *active = nullptr, *n_active = nullptr, *errflag = nullptr;
     int32_t *done = nullptr;    // fused decode router's completion counter (self-resetting)
+    uint16_t *hsplit = nullptr; // tensor-core router input [Tm, 2H]
+    int32_t *rt_cnt = nullptr;  // its single-group {count, offset, end}
     uint16_t *xp = nullptr, *yp = nullptr, *op = nullptr;
     uint16_t *Wd = nullptr;     // dense routing matrix [Tm,E]
     int32_t *idx2 = nullptr;    // dense pair lists [Pcap]
@@ -257,6 +259,8 @@ extern "C" apt_status apt_moe_create(const apt_moe_config *cfg, apt_moe_handle *
     ALLOC(n_active, 1);
     ALLOC(errflag, 4);
     ALLOC(done, 1);
+    ALLOC(hsplit, (size_t)h->Tm * 2 * H);
+    ALLOC(rt_cnt, 4);
     ALLOC(xp, (size_t)h->Pcap * H);
     ALLOC(yp, (size_t)h->Pcap * I);
     ALLOC(op, (size_t)h->Pcap * H);
@@ -287,7 +291,7 @@ extern "C" apt_status apt_moe_destroy(apt_moe_handle *h) {
     DeviceGuard g(h->cfg.device);
     void *ptrs[] = {h->proj, h->scale, h->pes, h->gu, h->dn, h->gu_q, h->dn_q, h->gu_s, h->gu_b,
                     h->dn_s, h->dn_b, h->scores, h->idx_i, h->w_i, h->counts, h->offsets,
-                    h->perm, h->inv, h->active, h->n_active, h->errflag, h->done, h->xp, h->yp, h->op,
+                    h->perm, h->inv, h->active, h->n_active, h->errflag, h->done, h->hsplit, h->rt_cnt, h->xp, h->yp, h->op,
                     h->Wd, h->idx2, h->w2, h->xin, h->xout};
     for (void *p : ptrs) dfree(p);
     for (int i = 0; i < APT_STAGE_COUNT; ++i)
@@ -450,6 +454,25 @@ apt_status check_T(apt_moe_handle *h, int T) {
     return APT_OK;
 }
 
+// Router scores [T,E] f32 into h->scores: tensor-core split GEMM for
+// prefill-sized T, f32 SIMT kernels otherwise.
+apt_status router_scores(apt_moe_handle *h, const uint16_t *x, int T, cudaStream_t s) {
+    const int H = h->cfg.hidden_size, E = h->cfg.num_experts;
+    if (T > 64 && E % 64 == 0 && gemm_supported(H, h->cfg.moe_intermediate_size)) {
+        STAGE(h, APT_STAGE_ROUTER_SCORES, s,
+              launch_router_norm_split(x, h->scale, T, H, h->cfg.rms_norm_eps, h->hsplit,
+                                       h->rt_cnt, s, &h->launches));
+        STAGE(h, APT_STAGE_ROUTER_SCORES, s,
+              launch_gemm_router(h->hsplit, h->proj, h->rt_cnt, T, H, E, h->scores, h->errflag, s,
+                                 &h->launches));
+        return APT_OK;
+    }
+    STAGE(h, APT_STAGE_ROUTER_SCORES, s,
+          launch_router_scores(x, h->proj, h->scale, T, H, E, h->cfg.rms_norm_eps, h->scores, s,
+                               &h->launches));
+    return APT_OK;
+}
+
 // Grouped experts over an already-dispatched pair list, then the combine.
 // idx/w: [T, Kp] pair lists (Kp = K for sparse, E for dense).
 apt_status run_experts(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
@@ -530,8 +553,8 @@ extern "C" apt_status apt_moe_route(apt_moe_handle *h, const uint16_t *x, int T,
     cudaStream_t s = (cudaStream_t)stream;
     begin_call(h);
     const int H = h->cfg.hidden_size, E = h->cfg.num_experts, K = h->cfg.top_k_experts;
-    STAGE(h, APT_STAGE_ROUTER_SCORES, s, launch_router_scores(x, h->proj, h->scale, T, H, E, h->cfg.rms_norm_eps,
-                                     h->scores, s, &h->launches));
+    (void)H;
+    if (apt_status st = router_scores(h, x, T, s)) return st;
     STAGE(h, APT_STAGE_ROUTER_SELECT, s, launch_router_select(h->scores, h->pes, T, E, K, idx, w, nullptr, s,
                                      &h->launches));
     return APT_OK;
@@ -601,8 +624,7 @@ extern "C" apt_status apt_moe_forward(apt_moe_handle *h, const uint16_t *x_route
                                      s, &h->launches));
         return run_experts(h, x_experts, idx, w, T, K, quant, out, s, true);
     }
-    STAGE(h, APT_STAGE_ROUTER_SCORES, s, launch_router_scores(x_router, h->proj, h->scale, T, H, E, h->cfg.rms_norm_eps,
-                                     h->scores, s, &h->launches));
+    if (apt_status st = router_scores(h, x_router, T, s)) return st;
     if (h->cfg.moe_sparse) {
         CUDA_TRY(h, cudaMemsetAsync(h->counts, 0, sizeof(int32_t) * E, s));
         STAGE(h, APT_STAGE_ROUTER_SELECT, s, launch_router_select(h->scores, h->pes, T, E, K, idx, w, h->counts, s,

@@ -41,7 +41,7 @@ constexpr int kAccStride = 256;          // TMEM columns between the two accumul
 constexpr long long kWaitLimit = 4000000000LL;  // cycles (~2 s) before giving up
 constexpr int kMaxExperts = 256;
 
-enum { EPI_GATEUP = 0, EPI_DOWN = 1 };
+enum { EPI_GATEUP = 0, EPI_DOWN = 1, EPI_F32 = 2 };
 
 template <int BN>
 struct Smem {
@@ -120,6 +120,8 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     pdl_trigger();
+    // EPI_F32 (router scores): one "expert", N = H outputs, and the B operand
+    // (proj [H, I]) is reused for every I-wide slice of the K = 2*I split input.
     const int NT = (EPI == EPI_GATEUP) ? I / BN2 : H / BN;
     const int tiles = mtp[E] * NT;
     const int KB = Kdim / kBK;
@@ -145,6 +147,8 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                         tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], kb * kBK, gate_row);
                         tma_load_2d(sB + s * B_BYTES + BN2 * kBK * 2, &tmB, &full[s], kb * kBK,
                                     gate_row + I);
+                    } else if (EPI == EPI_F32) {
+                        tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], (kb * kBK) % I, nt * BN);
                     } else {
                         tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], kb * kBK, e * H + nt * BN);
                     }
@@ -220,6 +224,21 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                         *reinterpret_cast<uint4 *>(dst + c * 8) = v;
                     }
                 }
+            } else if (EPI == EPI_F32) {
+                float *dst = reinterpret_cast<float *>(out) + (size_t)row * out_ld + nt * BN;
+#pragma unroll 1
+                for (int c = 0; c < BN / 8; ++c) {
+                    uint32_t a[8];
+                    tmem_ld8(taddr + c * 8, a);
+                    tmem_ld_wait();
+                    if (r < nvalid) {
+                        float4 *d4 = reinterpret_cast<float4 *>(dst + c * 8);
+                        d4[0] = make_float4(__uint_as_float(a[0]), __uint_as_float(a[1]),
+                                            __uint_as_float(a[2]), __uint_as_float(a[3]));
+                        d4[1] = make_float4(__uint_as_float(a[4]), __uint_as_float(a[5]),
+                                            __uint_as_float(a[6]), __uint_as_float(a[7]));
+                    }
+                }
             } else {
                 uint16_t *dst = out + (size_t)row * out_ld + nt * BN;
 #pragma unroll 1
@@ -279,12 +298,13 @@ cudaError_t launch(const CUtensorMap &a, const CUtensorMap &b, const Dispatch &d
 }
 
 // gate_up tile: BN2 gate + BN2 up rows; down tile: BN rows of W_down.
-constexpr int kGuStages = 5, kDnStages = 4;
+constexpr int kGuStages = 5, kDnStages = 4, kRtStages = 6;
 
 }  // namespace
 
 cudaError_t gemm_init() {
     cudaError_t e;
+    if ((e = set_attr<EPI_F32, 64, 0, kRtStages>())) return e;
     if ((e = set_attr<EPI_GATEUP, 176, 88, kGuStages>())) return e;
     if ((e = set_attr<EPI_GATEUP, 128, 64, kGuStages>())) return e;
     if ((e = set_attr<EPI_DOWN, 256, 0, kDnStages>())) return e;
@@ -321,6 +341,28 @@ cudaError_t launch_gemm_down(const uint16_t *yp, const Dispatch &d, const Expert
     cudaError_t e = (bn == 256)
         ? launch<EPI_DOWN, 256, 0, kDnStages>(a, b, d, E, I, I, H, op, H, err, s)
         : launch<EPI_DOWN, 128, 0, kDnStages>(a, b, d, E, I, I, H, op, H, err, s);
+    if (launches) ++*launches;
+    return e;
+}
+
+}  // namespace apt
+
+namespace apt {
+
+// Router scores on the tensor cores: scores [T,E] f32 = hs [T, 2H] . [proj|proj]^T
+// where hs = (h1 | h2) is the two-term bf16 split of the f32 router input.
+cudaError_t launch_gemm_router(const uint16_t *hs, const uint16_t *proj, const int32_t *cnt_off,
+                               int T, int H, int E, float *scores, int32_t *err, cudaStream_t s,
+                               int *launches) {
+    CUtensorMap a, b;
+    if (!make_map(&a, hs, 2 * (uint64_t)H, T, kBM) || !make_map(&b, proj, H, E, 64))
+        return cudaErrorInvalidValue;
+    Dispatch d{};
+    d.counts = const_cast<int32_t *>(cnt_off);
+    d.offsets = const_cast<int32_t *>(cnt_off + 1);
+    cudaError_t e = launch<EPI_F32, 64, 0, kRtStages>(a, b, d, 1, 2 * H, H, E,
+                                                     reinterpret_cast<uint16_t *>(scores), E, err,
+                                                     s);
     if (launches) ++*launches;
     return e;
 }

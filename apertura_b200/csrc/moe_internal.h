@@ -37,6 +37,14 @@ cudaError_t launch_router_dispatch(const uint16_t *x, const uint16_t *proj, cons
                                    const uint16_t *pes, int T, int H, int E, int K, float eps,
                                    float *scores, int32_t *idx, uint16_t *w, const Dispatch &d,
                                    int32_t *done, cudaStream_t s, int *launches);
+// Tensor-core router path: two-term bf16 split of the f32 router input, then
+// an f32-output tcgen05 GEMM against proj (gemm_sm100.cu).
+cudaError_t launch_router_norm_split(const uint16_t *x, const uint16_t *scale, int T, int H,
+                                     float eps, uint16_t *hs, int32_t *cnt_off, cudaStream_t s,
+                                     int *launches);
+cudaError_t launch_gemm_router(const uint16_t *hs, const uint16_t *proj, const int32_t *cnt_off,
+                               int T, int H, int E, float *scores, int32_t *err, cudaStream_t s,
+                               int *launches);
 // dense routeWeights scatter: W [T,E] = 0 except W[t, idx[t,k]] = w[t,k]
 cudaError_t launch_scatter_dense(const int32_t *idx, const uint16_t *w, int T, int E, int K,
                                  uint16_t *W, cudaStream_t s, int *launches);

@@ -418,6 +418,56 @@ router_dispatch_small(const uint16_t *__restrict__ x, const uint16_t *__restrict
     }
 }
 
+// Router input for the tensor-core score GEMM: h = ((x*r)*scale)*H^-1/2 in
+// f32 (the reference's rounding points), written as a two-term bf16 split
+// hs[t] = (h1 | h2), h1 = bf16(h), h2 = bf16(h - h1), so that
+// h1.p + h2.p reproduces h.p to ~2^-17 relative per term with exact bf16
+// products and f32 accumulation.  One warp per token.  Thread 0 of block 0
+// writes the single-group counts/offsets {T, 0, T} the GEMM scheduler reads.
+__global__ void router_norm_split(const uint16_t *__restrict__ x,
+                                  const uint16_t *__restrict__ scale, int T, int H, float eps,
+                                  float root, uint16_t *__restrict__ hs,
+                                  int32_t *__restrict__ cnt_off) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        cnt_off[0] = T;
+        cnt_off[1] = 0;
+        cnt_off[2] = T;
+    }
+    if (warp >= T) return;
+    const uint16_t *xr = x + (size_t)warp * H;
+    float ss = 0.f;
+    for (int i = lane * 8; i < H; i += 256) {
+        float f[8];
+        unpack8(*reinterpret_cast<const uint4 *>(xr + i), f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+    }
+    ss = warp_sum(ss);
+    const float r = 1.0f / sqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / (float)H), eps));
+    uint16_t *d1 = hs + (size_t)warp * 2 * H;
+    uint16_t *d2 = d1 + H;
+    for (int i = lane * 8; i < H; i += 256) {
+        float f[8], sf[8];
+        unpack8(*reinterpret_cast<const uint4 *>(xr + i), f);
+        unpack8(*reinterpret_cast<const uint4 *>(scale + i), sf);
+        float h1[8], h2[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float h = router_h(f[j], r, sf[j], root);
+            h1[j] = rbf(h);
+            h2[j] = rbf(__fsub_rn(h, h1[j]));
+        }
+        uint4 v1, v2;
+        v1.x = pack_bf2(h1[0], h1[1]); v1.y = pack_bf2(h1[2], h1[3]);
+        v1.z = pack_bf2(h1[4], h1[5]); v1.w = pack_bf2(h1[6], h1[7]);
+        v2.x = pack_bf2(h2[0], h2[1]); v2.y = pack_bf2(h2[2], h2[3]);
+        v2.z = pack_bf2(h2[4], h2[5]); v2.w = pack_bf2(h2[6], h2[7]);
+        *reinterpret_cast<uint4 *>(d1 + i) = v1;
+        *reinterpret_cast<uint4 *>(d2 + i) = v2;
+    }
+}
+
 __global__ void scatter_dense(const int32_t *__restrict__ idx, const uint16_t *__restrict__ w,
                               int T, int E, int K, uint16_t *__restrict__ W) {
     const int t = blockIdx.x;
@@ -493,6 +543,17 @@ cudaError_t launch_router_scores(const uint16_t *x, const uint16_t *proj, const 
         dim3 grid((E + kEB - 1) / kEB, (T + kTT - 1) / kTT);
         router_scores_tiled<<<grid, 256, 0, s>>>(x, proj, scale, T, H, E, eps, root, scores);
     }
+    if (launches) ++*launches;
+    return cudaGetLastError();
+}
+
+cudaError_t launch_router_norm_split(const uint16_t *x, const uint16_t *scale, int T, int H,
+                                     float eps, uint16_t *hs, int32_t *cnt_off, cudaStream_t s,
+                                     int *launches) {
+    const float root = (float)(1.0 / sqrt((double)H));
+    const int wpb = 8;
+    router_norm_split<<<(T + wpb - 1) / wpb, wpb * 32, 0, s>>>(x, scale, T, H, eps, root, hs,
+                                                               cnt_off);
     if (launches) ++*launches;
     return cudaGetLastError();
 }
