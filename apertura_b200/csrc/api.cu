@@ -638,6 +638,59 @@ extern "C" apt_status apt_moe_forward(apt_moe_handle *h, const uint16_t *x_route
     return experts_dense(h, x_experts, h->Wd, T, out, s);
 }
 
+// ---- expert-parallel halves: the routing + dispatch before the all-to-all,
+// and the combine after it (the remote expert compute is apt_moe_experts on a
+// handle holding the rank's local experts).
+
+extern "C" apt_status apt_moe_ep_dispatch(apt_moe_handle *h, const uint16_t *x, int T,
+                                          int32_t *idx, uint16_t *w, uint16_t *rows_out,
+                                          int32_t *counts_out, void *stream) {
+    if (!h) return APT_ERR_INVALID;
+    if (check_T(h, T)) return APT_ERR_INVALID;
+    if (T == 0) return APT_OK;
+    if (!x || !idx || !w || !rows_out || !counts_out)
+        return fail(h, APT_ERR_INVALID, "null pointer");
+    if (!h->proj) return fail(h, APT_ERR_STATE, "router weights not loaded");
+    DeviceGuard g(h->cfg.device);
+    cudaStream_t s = (cudaStream_t)stream;
+    begin_call(h);
+    const int H = h->cfg.hidden_size, E = h->cfg.num_experts, K = h->cfg.top_k_experts;
+    Dispatch d = h->disp();
+    if (router_dispatch_fusable(T, H, E, K)) {
+        STAGE(h, APT_STAGE_ROUTER_SCORES, s,
+              launch_router_dispatch(x, h->proj, h->scale, h->pes, T, H, E, K,
+                                     h->cfg.rms_norm_eps, h->scores, idx, w, d, h->done, s,
+                                     &h->launches));
+    } else {
+        if (apt_status st = router_scores(h, x, T, s)) return st;
+        CUDA_TRY(h, cudaMemsetAsync(h->counts, 0, sizeof(int32_t) * E, s));
+        STAGE(h, APT_STAGE_ROUTER_SELECT, s,
+              launch_router_select(h->scores, h->pes, T, E, K, idx, w, h->counts, s,
+                                   &h->launches));
+        STAGE(h, APT_STAGE_DISPATCH, s, launch_dispatch(idx, T * K, E, d, s, &h->launches));
+    }
+    STAGE(h, APT_STAGE_GATHER, s,
+          launch_gather_rows(x, H, K, E, d, T * K, rows_out, s, &h->launches));
+    CUDA_TRY(h, cudaMemcpyAsync(counts_out, h->counts, sizeof(int32_t) * E,
+                                cudaMemcpyDeviceToDevice, s));
+    return APT_OK;
+}
+
+extern "C" apt_status apt_moe_ep_combine(apt_moe_handle *h, const uint16_t *rows,
+                                         const int32_t *idx, const uint16_t *w, int T,
+                                         uint16_t *out, void *stream) {
+    if (!h) return APT_ERR_INVALID;
+    if (check_T(h, T)) return APT_ERR_INVALID;
+    if (T == 0) return APT_OK;
+    if (!rows || !idx || !w || !out) return fail(h, APT_ERR_INVALID, "null pointer");
+    DeviceGuard g(h->cfg.device);
+    cudaStream_t s = (cudaStream_t)stream;
+    STAGE(h, APT_STAGE_COMBINE, s,
+          launch_combine(rows, idx, w, h->disp(), T, h->cfg.top_k_experts, h->cfg.hidden_size,
+                         out, s, &h->launches));
+    return APT_OK;
+}
+
 extern "C" apt_status apt_moe_forward_host(apt_moe_handle *h, const uint16_t *x_host, int T,
                                            uint16_t *out_host, void *stream) {
     if (!h) return APT_ERR_INVALID;

@@ -19,7 +19,8 @@
 // For gate_up a B tile is BN2 gate rows followed by the BN2 matching up rows
 // (two TMA boxes), so each accumulator row holds g and u for the same j.
 // Every mbarrier wait is bounded; on expiry the kernel records an error code
-// and leaves through the normal exit (TMEM released).  No cluster multicast.
+// and leaves through the normal exit (TMEM released).  Every TMA load is a
+// plain per-CTA load from this GPU's own memory.
 #include <cuda.h>
 
 #include "common.cuh"

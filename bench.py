@@ -320,6 +320,7 @@ def run_ours(args):
            "h2d_bytes_per_step": sum(SWEEP) * H * 2, "d2h_bytes_per_step": sum(SWEEP) * H * 2}
 
     prefill = run_prefill(blk, dev, peaks, flush) if args.prefill else None
+    ep = run_ep(args, dev, world, rank) if (world > 1 and args.ep) else None
 
     cpu = None
     if rank == 0 and world == 1 and args.cpu_baseline:
@@ -349,12 +350,59 @@ def run_ours(args):
         }
         if prefill:
             line["prefill"] = prefill
+        if ep:
+            line["ep"] = ep
         if cpu:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
     return 0
+
+
+def run_ep(args, dev, world, rank, T=4096, steps=5, warmup=3):
+    """expert parallelism, 128/N experts per GPU, T tokens per
+    GPU with Zipf(1.1) routing, NCCL all-to-all dispatch/combine.  Timed with
+    CUDA events around each step (barrier + sync on both sides), max over ranks."""
+    import torch
+    import torch.distributed as dist
+    import apertura_b200 as A
+    from apertura_b200.ep import ExpertParallelMoE
+    from apertura_b200.synthetic import block_inputs, expert_bank, zipf_targets
+    d = block_inputs(T * world, seed=5, device=dev, routing="zipf", with_experts=False,
+                     calib_tokens=4096)
+    x = d["x"][rank * T:(rank + 1) * T].contiguous()
+    gu, dn = expert_bank(E, H, I, 0, dev)
+    cfg = A.ESModelConfig(moe_sparse=True, max_tokens=T, device=dev.index)
+    ep = ExpertParallelMoE(cfg, d["proj"], d["scale"], d["pes"], gu, dn,
+                           loads=zipf_targets(E, K).tolist(), max_tokens_per_rank=T)
+    del gu, dn
+    torch.cuda.empty_cache()
+    for _ in range(warmup):
+        ep(x)
+    stream = torch.cuda.current_stream(dev)
+    ms = 0.0
+    for _ in range(steps):
+        dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        ep(x)
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms += a.elapsed_time(b) / steps
+    t = torch.tensor([ms, float(ep.last_recv_rows)], device=dev)
+    mx = t.clone()
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    loads = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(loads, t)
+    recv = [int(l[1].item()) for l in loads]
+    return {"config": f"expert parallel, 128/{world} experts per GPU, {T} tokens per GPU, "
+                      f"Zipf s=1.1, LPT placement, NCCL all-to-all",
+            "ms_per_step": float(mx[0].item()),
+            "tokens_per_s": world * T / (float(mx[0].item()) / 1e3),
+            "recv_rows_per_rank": recv,
+            "load_max_over_mean": max(recv) / (sum(recv) / len(recv))}
 
 
 def run_prefill(blk, dev, peaks, flush, T=8192, steps=3):
@@ -421,6 +469,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-prefill", dest="prefill", action="store_false")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--no-ep", dest="ep", action="store_false",
+                    help="skip the expert-parallel measurement on multi-GPU runs")
     ap.add_argument("--gemv-max-tokens", type=int, default=None,
                     help="largest T that uses the GEMV expert kernels (default: library's)")
     ap.add_argument("--prefill-only", type=int, default=0, metavar="T",

@@ -157,6 +157,26 @@ APT_API apt_status apt_moe_forward(apt_moe_handle *h, const uint16_t *x_router,
 APT_API apt_status apt_moe_forward_host(apt_moe_handle *h, const uint16_t *x_host, int T,
                                 uint16_t *out_host, void *stream);
 
+/*
+ * Expert parallelism (no reference counterpart: the reference is one device).
+ * The block splits at the token exchange:
+ *   apt_moe_ep_dispatch: router + top-K + dispatch on this rank's tokens, and the
+ *     routed rows gathered in expert order into rows_out [T*K, H] (device);
+ *     counts_out [E] (device) receives the per-expert row counts.  With experts
+ *     numbered so that each rank owns a contiguous id range, rows_out is already
+ *     grouped by destination rank: it is the all-to-all send buffer.
+ *   (remote) apt_moe_experts on a handle holding the rank's local experts, with
+ *     idx = local expert id, w = 1, K = 1, returns the unweighted expert rows.
+ *   apt_moe_ep_combine: rows [T*K, H] returned in the same order as rows_out ->
+ *     out [T,H] = sum_k bf16(w * row), in k order (ESExperts.mm:58-59), using
+ *     the dispatch of the last apt_moe_ep_dispatch on this handle.
+ */
+APT_API apt_status apt_moe_ep_dispatch(apt_moe_handle *h, const uint16_t *x, int T, int32_t *idx,
+                                       uint16_t *w, uint16_t *rows_out, int32_t *counts_out,
+                                       void *stream);
+APT_API apt_status apt_moe_ep_combine(apt_moe_handle *h, const uint16_t *rows, const int32_t *idx,
+                                      const uint16_t *w, int T, uint16_t *out, void *stream);
+
 /* Synchronise the handle's device and report any pending CUDA error. */
 APT_API apt_status apt_moe_sync(apt_moe_handle *h);
 
