@@ -39,6 +39,8 @@ struct apt_moe_handle {
     uint16_t *proj = nullptr, *scale = nullptr, *pes = nullptr;
     // experts, bf16 (kept when quantised from bf16 so the dense path works)
     uint16_t *gu = nullptr, *dn = nullptr;
+    // bf16 expansion of the quantised experts for the tensor-core path (lazy)
+    uint16_t *dq_gu = nullptr, *dq_dn = nullptr;
     // experts, affine quantised
     uint32_t *gu_q = nullptr, *dn_q = nullptr;
     uint16_t *gu_s = nullptr, *gu_b = nullptr, *dn_s = nullptr, *dn_b = nullptr;
@@ -292,7 +294,7 @@ extern "C" apt_status apt_moe_destroy(apt_moe_handle *h) {
     void *ptrs[] = {h->proj, h->scale, h->pes, h->gu, h->dn, h->gu_q, h->dn_q, h->gu_s, h->gu_b,
                     h->dn_s, h->dn_b, h->scores, h->idx_i, h->w_i, h->counts, h->offsets,
                     h->perm, h->inv, h->active, h->n_active, h->errflag, h->done, h->hsplit, h->rt_cnt, h->xp, h->yp, h->op,
-                    h->Wd, h->idx2, h->w2, h->xin, h->xout};
+                    h->Wd, h->idx2, h->w2, h->xin, h->xout, h->dq_gu, h->dq_dn};
     for (void *p : ptrs) dfree(p);
     for (int i = 0; i < APT_STAGE_COUNT; ++i)
         for (int j = 0; j < 2; ++j)
@@ -485,7 +487,22 @@ apt_status run_experts(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
         STAGE(h, APT_STAGE_DISPATCH, s, launch_dispatch(idx, P, E, d, s, &h->launches));
     ExpertWeights ew = weights_for(h, quant);
     const int max_rows = T;  // an expert appears at most once per token
-    const bool gemm = !quant && T > h->gemv_max_tokens && gemm_supported(H, I);
+    const bool gemm = T > h->gemv_max_tokens && gemm_supported(H, I);
+    if (gemm && quant) {
+        // expand the touched quantised experts to bf16, then the bf16 GEMM
+        if (!h->dq_gu) {
+            CUDA_TRY(h, dalloc(&h->dq_gu, (size_t)E * 2 * I * H));
+            CUDA_TRY(h, dalloc(&h->dq_dn, (size_t)E * H * I));
+        }
+        STAGE(h, APT_STAGE_GATHER, s,
+              launch_dequant_active(h->gu_q, h->gu_s, h->gu_b, 2 * I, H, h->qbits, d, E, h->dq_gu,
+                                    s, &h->launches));
+        STAGE(h, APT_STAGE_GATHER, s,
+              launch_dequant_active(h->dn_q, h->dn_s, h->dn_b, H, I, h->qbits, d, E, h->dq_dn, s,
+                                    &h->launches));
+        ew.gu = h->dq_gu;
+        ew.dn = h->dq_dn;
+    }
     if (gemm) {
         const int rows_cap = P < h->Pcap ? P : h->Pcap;
         STAGE(h, APT_STAGE_GATHER, s, launch_gather_rows(x, H, Kp, E, d, rows_cap, h->xp, s, &h->launches));

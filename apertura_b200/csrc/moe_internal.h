@@ -103,5 +103,9 @@ cudaError_t launch_gemm_down(const uint16_t *yp, const Dispatch &d, const Expert
 // ---- quantisation (quant.cu)
 cudaError_t launch_quantize_affine(const uint16_t *w, int64_t rows, int cols, int gs, int bits,
                                    uint32_t *q, uint16_t *sc, uint16_t *bi, cudaStream_t s);
+// bf16 copy of the active experts' quantised rows (prefill path)
+cudaError_t launch_dequant_active(const uint32_t *q, const uint16_t *sc, const uint16_t *bi,
+                                  int rows, int cols, int bits, const Dispatch &d, int E,
+                                  uint16_t *out, cudaStream_t s, int *launches);
 
 }  // namespace apt

@@ -9,6 +9,7 @@
 //   computed against the stored bf16 scale and bias; 32/bits values per uint32,
 //   element i at bit (i*bits) % 32 of word i*bits/32 (low bits first).
 #include "common.cuh"
+#include "launch_util.h"
 #include "moe_internal.h"
 
 namespace apt {
@@ -50,7 +51,58 @@ __global__ void quantize_affine_kernel(const uint16_t *__restrict__ w, int64_t r
     }
 }
 
+// Dequantise the rows of every active expert into a bf16 bank with the same
+// [E, rows, cols] layout as the original weights: w = bf16(scale*q + bias).
+// The prefill path runs the bf16 tensor-core GEMM on this bank.  Each thread
+// expands 8 consecutive elements (one 16-byte store).
+__global__ void dequant_active_kernel(const uint32_t *__restrict__ q, const uint16_t *__restrict__ sc,
+                                      const uint16_t *__restrict__ bi, int rows, int cols, int bits,
+                                      const int32_t *__restrict__ active,
+                                      const int32_t *__restrict__ n_active,
+                                      uint16_t *__restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
+    if ((int)blockIdx.y >= *n_active) return;
+    const int e = active[blockIdx.y];
+    const int per_row = cols / 8;
+    const int64_t nvec = (int64_t)rows * per_row;
+    const int per_word = 32 / bits;
+    const uint32_t mask = (1u << bits) - 1u;
+    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec;
+         v += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = (int64_t)e * rows + v / per_row;
+        const int c0 = (int)(v % per_row) * 8;
+        const float s = bf2f(sc[r * (cols / 64) + c0 / 64]);
+        const float b = bf2f(bi[r * (cols / 64) + c0 / 64]);
+        const uint32_t *qr = q + r * (cols / per_word);
+        float f[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int c = c0 + i;
+            const uint32_t qi = (qr[c / per_word] >> ((c % per_word) * bits)) & mask;
+            f[i] = fmaf(s, (float)qi, b);
+        }
+        uint4 o;
+        o.x = pack_bf2(f[0], f[1]);
+        o.y = pack_bf2(f[2], f[3]);
+        o.z = pack_bf2(f[4], f[5]);
+        o.w = pack_bf2(f[6], f[7]);
+        *reinterpret_cast<uint4 *>(out + r * cols + c0) = o;
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_dequant_active(const uint32_t *q, const uint16_t *sc, const uint16_t *bi,
+                                  int rows, int cols, int bits, const Dispatch &d, int E,
+                                  uint16_t *out, cudaStream_t s, int *launches) {
+    dim3 grid(64, E);
+    cudaError_t err = launch_ex(dequant_active_kernel, grid, dim3(256), 0, s, true, q, sc, bi,
+                                rows, cols, bits, (const int32_t *)d.active,
+                                (const int32_t *)d.n_active, out);
+    if (launches) ++*launches;
+    return err;
+}
 
 cudaError_t launch_quantize_affine(const uint16_t *w, int64_t rows, int cols, int gs, int bits,
                                    uint32_t *q, uint16_t *sc, uint16_t *bi, cudaStream_t s) {

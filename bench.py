@@ -321,6 +321,7 @@ def run_ours(args):
 
     prefill = run_prefill(blk, dev, peaks, flush) if args.prefill else None
     ep = run_ep(args, dev, world, rank) if (world > 1 and args.ep) else None
+    quant = run_quant(dev, peaks, flush) if args.quant else None
 
     cpu = None
     if rank == 0 and world == 1 and args.cpu_baseline:
@@ -352,6 +353,8 @@ def run_ours(args):
             line["prefill"] = prefill
         if ep:
             line["ep"] = ep
+        if quant:
+            line["quant"] = quant
         if cpu:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -403,6 +406,39 @@ def run_ep(args, dev, world, rank, T=4096, steps=5, warmup=3):
             "tokens_per_s": world * T / (float(mx[0].item()) / 1e3),
             "recv_rows_per_rank": recv,
             "load_max_over_mean": max(recv) / (sum(recv) / len(recv))}
+
+
+def run_quant(dev, peaks, flush, bits=4, Ts=(1, 4096), steps=5):
+    """experts in MLX affine 4-bit (group 64), quantised on
+    the device at load as ESExperts does with quantBits > 0; T=1 and T=4096."""
+    import torch
+    import apertura_b200 as A
+    from apertura_b200.synthetic import block_inputs, expert_bank
+    gu, dn = expert_bank(E, H, I, 0, dev)
+    res = {}
+    for T in Ts:
+        d = block_inputs(T, seed=11, device=dev, routing="zipf" if T > 64 else "uniform",
+                         with_experts=False)
+        cfg = A.ESModelConfig(moe_sparse=True, quant_bits=bits, max_tokens=T, device=dev.index)
+        blk = A.MoEBlock(cfg, d["proj"], d["scale"], d["pes"], gu, dn)
+        out, tk = blk.forward(d["x"], return_routing=True)
+        U = n_unique(tk.idx)
+        stream = torch.cuda.current_stream(dev)
+        ms = 0.0
+        for _ in range(steps):
+            flush.sum()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            blk.forward(d["x"])
+            b.record(stream)
+            b.synchronize()
+            ms += a.elapsed_time(b) / steps
+        qbytes = U * ((2 * I * H + H * I) * bits // 8 + (2 * I * H + H * I) // 64 * 4)
+        res[str(T)] = {"ms": ms, "tokens_per_s": T / (ms / 1e3), "U": U,
+                       "expert_bytes": qbytes,
+                       "block_hbm_frac": qbytes / (ms / 1e3) / 1e9 / peaks["hbm"]}
+        del blk
+    return {"bits": bits, "group": 64, **res}
 
 
 def run_prefill(blk, dev, peaks, flush, T=8192, steps=3):
@@ -469,6 +505,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-prefill", dest="prefill", action="store_false")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--no-quant", dest="quant", action="store_false",
+                    help="skip the 4-bit expert measurement")
     ap.add_argument("--no-ep", dest="ep", action="store_false",
                     help="skip the expert-parallel measurement on multi-GPU runs")
     ap.add_argument("--gemv-max-tokens", type=int, default=None,

@@ -89,3 +89,27 @@ def test_quant_bundle_has_no_dense_path():
     with pytest.raises(A.AptError) as ei:
         blk.forward(d["x"])
     assert ei.value.status == 6
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_quant_prefill_tensor_core_path(oracle, bits):
+    """Prefill-sized T with quantised experts: the touched experts are expanded
+    to bf16 (w = bf16(scale*q + bias)) and run on the tcgen05 GEMM.  Compared
+    with the oracle's f32 dequantisation on a sample of tokens; the extra bf16
+    rounding of w stays inside a few output ulps."""
+    H, E, K, I, T = 2816, 128, 8, 704, 1024
+    d = block_inputs(T, seed=77, device=DEV, routing="zipf", H=H, E=E, K=K, I=I)
+    gq, dq = _quantize(oracle, d, bits)
+    cfg = A.ESModelConfig(moe_sparse=True, max_tokens=T)
+    q = dict(gu_q=_dev(gq[0]), gu_s=_dev(gq[1]), gu_b=_dev(gq[2]), dn_q=_dev(dq[0]),
+             dn_s=_dev(dq[1]), dn_b=_dev(dq[2]), bits=bits, group_size=64)
+    blk = A.MoEBlock(cfg, d["proj"], d["scale"], d["pes"], quantized=q)
+    out, tk = blk.forward(d["x"], return_routing=True)
+    torch.cuda.synchronize()
+    blk.handle.sync()
+    rows = np.sort(np.random.default_rng(1).choice(T, 16, replace=False))
+    ref = oracle.experts_sparse_q(_np(d["x"][rows]), *gq, *dq, bits, 64,
+                                  tk.idx.cpu().numpy()[rows], _np(tk.w)[rows], I)
+    got, refv = bf16_to_f32(_np(out))[rows], bf16_to_f32(ref)
+    ok, ma, cos = block_close(got, refv)
+    assert ok and ma <= TIGHT_REL * np.abs(refv).max(), (ma, cos)
