@@ -44,6 +44,7 @@ struct apt_moe_handle {
     // experts, affine quantised
     uint32_t *gu_q = nullptr, *dn_q = nullptr;
     uint16_t *gu_s = nullptr, *gu_b = nullptr, *dn_s = nullptr, *dn_b = nullptr;
+    uint32_t *gu_sb = nullptr, *dn_sb = nullptr;  // (scale, bias) pairs, per-row contiguous
     int qbits = 0, qgs = 64;
 
     // workspace
@@ -126,6 +127,8 @@ ExpertWeights weights_for(const apt_moe_handle *h, bool quant) {
         w.gu_b = h->gu_b;
         w.dn_s = h->dn_s;
         w.dn_b = h->dn_b;
+        w.gu_sb = h->gu_sb;
+        w.dn_sb = h->dn_sb;
         w.bits = h->qbits;
         w.gs = h->qgs;
     }
@@ -294,7 +297,7 @@ extern "C" apt_status apt_moe_destroy(apt_moe_handle *h) {
     void *ptrs[] = {h->proj, h->scale, h->pes, h->gu, h->dn, h->gu_q, h->dn_q, h->gu_s, h->gu_b,
                     h->dn_s, h->dn_b, h->scores, h->idx_i, h->w_i, h->counts, h->offsets,
                     h->perm, h->inv, h->active, h->n_active, h->errflag, h->done, h->hsplit, h->rt_cnt, h->xp, h->yp, h->op,
-                    h->Wd, h->idx2, h->w2, h->xin, h->xout, h->dq_gu, h->dq_dn};
+                    h->Wd, h->idx2, h->w2, h->xin, h->xout, h->dq_gu, h->dq_dn, h->gu_sb, h->dn_sb};
     for (void *p : ptrs) dfree(p);
     for (int i = 0; i < APT_STAGE_COUNT; ++i)
         for (int j = 0; j < 2; ++j)
@@ -357,6 +360,22 @@ extern "C" apt_status apt_moe_sync(apt_moe_handle *h) {
 
 // ------------------------------------------------------------------ weights
 
+namespace {
+apt_status build_sb(apt_moe_handle *h) {
+    const size_t H = h->cfg.hidden_size, E = h->cfg.num_experts, I = h->cfg.moe_intermediate_size;
+    const size_t ngu = E * 2 * I * H / 64, ndn = E * H * I / 64;
+    dfree(h->gu_sb);
+    dfree(h->dn_sb);
+    h->gu_sb = h->dn_sb = nullptr;
+    CUDA_TRY(h, dalloc(&h->gu_sb, ngu));
+    CUDA_TRY(h, dalloc(&h->dn_sb, ndn));
+    CUDA_TRY(h, launch_interleave_sb(h->gu_s, h->gu_b, (int64_t)ngu, h->gu_sb, 0));
+    CUDA_TRY(h, launch_interleave_sb(h->dn_s, h->dn_b, (int64_t)ndn, h->dn_sb, 0));
+    CUDA_TRY(h, cudaDeviceSynchronize());
+    return APT_OK;
+}
+}  // namespace
+
 extern "C" apt_status apt_moe_load_router(apt_moe_handle *h, const uint16_t *proj,
                                           const uint16_t *scale, const uint16_t *pes,
                                           int on_device) {
@@ -406,6 +425,7 @@ extern "C" apt_status apt_moe_load_experts_bf16(apt_moe_handle *h, const uint16_
         CUDA_TRY(h, cudaDeviceSynchronize());
         h->qbits = bits;
         h->qgs = gs;
+        if (apt_status st = build_sb(h)) return st;
     }
     return APT_OK;
 }
@@ -443,7 +463,7 @@ extern "C" apt_status apt_moe_load_experts_quant(apt_moe_handle *h, const uint32
     h->gu = h->dn = nullptr;
     h->qbits = bits;
     h->qgs = gs;
-    return APT_OK;
+    return build_sb(h);
 }
 
 // ------------------------------------------------------------------ compute
@@ -509,6 +529,13 @@ apt_status run_experts(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
         STAGE(h, APT_STAGE_GATE_UP, s, launch_gemm_gateup(h->xp, d, ew, rows_cap, H, I, E, h->yp, h->errflag, s,
                                        &h->launches));
         STAGE(h, APT_STAGE_DOWN, s, launch_gemm_down(h->yp, d, ew, rows_cap, H, I, E, h->op, h->errflag, s,
+                                     &h->launches));
+    } else if (quant && h->gemv_tma && gemv_tma_q_supported(H, I, h->qbits)) {
+        STAGE(h, APT_STAGE_GATE_UP, s,
+              launch_gemv_tma_q_gateup(x, Kp, d, ew, H, I, E, max_rows, h->yp, h->errflag, s,
+                                       &h->launches));
+        STAGE(h, APT_STAGE_DOWN, s,
+              launch_gemv_tma_q_down(h->yp, d, ew, H, I, E, Kp, max_rows, h->op, h->errflag, s,
                                      &h->launches));
     } else if (!quant && h->gemv_tma && gemv_tma_supported(H, I)) {
         STAGE(h, APT_STAGE_GATE_UP, s, launch_gemv_tma_gateup(x, Kp, d, ew, H, I, E, max_rows, h->yp,

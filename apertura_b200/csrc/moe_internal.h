@@ -70,6 +70,7 @@ struct ExpertWeights {
     const uint16_t *gu, *dn;                // bf16 [E,2I,H], [E,H,I]
     const uint32_t *gu_q, *dn_q;            // packed
     const uint16_t *gu_s, *gu_b, *dn_s, *dn_b;
+    const uint32_t *gu_sb, *dn_sb;          // interleaved (scale, bias) pairs
     int bits, gs;
 };
 // max_rows_per_expert bounds counts[e] for this call (T for top-k routing).
@@ -90,6 +91,15 @@ cudaError_t launch_gemv_tma_down(const uint16_t *yp, const Dispatch &d, const Ex
                                  int H, int I, int E, int max_k, int max_rows, uint16_t *op, int32_t *err,
                                  cudaStream_t s, int *launches);
 
+// ---- decode GEMV with TMA-streamed MLX affine 4/8-bit weights (gemv_tma_q.cu)
+bool gemv_tma_q_supported(int H, int I, int bits);
+cudaError_t launch_gemv_tma_q_gateup(const uint16_t *x, int K, const Dispatch &d,
+                                     const ExpertWeights &w, int H, int I, int E, int max_rows,
+                                     uint16_t *yp, int32_t *err, cudaStream_t s, int *launches);
+cudaError_t launch_gemv_tma_q_down(const uint16_t *yp, const Dispatch &d, const ExpertWeights &w,
+                                   int H, int I, int E, int max_k, int max_rows, uint16_t *op,
+                                   int32_t *err, cudaStream_t s, int *launches);
+
 // ---- prefill grouped GEMM (gemm_sm100.cu), bf16 tcgen05 tiles
 struct GemmPlan;  // opaque, owns tensor maps
 bool gemm_supported(int H, int I);
@@ -103,6 +113,9 @@ cudaError_t launch_gemm_down(const uint16_t *yp, const Dispatch &d, const Expert
 // ---- quantisation (quant.cu)
 cudaError_t launch_quantize_affine(const uint16_t *w, int64_t rows, int cols, int gs, int bits,
                                    uint32_t *q, uint16_t *sc, uint16_t *bi, cudaStream_t s);
+// (scale, bias) pairs interleaved per group: [rows, groups] uint32
+cudaError_t launch_interleave_sb(const uint16_t *sc, const uint16_t *bi, int64_t n, uint32_t *out,
+                                 cudaStream_t s);
 // bf16 copy of the active experts' quantised rows (prefill path)
 cudaError_t launch_dequant_active(const uint32_t *q, const uint16_t *sc, const uint16_t *bi,
                                   int rows, int cols, int bits, const Dispatch &d, int E,

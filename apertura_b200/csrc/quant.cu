@@ -91,7 +91,24 @@ __global__ void dequant_active_kernel(const uint32_t *__restrict__ q, const uint
     }
 }
 
+// Repack scales/biases [rows, groups] x2 into one [rows, groups] uint32 array
+// of (scale | bias << 16) pairs: a row's pairs are contiguous (groups*4 bytes),
+// so a kernel stages a block of rows with plain 16-byte loads.
+__global__ void interleave_sb_kernel(const uint16_t *__restrict__ sc,
+                                     const uint16_t *__restrict__ bi, int64_t n,
+                                     uint32_t *__restrict__ out) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = (uint32_t)sc[i] | ((uint32_t)bi[i] << 16);
+}
+
 }  // namespace
+
+cudaError_t launch_interleave_sb(const uint16_t *sc, const uint16_t *bi, int64_t n, uint32_t *out,
+                                 cudaStream_t s) {
+    interleave_sb_kernel<<<1024, 256, 0, s>>>(sc, bi, n, out);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_dequant_active(const uint32_t *q, const uint16_t *sc, const uint16_t *bi,
                                   int rows, int cols, int bits, const Dispatch &d, int E,
