@@ -23,6 +23,8 @@
 // plain per-CTA load from this GPU's own memory.
 #include <cuda.h>
 
+#include <cstdlib>
+
 #include "common.cuh"
 #include "moe_internal.h"
 #include "launch_util.h"
@@ -123,7 +125,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     pdl_trigger();
     // EPI_F32 (router scores): one "expert", N = H outputs, and the B operand
     // (proj [H, I]) is reused for every I-wide slice of the K = 2*I split input.
-    const int NT = (EPI == EPI_GATEUP) ? I / BN2 : H / BN;
+    const int NT = (EPI == EPI_GATEUP) ? (I + BN2 - 1) / BN2 : H / BN;
     const int tiles = mtp[E] * NT;
     const int KB = Kdim / kBK;
 
@@ -206,8 +208,10 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             const uint32_t taddr = tmem_base + buf * kAccStride + ((uint32_t)(q * 32) << 16);
             if (EPI == EPI_GATEUP) {
                 uint16_t *dst = out + (size_t)row * out_ld + nt * BN2;
+                // the last n-tile may be partial (I not a multiple of BN2)
+                const int cmax = min(BN2, I - nt * BN2) / 8;
 #pragma unroll 1
-                for (int c = 0; c < BN2 / 8; ++c) {
+                for (int c = 0; c < cmax; ++c) {
                     uint32_t gr[8], ur[8];
                     tmem_ld8(taddr + c * 8, gr);
                     tmem_ld8(taddr + BN2 + c * 8, ur);
@@ -307,6 +311,7 @@ cudaError_t gemm_init() {
     cudaError_t e;
     if ((e = set_attr<EPI_F32, 64, 0, kRtStages>())) return e;
     if ((e = set_attr<EPI_GATEUP, 176, 88, kGuStages>())) return e;
+    if ((e = set_attr<EPI_GATEUP, 256, 128, kDnStages>())) return e;
     if ((e = set_attr<EPI_GATEUP, 128, 64, kGuStages>())) return e;
     if ((e = set_attr<EPI_DOWN, 256, 0, kDnStages>())) return e;
     return set_attr<EPI_DOWN, 128, 0, kDnStages>();
@@ -320,12 +325,20 @@ cudaError_t launch_gemm_gateup(const uint16_t *xp, const Dispatch &d, const Expe
                                int rows_cap, int H, int I, int E, uint16_t *yp, int32_t *err,
                                cudaStream_t s, int *launches) {
     if (E > kMaxExperts) return cudaErrorInvalidValue;
-    const int bn2 = (I % 88 == 0) ? 88 : 64;
+    // 128 gate + 128 up columns per tile (the last tile of I=704 is half
+    // used); APT_GATEUP_BN2=88 selects exact 88+88 tiles instead.
+    static const int pref = [] {
+        const char *v = getenv("APT_GATEUP_BN2");
+        return v ? atoi(v) : 128;
+    }();
+    const int bn2 = (pref == 88 && I % 88 == 0) ? 88 : (I >= 128 ? 128 : 64);
     CUtensorMap a, b;
     if (!make_map(&a, xp, H, rows_cap, kBM) || !make_map(&b, w.gu, H, (uint64_t)E * 2 * I, bn2))
         return cudaErrorInvalidValue;
     cudaError_t e = (bn2 == 88)
         ? launch<EPI_GATEUP, 176, 88, kGuStages>(a, b, d, E, H, I, H, yp, I, err, s)
+        : (bn2 == 128)
+        ? launch<EPI_GATEUP, 256, 128, kDnStages>(a, b, d, E, H, I, H, yp, I, err, s)
         : launch<EPI_GATEUP, 128, 64, kGuStages>(a, b, d, E, H, I, H, yp, I, err, s);
     if (launches) ++*launches;
     return e;
