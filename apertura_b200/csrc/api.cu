@@ -263,7 +263,7 @@ extern "C" apt_status apt_moe_create(const apt_moe_config *cfg, apt_moe_handle *
     ALLOC(active, E);
     ALLOC(n_active, 1);
     ALLOC(errflag, 4);
-    ALLOC(done, 1);
+    ALLOC(done, 16);
     ALLOC(hsplit, (size_t)h->Tm * 2 * H);
     ALLOC(rt_cnt, 4);
     ALLOC(xp, (size_t)h->Pcap * H);
@@ -280,7 +280,7 @@ extern "C" apt_status apt_moe_create(const apt_moe_config *cfg, apt_moe_handle *
     if (e1 == cudaSuccess) e1 = gemm_init();
     if (e1 == cudaSuccess) e1 = gemv_tma_init();
     if (e1 == cudaSuccess) e1 = cudaMemset(h->errflag, 0, 16);
-    if (e1 == cudaSuccess) e1 = cudaMemset(h->done, 0, 4);
+    if (e1 == cudaSuccess) e1 = cudaMemset(h->done, 0, 16 * sizeof(int32_t));
     for (int i = 0; i < APT_STAGE_COUNT && e1 == cudaSuccess; ++i)
         for (int j = 0; j < 2 && e1 == cudaSuccess; ++j) e1 = cudaEventCreate(&h->ev[i][j]);
     if (e1 != cudaSuccess) {

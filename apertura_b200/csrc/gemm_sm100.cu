@@ -325,13 +325,16 @@ cudaError_t launch_gemm_gateup(const uint16_t *xp, const Dispatch &d, const Expe
                                int rows_cap, int H, int I, int E, uint16_t *yp, int32_t *err,
                                cudaStream_t s, int *launches) {
     if (E > kMaxExperts) return cudaErrorInvalidValue;
-    // 128 gate + 128 up columns per tile (the last tile of I=704 is half
-    // used); APT_GATEUP_BN2=88 selects exact 88+88 tiles instead.
+    // Prefill (many rows per expert, tensor-bound): 128 gate + 128 up columns
+    // per tile, fewer staged bytes per flop; the last tile of I=704 is half
+    // used.  Decode-sized calls are HBM-bound, so they use exact 88+88 tiles
+    // that read no padding.  APT_GATEUP_BN2 (88 / 128) overrides.
     static const int pref = [] {
         const char *v = getenv("APT_GATEUP_BN2");
-        return v ? atoi(v) : 128;
+        return v ? atoi(v) : 0;
     }();
-    const int bn2 = (pref == 88 && I % 88 == 0) ? 88 : (I >= 128 ? 128 : 64);
+    const int want = pref ? pref : (rows_cap > 4096 ? 128 : 88);
+    const int bn2 = (want == 88 && I % 88 == 0) ? 88 : (I >= 128 ? 128 : 64);
     CUtensorMap a, b;
     if (!make_map(&a, xp, H, rows_cap, kBM) || !make_map(&b, w.gu, H, (uint64_t)E * 2 * I, bn2))
         return cudaErrorInvalidValue;

@@ -307,10 +307,12 @@ __global__ void router_select(const float *__restrict__ scores, const uint16_t *
     }
 }
 
-// Decode-sized fused routing: the scores of router_scores_small, then the
-// last CTA to finish (threadfence + counter, self-resetting) selects the
-// top-K of every token and builds the whole dispatch -- counts, offsets,
-// active-expert list and the stable sorted order -- in shared memory.
+// Decode-sized fused routing: the scores of router_scores_small; the last CTA
+// of each 8-token chunk (threadfence + per-chunk counter) selects the top-K of
+// the chunk's tokens, one warp per token; the last chunk to finish builds the
+// whole dispatch -- counts, offsets, active-expert list and the stable sorted
+// order -- in shared memory.  Counters live in `done` ([0] chunks, [1+c] CTAs
+// of chunk c) and are reset by the kernel itself.
 // Requires T <= 64, T*K <= kFusedMaxPairs, E <= 256.
 constexpr int kFusedMaxPairs = 512;
 
@@ -328,32 +330,49 @@ router_dispatch_small(const uint16_t *__restrict__ x, const uint16_t *__restrict
     __shared__ int s_cur[256];
     pdl_trigger();
     scores_small_block(x, proj, scale, T, H, E, eps, root, scores, hs);
+    // level 1: the last CTA of this token chunk selects the chunk's tokens
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
-        const int prev = atomicAdd(done, 1);
-        s_last = (prev == (int)(gridDim.x * gridDim.y) - 1);
+        const int prev = atomicAdd(done + 1 + blockIdx.y, 1);
+        s_last = (prev == (int)gridDim.x - 1);
     }
     __syncthreads();
     if (!s_last) return;
     __threadfence();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    constexpr int NW = kSmallThreads / 32;
+    {
+        const int t = blockIdx.y * kSmallTok + warp;  // 8 warps, 8 tokens per chunk
+        if (t < T) {
+            int e;
+            float wk;
+            select_token(scores + (size_t)t * E, pes, E, K, lane, e, wk);
+            if (lane < K) {
+                idx[(size_t)t * K + lane] = e;
+                w[(size_t)t * K + lane] = f2bf(wk);
+            }
+        }
+    }
+    if (tid == 0) done[1 + blockIdx.y] = 0;  // ready for the next call
+    // level 2: the last chunk builds the dispatch for all tokens
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const int prev = atomicAdd(done, 1);
+        s_last = (prev == (int)gridDim.y - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
     for (int e = tid; e < E; e += blockDim.x) {
         s_cnt[e] = 0;
         s_cur[e] = 0;
     }
     __syncthreads();
-    for (int t = warp; t < T; t += NW) {
-        int e;
-        float wk;
-        select_token(scores + (size_t)t * E, pes, E, K, lane, e, wk);
-        if (lane < K) {
-            idx[(size_t)t * K + lane] = e;
-            w[(size_t)t * K + lane] = f2bf(wk);
-            s_idx[t * K + lane] = e;
-            atomicAdd(&s_cnt[e], 1);
-        }
+    for (int p = tid; p < T * K; p += blockDim.x) {
+        const int e = __ldcg(idx + p);  // written by other CTAs of this grid
+        s_idx[p] = e;
+        atomicAdd(&s_cnt[e], 1);
     }
     __syncthreads();
     if (warp == 0) {  // exclusive scan of the counts, 8 experts per lane
