@@ -735,6 +735,38 @@ extern "C" apt_status apt_moe_ep_combine(apt_moe_handle *h, const uint16_t *rows
     return APT_OK;
 }
 
+extern "C" apt_status apt_moe_experts_grouped(apt_moe_handle *h, const uint16_t *rows, int R,
+                                              const int32_t *group_counts,
+                                              const int32_t *group_expert, int G, uint16_t *out,
+                                              void *stream) {
+    if (!h) return APT_ERR_INVALID;
+    if (R < 0 || R > h->Pcap)
+        return fail(h, APT_ERR_INVALID, "R=%d outside [0, max_tokens*top_k=%d]", R, h->Pcap);
+    if (R == 0) return APT_OK;
+    if (!rows || !group_counts || !group_expert || !out || G <= 0 || G > 256)
+        return fail(h, APT_ERR_INVALID, "bad grouped-experts arguments");
+    if (!h->gu) return fail(h, APT_ERR_STATE, "bf16 expert weights not loaded");
+    const int H = h->cfg.hidden_size, I = h->cfg.moe_intermediate_size, E = h->cfg.num_experts;
+    if (!gemm_supported(H, I)) return fail(h, APT_ERR_UNSUPPORTED, "shape not covered by the GEMM");
+    DeviceGuard g(h->cfg.device);
+    cudaStream_t s = (cudaStream_t)stream;
+    begin_call(h);
+    Dispatch d{};
+    d.counts = const_cast<int32_t *>(group_counts);
+    // group offsets go to the offsets workspace, or to the (larger) perm
+    // workspace when there are more groups than this handle has experts
+    d.offsets = (G > E) ? h->perm : h->offsets;
+    ExpertWeights ew = weights_for(h, false);
+    CUDA_TRY(h, launch_group_offsets(group_counts, G, d.offsets, s, &h->launches));
+    STAGE(h, APT_STAGE_GATE_UP, s,
+          launch_gemm_gateup_grouped(rows, d, group_expert, ew, R, H, I, E, G, h->yp, h->errflag,
+                                     s, &h->launches));
+    STAGE(h, APT_STAGE_DOWN, s,
+          launch_gemm_down_grouped(h->yp, d, group_expert, ew, R, H, I, E, G, out, h->errflag, s,
+                                   &h->launches));
+    return APT_OK;
+}
+
 extern "C" apt_status apt_moe_forward_host(apt_moe_handle *h, const uint16_t *x_host, int T,
                                            uint16_t *out_host, void *stream) {
     if (!h) return APT_ERR_INVALID;

@@ -174,7 +174,29 @@ __global__ void combine_kernel(const uint16_t *__restrict__ op, const int32_t *_
     }
 }
 
+__global__ void group_offsets_kernel(const int32_t *__restrict__ counts, int G,
+                                     int32_t *__restrict__ offsets) {
+    pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x == 0) {
+        int acc = 0;
+        for (int g = 0; g < G; ++g) {
+            offsets[g] = acc;
+            acc += counts[g];
+        }
+        offsets[G] = acc;
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_group_offsets(const int32_t *counts, int G, int32_t *offsets, cudaStream_t s,
+                                 int *launches) {
+    cudaError_t err = launch_ex(group_offsets_kernel, dim3(1), dim3(32), 0, s, true, counts, G,
+                                offsets);
+    if (launches) ++*launches;
+    return err;
+}
 
 cudaError_t launch_count(const int32_t *idx, int P, int E, int32_t *counts, cudaStream_t s,
                          int *launches) {

@@ -76,7 +76,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const int32_t *__restrict__ counts, const int32_t *__restrict__ offsets, int E,
                 int Kdim, int I, int H, uint16_t *__restrict__ out, int out_ld,
-                int32_t *__restrict__ err) {
+                int32_t *__restrict__ err, const int32_t *__restrict__ g2e) {
     constexpr int A_BYTES = Smem<BN>::A_BYTES, B_BYTES = Smem<BN>::B_BYTES;
     constexpr uint32_t IDESC = idesc_bf16_f32(kBM, BN);
     extern __shared__ uint8_t smem_raw[];
@@ -146,14 +146,17 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
                     tma_load_2d(sA + s * A_BYTES, &tmA, &full[s], kb * kBK, row0);
                     if (EPI == EPI_GATEUP) {
-                        const int gate_row = e * 2 * I + nt * BN2;
+                        // g2e: row group -> expert (grouped entry point); else identity
+                        const int ew = g2e ? g2e[e] : e;
+                        const int gate_row = ew * 2 * I + nt * BN2;
                         tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], kb * kBK, gate_row);
                         tma_load_2d(sB + s * B_BYTES + BN2 * kBK * 2, &tmB, &full[s], kb * kBK,
                                     gate_row + I);
                     } else if (EPI == EPI_F32) {
                         tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], (kb * kBK) % I, nt * BN);
                     } else {
-                        tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], kb * kBK, e * H + nt * BN);
+                        const int ew = g2e ? g2e[e] : e;
+                        tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], kb * kBK, ew * H + nt * BN);
                     }
                 }
             }
@@ -295,11 +298,12 @@ cudaError_t set_attr() {
 
 template <int EPI, int BN, int BN2, int STAGES>
 cudaError_t launch(const CUtensorMap &a, const CUtensorMap &b, const Dispatch &d, int E, int Kdim,
-                   int I, int H, uint16_t *out, int out_ld, int32_t *err, cudaStream_t s) {
+                   int I, int H, uint16_t *out, int out_ld, int32_t *err, cudaStream_t s,
+                   const int32_t *g2e = nullptr) {
     const int sms = num_sms(current_device());
     return launch_ex(moe_gemm_kernel<EPI, BN, BN2, STAGES>, dim3(sms), dim3(kThreads),
                      smem_bytes<EPI, BN, BN2, STAGES>(), s, true, a, b, d.counts, d.offsets, E,
-                     Kdim, I, H, out, out_ld, err);
+                     Kdim, I, H, out, out_ld, err, g2e);
 }
 
 // gate_up tile: BN2 gate + BN2 up rows; down tile: BN rows of W_down.
@@ -343,6 +347,40 @@ cudaError_t launch_gemm_gateup(const uint16_t *xp, const Dispatch &d, const Expe
         : (bn2 == 128)
         ? launch<EPI_GATEUP, 256, 128, kDnStages>(a, b, d, E, H, I, H, yp, I, err, s)
         : launch<EPI_GATEUP, 128, 64, kGuStages>(a, b, d, E, H, I, H, yp, I, err, s);
+    if (launches) ++*launches;
+    return e;
+}
+
+cudaError_t launch_gemm_gateup_grouped(const uint16_t *rows, const Dispatch &d,
+                                       const int32_t *g2e, const ExpertWeights &w, int rows_cap,
+                                       int H, int I, int E_w, int G, uint16_t *yp, int32_t *err,
+                                       cudaStream_t s, int *launches) {
+    if (G > kMaxExperts) return cudaErrorInvalidValue;
+    const int bn2 = (rows_cap > 4096 || I % 88) ? (I >= 128 ? 128 : 64) : 88;
+    CUtensorMap a, b;
+    if (!make_map(&a, rows, H, rows_cap, kBM) || !make_map(&b, w.gu, H, (uint64_t)E_w * 2 * I, bn2))
+        return cudaErrorInvalidValue;
+    cudaError_t e = (bn2 == 88)
+        ? launch<EPI_GATEUP, 176, 88, kGuStages>(a, b, d, G, H, I, H, yp, I, err, s, g2e)
+        : (bn2 == 128)
+        ? launch<EPI_GATEUP, 256, 128, kDnStages>(a, b, d, G, H, I, H, yp, I, err, s, g2e)
+        : launch<EPI_GATEUP, 128, 64, kGuStages>(a, b, d, G, H, I, H, yp, I, err, s, g2e);
+    if (launches) ++*launches;
+    return e;
+}
+
+cudaError_t launch_gemm_down_grouped(const uint16_t *yp, const Dispatch &d, const int32_t *g2e,
+                                     const ExpertWeights &w, int rows_cap, int H, int I, int E_w,
+                                     int G, uint16_t *out, int32_t *err, cudaStream_t s,
+                                     int *launches) {
+    if (G > kMaxExperts) return cudaErrorInvalidValue;
+    const int bn = (H % 256 == 0) ? 256 : 128;
+    CUtensorMap a, b;
+    if (!make_map(&a, yp, I, rows_cap, kBM) || !make_map(&b, w.dn, I, (uint64_t)E_w * H, bn))
+        return cudaErrorInvalidValue;
+    cudaError_t e = (bn == 256)
+        ? launch<EPI_DOWN, 256, 0, kDnStages>(a, b, d, G, I, I, H, out, H, err, s, g2e)
+        : launch<EPI_DOWN, 128, 0, kDnStages>(a, b, d, G, I, I, H, out, H, err, s, g2e);
     if (launches) ++*launches;
     return e;
 }

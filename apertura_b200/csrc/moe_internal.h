@@ -110,6 +110,20 @@ cudaError_t launch_gemm_down(const uint16_t *yp, const Dispatch &d, const Expert
                              int rows_cap, int H, int I, int E, uint16_t *op, int32_t *err,
                              cudaStream_t s, int *launches);
 
+// Grouped variants: G row groups (counts/offsets in d), group g uses the
+// weights of expert g2e[g]; rows are consumed in place (no gather).
+cudaError_t launch_gemm_gateup_grouped(const uint16_t *rows, const Dispatch &d,
+                                       const int32_t *g2e, const ExpertWeights &w, int rows_cap,
+                                       int H, int I, int E_w, int G, uint16_t *yp, int32_t *err,
+                                       cudaStream_t s, int *launches);
+cudaError_t launch_gemm_down_grouped(const uint16_t *yp, const Dispatch &d, const int32_t *g2e,
+                                     const ExpertWeights &w, int rows_cap, int H, int I, int E_w,
+                                     int G, uint16_t *out, int32_t *err, cudaStream_t s,
+                                     int *launches);
+// offsets = exclusive scan of G group counts (one CTA); offsets[G] = total
+cudaError_t launch_group_offsets(const int32_t *counts, int G, int32_t *offsets, cudaStream_t s,
+                                 int *launches);
+
 // ---- quantisation (quant.cu)
 cudaError_t launch_quantize_affine(const uint16_t *w, int64_t rows, int cols, int gs, int bits,
                                    uint32_t *q, uint16_t *sc, uint16_t *bi, cudaStream_t s);

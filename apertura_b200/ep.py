@@ -18,7 +18,8 @@ rows are already grouped by destination rank: they are the send buffer.
 Per step (one process per GPU, torch.distributed over NCCL for the plumbing):
   1. apt_moe_ep_dispatch: route, top-K, dispatch, gather rows (send buffer)
   2. all_to_all of the per-expert counts (E ints), then of the rows
-  3. apt_moe_experts on the local experts (K=1, w=1): unweighted expert rows
+  3. apt_moe_experts_grouped on the local experts: the received rows, grouped
+     by (source rank, local expert), run in place -> unweighted expert rows
   4. all_to_all of the result rows back (reverse splits)
   5. apt_moe_ep_combine: weighted k-order combine on the home rank
 The compute steps go through a backend object built by a factory; the
@@ -90,15 +91,17 @@ class CudaBackend:
                                                     _ptr(rows), _ptr(counts), _stream(x.device)))
         return idx, w, rows, counts
 
-    def experts(self, rows, local_ids):
+    def experts(self, rows, group_counts, group_expert):
+        """Rows grouped as (source rank, local expert): apt_moe_experts_grouped
+        consumes them in place."""
         R, H = rows.shape
         out = torch.empty_like(rows)
         if R == 0:
             return out
-        w1 = torch.ones(R, 1, dtype=torch.bfloat16, device=rows.device)
-        ids = local_ids.view(R, 1).to(torch.int32).contiguous()
-        self.local.check(lib().apt_moe_experts(self.local.h, _ptr(rows), _ptr(ids), _ptr(w1), R,
-                                               _ptr(out), _stream(rows.device)))
+        G = group_counts.numel()
+        self.local.check(lib().apt_moe_experts_grouped(
+            self.local.h, _ptr(rows), R, _ptr(group_counts), _ptr(group_expert), G, _ptr(out),
+            _stream(rows.device)))
         return out
 
     def combine(self, back, idx, w):
@@ -142,6 +145,9 @@ class ExpertParallelMoE:
         self.max_recv = int(capacity_factor * max_tokens_per_rank * K)
         cfg_r = ESModelConfig(**{**cfg.__dict__, "moe_sparse": True,
                                  "max_tokens": max_tokens_per_rank})
+        # group g = (source rank g // E_loc, local expert g % E_loc)
+        self.group_expert = torch.arange(self.E_loc, dtype=torch.int32).repeat(self.world).to(
+            proj.device)
         make = backend or CudaBackend  # a factory with CudaBackend's signature
         self.backend = make(cfg_r, proj_r, scale, pes_r, gu_loc, dn_loc, self.max_recv)
         self.last_recv_rows = 0
@@ -165,11 +171,9 @@ class ExpertParallelMoE:
         # 2. token rows to the expert owners
         recv_rows = torch.empty(R, H, dtype=rows.dtype, device=rows.device)
         dist.all_to_all_single(recv_rows, rows, recv_splits, send_splits, group=self.group)
-        # rows from each source arrive grouped by local expert, ascending
-        local_ids = torch.repeat_interleave(
-            torch.arange(E_loc, dtype=torch.int32).repeat(N), recv_per.flatten()).to(rows.device)
-        # 3. local experts, unweighted
-        out_rows = self.backend.experts(recv_rows, local_ids)
+        # 3. local experts, unweighted: rows from each source arrive grouped by
+        #    local expert, so (source, expert) groups run in place
+        out_rows = self.backend.experts(recv_rows, recv_counts, self.group_expert)
         # 4. back to the home ranks, in the send order
         back = torch.empty_like(rows)
         dist.all_to_all_single(back, out_rows, send_splits, recv_splits, group=self.group)

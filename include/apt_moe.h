@@ -177,6 +177,19 @@ APT_API apt_status apt_moe_ep_dispatch(apt_moe_handle *h, const uint16_t *x, int
 APT_API apt_status apt_moe_ep_combine(apt_moe_handle *h, const uint16_t *rows, const int32_t *idx,
                                       const uint16_t *w, int T, uint16_t *out, void *stream);
 
+/*
+ * Expert-parallel remote compute on rows that arrive already grouped: R rows
+ * [R,H] (device) in G consecutive groups of group_counts[g] rows (device,
+ * int32 [G]); group g runs expert group_expert[g] (device, int32 [G]) of this
+ * handle's bank.  out [R,H] receives the unweighted expert outputs in the
+ * same row order.  No gather and no combine: the rows are consumed in place.
+ * Requires R <= max_tokens * top_k_experts and G <= 256.
+ */
+APT_API apt_status apt_moe_experts_grouped(apt_moe_handle *h, const uint16_t *rows, int R,
+                                           const int32_t *group_counts,
+                                           const int32_t *group_expert, int G, uint16_t *out,
+                                           void *stream);
+
 /* Synchronise the handle's device and report any pending CUDA error. */
 APT_API apt_status apt_moe_sync(apt_moe_handle *h);
 

@@ -63,12 +63,12 @@ class OracleBackend:
         t = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16)
         return (torch.from_numpy(idx), t(w), t(rows), torch.from_numpy(counts))
 
-    def experts(self, rows, local_ids):
+    def experts(self, rows, group_counts, group_expert):
         R = rows.shape[0]
         if R == 0:
             return rows.clone()
         rb = rows.contiguous().view(torch.int16).numpy().view(np.uint16)
-        ids = local_ids.numpy().astype(np.int32).reshape(R, 1)
+        ids = np.repeat(group_expert.numpy(), group_counts.numpy()).astype(np.int32).reshape(R, 1)
         ones = self.O.f32_to_bf16(np.ones((R, 1), np.float32))
         out = self.O.experts_sparse(rb, self.gu, self.dn, ids, ones)
         return torch.from_numpy(out.view(np.int16)).view(torch.bfloat16)

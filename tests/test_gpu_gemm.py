@@ -76,3 +76,36 @@ def test_gemm_prefill_sample_vs_oracle(oracle):
     got, refv = bf16_to_f32(_np(out))[rows], bf16_to_f32(ref)
     ok, ma, cos = block_close(got, refv)
     assert ok and ma <= TIGHT_REL * np.abs(refv).max(), (ma, cos)
+
+
+def test_experts_grouped_in_place(oracle):
+    """apt_moe_experts_grouped (the expert-parallel remote step): rows in G
+    groups, group g on expert g2e[g], unweighted outputs in row order."""
+    import ctypes
+    H, E, I = 2816, 16, 704
+    d = block_inputs(4, seed=31, device=DEV, H=H, E=E, K=4, I=I)
+    rng = np.random.default_rng(4)
+    G = 32
+    counts = rng.integers(0, 40, size=G).astype(np.int32)
+    counts[5] = 0
+    g2e = rng.integers(0, E, size=G).astype(np.int32)
+    R = int(counts.sum())
+    rows = torch.randn(R, H, device=DEV).to(torch.bfloat16)
+    cfg = A.ESModelConfig(hidden_size=H, num_experts=E, top_k_experts=1, moe_intermediate_size=I,
+                          moe_sparse=True, max_tokens=R)
+    h = A.Handle(cfg)
+    ex = A.ESExperts(d["gate_up"], d["down"], handle=h)
+    out = torch.empty_like(rows)
+    c_t = torch.from_numpy(counts).to(DEV)
+    g_t = torch.from_numpy(g2e).to(DEV)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    h.check(A.lib().apt_moe_experts_grouped(h.h, P(rows), R, P(c_t), P(g_t), G, P(out), None))
+    torch.cuda.synchronize()
+    h.sync()
+    ids = np.repeat(g2e, counts).reshape(R, 1).astype(np.int32)
+    ones = oracle.f32_to_bf16(np.ones((R, 1), np.float32))
+    ref = oracle.experts_sparse(_np(rows), _np(d["gate_up"]), _np(d["down"]), ids, ones)
+    got, refv = bf16_to_f32(_np(out)), bf16_to_f32(ref)
+    ok, ma, cos = block_close(got, refv)
+    assert ok and ma <= TIGHT_REL * np.abs(refv).max(), (ma, cos)
+    del ex
