@@ -62,6 +62,8 @@ struct apt_moe_handle {
     int32_t *idx2 = nullptr;    // dense pair lists [Pcap]
     uint16_t *w2 = nullptr;
     uint16_t *xin = nullptr, *xout = nullptr;  // host-API staging [Tm,H]
+    uint16_t *xn = nullptr;                    // pre_ff_ln_2(x1) [Tm,H] (layer entry point)
+    const uint16_t *cur_post_w = nullptr;      // post_ff_ln_2 weight of the current call
 
     Dispatch disp() const { return Dispatch{counts, offsets, perm, inv, active, n_active}; }
 };
@@ -274,6 +276,7 @@ extern "C" apt_status apt_moe_create(const apt_moe_config *cfg, apt_moe_handle *
     ALLOC(w2, h->Pcap);
     ALLOC(xin, (size_t)h->Tm * H);
     ALLOC(xout, (size_t)h->Tm * H);
+    ALLOC(xn, (size_t)h->Tm * H);
 #undef ALLOC
     if (e1 == cudaSuccess) e1 = router_init();
     if (e1 == cudaSuccess) e1 = gemv_init();
@@ -297,7 +300,7 @@ extern "C" apt_status apt_moe_destroy(apt_moe_handle *h) {
     void *ptrs[] = {h->proj, h->scale, h->pes, h->gu, h->dn, h->gu_q, h->dn_q, h->gu_s, h->gu_b,
                     h->dn_s, h->dn_b, h->scores, h->idx_i, h->w_i, h->counts, h->offsets,
                     h->perm, h->inv, h->active, h->n_active, h->errflag, h->done, h->hsplit, h->rt_cnt, h->xp, h->yp, h->op,
-                    h->Wd, h->idx2, h->w2, h->xin, h->xout, h->dq_gu, h->dq_dn, h->gu_sb, h->dn_sb};
+                    h->Wd, h->idx2, h->w2, h->xin, h->xout, h->dq_gu, h->dq_dn, h->gu_sb, h->dn_sb, h->xn};
     for (void *p : ptrs) dfree(p);
     for (int i = 0; i < APT_STAGE_COUNT; ++i)
         for (int j = 0; j < 2; ++j)
@@ -478,17 +481,22 @@ apt_status check_T(apt_moe_handle *h, int T) {
 
 // Router scores [T,E] f32 into h->scores: tensor-core split GEMM for
 // prefill-sized T, f32 SIMT kernels otherwise.
-apt_status router_scores(apt_moe_handle *h, const uint16_t *x, int T, cudaStream_t s) {
+apt_status router_scores(apt_moe_handle *h, const uint16_t *x, int T, cudaStream_t s,
+                         const uint16_t *pre_w = nullptr) {
     const int H = h->cfg.hidden_size, E = h->cfg.num_experts;
     if (T > 64 && E % 64 == 0 && gemm_supported(H, h->cfg.moe_intermediate_size)) {
         STAGE(h, APT_STAGE_ROUTER_SCORES, s,
               launch_router_norm_split(x, h->scale, T, H, h->cfg.rms_norm_eps, h->hsplit,
-                                       h->rt_cnt, s, &h->launches));
+                                       h->rt_cnt, s, &h->launches, pre_w,
+                                       pre_w ? h->xn : nullptr));
         STAGE(h, APT_STAGE_ROUTER_SCORES, s,
               launch_gemm_router(h->hsplit, h->proj, h->rt_cnt, T, H, E, h->scores, h->errflag, s,
                                  &h->launches));
         return APT_OK;
     }
+    if (pre_w)
+        STAGE(h, APT_STAGE_ROUTER_SCORES, s,
+              launch_rmsnorm(x, pre_w, T, H, h->cfg.rms_norm_eps, h->xn, s, &h->launches));
     STAGE(h, APT_STAGE_ROUTER_SCORES, s,
           launch_router_scores(x, h->proj, h->scale, T, H, E, h->cfg.rms_norm_eps, h->scores, s,
                                &h->launches));
@@ -546,7 +554,9 @@ apt_status run_experts(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
         STAGE(h, APT_STAGE_GATE_UP, s, launch_gemv_gateup(x, Kp, d, ew, H, I, E, max_rows, h->yp, s, &h->launches));
         STAGE(h, APT_STAGE_DOWN, s, launch_gemv_down(h->yp, d, ew, H, I, E, max_rows, h->op, s, &h->launches));
     }
-    STAGE(h, APT_STAGE_COMBINE, s, launch_combine(h->op, idx, w, d, T, Kp, H, out, s, &h->launches));
+    STAGE(h, APT_STAGE_COMBINE, s,
+          launch_combine(h->op, idx, w, d, T, Kp, H, out, s, &h->launches, h->cur_post_w,
+                         h->cfg.rms_norm_eps));
     return APT_OK;
 }
 
@@ -642,9 +652,13 @@ extern "C" apt_status apt_moe_experts_dense(apt_moe_handle *h, const uint16_t *x
     return experts_dense(h, x, W, T, out, (cudaStream_t)stream);
 }
 
-extern "C" apt_status apt_moe_forward(apt_moe_handle *h, const uint16_t *x_router,
-                                      const uint16_t *x_experts, int T, uint16_t *out,
-                                      int32_t *idx_out, uint16_t *w_out, void *stream) {
+namespace {
+// The MoE section of ESDecoderLayer::forward.  With pre_w, the expert input is
+// pre_ff_ln_2(x_router) computed on the way (x_experts ignored); with post_w,
+// the output is post_ff_ln_2 of the block output (fused into the combine).
+apt_status forward_impl(apt_moe_handle *h, const uint16_t *x_router, const uint16_t *x_experts,
+                        int T, uint16_t *out, int32_t *idx_out, uint16_t *w_out, void *stream,
+                        const uint16_t *pre_w, const uint16_t *post_w) {
     if (!h) return APT_ERR_INVALID;
     if (check_T(h, T)) return APT_ERR_INVALID;
     if (T == 0) return APT_OK;
@@ -657,6 +671,12 @@ extern "C" apt_status apt_moe_forward(apt_moe_handle *h, const uint16_t *x_route
     const int H = h->cfg.hidden_size, E = h->cfg.num_experts, K = h->cfg.top_k_experts;
     int32_t *idx = idx_out ? idx_out : h->idx_i;
     uint16_t *w = w_out ? w_out : h->w_i;
+    if (pre_w) x_experts = h->xn;
+    h->cur_post_w = post_w;
+    struct ClearPost {
+        apt_moe_handle *h;
+        ~ClearPost() { h->cur_post_w = nullptr; }
+    } clear_post{h};
     if (h->cfg.moe_sparse && router_dispatch_fusable(T, H, E, K)) {
         // decode: router + top-k + dispatch in one launch
         const bool quant = h->qbits > 0;
@@ -665,10 +685,10 @@ extern "C" apt_status apt_moe_forward(apt_moe_handle *h, const uint16_t *x_route
         STAGE(h, APT_STAGE_ROUTER_SCORES, s,
               launch_router_dispatch(x_router, h->proj, h->scale, h->pes, T, H, E, K,
                                      h->cfg.rms_norm_eps, h->scores, idx, w, h->disp(), h->done,
-                                     s, &h->launches));
+                                     s, &h->launches, pre_w, pre_w ? h->xn : nullptr));
         return run_experts(h, x_experts, idx, w, T, K, quant, out, s, true);
     }
-    if (apt_status st = router_scores(h, x_router, T, s)) return st;
+    if (apt_status st = router_scores(h, x_router, T, s, pre_w)) return st;
     if (h->cfg.moe_sparse) {
         CUDA_TRY(h, cudaMemsetAsync(h->counts, 0, sizeof(int32_t) * E, s));
         STAGE(h, APT_STAGE_ROUTER_SELECT, s, launch_router_select(h->scores, h->pes, T, E, K, idx, w, h->counts, s,
@@ -680,6 +700,25 @@ extern "C" apt_status apt_moe_forward(apt_moe_handle *h, const uint16_t *x_route
                                      &h->launches));
     STAGE(h, APT_STAGE_ROUTER_SELECT, s, launch_scatter_dense(idx, w, T, E, K, h->Wd, s, &h->launches));
     return experts_dense(h, x_experts, h->Wd, T, out, s);
+}
+
+}  // namespace
+
+extern "C" apt_status apt_moe_forward(apt_moe_handle *h, const uint16_t *x_router,
+                                      const uint16_t *x_experts, int T, uint16_t *out,
+                                      int32_t *idx_out, uint16_t *w_out, void *stream) {
+    return forward_impl(h, x_router, x_experts, T, out, idx_out, w_out, stream, nullptr, nullptr);
+}
+
+extern "C" apt_status apt_moe_layer_forward(apt_moe_handle *h, const uint16_t *x1,
+                                            const uint16_t *pre_ff_ln_2_w,
+                                            const uint16_t *post_ff_ln_2_w, int T, uint16_t *out,
+                                            void *stream) {
+    if (!h) return APT_ERR_INVALID;
+    if (!pre_ff_ln_2_w || !post_ff_ln_2_w) return fail(h, APT_ERR_INVALID, "null norm weight");
+    if (h->cfg.hidden_size % 8) return fail(h, APT_ERR_UNSUPPORTED, "hidden_size % 8");
+    return forward_impl(h, x1, nullptr, T, out, nullptr, nullptr, stream, pre_ff_ln_2_w,
+                        post_ff_ln_2_w);
 }
 
 // ---- expert-parallel halves: the routing + dispatch before the all-to-all,

@@ -131,9 +131,12 @@ constexpr int kMaxK = 256;
 
 __global__ void combine_kernel(const uint16_t *__restrict__ op, const int32_t *__restrict__ idx,
                                const uint16_t *__restrict__ w, const int32_t *__restrict__ inv,
-                               int T, int K, int H, uint16_t *__restrict__ out) {
+                               int T, int K, int H, uint16_t *__restrict__ out,
+                               const uint16_t *__restrict__ post_w, float eps) {
     __shared__ int s_row[kMaxK];
     __shared__ float s_w[kMaxK];
+    __shared__ float s_red[32];
+    extern __shared__ float s_moe[];  // [H] when post_w: the bf16 block output before the norm
     const int t = blockIdx.x;
     pdl_trigger();
     pdl_wait();
@@ -144,6 +147,7 @@ __global__ void combine_kernel(const uint16_t *__restrict__ op, const int32_t *_
         s_w[k] = live ? bf2f(w[p]) : 0.f;
     }
     __syncthreads();
+    float ss = 0.f;
     for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
         float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
         constexpr int B = 8;  // rows in flight per batch
@@ -165,12 +169,45 @@ __global__ void combine_kernel(const uint16_t *__restrict__ op, const int32_t *_
                 for (int q = 0; q < 8; ++q) acc[q] = __fadd_rn(acc[q], rbf(__fmul_rn(wk, f[q])));
             }
         }
-        uint4 r;
-        r.x = pack_bf2(acc[0], acc[1]);
-        r.y = pack_bf2(acc[2], acc[3]);
-        r.z = pack_bf2(acc[4], acc[5]);
-        r.w = pack_bf2(acc[6], acc[7]);
-        *reinterpret_cast<uint4 *>(out + (size_t)t * H + v * 8) = r;
+        if (post_w) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float m = rbf(acc[q]);  // the MoE output is bf16 before post_ff_ln_2
+                s_moe[v * 8 + q] = m;
+                ss = fmaf(m, m, ss);
+            }
+        } else {
+            uint4 r;
+            r.x = pack_bf2(acc[0], acc[1]);
+            r.y = pack_bf2(acc[2], acc[3]);
+            r.z = pack_bf2(acc[4], acc[5]);
+            r.w = pack_bf2(acc[6], acc[7]);
+            *reinterpret_cast<uint4 *>(out + (size_t)t * H + v * 8) = r;
+        }
+    }
+    if (!post_w) return;
+    // post_ff_ln_2 (ESRMSNorm.mm:14-28) over the finished row
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = (threadIdx.x < (blockDim.x + 31) / 32) ? s_red[threadIdx.x] : 0.f;
+        v = warp_sum(v);
+        if (threadIdx.x == 0) s_red[0] = v;
+    }
+    __syncthreads();
+    const float r = 1.0f / sqrtf(__fadd_rn(__fmul_rn(s_red[0], 1.0f / (float)H), eps));
+    for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
+        float wf[8], o[8];
+        unpack8(*reinterpret_cast<const uint4 *>(post_w + v * 8), wf);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) o[q] = __fmul_rn(__fmul_rn(s_moe[v * 8 + q], r), wf[q]);
+        uint4 rr;
+        rr.x = pack_bf2(o[0], o[1]);
+        rr.y = pack_bf2(o[2], o[3]);
+        rr.z = pack_bf2(o[4], o[5]);
+        rr.w = pack_bf2(o[6], o[7]);
+        *reinterpret_cast<uint4 *>(out + (size_t)t * H + v * 8) = rr;
     }
 }
 
@@ -228,10 +265,11 @@ cudaError_t launch_gather_rows(const uint16_t *x, int H, int K, int E, const Dis
 
 cudaError_t launch_combine(const uint16_t *op, const int32_t *idx, const uint16_t *w,
                            const Dispatch &d, int T, int K, int H, uint16_t *out, cudaStream_t s,
-                           int *launches) {
+                           int *launches, const uint16_t *post_w, float eps) {
     const int threads = min(512, ((H / 8 + 31) / 32) * 32);
-    cudaError_t err = launch_ex(combine_kernel, dim3(T), dim3(threads), 0, s, true, op, idx, w,
-                                (const int32_t *)d.inv, T, K, H, out);
+    const size_t smem = post_w ? (size_t)H * sizeof(float) : 0;
+    cudaError_t err = launch_ex(combine_kernel, dim3(T), dim3(threads), smem, s, true, op, idx, w,
+                                (const int32_t *)d.inv, T, K, H, out, post_w, eps);
     if (launches) ++*launches;
     return err;
 }

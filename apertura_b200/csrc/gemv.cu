@@ -385,8 +385,10 @@ void launch_down_fmt(const GemvArgs &a, int E, int max_rows, size_t smem, cudaSt
     }
 }
 
+// Token rows staged per pass: the power of two the kernel is specialised for
+// (1, 2, 4 or 8), so every specialised inner loop stays inside the staged rows.
 int tok_chunk_for(int max_rows) {
-    return max_rows < kTokChunk ? (max_rows < 1 ? 1 : max_rows) : kTokChunk;
+    return max_rows <= 1 ? 1 : max_rows <= 2 ? 2 : max_rows <= 4 ? 4 : kTokChunk;
 }
 
 }  // namespace

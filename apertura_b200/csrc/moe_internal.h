@@ -36,12 +36,18 @@ bool router_dispatch_fusable(int T, int H, int E, int K);
 cudaError_t launch_router_dispatch(const uint16_t *x, const uint16_t *proj, const uint16_t *scale,
                                    const uint16_t *pes, int T, int H, int E, int K, float eps,
                                    float *scores, int32_t *idx, uint16_t *w, const Dispatch &d,
-                                   int32_t *done, cudaStream_t s, int *launches);
+                                   int32_t *done, cudaStream_t s, int *launches,
+                                   const uint16_t *pre_w = nullptr, uint16_t *xn = nullptr);
 // Tensor-core router path: two-term bf16 split of the f32 router input, then
 // an f32-output tcgen05 GEMM against proj (gemm_sm100.cu).
+// pre_w/xn (optional): also write xn = RMSNorm(x) * pre_w (pre_ff_ln_2)
 cudaError_t launch_router_norm_split(const uint16_t *x, const uint16_t *scale, int T, int H,
                                      float eps, uint16_t *hs, int32_t *cnt_off, cudaStream_t s,
-                                     int *launches);
+                                     int *launches, const uint16_t *pre_w = nullptr,
+                                     uint16_t *xn = nullptr);
+// out = RMSNorm(x) * w (ESRMSNorm.mm:14-28), one warp per row
+cudaError_t launch_rmsnorm(const uint16_t *x, const uint16_t *w, int T, int H, float eps,
+                          uint16_t *out, cudaStream_t s, int *launches);
 cudaError_t launch_gemm_router(const uint16_t *hs, const uint16_t *proj, const int32_t *cnt_off,
                                int T, int H, int E, float *scores, int32_t *err, cudaStream_t s,
                                int *launches);
@@ -61,9 +67,11 @@ cudaError_t launch_dispatch(const int32_t *idx, int P, int E, const Dispatch &d,
 cudaError_t launch_gather_rows(const uint16_t *x, int H, int K, int E, const Dispatch &d,
                                int max_rows, uint16_t *xp, cudaStream_t s, int *launches);
 // out[t] = bf16( sum_k f32(bf16(w[t,k] * op[inv[t*K+k]])) )
+// post_w (optional): out = RMSNorm(combine) * post_w, eps (post_ff_ln_2)
 cudaError_t launch_combine(const uint16_t *op, const int32_t *idx, const uint16_t *w,
                            const Dispatch &d, int T, int K, int H, uint16_t *out,
-                           cudaStream_t s, int *launches);
+                           cudaStream_t s, int *launches, const uint16_t *post_w = nullptr,
+                           float eps = 0.f);
 
 // ---- decode GEMV (gemv.cu).  Weight formats: bits == 0 -> bf16, else affine.
 struct ExpertWeights {

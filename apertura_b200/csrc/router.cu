@@ -54,7 +54,9 @@ __device__ __forceinline__ void scores_small_block(const uint16_t *__restrict__ 
                                                    const uint16_t *__restrict__ proj,
                                                    const uint16_t *__restrict__ scale, int T,
                                                    int H, int E, float eps, float root,
-                                                   float *__restrict__ scores, float *hs) {
+                                                   float *__restrict__ scores, float *hs,
+                                                   const uint16_t *__restrict__ pre_w = nullptr,
+                                                   uint16_t *__restrict__ xn = nullptr) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e = blockIdx.x * kSmallWarps + (warp & (kSmallWarps - 1));
     const int tg = warp / kSmallWarps;  // token group of this warp in the dot phase
@@ -98,6 +100,24 @@ __device__ __forceinline__ void scores_small_block(const uint16_t *__restrict__ 
                 *reinterpret_cast<float4 *>(dst + i * 256) = make_float4(hv[0], hv[1], hv[2], hv[3]);
                 *reinterpret_cast<float4 *>(dst + i * 256 + 4) = make_float4(hv[4], hv[5], hv[6], hv[7]);
             }
+        // pre_ff_ln_2(x1) as a by-product: the same r, times the norm weight
+        // (ESRMSNorm.mm:21-26), written once per token (expert group 0)
+        if (xn && blockIdx.x == 0) {
+            uint16_t *xo = xn + (size_t)(t0 + warp) * H + lane * 8;
+#pragma unroll
+            for (int i = 0; i < kMaxVec; ++i)
+                if (i < nv) {
+                    float f[8], wf[8];
+                    unpack8(xv[i], f);
+                    unpack8(__ldg(reinterpret_cast<const uint4 *>(pre_w + i * 256 + lane * 8)), wf);
+                    uint4 o;
+                    o.x = pack_bf2(__fmul_rn(__fmul_rn(f[0], r), wf[0]), __fmul_rn(__fmul_rn(f[1], r), wf[1]));
+                    o.y = pack_bf2(__fmul_rn(__fmul_rn(f[2], r), wf[2]), __fmul_rn(__fmul_rn(f[3], r), wf[3]));
+                    o.z = pack_bf2(__fmul_rn(__fmul_rn(f[4], r), wf[4]), __fmul_rn(__fmul_rn(f[5], r), wf[5]));
+                    o.w = pack_bf2(__fmul_rn(__fmul_rn(f[6], r), wf[6]), __fmul_rn(__fmul_rn(f[7], r), wf[7]));
+                    *reinterpret_cast<uint4 *>(xo + i * 256) = o;
+                }
+        }
     }
     __syncthreads();
     constexpr int TPW = kSmallTok / (kSmallThreads / 32 / kSmallWarps);  // tokens per warp
@@ -321,7 +341,8 @@ router_dispatch_small(const uint16_t *__restrict__ x, const uint16_t *__restrict
                       const uint16_t *__restrict__ scale, const uint16_t *__restrict__ pes, int T,
                       int H, int E, int K, float eps, float root, float *__restrict__ scores,
                       int32_t *__restrict__ idx, uint16_t *__restrict__ w, Dispatch d,
-                      int32_t *__restrict__ done) {
+                      int32_t *__restrict__ done, const uint16_t *__restrict__ pre_w,
+                      uint16_t *__restrict__ xn) {
     extern __shared__ float hs[];
     __shared__ int s_last;
     __shared__ int s_idx[kFusedMaxPairs];
@@ -329,7 +350,7 @@ router_dispatch_small(const uint16_t *__restrict__ x, const uint16_t *__restrict
     __shared__ int s_off[257];
     __shared__ int s_cur[256];
     pdl_trigger();
-    scores_small_block(x, proj, scale, T, H, E, eps, root, scores, hs);
+    scores_small_block(x, proj, scale, T, H, E, eps, root, scores, hs, pre_w, xn);
     // level 1: the last CTA of this token chunk selects the chunk's tokens
     __threadfence();
     __syncthreads();
@@ -446,7 +467,8 @@ router_dispatch_small(const uint16_t *__restrict__ x, const uint16_t *__restrict
 __global__ void router_norm_split(const uint16_t *__restrict__ x,
                                   const uint16_t *__restrict__ scale, int T, int H, float eps,
                                   float root, uint16_t *__restrict__ hs,
-                                  int32_t *__restrict__ cnt_off) {
+                                  int32_t *__restrict__ cnt_off,
+                                  const uint16_t *__restrict__ pre_w, uint16_t *__restrict__ xn) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         cnt_off[0] = T;
@@ -484,6 +506,46 @@ __global__ void router_norm_split(const uint16_t *__restrict__ x,
         v2.z = pack_bf2(h2[4], h2[5]); v2.w = pack_bf2(h2[6], h2[7]);
         *reinterpret_cast<uint4 *>(d1 + i) = v1;
         *reinterpret_cast<uint4 *>(d2 + i) = v2;
+        if (xn) {  // pre_ff_ln_2(x1): the same r times the norm weight
+            float wf[8], o[8];
+            unpack8(*reinterpret_cast<const uint4 *>(pre_w + i), wf);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = __fmul_rn(__fmul_rn(f[j], r), wf[j]);
+            uint4 v;
+            v.x = pack_bf2(o[0], o[1]); v.y = pack_bf2(o[2], o[3]);
+            v.z = pack_bf2(o[4], o[5]); v.w = pack_bf2(o[6], o[7]);
+            *reinterpret_cast<uint4 *>(xn + (size_t)warp * H + i) = v;
+        }
+    }
+}
+
+// Standalone RMSNorm with weight (ESRMSNorm.mm:14-28), one warp per row.
+__global__ void rmsnorm_kernel(const uint16_t *__restrict__ x, const uint16_t *__restrict__ wgt,
+                               int T, int H, float eps, uint16_t *__restrict__ out) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    pdl_trigger();
+    pdl_wait();
+    if (warp >= T) return;
+    const uint16_t *xr = x + (size_t)warp * H;
+    float ss = 0.f;
+    for (int i = lane * 8; i < H; i += 256) {
+        float f[8];
+        unpack8(*reinterpret_cast<const uint4 *>(xr + i), f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+    }
+    ss = warp_sum(ss);
+    const float r = 1.0f / sqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / (float)H), eps));
+    for (int i = lane * 8; i < H; i += 256) {
+        float f[8], wf[8], o[8];
+        unpack8(*reinterpret_cast<const uint4 *>(xr + i), f);
+        unpack8(*reinterpret_cast<const uint4 *>(wgt + i), wf);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = __fmul_rn(__fmul_rn(f[j], r), wf[j]);
+        uint4 v;
+        v.x = pack_bf2(o[0], o[1]); v.y = pack_bf2(o[2], o[3]);
+        v.z = pack_bf2(o[4], o[5]); v.w = pack_bf2(o[6], o[7]);
+        *reinterpret_cast<uint4 *>(out + (size_t)warp * H + i) = v;
     }
 }
 
@@ -539,12 +601,14 @@ bool router_dispatch_fusable(int T, int H, int E, int K) {
 cudaError_t launch_router_dispatch(const uint16_t *x, const uint16_t *proj, const uint16_t *scale,
                                    const uint16_t *pes, int T, int H, int E, int K, float eps,
                                    float *scores, int32_t *idx, uint16_t *w, const Dispatch &d,
-                                   int32_t *done, cudaStream_t s, int *launches) {
+                                   int32_t *done, cudaStream_t s, int *launches,
+                                   const uint16_t *pre_w, uint16_t *xn) {
     const float root = (float)(1.0 / sqrt((double)H));
     const size_t smem = (size_t)(T < kSmallTok ? T : kSmallTok) * H * sizeof(float);
     dim3 grid((E + kSmallWarps - 1) / kSmallWarps, (T + kSmallTok - 1) / kSmallTok);
     router_dispatch_small<<<grid, kSmallThreads, smem, s>>>(x, proj, scale, pes, T, H, E, K,
-                                                               eps, root, scores, idx, w, d, done);
+                                                               eps, root, scores, idx, w, d, done,
+                                                               pre_w, xn);
     if (launches) ++*launches;
     return cudaGetLastError();
 }
@@ -566,13 +630,22 @@ cudaError_t launch_router_scores(const uint16_t *x, const uint16_t *proj, const 
     return cudaGetLastError();
 }
 
+cudaError_t launch_rmsnorm(const uint16_t *x, const uint16_t *w, int T, int H, float eps,
+                          uint16_t *out, cudaStream_t s, int *launches) {
+    const int wpb = 8;
+    cudaError_t err = launch_ex(rmsnorm_kernel, dim3((T + wpb - 1) / wpb), dim3(wpb * 32), 0, s,
+                                true, x, w, T, H, eps, out);
+    if (launches) ++*launches;
+    return err;
+}
+
 cudaError_t launch_router_norm_split(const uint16_t *x, const uint16_t *scale, int T, int H,
                                      float eps, uint16_t *hs, int32_t *cnt_off, cudaStream_t s,
-                                     int *launches) {
+                                     int *launches, const uint16_t *pre_w, uint16_t *xn) {
     const float root = (float)(1.0 / sqrt((double)H));
     const int wpb = 8;
     router_norm_split<<<(T + wpb - 1) / wpb, wpb * 32, 0, s>>>(x, scale, T, H, eps, root, hs,
-                                                               cnt_off);
+                                                               cnt_off, pre_w, xn);
     if (launches) ++*launches;
     return cudaGetLastError();
 }

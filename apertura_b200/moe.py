@@ -313,6 +313,21 @@ class MoEBlock:
                                                 _ptr(out), _ptr(idx), _ptr(w), _stream(x1.device)))
         return (out, TopK(idx, w)) if return_routing else out
 
+    def forward_with_norms(self, x1: torch.Tensor, pre_ff_ln_2_w: torch.Tensor,
+                           post_ff_ln_2_w: torch.Tensor) -> torch.Tensor:
+        """post_ff_ln_2(experts(pre_ff_ln_2(x1), router(x1))): the MoE half of
+        ESDecoderLayer::forward (ESDecoderLayer.mm:69-74) with both norms fused."""
+        _need_cuda_bf16("x1", x1)
+        H = self.cfg.hidden_size
+        _need_cuda_bf16("pre_ff_ln_2_w", pre_ff_ln_2_w, (H,))
+        _need_cuda_bf16("post_ff_ln_2_w", post_ff_ln_2_w, (H,))
+        T = x1.shape[0]
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=x1.device)
+        self.handle.check(lib().apt_moe_layer_forward(self.handle.h, _ptr(x1), _ptr(pre_ff_ln_2_w),
+                                                      _ptr(post_ff_ln_2_w), T, _ptr(out),
+                                                      _stream(x1.device)))
+        return out
+
     def forward_host(self, x_host: torch.Tensor, out_host: Optional[torch.Tensor] = None):
         """End-to-end call with host buffers (pinned for speed)."""
         if x_host.is_cuda or x_host.dtype != torch.bfloat16:

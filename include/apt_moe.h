@@ -150,6 +150,20 @@ APT_API apt_status apt_moe_forward(apt_moe_handle *h, const uint16_t *x_router,
                            uint16_t *w_out, void *stream);
 
 /*
+ * The MoE half of ESDecoderLayer::forward with its norms (ESDecoderLayer.mm:
+ * 69-74): out = post_ff_ln_2( experts( pre_ff_ln_2(x1), router(x1) ) ).
+ * pre_ff_ln_2_w / post_ff_ln_2_w are the two RMSNorm weights [H] bf16
+ * (device); eps = cfg.rms_norm_eps (ESRMSNorm.mm:14-28).  The pre-norm is
+ * computed by the router kernels from the same sum of squares the router
+ * uses; the post-norm is applied in the combine kernel.  (The dense MLP path
+ * and post_ff_ln_1 that the layer adds to this are outside this library.)
+ */
+APT_API apt_status apt_moe_layer_forward(apt_moe_handle *h, const uint16_t *x1,
+                                         const uint16_t *pre_ff_ln_2_w,
+                                         const uint16_t *post_ff_ln_2_w, int T, uint16_t *out,
+                                         void *stream);
+
+/*
  * Same as apt_moe_forward with HOST buffers: copies x to the device, runs
  * the block, copies out back and synchronises the stream.  x_host [T,H],
  * out_host [T,H] bf16.

@@ -89,6 +89,30 @@ void oracle_gelu_tanh_bf16(const uint16_t *x, uint16_t *y, int64_t n) {
     for (int64_t i = 0; i < n; ++i) y[i] = f2bf(oracle_gelu_tanh_f32(bf2f(x[i])));
 }
 
+/* ---------------- RMSNorm (ESRMSNorm.mm:14-28, unfused path) ----------------
+ * out = bf16( (xf * rsqrt(mean(xf^2) + eps)) * f32(weight) ), weight may be NULL
+ * (weightless).  Used for pre_ff_ln_2 / post_ff_ln_2 around the MoE block
+ * (ESDecoderLayer.mm:67-75). */
+void oracle_rms_norm(const uint16_t *x, const uint16_t *weight, int T, int H, float eps,
+                     uint16_t *out) {
+#pragma omp parallel for schedule(static)
+    for (int t = 0; t < T; ++t) {
+        const uint16_t *xr = x + (int64_t)t * H;
+        float s8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        int i = 0;
+        for (; i + 8 <= H; i += 8)
+            for (int l = 0; l < 8; ++l) s8[l] += bf2f(xr[i + l]) * bf2f(xr[i + l]);
+        for (; i < H; ++i) s8[i & 7] += bf2f(xr[i]) * bf2f(xr[i]);
+        float ss = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
+        float inv = 1.0f / sqrtf(ss * (1.0f / (float)H) + eps);
+        for (int j = 0; j < H; ++j) {
+            float v = bf2f(xr[j]) * inv;
+            if (weight) v = v * bf2f(weight[j]);
+            out[(int64_t)t * H + j] = f2bf(v);
+        }
+    }
+}
+
 /* ---------------- router (ESRouter.mm:14-32) ---------------- */
 
 /*

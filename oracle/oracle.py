@@ -60,6 +60,7 @@ def lib():
         L.oracle_quantize_affine.argtypes = [P, i64, i32, i32, i32, P, P, P]
         L.oracle_quantize_affine.restype = i32
         L.oracle_dequantize_affine.argtypes = [P, P, P, i64, i32, i32, i32, P]
+        L.oracle_rms_norm.argtypes = [P, P, i32, i32, f32, P]
         L.oracle_num_threads.restype = i32
         L.oracle_set_num_threads.argtypes = [i32]
         _lib = L
@@ -192,6 +193,25 @@ def dequantize_affine(q, s, b, group_size=64, bits=4):
     out = np.zeros(q.shape[:-1] + (cols,), np.float32)
     lib().oracle_dequantize_affine(_p(q), _p(s), _p(b), rows, cols, group_size, bits, _p(out))
     return out
+
+
+def rms_norm(x, weight=None, eps=1e-6):
+    """ESRMSNorm::forward (ESRMSNorm.mm:14-28): f32 inside, bf16 out."""
+    x = _c(x, np.uint16)
+    T, H = x.shape
+    out = np.zeros_like(x)
+    wt = None if weight is None else _c(weight, np.uint16)
+    lib().oracle_rms_norm(_p(x), _p(wt), T, H, eps, _p(out))
+    return out
+
+
+def layer_moe(x1, pre_w, post_w, proj, scale, pes, gate_up, down, top_k, eps=1e-6):
+    """The MoE part of ESDecoderLayer::forward (ESDecoderLayer.mm:69-74):
+    post_ff_ln_2(experts(pre_ff_ln_2(x1), router(x1)))."""
+    exp_in = rms_norm(x1, pre_w, eps)
+    idx, w = route_topk(x1, proj, scale, pes, top_k, eps)
+    moe = experts_sparse(exp_in, gate_up, down, idx, w)
+    return rms_norm(moe, post_w, eps), idx, w
 
 
 def num_threads() -> int:

@@ -168,7 +168,7 @@ def test_experts_dense_api(oracle, gemma16, gemma16_np):
     assert ok and ma <= TIGHT_REL * np.abs(bf16_to_f32(ref)).max(), (ma, cos)
 
 
-@pytest.mark.parametrize("T", [0, 3, 37])
+@pytest.mark.parametrize("T", [0, 3, 5, 7, 37])
 def test_small_shapes_and_ragged(oracle, T):
     """Reference unit-test shape family (H=64, E=16, K=4) plus ragged T."""
     d = block_inputs(max(T, 1), seed=7, device=DEV, H=64, E=16, K=4, I=64, nonunit=True)
