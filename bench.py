@@ -34,6 +34,10 @@ SWEEP = (1, 4, 16, 64)
 H, E, K, I = 2816, 128, 8, 704
 EXPERT_BYTES = (2 * I * H + H * I) * 2          # 11,894,784 B per touched expert
 GATEUP_BYTES = 2 * I * H * 2                    # gate_up part of it
+# DRAM bytes read by the four gate_up launches of one sweep step (T=1,4,16,64),
+# from an ncu capture (dram__bytes_read.sum); the command and the per-T figures
+# are in profiles/gate_up_decode_sweep_traffic.txt.
+GATEUP_SWEEP_TRAFFIC = 1999.3e6
 ROUTER_BYTES = E * H * 2                        # 720,896 B
 
 
@@ -341,9 +345,14 @@ def run_ours(args):
                                    "(H=2816,E=128,K=8,I=704), bf16, uniform routing",
                        "l2": "flushed before every timed forward (256 MiB read, untimed)",
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
-            "roofline": {"bound": "hbm", "kernel": "gemv_gateup", "achieved": achieved,
-                         "peak": peaks["hbm"], "unit": "GB/s", "frac": achieved / peaks["hbm"],
-                         "peak_source": peaks["src"], "traffic": args.traffic},
+            "roofline": {"bound": "hbm",
+                         "kernel": "gate_up stage: gemv_tma_kernel (T<=8), moe_gemm_kernel (T>8)",
+                         "achieved": achieved, "peak": peaks["hbm"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm"], "peak_source": peaks["src"],
+                         "traffic": args.traffic if args.traffic else GATEUP_SWEEP_TRAFFIC,
+                         "scope": "sums over the 4 gate_up launches of one sweep step; "
+                                  "traffic = ncu dram__bytes_read.sum",
+                         "algorithmic_bytes": gu_bytes},
             "sweep": sweep_detail,
             "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps,
