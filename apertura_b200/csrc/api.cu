@@ -691,9 +691,17 @@ apt_status forward_impl(apt_moe_handle *h, const uint16_t *x_router, const uint1
     if (apt_status st = router_scores(h, x_router, T, s, pre_w)) return st;
     if (h->cfg.moe_sparse) {
         CUDA_TRY(h, cudaMemsetAsync(h->counts, 0, sizeof(int32_t) * E, s));
-        STAGE(h, APT_STAGE_ROUTER_SELECT, s, launch_router_select(h->scores, h->pes, T, E, K, idx, w, h->counts, s,
-                                         &h->launches));
-        return experts_sparse(h, x_experts, idx, w, T, out, s, true);
+        // slots claimed at selection; one parallel placement replaces the
+        // per-expert scan of the dispatch kernel
+        STAGE(h, APT_STAGE_ROUTER_SELECT, s,
+              launch_router_select(h->scores, h->pes, T, E, K, idx, w, h->counts, s,
+                                   &h->launches, h->idx2));
+        STAGE(h, APT_STAGE_DISPATCH, s,
+              launch_place(idx, h->idx2, T * K, E, h->disp(), s, &h->launches));
+        const bool quant = h->qbits > 0;
+        if (!quant && !h->gu) return fail(h, APT_ERR_STATE, "expert weights not loaded");
+        if (quant && !h->gu_q) return fail(h, APT_ERR_STATE, "quantised expert weights not loaded");
+        return run_experts(h, x_experts, idx, w, T, K, quant, out, s, true);
     }
     // dense (reference default): routeWeights then ESExperts::forward
     STAGE(h, APT_STAGE_ROUTER_SELECT, s, launch_router_select(h->scores, h->pes, T, E, K, idx, w, nullptr, s,
@@ -749,8 +757,8 @@ extern "C" apt_status apt_moe_ep_dispatch(apt_moe_handle *h, const uint16_t *x, 
         CUDA_TRY(h, cudaMemsetAsync(h->counts, 0, sizeof(int32_t) * E, s));
         STAGE(h, APT_STAGE_ROUTER_SELECT, s,
               launch_router_select(h->scores, h->pes, T, E, K, idx, w, h->counts, s,
-                                   &h->launches));
-        STAGE(h, APT_STAGE_DISPATCH, s, launch_dispatch(idx, T * K, E, d, s, &h->launches));
+                                   &h->launches, h->idx2));
+        STAGE(h, APT_STAGE_DISPATCH, s, launch_place(idx, h->idx2, T * K, E, d, s, &h->launches));
     }
     STAGE(h, APT_STAGE_GATHER, s,
           launch_gather_rows(x, H, K, E, d, T * K, rows_out, s, &h->launches));

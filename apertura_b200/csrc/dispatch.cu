@@ -211,6 +211,72 @@ __global__ void combine_kernel(const uint16_t *__restrict__ op, const int32_t *_
     }
 }
 
+// Placement from per-pair slots (rank = position of the pair inside its
+// expert's group, claimed with an atomic when the router selected it): every
+// CTA scans the E counts itself, CTA 0 publishes offsets and the active list,
+// and each thread places one pair.  Row order inside a group does not change
+// any output (rows are computed independently, the combine sums in k order).
+__global__ void __launch_bounds__(256)
+place_kernel(const int32_t *__restrict__ idx, const int32_t *__restrict__ rank, int P, int E,
+             const int32_t *__restrict__ counts, int32_t *__restrict__ offsets,
+             int32_t *__restrict__ perm, int32_t *__restrict__ inv, int32_t *__restrict__ active,
+             int32_t *__restrict__ n_active) {
+    __shared__ int s_off[257];
+    pdl_trigger();
+    pdl_wait();
+    const int tid = threadIdx.x, lane = tid & 31;
+    if (tid < 32) {  // exclusive scan of <= 256 counts, 8 per lane
+        int loc[8], sum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = lane * 8 + j;
+            loc[j] = e < E ? counts[e] : 0;
+            sum += loc[j];
+        }
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        int run = incl - sum;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = lane * 8 + j;
+            if (e < E) {
+                s_off[e] = run;
+                if (blockIdx.x == 0) offsets[e] = run;
+            }
+            run += loc[j];
+        }
+        if (lane == 31) {
+            s_off[E] = incl;
+            if (blockIdx.x == 0) offsets[E] = incl;
+        }
+        if (blockIdx.x == 0) {
+            int na = 0;
+            for (int e0 = 0; e0 < E; e0 += 32) {
+                const int e = e0 + lane;
+                const bool act = e < E && counts[e] > 0;
+                const unsigned m = __ballot_sync(0xffffffffu, act);
+                if (act) active[na + __popc(m & ((1u << lane) - 1u))] = e;
+                na += __popc(m);
+            }
+            if (lane == 0) *n_active = na;
+        }
+    }
+    __syncthreads();
+    const int p = blockIdx.x * blockDim.x + tid;
+    if (p < P) {
+        const int e = idx[p];
+        if (e >= 0 && e < E) {
+            const int pos = s_off[e] + rank[p];
+            perm[pos] = p;
+            inv[p] = pos;
+        }
+    }
+}
+
 __global__ void group_offsets_kernel(const int32_t *__restrict__ counts, int G,
                                      int32_t *__restrict__ offsets) {
     pdl_trigger();
@@ -226,6 +292,15 @@ __global__ void group_offsets_kernel(const int32_t *__restrict__ counts, int G,
 }
 
 }  // namespace
+
+cudaError_t launch_place(const int32_t *idx, const int32_t *rank, int P, int E, const Dispatch &d,
+                         cudaStream_t s, int *launches) {
+    cudaError_t err = launch_ex(place_kernel, dim3((P + 255) / 256), dim3(256), 0, s, true, idx,
+                                rank, P, E, (const int32_t *)d.counts, d.offsets, d.perm, d.inv,
+                                d.active, d.n_active);
+    if (launches) ++*launches;
+    return err;
+}
 
 cudaError_t launch_group_offsets(const int32_t *counts, int G, int32_t *offsets, cudaStream_t s,
                                  int *launches) {

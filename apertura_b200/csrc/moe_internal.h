@@ -27,9 +27,10 @@ cudaError_t launch_router_scores(const uint16_t *x, const uint16_t *proj, const 
                                  int T, int H, int E, float eps, float *scores,
                                  cudaStream_t s, int *launches);
 // softmax + top-K + renorm + per-expert scale; optional per-expert counts
+// rank (optional, needs counts): each pair's slot in its expert group (atomic)
 cudaError_t launch_router_select(const float *scores, const uint16_t *pes, int T, int E, int K,
                                  int32_t *idx, uint16_t *w, int32_t *counts, cudaStream_t s,
-                                 int *launches);
+                                 int *launches, int32_t *rank = nullptr);
 // Decode-sized fused router + dispatch (one launch): writes idx/w and the full
 // Dispatch.  `done` is a zero-initialised device counter the kernel resets.
 bool router_dispatch_fusable(int T, int H, int E, int K);
@@ -63,6 +64,10 @@ cudaError_t launch_count(const int32_t *idx, int P, int E, int32_t *counts, cuda
                          int *launches);
 cudaError_t launch_dispatch(const int32_t *idx, int P, int E, const Dispatch &d, cudaStream_t s,
                             int *launches);
+// Dispatch from per-pair slots (router_select's rank output): offsets,
+// active list, perm and inv in one launch
+cudaError_t launch_place(const int32_t *idx, const int32_t *rank, int P, int E, const Dispatch &d,
+                         cudaStream_t s, int *launches);
 // xp[row] = x[perm[row] / K] for row < offsets[E]
 cudaError_t launch_gather_rows(const uint16_t *x, int H, int K, int E, const Dispatch &d,
                                int max_rows, uint16_t *xp, cudaStream_t s, int *launches);

@@ -312,7 +312,8 @@ __device__ __forceinline__ void select_token(const float *__restrict__ sr,
 // One warp per token.
 __global__ void router_select(const float *__restrict__ scores, const uint16_t *__restrict__ pes,
                               int T, int E, int K, int32_t *__restrict__ idx,
-                              uint16_t *__restrict__ w, int32_t *__restrict__ counts) {
+                              uint16_t *__restrict__ w, int32_t *__restrict__ counts,
+                              int32_t *__restrict__ rank) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     pdl_trigger();
     pdl_wait();
@@ -323,7 +324,10 @@ __global__ void router_select(const float *__restrict__ scores, const uint16_t *
     if (lane < K) {
         idx[(size_t)warp * K + lane] = e;
         w[(size_t)warp * K + lane] = f2bf(wk);
-        if (counts) atomicAdd(counts + e, 1);
+        if (counts) {
+            const int r = atomicAdd(counts + e, 1);  // slot of this pair in its expert's group
+            if (rank) rank[(size_t)warp * K + lane] = r;
+        }
     }
 }
 
@@ -652,11 +656,11 @@ cudaError_t launch_router_norm_split(const uint16_t *x, const uint16_t *scale, i
 
 cudaError_t launch_router_select(const float *scores, const uint16_t *pes, int T, int E, int K,
                                  int32_t *idx, uint16_t *w, int32_t *counts, cudaStream_t s,
-                                 int *launches) {
+                                 int *launches, int32_t *rank) {
     const int warps_per_block = 8;
     dim3 grid((T + warps_per_block - 1) / warps_per_block);
     cudaError_t err = launch_ex(router_select, grid, dim3(warps_per_block * 32), 0, s, true,
-                                (const float *)scores, pes, T, E, K, idx, w, counts);
+                                (const float *)scores, pes, T, E, K, idx, w, counts, rank);
     if (launches) ++*launches;
     return err;
 }
