@@ -29,6 +29,7 @@
 #include "moe_internal.h"
 #include "launch_util.h"
 #include "sm100_ptx.cuh"
+#include "gemm_epilogue.cuh"
 
 namespace apt {
 
@@ -43,6 +44,7 @@ constexpr int kTmemCols = 512;
 constexpr int kAccStride = 256;          // TMEM columns between the two accumulators
 constexpr long long kWaitLimit = 4000000000LL;  // cycles (~2 s) before giving up
 constexpr int kMaxExperts = 256;
+constexpr int kStageC = 4 * 2 * 4096;    // down: 2 x 4 KB store boxes per epilogue warp
 
 enum { EPI_GATEUP = 0, EPI_DOWN = 1, EPI_F32 = 2 };
 
@@ -74,7 +76,7 @@ __device__ __forceinline__ void decode_tile(int t, int NT, const int *mtp, int E
 template <int EPI, int BN, int BN2, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
 moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const int32_t *__restrict__ counts, const int32_t *__restrict__ offsets, int E,
+                const __grid_constant__ CUtensorMap tmC, const int32_t *__restrict__ counts, const int32_t *__restrict__ offsets, int E,
                 int Kdim, int I, int H, uint16_t *__restrict__ out, int out_ld,
                 int32_t *__restrict__ err, const int32_t *__restrict__ g2e) {
     constexpr int A_BYTES = Smem<BN>::A_BYTES, B_BYTES = Smem<BN>::B_BYTES;
@@ -84,7 +86,8 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                                                 ~uintptr_t(1023));
     uint8_t *sA = smem;
     uint8_t *sB = smem + STAGES * A_BYTES;
-    uint64_t *full = reinterpret_cast<uint64_t *>(sB + STAGES * B_BYTES);
+    uint8_t *sC = sB + STAGES * B_BYTES;  // down: per-epilogue-warp store staging
+    uint64_t *full = reinterpret_cast<uint64_t *>(sC + (EPI == EPI_DOWN ? kStageC : 0));
     uint64_t *empty = full + STAGES;
     uint64_t *tfull = empty + STAGES;
     uint64_t *tempty = tfull + 2;
@@ -195,7 +198,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     } else {
         const int q = warp & 3;             // TMEM lane quarter this warp may read
         const int r = q * 32 + lane;        // accumulator row of this thread
-        int i = 0;
+        int i = 0, bufsel = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
             int e, mloc, nt;
             decode_tile(t, NT, mtp, E, e, mloc, nt);
@@ -209,30 +212,11 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             }
             tc_fence_after();
             const uint32_t taddr = tmem_base + buf * kAccStride + ((uint32_t)(q * 32) << 16);
-            if (EPI == EPI_GATEUP) {
-                uint16_t *dst = out + (size_t)row * out_ld + nt * BN2;
+            if constexpr (EPI == EPI_GATEUP) {
                 // the last n-tile may be partial (I not a multiple of BN2)
-                const int cmax = min(BN2, I - nt * BN2) / 8;
-#pragma unroll 1
-                for (int c = 0; c < cmax; ++c) {
-                    uint32_t gr[8], ur[8];
-                    tmem_ld8(taddr + c * 8, gr);
-                    tmem_ld8(taddr + BN2 + c * 8, ur);
-                    tmem_ld_wait();
-                    float y[8];
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        y[j] = geglu_bf16(rbf(__uint_as_float(gr[j])), rbf(__uint_as_float(ur[j])));
-                    if (r < nvalid) {
-                        uint4 v;
-                        v.x = pack_bf2(y[0], y[1]);
-                        v.y = pack_bf2(y[2], y[3]);
-                        v.z = pack_bf2(y[4], y[5]);
-                        v.w = pack_bf2(y[6], y[7]);
-                        *reinterpret_cast<uint4 *>(dst + c * 8) = v;
-                    }
-                }
-            } else if (EPI == EPI_F32) {
+                epilogue_geglu(taddr, BN2, min(BN2, I - nt * BN2), r < nvalid,
+                               out + (size_t)row * out_ld + nt * BN2);
+            } else if constexpr (EPI == EPI_F32) {
                 float *dst = reinterpret_cast<float *>(out) + (size_t)row * out_ld + nt * BN;
 #pragma unroll 1
                 for (int c = 0; c < BN / 8; ++c) {
@@ -247,26 +231,16 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                                             __uint_as_float(a[6]), __uint_as_float(a[7]));
                     }
                 }
-            } else {
-                uint16_t *dst = out + (size_t)row * out_ld + nt * BN;
-#pragma unroll 1
-                for (int c = 0; c < BN / 8; ++c) {
-                    uint32_t a[8];
-                    tmem_ld8(taddr + c * 8, a);
-                    tmem_ld_wait();
-                    if (r < nvalid) {
-                        uint4 v;
-                        v.x = pack_bf2(__uint_as_float(a[0]), __uint_as_float(a[1]));
-                        v.y = pack_bf2(__uint_as_float(a[2]), __uint_as_float(a[3]));
-                        v.z = pack_bf2(__uint_as_float(a[4]), __uint_as_float(a[5]));
-                        v.w = pack_bf2(__uint_as_float(a[6]), __uint_as_float(a[7]));
-                        *reinterpret_cast<uint4 *>(dst + c * 8) = v;
-                    }
-                }
+            } else if (q * 32 + 32 <= nvalid) {
+                epilogue_bf16_tma<BN>(taddr, sC + q * 8192, bufsel, &tmC, nt * BN, row - lane,
+                                      lane);
+            } else if (q * 32 < nvalid) {
+                epilogue_bf16<BN>(taddr, r < nvalid, out + (size_t)row * out_ld + nt * BN);
             }
             tc_fence_before();
             mbar_arrive(&tempty[buf]);
         }
+        if (EPI == EPI_DOWN && lane == 0) bulk_wait<0>();  // stores complete before exit
     }
 done:
     __syncthreads();
@@ -285,8 +259,8 @@ bool make_map(CUtensorMap *m, const void *base, uint64_t inner, uint64_t rows, u
 
 template <int EPI, int BN, int BN2, int STAGES>
 constexpr size_t smem_bytes() {
-    return 1024 + (size_t)STAGES * (Smem<BN>::A_BYTES + Smem<BN>::B_BYTES) + 8 * (2 * STAGES + 4) +
-           16 + 4 * (kMaxExperts + 1);
+    return 1024 + (size_t)STAGES * (Smem<BN>::A_BYTES + Smem<BN>::B_BYTES) +
+           (EPI == EPI_DOWN ? kStageC : 0) + 8 * (2 * STAGES + 4) + 16 + 4 * (kMaxExperts + 1);
 }
 
 template <int EPI, int BN, int BN2, int STAGES>
@@ -299,11 +273,11 @@ cudaError_t set_attr() {
 template <int EPI, int BN, int BN2, int STAGES>
 cudaError_t launch(const CUtensorMap &a, const CUtensorMap &b, const Dispatch &d, int E, int Kdim,
                    int I, int H, uint16_t *out, int out_ld, int32_t *err, cudaStream_t s,
-                   const int32_t *g2e = nullptr) {
+                   const int32_t *g2e = nullptr, const CUtensorMap *c = nullptr) {
     const int sms = num_sms(current_device());
     return launch_ex(moe_gemm_kernel<EPI, BN, BN2, STAGES>, dim3(sms), dim3(kThreads),
-                     smem_bytes<EPI, BN, BN2, STAGES>(), s, true, a, b, d.counts, d.offsets, E,
-                     Kdim, I, H, out, out_ld, err, g2e);
+                     smem_bytes<EPI, BN, BN2, STAGES>(), s, true, a, b, c ? *c : a, d.counts,
+                     d.offsets, E, Kdim, I, H, out, out_ld, err, g2e);
 }
 
 // gate_up tile: BN2 gate + BN2 up rows; down tile: BN rows of W_down.
@@ -375,12 +349,13 @@ cudaError_t launch_gemm_down_grouped(const uint16_t *yp, const Dispatch &d, cons
                                      int *launches) {
     if (G > kMaxExperts) return cudaErrorInvalidValue;
     const int bn = (H % 256 == 0) ? 256 : 128;
-    CUtensorMap a, b;
-    if (!make_map(&a, yp, I, rows_cap, kBM) || !make_map(&b, w.dn, I, (uint64_t)E_w * H, bn))
+    CUtensorMap a, b, c;
+    if (!make_map(&a, yp, I, rows_cap, kBM) || !make_map(&b, w.dn, I, (uint64_t)E_w * H, bn) ||
+        !bf16_map_2d(&c, out, H, rows_cap, 64, 32, true))
         return cudaErrorInvalidValue;
     cudaError_t e = (bn == 256)
-        ? launch<EPI_DOWN, 256, 0, kDnStages>(a, b, d, G, I, I, H, out, H, err, s, g2e)
-        : launch<EPI_DOWN, 128, 0, kDnStages>(a, b, d, G, I, I, H, out, H, err, s, g2e);
+        ? launch<EPI_DOWN, 256, 0, kDnStages>(a, b, d, G, I, I, H, out, H, err, s, g2e, &c)
+        : launch<EPI_DOWN, 128, 0, kDnStages>(a, b, d, G, I, I, H, out, H, err, s, g2e, &c);
     if (launches) ++*launches;
     return e;
 }
@@ -390,12 +365,13 @@ cudaError_t launch_gemm_down(const uint16_t *yp, const Dispatch &d, const Expert
                              cudaStream_t s, int *launches) {
     if (E > kMaxExperts) return cudaErrorInvalidValue;
     const int bn = (H % 256 == 0) ? 256 : 128;
-    CUtensorMap a, b;
-    if (!make_map(&a, yp, I, rows_cap, kBM) || !make_map(&b, w.dn, I, (uint64_t)E * H, bn))
+    CUtensorMap a, b, c;
+    if (!make_map(&a, yp, I, rows_cap, kBM) || !make_map(&b, w.dn, I, (uint64_t)E * H, bn) ||
+        !bf16_map_2d(&c, op, H, rows_cap, 64, 32, true))
         return cudaErrorInvalidValue;
     cudaError_t e = (bn == 256)
-        ? launch<EPI_DOWN, 256, 0, kDnStages>(a, b, d, E, I, I, H, op, H, err, s)
-        : launch<EPI_DOWN, 128, 0, kDnStages>(a, b, d, E, I, I, H, op, H, err, s);
+        ? launch<EPI_DOWN, 256, 0, kDnStages>(a, b, d, E, I, I, H, op, H, err, s, nullptr, &c)
+        : launch<EPI_DOWN, 128, 0, kDnStages>(a, b, d, E, I, I, H, op, H, err, s, nullptr, &c);
     if (launches) ++*launches;
     return e;
 }

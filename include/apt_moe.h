@@ -224,6 +224,15 @@ APT_API int apt_moe_last_launches(const apt_moe_handle *h);
 APT_API apt_status apt_moe_set_gemv_max_tokens(apt_moe_handle *h, int t);
 
 /*
+ * Tensor-core tile form: 1 = CTA pairs (one M=256 tcgen05.mma over two SMs,
+ * each SM staging half the weight tile), 0 = one CTA per 128-row tile,
+ * -1 (default) = chosen by size (environment APT_GEMM_PAIR=0/1 overrides the
+ * default).  Both forms accumulate in the same k order with the same
+ * rounding points.
+ */
+APT_API apt_status apt_moe_set_gemm_pair(apt_moe_handle *h, int mode);
+
+/*
  * Per-stage timing for measurement: when enabled, every compute call records
  * a CUDA event pair on its stream around each stage's kernel;
  * apt_moe_stage_times fills ms[APT_STAGE_COUNT] with the last call's
