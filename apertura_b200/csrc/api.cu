@@ -481,6 +481,9 @@ extern "C" apt_status apt_moe_load_experts_quant(apt_moe_handle *h, const uint32
 
 namespace {
 
+// Routed rows (T*K) up to which gate_up gathers its A rows itself.
+constexpr int kGatherInGemmRows = 4096;
+
 // CTA-pair GEMM selection: the handle's setting, else APT_GEMM_PAIR (0/1),
 // else by size.
 bool use_pair_gemm(const apt_moe_handle *h, int H, int I, int rows) {
@@ -555,8 +558,14 @@ apt_status run_experts(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
     }
     if (gemm) {
         const int rows_cap = P < h->Pcap ? P : h->Pcap;
-        STAGE(h, APT_STAGE_GATHER, s, launch_gather_rows(x, H, Kp, E, d, rows_cap, h->xp, s, &h->launches));
-        if (use_pair_gemm(h, H, I, rows_cap)) {
+        // Few rows per expert: A rows gathered inside the GEMM (tile::gather4);
+        // prefill-sized groups: one gather pass, then full-tile TMA copies.
+        const bool pair = use_pair_gemm(h, H, I, rows_cap);
+        const bool gather_in_gemm = !pair && rows_cap <= kGatherInGemmRows;
+        if (!gather_in_gemm)
+            STAGE(h, APT_STAGE_GATHER, s,
+                  launch_gather_rows(x, H, Kp, E, d, rows_cap, h->xp, s, &h->launches));
+        if (pair) {
             STAGE(h, APT_STAGE_GATE_UP, s,
                   launch_gemm_pair_gateup(h->xp, d, nullptr, ew, rows_cap, H, I, E, E, h->yp,
                                           h->errflag, s, &h->launches));
@@ -564,9 +573,14 @@ apt_status run_experts(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
                   launch_gemm_pair_down(h->yp, d, nullptr, ew, rows_cap, H, I, E, E, h->op,
                                         h->errflag, s, &h->launches));
         } else {
-            STAGE(h, APT_STAGE_GATE_UP, s,
-                  launch_gemm_gateup(h->xp, d, ew, rows_cap, H, I, E, h->yp, h->errflag, s,
-                                     &h->launches));
+            if (gather_in_gemm)
+                STAGE(h, APT_STAGE_GATE_UP, s,
+                      launch_gemm_gateup_gather(x, T, Kp, d, ew, rows_cap, H, I, E, h->yp,
+                                                h->errflag, s, &h->launches));
+            else
+                STAGE(h, APT_STAGE_GATE_UP, s,
+                      launch_gemm_gateup(h->xp, d, ew, rows_cap, H, I, E, h->yp, h->errflag, s,
+                                         &h->launches));
             STAGE(h, APT_STAGE_DOWN, s,
                   launch_gemm_down(h->yp, d, ew, rows_cap, H, I, E, h->op, h->errflag, s,
                                    &h->launches));

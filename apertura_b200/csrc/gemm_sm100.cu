@@ -46,7 +46,13 @@ constexpr long long kWaitLimit = 4000000000LL;  // cycles (~2 s) before giving u
 constexpr int kMaxExperts = 256;
 constexpr int kStageC = 4 * 2 * 4096;    // down: 2 x 4 KB store boxes per epilogue warp
 
-enum { EPI_GATEUP = 0, EPI_DOWN = 1, EPI_F32 = 2 };
+// EPI_GATEUP_G: gate_up whose A rows are gathered from the token rows by the
+// TMA (tile::gather4, 4 rows per copy) through the dispatch permutation, so no
+// expert-sorted copy of the activations is materialised.  Used for small row
+// counts per expert: a full 128-row stage takes 32 gather copies, which the
+// TMA issues far slower than one tiled copy (measured 2.8x slower gate_up at
+// 512 rows per expert), while a tile of a few rows takes one or two.
+enum { EPI_GATEUP = 0, EPI_DOWN = 1, EPI_F32 = 2, EPI_GATEUP_G = 3 };
 
 template <int BN>
 struct Smem {
@@ -78,7 +84,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const int32_t *__restrict__ counts, const int32_t *__restrict__ offsets, int E,
                 int Kdim, int I, int H, uint16_t *__restrict__ out, int out_ld,
-                int32_t *__restrict__ err, const int32_t *__restrict__ g2e) {
+                int32_t *__restrict__ err, const int32_t *__restrict__ g2e,
+                const int32_t *__restrict__ gperm, int gk) {
+    constexpr bool GU = (EPI == EPI_GATEUP || EPI == EPI_GATEUP_G);
     constexpr int A_BYTES = Smem<BN>::A_BYTES, B_BYTES = Smem<BN>::B_BYTES;
     constexpr uint32_t IDESC = idesc_bf16_f32(kBM, BN);
     extern __shared__ uint8_t smem_raw[];
@@ -128,11 +136,55 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     pdl_trigger();
     // EPI_F32 (router scores): one "expert", N = H outputs, and the B operand
     // (proj [H, I]) is reused for every I-wide slice of the K = 2*I split input.
-    const int NT = (EPI == EPI_GATEUP) ? (I + BN2 - 1) / BN2 : H / BN;
+    const int NT = GU ? (I + BN2 - 1) / BN2 : H / BN;
     const int tiles = mtp[E] * NT;
     const int KB = Kdim / kBK;
 
-    if (warp == 0) {
+    if (EPI == EPI_GATEUP_G && warp == 0) {
+        // all 32 lanes: lane l gathers tile rows 4l..4l+3 of every A stage
+        int g = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+            int e, mloc, nt;
+            decode_tile(t, NT, mtp, E, e, mloc, nt);
+            const int row0 = offsets[e] + mloc * kBM;
+            const int nvalid = counts[e] - mloc * kBM;
+            // rows past the group's end read the group's first token (never stored)
+            const int first = gperm[row0] / gk;
+            int tok[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int rr = lane * 4 + j;
+                tok[j] = rr < nvalid ? gperm[row0 + rr] / gk : first;
+            }
+            const int ew = g2e ? g2e[e] : e;
+            const int gate_row = ew * 2 * I + nt * BN2;
+            // only the 4-row groups holding valid rows are fetched; the rest of
+            // the A stage keeps stale data, which only feeds accumulator rows
+            // that are never stored (rows of D are independent)
+            const int nact = min(32, (nvalid + 3) >> 2);
+            for (int kb = 0; kb < KB; ++kb, ++g) {
+                const int s = g % STAGES;
+                const uint32_t ph = (g / STAGES) & 1;
+                int ok = 1;
+                if (lane == 0) ok = mbar_wait(&empty[s], ph ^ 1, kWaitLimit);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) {
+                    if (lane == 0) record_error(err, 1, t);
+                    goto done;
+                }
+                if (lane == 0) mbar_arrive_expect_tx(&full[s], nact * 512 + B_BYTES);
+                __syncwarp();
+                if (lane < nact)
+                    tma_gather4(sA + s * A_BYTES + lane * 512, &tmA, &full[s], kb * kBK, tok[0],
+                            tok[1], tok[2], tok[3]);
+                if (lane == 0) {
+                    tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], kb * kBK, gate_row);
+                    tma_load_2d(sB + s * B_BYTES + BN2 * kBK * 2, &tmB, &full[s], kb * kBK,
+                                gate_row + I);
+                }
+            }
+        }
+    } else if (warp == 0) {
         if (lane == 0) {
             int g = 0;
             for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
@@ -212,7 +264,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             }
             tc_fence_after();
             const uint32_t taddr = tmem_base + buf * kAccStride + ((uint32_t)(q * 32) << 16);
-            if constexpr (EPI == EPI_GATEUP) {
+            if constexpr (GU) {
                 // the last n-tile may be partial (I not a multiple of BN2)
                 epilogue_geglu(taddr, BN2, min(BN2, I - nt * BN2), r < nvalid,
                                out + (size_t)row * out_ld + nt * BN2);
@@ -273,11 +325,12 @@ cudaError_t set_attr() {
 template <int EPI, int BN, int BN2, int STAGES>
 cudaError_t launch(const CUtensorMap &a, const CUtensorMap &b, const Dispatch &d, int E, int Kdim,
                    int I, int H, uint16_t *out, int out_ld, int32_t *err, cudaStream_t s,
-                   const int32_t *g2e = nullptr, const CUtensorMap *c = nullptr) {
+                   const int32_t *g2e = nullptr, const CUtensorMap *c = nullptr,
+                   const int32_t *gperm = nullptr, int gk = 1) {
     const int sms = num_sms(current_device());
     return launch_ex(moe_gemm_kernel<EPI, BN, BN2, STAGES>, dim3(sms), dim3(kThreads),
                      smem_bytes<EPI, BN, BN2, STAGES>(), s, true, a, b, c ? *c : a, d.counts,
-                     d.offsets, E, Kdim, I, H, out, out_ld, err, g2e);
+                     d.offsets, E, Kdim, I, H, out, out_ld, err, g2e, gperm, gk);
 }
 
 // gate_up tile: BN2 gate + BN2 up rows; down tile: BN rows of W_down.
@@ -291,6 +344,9 @@ cudaError_t gemm_init() {
     if ((e = set_attr<EPI_GATEUP, 176, 88, kGuStages>())) return e;
     if ((e = set_attr<EPI_GATEUP, 256, 128, kDnStages>())) return e;
     if ((e = set_attr<EPI_GATEUP, 128, 64, kGuStages>())) return e;
+    if ((e = set_attr<EPI_GATEUP_G, 176, 88, kGuStages>())) return e;
+    if ((e = set_attr<EPI_GATEUP_G, 256, 128, kDnStages>())) return e;
+    if ((e = set_attr<EPI_GATEUP_G, 128, 64, kGuStages>())) return e;
     if ((e = set_attr<EPI_DOWN, 256, 0, kDnStages>())) return e;
     return set_attr<EPI_DOWN, 128, 0, kDnStages>();
 }
@@ -321,6 +377,34 @@ cudaError_t launch_gemm_gateup(const uint16_t *xp, const Dispatch &d, const Expe
         : (bn2 == 128)
         ? launch<EPI_GATEUP, 256, 128, kDnStages>(a, b, d, E, H, I, H, yp, I, err, s)
         : launch<EPI_GATEUP, 128, 64, kGuStages>(a, b, d, E, H, I, H, yp, I, err, s);
+    if (launches) ++*launches;
+    return e;
+}
+
+cudaError_t launch_gemm_gateup_gather(const uint16_t *x, int T, int Kp, const Dispatch &d,
+                                      const ExpertWeights &w, int rows_cap, int H, int I, int E,
+                                      uint16_t *yp, int32_t *err, cudaStream_t s, int *launches) {
+    if (E > kMaxExperts || T <= 0) return cudaErrorInvalidValue;
+    static const int pref = [] {
+        const char *v = getenv("APT_GATEUP_BN2");
+        return v ? atoi(v) : 0;
+    }();
+    const int want = pref ? pref : (rows_cap > 4096 ? 128 : 88);
+    const int bn2 = (want == 88 && I % 88 == 0) ? 88 : (I >= 128 ? 128 : 64);
+    CUtensorMap a, b;
+    // token rows [T, H], one-row boxes: each tile::gather4 copy fetches 4 rows
+    if (!bf16_map_2d(&a, x, H, T, kBK, 1, true) ||
+        !make_map(&b, w.gu, H, (uint64_t)E * 2 * I, bn2))
+        return cudaErrorInvalidValue;
+    const int32_t *perm = d.perm;
+    cudaError_t e = (bn2 == 88)
+        ? launch<EPI_GATEUP_G, 176, 88, kGuStages>(a, b, d, E, H, I, H, yp, I, err, s, nullptr,
+                                                  nullptr, perm, Kp)
+        : (bn2 == 128)
+        ? launch<EPI_GATEUP_G, 256, 128, kDnStages>(a, b, d, E, H, I, H, yp, I, err, s, nullptr,
+                                                   nullptr, perm, Kp)
+        : launch<EPI_GATEUP_G, 128, 64, kGuStages>(a, b, d, E, H, I, H, yp, I, err, s, nullptr,
+                                                  nullptr, perm, Kp);
     if (launches) ++*launches;
     return e;
 }

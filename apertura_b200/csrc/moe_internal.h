@@ -119,6 +119,11 @@ bool gemm_supported(int H, int I);
 cudaError_t launch_gemm_gateup(const uint16_t *xp, const Dispatch &d, const ExpertWeights &w,
                                int rows_cap, int H, int I, int E, uint16_t *yp, int32_t *err,
                                cudaStream_t s, int *launches);
+// gate_up with A rows gathered by the TMA from x [T, H] through d.perm (no
+// separate gather launch); same results as gather + launch_gemm_gateup.
+cudaError_t launch_gemm_gateup_gather(const uint16_t *x, int T, int Kp, const Dispatch &d,
+                                      const ExpertWeights &w, int rows_cap, int H, int I, int E,
+                                      uint16_t *yp, int32_t *err, cudaStream_t s, int *launches);
 cudaError_t launch_gemm_down(const uint16_t *yp, const Dispatch &d, const ExpertWeights &w,
                              int rows_cap, int H, int I, int E, uint16_t *op, int32_t *err,
                              cudaStream_t s, int *launches);

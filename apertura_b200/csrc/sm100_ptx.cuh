@@ -80,6 +80,19 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
         : "memory");
 }
 
+// Row gather: 4 rows (r0..r3) of a one-row-box tensor map at inner
+// coordinate c0, landing as 4 consecutive box rows at dst (swizzled by the
+// shared-memory address like a tiled load).  Completes bytes on `bar`.
+__device__ __forceinline__ void tma_gather4(void *dst, const CUtensorMap *map, uint64_t *bar,
+                                            int c0, int r0, int r1, int r2, int r3) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3),
+        "r"(smem_u32(bar))
+        : "memory");
+}
+
 // 2-D tiled store of a shared-memory box to global (bulk-group completion).
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int c0,
                                              int c1) {
