@@ -139,6 +139,10 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     const int NT = GU ? (I + BN2 - 1) / BN2 : H / BN;
     const int tiles = mtp[E] * NT;
     const int KB = Kdim / kBK;
+    // gate_up: the last n-tile covers TW = I - (NT-1)*BN2 columns; when that is
+    // less than BN2 it runs as a narrower tile (N = 2*TW MMAs, B rows through
+    // the TW-row tensor map tmC) instead of computing padding
+    const int TW = GU ? I - (NT - 1) * BN2 : BN2;
 
     if (EPI == EPI_GATEUP_G && warp == 0) {
         // all 32 lanes: lane l gathers tile rows 4l..4l+3 of every A stage
@@ -158,6 +162,9 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             }
             const int ew = g2e ? g2e[e] : e;
             const int gate_row = ew * 2 * I + nt * BN2;
+            const bool tail = nt == NT - 1 && TW < BN2;
+            const int wrows = tail ? TW : BN2;
+            const CUtensorMap *mb = tail ? &tmC : &tmB;
             // only the 4-row groups holding valid rows are fetched; the rest of
             // the A stage keeps stale data, which only feeds accumulator rows
             // that are never stored (rows of D are independent)
@@ -172,14 +179,14 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     if (lane == 0) record_error(err, 1, t);
                     goto done;
                 }
-                if (lane == 0) mbar_arrive_expect_tx(&full[s], nact * 512 + B_BYTES);
+                if (lane == 0) mbar_arrive_expect_tx(&full[s], nact * 512 + 2 * wrows * kBK * 2);
                 __syncwarp();
                 if (lane < nact)
                     tma_gather4(sA + s * A_BYTES + lane * 512, &tmA, &full[s], kb * kBK, tok[0],
                             tok[1], tok[2], tok[3]);
                 if (lane == 0) {
-                    tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], kb * kBK, gate_row);
-                    tma_load_2d(sB + s * B_BYTES + BN2 * kBK * 2, &tmB, &full[s], kb * kBK,
+                    tma_load_2d(sB + s * B_BYTES, mb, &full[s], kb * kBK, gate_row);
+                    tma_load_2d(sB + s * B_BYTES + wrows * kBK * 2, mb, &full[s], kb * kBK,
                                 gate_row + I);
                 }
             }
@@ -191,6 +198,9 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 int e, mloc, nt;
                 decode_tile(t, NT, mtp, E, e, mloc, nt);
                 const int row0 = offsets[e] + mloc * kBM;
+                const bool tail = GU && nt == NT - 1 && TW < BN2;
+                const int wrows = tail ? TW : BN2;
+                const CUtensorMap *mb = tail ? &tmC : &tmB;
                 for (int kb = 0; kb < KB; ++kb, ++g) {
                     const int s = g % STAGES;
                     const uint32_t ph = (g / STAGES) & 1;
@@ -198,14 +208,15 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                         record_error(err, 1, t);
                         goto done;
                     }
-                    mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
+                    mbar_arrive_expect_tx(&full[s], GU ? A_BYTES + 2 * wrows * kBK * 2
+                                                       : A_BYTES + B_BYTES);
                     tma_load_2d(sA + s * A_BYTES, &tmA, &full[s], kb * kBK, row0);
                     if (EPI == EPI_GATEUP) {
                         // g2e: row group -> expert (grouped entry point); else identity
                         const int ew = g2e ? g2e[e] : e;
                         const int gate_row = ew * 2 * I + nt * BN2;
-                        tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], kb * kBK, gate_row);
-                        tma_load_2d(sB + s * B_BYTES + BN2 * kBK * 2, &tmB, &full[s], kb * kBK,
+                        tma_load_2d(sB + s * B_BYTES, mb, &full[s], kb * kBK, gate_row);
+                        tma_load_2d(sB + s * B_BYTES + wrows * kBK * 2, mb, &full[s], kb * kBK,
                                     gate_row + I);
                     } else if (EPI == EPI_F32) {
                         tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], (kb * kBK) % I, nt * BN);
@@ -228,6 +239,8 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 }
                 tc_fence_after();
                 const uint32_t d = tmem_base + buf * kAccStride;
+                const bool tail = GU && t % NT == NT - 1 && TW < BN2;
+                const uint32_t idesc = tail ? idesc_bf16_f32(kBM, 2 * TW) : IDESC;
                 for (int kb = 0; kb < KB; ++kb, ++g) {
                     const int s = g % STAGES;
                     const uint32_t ph = (g / STAGES) & 1;
@@ -241,7 +254,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; ++kk)
                         mma_bf16(d, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32),
-                                 IDESC, (kb | kk) != 0);
+                                 idesc, (kb | kk) != 0);
                     mma_commit(&empty[s]);  // frees the stage once these MMAs finish
                 }
                 mma_commit(&tfull[buf]);    // accumulator ready for the epilogue
@@ -265,8 +278,9 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             tc_fence_after();
             const uint32_t taddr = tmem_base + buf * kAccStride + ((uint32_t)(q * 32) << 16);
             if constexpr (GU) {
-                // the last n-tile may be partial (I not a multiple of BN2)
-                epilogue_geglu(taddr, BN2, min(BN2, I - nt * BN2), r < nvalid,
+                // a narrow last tile holds g in columns [0, TW), u in [TW, 2*TW)
+                const int w = min(BN2, I - nt * BN2);
+                epilogue_geglu(taddr, w, w, r < nvalid,
                                out + (size_t)row * out_ld + nt * BN2);
             } else if constexpr (EPI == EPI_F32) {
                 float *dst = reinterpret_cast<float *>(out) + (size_t)row * out_ld + nt * BN;
@@ -355,6 +369,18 @@ bool gemm_supported(int H, int I) {
     return encode_tiled_fn() != nullptr && H % 128 == 0 && (I % 88 == 0 || I % 64 == 0) && I % 64 == 0;
 }
 
+// Tensor map of the narrow last gate_up tile (TW = I mod bn2 rows per box);
+// a copy of the main B map when I is a multiple of bn2 (never read then).
+bool tail_map(CUtensorMap *c, const CUtensorMap &b, const uint16_t *gu, int H, int I, int E_w,
+              int bn2) {
+    const int tw = I % bn2;
+    if (!tw) {
+        *c = b;
+        return true;
+    }
+    return bf16_map_2d(c, gu, H, (uint64_t)E_w * 2 * I, kBK, tw, true);
+}
+
 cudaError_t launch_gemm_gateup(const uint16_t *xp, const Dispatch &d, const ExpertWeights &w,
                                int rows_cap, int H, int I, int E, uint16_t *yp, int32_t *err,
                                cudaStream_t s, int *launches) {
@@ -370,13 +396,15 @@ cudaError_t launch_gemm_gateup(const uint16_t *xp, const Dispatch &d, const Expe
     const int want = pref ? pref : (rows_cap > 4096 ? 128 : 88);
     const int bn2 = (want == 88 && I % 88 == 0) ? 88 : (I >= 128 ? 128 : 64);
     CUtensorMap a, b;
-    if (!make_map(&a, xp, H, rows_cap, kBM) || !make_map(&b, w.gu, H, (uint64_t)E * 2 * I, bn2))
+    CUtensorMap c;
+    if (!make_map(&a, xp, H, rows_cap, kBM) || !make_map(&b, w.gu, H, (uint64_t)E * 2 * I, bn2) ||
+        !tail_map(&c, b, w.gu, H, I, E, bn2))
         return cudaErrorInvalidValue;
     cudaError_t e = (bn2 == 88)
-        ? launch<EPI_GATEUP, 176, 88, kGuStages>(a, b, d, E, H, I, H, yp, I, err, s)
+        ? launch<EPI_GATEUP, 176, 88, kGuStages>(a, b, d, E, H, I, H, yp, I, err, s, nullptr, &c)
         : (bn2 == 128)
-        ? launch<EPI_GATEUP, 256, 128, kDnStages>(a, b, d, E, H, I, H, yp, I, err, s)
-        : launch<EPI_GATEUP, 128, 64, kGuStages>(a, b, d, E, H, I, H, yp, I, err, s);
+        ? launch<EPI_GATEUP, 256, 128, kDnStages>(a, b, d, E, H, I, H, yp, I, err, s, nullptr, &c)
+        : launch<EPI_GATEUP, 128, 64, kGuStages>(a, b, d, E, H, I, H, yp, I, err, s, nullptr, &c);
     if (launches) ++*launches;
     return e;
 }
@@ -393,18 +421,19 @@ cudaError_t launch_gemm_gateup_gather(const uint16_t *x, int T, int Kp, const Di
     const int bn2 = (want == 88 && I % 88 == 0) ? 88 : (I >= 128 ? 128 : 64);
     CUtensorMap a, b;
     // token rows [T, H], one-row boxes: each tile::gather4 copy fetches 4 rows
+    CUtensorMap c;
     if (!bf16_map_2d(&a, x, H, T, kBK, 1, true) ||
-        !make_map(&b, w.gu, H, (uint64_t)E * 2 * I, bn2))
+        !make_map(&b, w.gu, H, (uint64_t)E * 2 * I, bn2) || !tail_map(&c, b, w.gu, H, I, E, bn2))
         return cudaErrorInvalidValue;
     const int32_t *perm = d.perm;
     cudaError_t e = (bn2 == 88)
         ? launch<EPI_GATEUP_G, 176, 88, kGuStages>(a, b, d, E, H, I, H, yp, I, err, s, nullptr,
-                                                  nullptr, perm, Kp)
+                                                  &c, perm, Kp)
         : (bn2 == 128)
         ? launch<EPI_GATEUP_G, 256, 128, kDnStages>(a, b, d, E, H, I, H, yp, I, err, s, nullptr,
-                                                   nullptr, perm, Kp)
+                                                   &c, perm, Kp)
         : launch<EPI_GATEUP_G, 128, 64, kGuStages>(a, b, d, E, H, I, H, yp, I, err, s, nullptr,
-                                                  nullptr, perm, Kp);
+                                                  &c, perm, Kp);
     if (launches) ++*launches;
     return e;
 }
@@ -416,13 +445,15 @@ cudaError_t launch_gemm_gateup_grouped(const uint16_t *rows, const Dispatch &d,
     if (G > kMaxExperts) return cudaErrorInvalidValue;
     const int bn2 = (rows_cap > 4096 || I % 88) ? (I >= 128 ? 128 : 64) : 88;
     CUtensorMap a, b;
-    if (!make_map(&a, rows, H, rows_cap, kBM) || !make_map(&b, w.gu, H, (uint64_t)E_w * 2 * I, bn2))
+    CUtensorMap c;
+    if (!make_map(&a, rows, H, rows_cap, kBM) ||
+        !make_map(&b, w.gu, H, (uint64_t)E_w * 2 * I, bn2) || !tail_map(&c, b, w.gu, H, I, E_w, bn2))
         return cudaErrorInvalidValue;
     cudaError_t e = (bn2 == 88)
-        ? launch<EPI_GATEUP, 176, 88, kGuStages>(a, b, d, G, H, I, H, yp, I, err, s, g2e)
+        ? launch<EPI_GATEUP, 176, 88, kGuStages>(a, b, d, G, H, I, H, yp, I, err, s, g2e, &c)
         : (bn2 == 128)
-        ? launch<EPI_GATEUP, 256, 128, kDnStages>(a, b, d, G, H, I, H, yp, I, err, s, g2e)
-        : launch<EPI_GATEUP, 128, 64, kGuStages>(a, b, d, G, H, I, H, yp, I, err, s, g2e);
+        ? launch<EPI_GATEUP, 256, 128, kDnStages>(a, b, d, G, H, I, H, yp, I, err, s, g2e, &c)
+        : launch<EPI_GATEUP, 128, 64, kGuStages>(a, b, d, G, H, I, H, yp, I, err, s, g2e, &c);
     if (launches) ++*launches;
     return e;
 }
