@@ -24,6 +24,26 @@ constexpr int kSmallTok = 8;     // tokens staged per CTA in the decode kernel
 constexpr int kSmallWarps = 4;   // experts per CTA in the decode kernel
 constexpr int kSmallThreads = 256;  // 8 warps: 4 experts x 2 token groups
 
+// Phase timestamps (%globaltimer, thread 0 of each CTA) for tuning builds
+// compiled with -DAPT_ROUTER_TRACE; absent from the library build.
+#ifdef APT_ROUTER_TRACE
+__device__ unsigned long long g_rtrace[1024][12];
+__device__ long long g_rclock[1024][12];
+#define RT_STAMP(i)                                                                    \
+    do {                                                                               \
+        if (threadIdx.x == 0) {                                                        \
+            unsigned long long t_;                                                     \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                     \
+            g_rtrace[blockIdx.y * gridDim.x + blockIdx.x][i] = t_;                     \
+            g_rclock[blockIdx.y * gridDim.x + blockIdx.x][i] = clock64();              \
+        }                                                                              \
+    } while (0)
+#else
+#define RT_STAMP(i) \
+    do {            \
+    } while (0)
+#endif
+
 // r_t = 1/sqrt(mean(x_t^2) + eps) for one token, computed by one warp.
 __device__ __forceinline__ float token_rrms(const uint16_t *xr, int H, float eps, int lane) {
     float s = 0.f;
@@ -63,20 +83,27 @@ __device__ __forceinline__ void scores_small_block(const uint16_t *__restrict__ 
     const int t0 = blockIdx.y * kSmallTok;
     const int nt = min(kSmallTok, T - t0);
     const int nv = H / 256;
+    // the scale vector into shared memory, the token row (its sum of squares
+    // is on the critical path) and the warp's proj row into registers: all
+    // issued before any is consumed
+    uint16_t *s_scale = reinterpret_cast<uint16_t *>(hs + min(T, kSmallTok) * H);
+    for (int v = threadIdx.x; v < H / 8; v += blockDim.x)
+        reinterpret_cast<uint4 *>(s_scale)[v] = __ldg(reinterpret_cast<const uint4 *>(scale) + v);
+    uint4 xv[kMaxVec];
+    if (warp < nt) {  // warp w stages token w
+        const uint16_t *xr = x + (size_t)(t0 + warp) * H + lane * 8;
+#pragma unroll
+        for (int i = 0; i < kMaxVec; ++i)
+            if (i < nv) xv[i] = __ldg(reinterpret_cast<const uint4 *>(xr + i * 256));
+    }
     uint4 pv[kMaxVec];
     const uint16_t *pr = proj + (size_t)(e < E ? e : 0) * H + lane * 8;
 #pragma unroll
     for (int i = 0; i < kMaxVec; ++i)
         if (i < nv) pv[i] = __ldg(reinterpret_cast<const uint4 *>(pr + i * 256));
-    if (warp < nt) {  // warp w stages token w
-        const uint16_t *xr = x + (size_t)(t0 + warp) * H + lane * 8;
-        uint4 xv[kMaxVec], sv[kMaxVec];
-#pragma unroll
-        for (int i = 0; i < kMaxVec; ++i)
-            if (i < nv) {
-                xv[i] = __ldg(reinterpret_cast<const uint4 *>(xr + i * 256));
-                sv[i] = __ldg(reinterpret_cast<const uint4 *>(scale + i * 256 + lane * 8));
-            }
+    __syncthreads();  // s_scale complete
+    RT_STAMP(7);
+    if (warp < nt) {
         float ss = 0.f;
 #pragma unroll
         for (int i = 0; i < kMaxVec; ++i)
@@ -94,7 +121,7 @@ __device__ __forceinline__ void scores_small_block(const uint16_t *__restrict__ 
             if (i < nv) {
                 float f[8], sf[8], hv[8];
                 unpack8(xv[i], f);
-                unpack8(sv[i], sf);
+                unpack8(*reinterpret_cast<const uint4 *>(s_scale + i * 256 + lane * 8), sf);
 #pragma unroll
                 for (int j = 0; j < 8; ++j) hv[j] = router_h(f[j], r, sf[j], root);
                 *reinterpret_cast<float4 *>(dst + i * 256) = make_float4(hv[0], hv[1], hv[2], hv[3]);
@@ -120,6 +147,7 @@ __device__ __forceinline__ void scores_small_block(const uint16_t *__restrict__ 
         }
     }
     __syncthreads();
+    RT_STAMP(8);
     constexpr int TPW = kSmallTok / (kSmallThreads / 32 / kSmallWarps);  // tokens per warp
     if (e < E) {
         float acc[TPW];
@@ -242,21 +270,25 @@ router_scores_tiled(const uint16_t *__restrict__ x, const uint16_t *__restrict__
 
 constexpr int kMaxPerLane = 8;  // E <= 256
 
-// Softmax, top-K (descending prob, lower id on ties), renormalise and
-// per-expert scale for one token, by one warp.  Lanes k < K return the k-th
-// choice in (sel_e, wk); other lanes return sel_e = -1.
-__device__ __forceinline__ void select_token(const float *__restrict__ sr,
-                                             const uint16_t *__restrict__ pes, int E, int K,
-                                             int lane, int &sel_e_out, float &wk_out) {
-    float p[kMaxPerLane];
+// Softmax and top-K (descending prob, lower id on ties) of one token's scores
+// p[j] = score of expert lane + 32 j (-inf past E), by one warp.  Lane k < K
+// returns the k-th choice (sel_e, sel_p); every lane returns the k-order sum
+// of the K chosen probabilities.
+// Order-preserving map of f32 to u32 (for single-instruction warp max).
+__device__ __forceinline__ unsigned fkey(float f) {
+    const unsigned b = __float_as_uint(f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float fkey_inv(unsigned k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+__device__ __forceinline__ void select_core(float (&p)[kMaxPerLane], int E, int K, int lane,
+                                            int &sel_e, float &sel_p, float &sum) {
     float m = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < kMaxPerLane; ++j) {
-        const int e = lane + 32 * j;
-        p[j] = (e < E) ? __ldcg(sr + e) : -INFINITY;  // written by other CTAs
-        m = fmaxf(m, p[j]);
-    }
-    m = warp_max(m);
+    for (int j = 0; j < kMaxPerLane; ++j) m = fmaxf(m, p[j]);
+    m = fkey_inv(__reduce_max_sync(0xffffffffu, fkey(m)));
     float den = 0.f;
 #pragma unroll
     for (int j = 0; j < kMaxPerLane; ++j) {
@@ -270,12 +302,12 @@ __device__ __forceinline__ void select_token(const float *__restrict__ sr,
         const int e = lane + 32 * j;
         p[j] = (e < E) ? __fdiv_rn(p[j], den) : -1.f;  // -1: never selected
     }
-    float sum = 0.f;
-    float sel_p = 0.f;
-    int sel_e = -1;
+    sum = 0.f;
+    sel_p = 0.f;
+    sel_e = -1;
     unsigned taken = 0;
     for (int k = 0; k < K; ++k) {
-        float bp = -2.f;  // lane-local best among untaken
+        float bp = -2.f;  // lane-local best among untaken (lowest id on ties)
         int be = 0x7fffffff;
 #pragma unroll
         for (int j = 0; j < kMaxPerLane; ++j) {
@@ -285,22 +317,35 @@ __device__ __forceinline__ void select_token(const float *__restrict__ sr,
                 be = e;
             }
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float op = __shfl_xor_sync(0xffffffffu, bp, o);
-            const int oe = __shfl_xor_sync(0xffffffffu, be, o);
-            if (op > bp || (op == bp && oe < be)) {
-                bp = op;
-                be = oe;
-            }
-        }
-        if ((be & 31) == lane) taken |= 1u << (be >> 5);
-        sum = __fadd_rn(sum, bp);  // sequential in k order, every lane the same
+        // warp-wide: the largest probability, then the lowest id holding it
+        const unsigned kb = fkey(bp);
+        const unsigned mk = __reduce_max_sync(0xffffffffu, kb);
+        const int we = (int)__reduce_min_sync(0xffffffffu, kb == mk ? (unsigned)be : 0xffffffffu);
+        const float wp = fkey_inv(mk);
+        if ((we & 31) == lane) taken |= 1u << (we >> 5);
+        sum = __fadd_rn(sum, wp);  // sequential in k order, every lane the same
         if (lane == k) {
-            sel_p = bp;
-            sel_e = be;
+            sel_p = wp;
+            sel_e = we;
         }
     }
+}
+
+// Softmax, top-K (descending prob, lower id on ties), renormalise and
+// per-expert scale for one token, by one warp.  Lanes k < K return the k-th
+// choice in (sel_e, wk); other lanes return sel_e = -1.
+__device__ __forceinline__ void select_token(const float *__restrict__ sr,
+                                             const uint16_t *__restrict__ pes, int E, int K,
+                                             int lane, int &sel_e_out, float &wk_out) {
+    float p[kMaxPerLane];
+#pragma unroll
+    for (int j = 0; j < kMaxPerLane; ++j) {
+        const int e = lane + 32 * j;
+        p[j] = (e < E) ? __ldcg(sr + e) : -INFINITY;  // written by other CTAs
+    }
+    int sel_e;
+    float sel_p, sum;
+    select_core(p, E, K, lane, sel_e, sel_p, sum);
     wk_out = 0.f;
     sel_e_out = -1;
     if (lane < K) {
@@ -340,7 +385,8 @@ __global__ void router_select(const float *__restrict__ scores, const uint16_t *
 // Requires T <= 64, T*K <= kFusedMaxPairs, E <= 256.
 constexpr int kFusedMaxPairs = 512;
 
-__global__ void __launch_bounds__(kSmallThreads)
+
+__global__ void __launch_bounds__(kSmallThreads, 2)
 router_dispatch_small(const uint16_t *__restrict__ x, const uint16_t *__restrict__ proj,
                       const uint16_t *__restrict__ scale, const uint16_t *__restrict__ pes, int T,
                       int H, int E, int K, float eps, float root, float *__restrict__ scores,
@@ -352,50 +398,65 @@ router_dispatch_small(const uint16_t *__restrict__ x, const uint16_t *__restrict
     __shared__ int s_idx[kFusedMaxPairs];
     __shared__ int s_cnt[256];
     __shared__ int s_off[257];
-    __shared__ int s_cur[256];
+    __shared__ float s_pes[256];
+    RT_STAMP(0);
     pdl_trigger();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // per_expert_scale for the select phase, fetched while the scores run
+    for (int e = tid; e < E; e += blockDim.x) s_pes[e] = bf2f(pes[e]);
     scores_small_block(x, proj, scale, T, H, E, eps, root, scores, hs, pre_w, xn);
+    RT_STAMP(1);
     // level 1: the last CTA of this token chunk selects the chunk's tokens
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (tid == 0) {
         const int prev = atomicAdd(done + 1 + blockIdx.y, 1);
         s_last = (prev == (int)gridDim.x - 1);
     }
     __syncthreads();
+    RT_STAMP(2);
     if (!s_last) return;
     __threadfence();
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const bool single = gridDim.y == 1;  // one chunk: this CTA also builds the dispatch
     {
         const int t = blockIdx.y * kSmallTok + warp;  // 8 warps, 8 tokens per chunk
         if (t < T) {
+            float p[kMaxPerLane];
+#pragma unroll
+            for (int j = 0; j < kMaxPerLane; ++j) {
+                const int e = lane + 32 * j;
+                p[j] = (e < E) ? __ldcg(scores + (size_t)t * E + e) : -INFINITY;
+            }
             int e;
-            float wk;
-            select_token(scores + (size_t)t * E, pes, E, K, lane, e, wk);
+            float sel_p, sum;
+            select_core(p, E, K, lane, e, sel_p, sum);
             if (lane < K) {
                 idx[(size_t)t * K + lane] = e;
-                w[(size_t)t * K + lane] = f2bf(wk);
+                w[(size_t)t * K + lane] = f2bf(__fmul_rn(__fdiv_rn(sel_p, sum), s_pes[e]));
+                if (single) s_idx[t * K + lane] = e;
             }
         }
     }
+    RT_STAMP(3);
     if (tid == 0) done[1 + blockIdx.y] = 0;  // ready for the next call
-    // level 2: the last chunk builds the dispatch for all tokens
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const int prev = atomicAdd(done, 1);
-        s_last = (prev == (int)gridDim.y - 1);
+    if (!single) {
+        // level 2: the last chunk builds the dispatch for all tokens
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            const int prev = atomicAdd(done, 1);
+            s_last = (prev == (int)gridDim.y - 1);
+        }
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
     }
+    RT_STAMP(4);
+    for (int e = tid; e < E; e += blockDim.x) s_cnt[e] = 0;
     __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    for (int e = tid; e < E; e += blockDim.x) {
-        s_cnt[e] = 0;
-        s_cur[e] = 0;
-    }
-    __syncthreads();
-    for (int p = tid; p < T * K; p += blockDim.x) {
-        const int e = __ldcg(idx + p);  // written by other CTAs of this grid
+    const int P = T * K;
+    for (int p = tid; p < P; p += blockDim.x) {
+        const int e = single ? s_idx[p] : __ldcg(idx + p);  // else written by other CTAs
         s_idx[p] = e;
         atomicAdd(&s_cnt[e], 1);
     }
@@ -425,10 +486,7 @@ router_dispatch_small(const uint16_t *__restrict__ x, const uint16_t *__restrict
             }
             run += loc[j];
         }
-        if (lane == 31) {
-            s_off[E] = incl;
-            d.offsets[E] = incl;
-        }
+        if (lane == 31) d.offsets[E] = incl;
         // active list: experts with nonzero count, ascending
         int na = 0;
         for (int e0 = 0; e0 < E; e0 += 32) {
@@ -440,26 +498,21 @@ router_dispatch_small(const uint16_t *__restrict__ x, const uint16_t *__restrict
         }
         if (lane == 0) {
             *d.n_active = na;
-            *done = 0;  // ready for the next call
+            if (!single) *done = 0;  // ready for the next call
         }
     }
     __syncthreads();
-    if (warp == 0) {  // stable positions: pairs in order, 32 at a time
-        const int P = T * K;
-        for (int p0 = 0; p0 < P; p0 += 32) {
-            const int p = p0 + lane;
-            const int e = p < P ? s_idx[p] : -1 - lane;
-            const unsigned m = __match_any_sync(0xffffffffu, e);
-            if (p < P) {
-                const int pos = s_off[e] + s_cur[e] + __popc(m & ((1u << lane) - 1u));
-                d.perm[pos] = p;
-                d.inv[p] = pos;
-            }
-            __syncwarp();
-            if (p < P && (m & ((1u << lane) - 1u)) == 0) s_cur[e] += __popc(m);
-            __syncwarp();
-        }
+    RT_STAMP(5);
+    // placement: each pair claims the next slot of its expert's group.  The
+    // order inside a group is arbitrary; every row is computed independently
+    // and found again through inv, so results do not depend on it.
+    for (int p = tid; p < P; p += blockDim.x) {
+        const int e = s_idx[p];
+        const int pos = atomicAdd(&s_off[e], 1);
+        d.perm[pos] = p;
+        d.inv[p] = pos;
     }
+    RT_STAMP(6);
 }
 
 // Router input for the tensor-core score GEMM: h = ((x*r)*scale)*H^-1/2 in
@@ -608,7 +661,7 @@ cudaError_t launch_router_dispatch(const uint16_t *x, const uint16_t *proj, cons
                                    int32_t *done, cudaStream_t s, int *launches,
                                    const uint16_t *pre_w, uint16_t *xn) {
     const float root = (float)(1.0 / sqrt((double)H));
-    const size_t smem = (size_t)(T < kSmallTok ? T : kSmallTok) * H * sizeof(float);
+    const size_t smem = (size_t)(T < kSmallTok ? T : kSmallTok) * H * sizeof(float) + H * 2;
     dim3 grid((E + kSmallWarps - 1) / kSmallWarps, (T + kSmallTok - 1) / kSmallTok);
     router_dispatch_small<<<grid, kSmallThreads, smem, s>>>(x, proj, scale, pes, T, H, E, K,
                                                                eps, root, scores, idx, w, d, done,
@@ -622,7 +675,7 @@ cudaError_t launch_router_scores(const uint16_t *x, const uint16_t *proj, const 
                                  int *launches) {
     const float root = (float)(1.0 / sqrt((double)H));
     if (T <= 64 && H % 256 == 0 && H <= 256 * kMaxVec) {
-        const size_t smem = (size_t)(T < kSmallTok ? T : kSmallTok) * H * sizeof(float);
+        const size_t smem = (size_t)(T < kSmallTok ? T : kSmallTok) * H * sizeof(float) + H * 2;
         dim3 grid((E + kSmallWarps - 1) / kSmallWarps, (T + kSmallTok - 1) / kSmallTok);
         router_scores_small<<<grid, kSmallThreads, smem, s>>>(x, proj, scale, T, H, E, eps,
                                                                  root, scores);
