@@ -64,7 +64,7 @@ struct apt_moe_handle {
     uint16_t *w2 = nullptr;
     uint16_t *xin = nullptr, *xout = nullptr;  // host-API staging [Tm,H]
     uint16_t *xn = nullptr;                    // pre_ff_ln_2(x1) [Tm,H] (layer entry point)
-    const uint16_t *cur_post_w = nullptr;      // post_ff_ln_2 weight of the current call
+    CombineTail cur_tail{};                    // norms the current call's combine applies
 
     Dispatch disp() const { return Dispatch{counts, offsets, perm, inv, active, n_active}; }
 };
@@ -602,8 +602,8 @@ apt_status run_experts(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
         STAGE(h, APT_STAGE_DOWN, s, launch_gemv_down(h->yp, d, ew, H, I, E, max_rows, h->op, s, &h->launches));
     }
     STAGE(h, APT_STAGE_COMBINE, s,
-          launch_combine(h->op, idx, w, d, T, Kp, H, out, s, &h->launches, h->cur_post_w,
-                         h->cfg.rms_norm_eps));
+          launch_combine(h->op, idx, w, d, T, Kp, H, out, s, &h->launches,
+                         h->cur_tail.post_w ? &h->cur_tail : nullptr));
     return APT_OK;
 }
 
@@ -701,11 +701,12 @@ extern "C" apt_status apt_moe_experts_dense(apt_moe_handle *h, const uint16_t *x
 
 namespace {
 // The MoE section of ESDecoderLayer::forward.  With pre_w, the expert input is
-// pre_ff_ln_2(x_router) computed on the way (x_experts ignored); with post_w,
-// the output is post_ff_ln_2 of the block output (fused into the combine).
+// pre_ff_ln_2(x_router) computed on the way (x_experts ignored); with a tail,
+// the norms after the block (post_ff_ln_2, and optionally post_ff_ln_1 of the
+// dense MLP, post_ff_ln and the residual add) are fused into the combine.
 apt_status forward_impl(apt_moe_handle *h, const uint16_t *x_router, const uint16_t *x_experts,
                         int T, uint16_t *out, int32_t *idx_out, uint16_t *w_out, void *stream,
-                        const uint16_t *pre_w, const uint16_t *post_w) {
+                        const uint16_t *pre_w, const CombineTail *tail) {
     if (!h) return APT_ERR_INVALID;
     if (check_T(h, T)) return APT_ERR_INVALID;
     if (T == 0) return APT_OK;
@@ -719,10 +720,10 @@ apt_status forward_impl(apt_moe_handle *h, const uint16_t *x_router, const uint1
     int32_t *idx = idx_out ? idx_out : h->idx_i;
     uint16_t *w = w_out ? w_out : h->w_i;
     if (pre_w) x_experts = h->xn;
-    h->cur_post_w = post_w;
+    if (tail) h->cur_tail = *tail;
     struct ClearPost {
         apt_moe_handle *h;
-        ~ClearPost() { h->cur_post_w = nullptr; }
+        ~ClearPost() { h->cur_tail = CombineTail{}; }
     } clear_post{h};
     if (h->cfg.moe_sparse && router_dispatch_fusable(T, H, E, K)) {
         // decode: router + top-k + dispatch in one launch
@@ -772,8 +773,33 @@ extern "C" apt_status apt_moe_layer_forward(apt_moe_handle *h, const uint16_t *x
     if (!h) return APT_ERR_INVALID;
     if (!pre_ff_ln_2_w || !post_ff_ln_2_w) return fail(h, APT_ERR_INVALID, "null norm weight");
     if (h->cfg.hidden_size % 8) return fail(h, APT_ERR_UNSUPPORTED, "hidden_size % 8");
-    return forward_impl(h, x1, nullptr, T, out, nullptr, nullptr, stream, pre_ff_ln_2_w,
-                        post_ff_ln_2_w);
+    CombineTail tail{};
+    tail.post_w = post_ff_ln_2_w;
+    tail.eps = h->cfg.rms_norm_eps;
+    return forward_impl(h, x1, nullptr, T, out, nullptr, nullptr, stream, pre_ff_ln_2_w, &tail);
+}
+
+extern "C" apt_status apt_moe_decoder_ff(apt_moe_handle *h, const uint16_t *x1,
+                                         const uint16_t *hmlp, const uint16_t *pre_ff_ln_2_w,
+                                         const uint16_t *post_ff_ln_1_w,
+                                         const uint16_t *post_ff_ln_2_w,
+                                         const uint16_t *post_ff_ln_w, int T, uint16_t *x2,
+                                         void *stream) {
+    if (!h) return APT_ERR_INVALID;
+    if (!x1 || !hmlp || !x2) return fail(h, APT_ERR_INVALID, "null pointer");
+    if (!pre_ff_ln_2_w || !post_ff_ln_1_w || !post_ff_ln_2_w || !post_ff_ln_w)
+        return fail(h, APT_ERR_INVALID, "null norm weight");
+    if (h->cfg.hidden_size % 8) return fail(h, APT_ERR_UNSUPPORTED, "hidden_size % 8");
+    if (x2 == x1 || x2 == hmlp)
+        return fail(h, APT_ERR_INVALID, "x2 must not alias x1 or hmlp");
+    CombineTail tail{};
+    tail.post_w = post_ff_ln_2_w;
+    tail.mlp = hmlp;
+    tail.mlp_w = post_ff_ln_1_w;
+    tail.ff_w = post_ff_ln_w;
+    tail.resid = x1;
+    tail.eps = h->cfg.rms_norm_eps;
+    return forward_impl(h, x1, nullptr, T, x2, nullptr, nullptr, stream, pre_ff_ln_2_w, &tail);
 }
 
 // ---- expert-parallel halves: the routing + dispatch before the all-to-all,

@@ -124,19 +124,52 @@ __global__ void gather_rows_kernel(const uint16_t *__restrict__ x, int H, int K,
     }
 }
 
+// Block-wide sum of two values (all threads get both results).
+__device__ __forceinline__ float2 block_sum2(float a, float b, float2 *red) {
+    a = warp_sum(a);
+    b = warp_sum(b);
+    __syncthreads();  // red may still be read from a previous call
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = make_float2(a, b);
+    __syncthreads();
+    float2 r = make_float2(0.f, 0.f);
+    for (int i = 0; i < (int)(blockDim.x + 31) / 32; ++i) {
+        r.x += red[i].x;
+        r.y += red[i].y;
+    }
+    return r;
+}
+
+__device__ __forceinline__ float rms_inv(float ss, int H, float eps) {
+    return 1.0f / sqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / (float)H), eps));
+}
+
+__device__ __forceinline__ void store8(uint16_t *dst, const float (&o)[8]) {
+    uint4 r;
+    r.x = pack_bf2(o[0], o[1]);
+    r.y = pack_bf2(o[2], o[3]);
+    r.z = pack_bf2(o[4], o[5]);
+    r.w = pack_bf2(o[6], o[7]);
+    *reinterpret_cast<uint4 *>(dst) = r;
+}
+
 // One CTA per token; each thread owns 8 consecutive hidden elements.  The
 // token's K (idx, w, inv) triples are read into shared memory first, so the
 // K row loads that follow are independent and all in flight at once.
+//
+// Optional layer tail (ESDecoderLayer.mm:66-78), each RMSNorm as
+// ESRMSNorm.mm:19-26 (f32, (x*r)*w, one bf16 rounding):
+//   post_w only:  out = post_ff_ln_2(moe)
+//   + mlp/ff_w:   out = resid + post_ff_ln( post_ff_ln_1(mlp) + post_ff_ln_2(moe) )
 constexpr int kMaxK = 256;
 
 __global__ void combine_kernel(const uint16_t *__restrict__ op, const int32_t *__restrict__ idx,
                                const uint16_t *__restrict__ w, const int32_t *__restrict__ inv,
-                               int T, int K, int H, uint16_t *__restrict__ out,
-                               const uint16_t *__restrict__ post_w, float eps) {
+                               int T, int K, int H, uint16_t *__restrict__ out, CombineTail tail) {
     __shared__ int s_row[kMaxK];
     __shared__ float s_w[kMaxK];
-    __shared__ float s_red[32];
-    extern __shared__ float s_moe[];  // [H] when post_w: the bf16 block output before the norm
+    __shared__ float2 s_red[32];
+    extern __shared__ float s_buf[];  // [H] bf16 MoE output before the norm; [H] mlp row
+    float *s_moe = s_buf, *s_mlp = s_buf + H;
     const int t = blockIdx.x;
     pdl_trigger();
     pdl_wait();
@@ -147,10 +180,13 @@ __global__ void combine_kernel(const uint16_t *__restrict__ op, const int32_t *_
         s_w[k] = live ? bf2f(w[p]) : 0.f;
     }
     __syncthreads();
-    float ss = 0.f;
+    const bool post = tail.post_w != nullptr, full = post && tail.mlp != nullptr;
+    float ss = 0.f, ssd = 0.f;
     for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
         float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
         constexpr int B = 8;  // rows in flight per batch
+        uint4 mv;
+        if (full) mv = *reinterpret_cast<const uint4 *>(tail.mlp + (size_t)t * H + v * 8);
         for (int k0 = 0; k0 < K; k0 += B) {
             uint4 o[B];
 #pragma unroll
@@ -169,45 +205,65 @@ __global__ void combine_kernel(const uint16_t *__restrict__ op, const int32_t *_
                 for (int q = 0; q < 8; ++q) acc[q] = __fadd_rn(acc[q], rbf(__fmul_rn(wk, f[q])));
             }
         }
-        if (post_w) {
+        if (post) {
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
                 const float m = rbf(acc[q]);  // the MoE output is bf16 before post_ff_ln_2
                 s_moe[v * 8 + q] = m;
                 ss = fmaf(m, m, ss);
             }
+            if (full) {
+                float f[8];
+                unpack8(mv, f);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    s_mlp[v * 8 + q] = f[q];
+                    ssd = fmaf(f[q], f[q], ssd);
+                }
+            }
         } else {
-            uint4 r;
-            r.x = pack_bf2(acc[0], acc[1]);
-            r.y = pack_bf2(acc[2], acc[3]);
-            r.z = pack_bf2(acc[4], acc[5]);
-            r.w = pack_bf2(acc[6], acc[7]);
-            *reinterpret_cast<uint4 *>(out + (size_t)t * H + v * 8) = r;
+            store8(out + (size_t)t * H + v * 8, acc);
         }
     }
-    if (!post_w) return;
-    // post_ff_ln_2 (ESRMSNorm.mm:14-28) over the finished row
-    ss = warp_sum(ss);
-    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        float v = (threadIdx.x < (blockDim.x + 31) / 32) ? s_red[threadIdx.x] : 0.f;
-        v = warp_sum(v);
-        if (threadIdx.x == 0) s_red[0] = v;
-    }
-    __syncthreads();
-    const float r = 1.0f / sqrtf(__fadd_rn(__fmul_rn(s_red[0], 1.0f / (float)H), eps));
-    for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
-        float wf[8], o[8];
-        unpack8(*reinterpret_cast<const uint4 *>(post_w + v * 8), wf);
+    if (!post) return;
+    const float2 sums = block_sum2(ss, ssd, s_red);
+    const float rm = rms_inv(sums.x, H, tail.eps);
+    if (!full) {  // post_ff_ln_2 only
+        for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
+            float wf[8], o[8];
+            unpack8(*reinterpret_cast<const uint4 *>(tail.post_w + v * 8), wf);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) o[q] = __fmul_rn(__fmul_rn(s_moe[v * 8 + q], r), wf[q]);
-        uint4 rr;
-        rr.x = pack_bf2(o[0], o[1]);
-        rr.y = pack_bf2(o[2], o[3]);
-        rr.z = pack_bf2(o[4], o[5]);
-        rr.w = pack_bf2(o[6], o[7]);
-        *reinterpret_cast<uint4 *>(out + (size_t)t * H + v * 8) = rr;
+            for (int q = 0; q < 8; ++q) o[q] = __fmul_rn(__fmul_rn(s_moe[v * 8 + q], rm), wf[q]);
+            store8(out + (size_t)t * H + v * 8, o);
+        }
+        return;
+    }
+    // ff = bf16( bf16(post_ff_ln_1(mlp)) + bf16(post_ff_ln_2(moe)) ), kept in s_moe
+    const float rd = rms_inv(sums.y, H, tail.eps);
+    float ssf = 0.f;
+    for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
+        float w2[8], w1[8];
+        unpack8(*reinterpret_cast<const uint4 *>(tail.post_w + v * 8), w2);
+        unpack8(*reinterpret_cast<const uint4 *>(tail.mlp_w + v * 8), w1);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const float m = rbf(__fmul_rn(__fmul_rn(s_moe[v * 8 + q], rm), w2[q]));
+            const float d = rbf(__fmul_rn(__fmul_rn(s_mlp[v * 8 + q], rd), w1[q]));
+            const float f = rbf(__fadd_rn(d, m));
+            s_moe[v * 8 + q] = f;
+            ssf = fmaf(f, f, ssf);
+        }
+    }
+    const float rf = rms_inv(block_sum2(ssf, 0.f, s_red).x, H, tail.eps);
+    // out = bf16( resid + bf16(post_ff_ln(ff)) )
+    for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
+        float wf[8], xr[8], o[8];
+        unpack8(*reinterpret_cast<const uint4 *>(tail.ff_w + v * 8), wf);
+        unpack8(*reinterpret_cast<const uint4 *>(tail.resid + (size_t)t * H + v * 8), xr);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+            o[q] = __fadd_rn(xr[q], rbf(__fmul_rn(__fmul_rn(s_moe[v * 8 + q], rf), wf[q])));
+        store8(out + (size_t)t * H + v * 8, o);
     }
 }
 
@@ -340,11 +396,13 @@ cudaError_t launch_gather_rows(const uint16_t *x, int H, int K, int E, const Dis
 
 cudaError_t launch_combine(const uint16_t *op, const int32_t *idx, const uint16_t *w,
                            const Dispatch &d, int T, int K, int H, uint16_t *out, cudaStream_t s,
-                           int *launches, const uint16_t *post_w, float eps) {
+                           int *launches, const CombineTail *tail) {
     const int threads = min(512, ((H / 8 + 31) / 32) * 32);
-    const size_t smem = post_w ? (size_t)H * sizeof(float) : 0;
+    CombineTail tl{};
+    if (tail) tl = *tail;
+    const size_t smem = tl.post_w ? (size_t)H * sizeof(float) * (tl.mlp ? 2 : 1) : 0;
     cudaError_t err = launch_ex(combine_kernel, dim3(T), dim3(threads), smem, s, true, op, idx, w,
-                                (const int32_t *)d.inv, T, K, H, out, post_w, eps);
+                                (const int32_t *)d.inv, T, K, H, out, tl);
     if (launches) ++*launches;
     return err;
 }

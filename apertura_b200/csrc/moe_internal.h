@@ -71,12 +71,22 @@ cudaError_t launch_place(const int32_t *idx, const int32_t *rank, int P, int E, 
 // xp[row] = x[perm[row] / K] for row < offsets[E]
 cudaError_t launch_gather_rows(const uint16_t *x, int H, int K, int E, const Dispatch &d,
                                int max_rows, uint16_t *xp, cudaStream_t s, int *launches);
-// out[t] = bf16( sum_k f32(bf16(w[t,k] * op[inv[t*K+k]])) )
-// post_w (optional): out = RMSNorm(combine) * post_w, eps (post_ff_ln_2)
+// Optional norms around the MoE output, applied by the combine
+// (ESDecoderLayer.mm:66-78).  post_w alone: out = post_ff_ln_2(moe).  With
+// mlp (+ mlp_w, ff_w, resid): out = resid + post_ff_ln(post_ff_ln_1(mlp) +
+// post_ff_ln_2(moe)).  All weights [H] bf16 on the device.
+struct CombineTail {
+    const uint16_t *post_w;  // post_ff_ln_2
+    const uint16_t *mlp;     // dense MLP output [T,H]
+    const uint16_t *mlp_w;   // post_ff_ln_1
+    const uint16_t *ff_w;    // post_ff_ln
+    const uint16_t *resid;   // x1 [T,H]
+    float eps;
+};
+// out[t] = bf16( sum_k f32(bf16(w[t,k] * op[inv[t*K+k]])) ), then the tail
 cudaError_t launch_combine(const uint16_t *op, const int32_t *idx, const uint16_t *w,
                            const Dispatch &d, int T, int K, int H, uint16_t *out,
-                           cudaStream_t s, int *launches, const uint16_t *post_w = nullptr,
-                           float eps = 0.f);
+                           cudaStream_t s, int *launches, const CombineTail *tail = nullptr);
 
 // ---- decode GEMV (gemv.cu).  Weight formats: bits == 0 -> bf16, else affine.
 struct ExpertWeights {

@@ -332,6 +332,25 @@ class MoEBlock:
                                                       _stream(x1.device)))
         return out
 
+    def forward_decoder_ff(self, x1: torch.Tensor, hmlp: torch.Tensor,
+                           pre_ff_ln_2_w: torch.Tensor, post_ff_ln_1_w: torch.Tensor,
+                           post_ff_ln_2_w: torch.Tensor, post_ff_ln_w: torch.Tensor) -> torch.Tensor:
+        """x2 = x1 + post_ff_ln(post_ff_ln_1(hmlp) + post_ff_ln_2(MoE(x1))): the
+        feed-forward tail of an MoE ESDecoderLayer (ESDecoderLayer.mm:61-78),
+        hmlp being the dense MLP's output; all trailing norms fused."""
+        _need_cuda_bf16("x1", x1)
+        H = self.cfg.hidden_size
+        T = x1.shape[0]
+        _need_cuda_bf16("hmlp", hmlp, (T, H))
+        for name, t in (("pre_ff_ln_2_w", pre_ff_ln_2_w), ("post_ff_ln_1_w", post_ff_ln_1_w),
+                        ("post_ff_ln_2_w", post_ff_ln_2_w), ("post_ff_ln_w", post_ff_ln_w)):
+            _need_cuda_bf16(name, t, (H,))
+        x2 = torch.empty(T, H, dtype=torch.bfloat16, device=x1.device)
+        self.handle.check(lib().apt_moe_decoder_ff(
+            self.handle.h, _ptr(x1), _ptr(hmlp), _ptr(pre_ff_ln_2_w), _ptr(post_ff_ln_1_w),
+            _ptr(post_ff_ln_2_w), _ptr(post_ff_ln_w), T, _ptr(x2), _stream(x1.device)))
+        return x2
+
     def forward_host(self, x_host: torch.Tensor, out_host: Optional[torch.Tensor] = None):
         """End-to-end call with host buffers (pinned for speed)."""
         if x_host.is_cuda or x_host.dtype != torch.bfloat16:

@@ -164,6 +164,23 @@ APT_API apt_status apt_moe_layer_forward(apt_moe_handle *h, const uint16_t *x1,
                                          void *stream);
 
 /*
+ * The whole feed-forward tail of an MoE decoder layer (ESDecoderLayer.mm:
+ * 61-78) given the dense MLP output hmlp = mlp(pre_ff_ln(x1)):
+ *   x2 = x1 + post_ff_ln( post_ff_ln_1(hmlp) + post_ff_ln_2(MoE(x1)) )
+ * with the MoE block as in apt_moe_layer_forward.  Every RMSNorm is f32 with
+ * one bf16 rounding (ESRMSNorm.mm:19-26), every add is bf16 + bf16 -> bf16.
+ * The three trailing norms and the residual add run inside the combine
+ * kernel.  x1, hmlp, x2 [T,H] bf16 on the device; x2 may not alias x1 or
+ * hmlp.  The four weights are [H] bf16 on the device.
+ */
+APT_API apt_status apt_moe_decoder_ff(apt_moe_handle *h, const uint16_t *x1, const uint16_t *hmlp,
+                                      const uint16_t *pre_ff_ln_2_w,
+                                      const uint16_t *post_ff_ln_1_w,
+                                      const uint16_t *post_ff_ln_2_w,
+                                      const uint16_t *post_ff_ln_w, int T, uint16_t *x2,
+                                      void *stream);
+
+/*
  * Same as apt_moe_forward with HOST buffers: copies x to the device, runs
  * the block, copies out back and synchronises the stream.  x_host [T,H],
  * out_host [T,H] bf16.

@@ -55,6 +55,20 @@ public:
                  void *stream = nullptr) {
         check(apt_moe_forward(h_, x1, expert_in, T, out, nullptr, nullptr, stream), "forward");
     }
+    // MoE half with its norms: post_ff_ln_2(experts(pre_ff_ln_2(x1), router(x1)))
+    void layerForward(const uint16_t *x1, const uint16_t *preFFLN2, const uint16_t *postFFLN2,
+                      int T, uint16_t *out, void *stream = nullptr) {
+        check(apt_moe_layer_forward(h_, x1, preFFLN2, postFFLN2, T, out, stream), "layer_forward");
+    }
+    // feed-forward tail of an MoE layer given the dense MLP output hmlp:
+    // x2 = x1 + post_ff_ln(post_ff_ln_1(hmlp) + post_ff_ln_2(MoE(x1)))
+    void decoderFF(const uint16_t *x1, const uint16_t *hmlp, const uint16_t *preFFLN2,
+                   const uint16_t *postFFLN1, const uint16_t *postFFLN2, const uint16_t *postFFLN,
+                   int T, uint16_t *x2, void *stream = nullptr) {
+        check(apt_moe_decoder_ff(h_, x1, hmlp, preFFLN2, postFFLN1, postFFLN2, postFFLN, T, x2,
+                                 stream),
+              "decoder_ff");
+    }
     // host buffers in and out (copies included)
     void forwardHost(const uint16_t *x_host, int T, uint16_t *out_host) {
         check(apt_moe_forward_host(h_, x_host, T, out_host, nullptr), "forward_host");

@@ -220,3 +220,20 @@ def num_threads() -> int:
 
 def set_num_threads(n: int) -> None:
     lib().oracle_set_num_threads(n)
+
+
+def bf16_add(a, b) -> np.ndarray:
+    """bf16 + bf16 -> bf16 (f32 add, one rounding), as mx::add on bf16 arrays."""
+    return f32_to_bf16(bf16_to_f32(a) + bf16_to_f32(b))
+
+
+def decoder_ff(x1, hmlp, pre_w, ln1_w, post_w, ff_w, proj, scale, pes, gate_up, down, top_k,
+               eps=1e-6):
+    """Feed-forward tail of an MoE decoder layer (ESDecoderLayer.mm:61-78) given
+    the dense MLP output hmlp: x2 = x1 + post_ff_ln(post_ff_ln_1(hmlp) +
+    post_ff_ln_2(MoE(x1)))."""
+    moe, idx, w = layer_moe(x1, pre_w, post_w, proj, scale, pes, gate_up, down, top_k, eps)
+    dense = rms_norm(hmlp, ln1_w, eps)
+    ff = bf16_add(dense, moe)
+    return bf16_add(x1, rms_norm(ff, ff_w, eps)), idx, w
+

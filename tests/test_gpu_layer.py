@@ -51,3 +51,33 @@ def test_layer_forward_with_norms(oracle, shape, T, sparse):
     peak = np.abs(refv).max()
     ok, ma, cos = block_close(got, refv, max_abs=2.0 ** -6 * peak)
     assert ok, (ma, cos, peak)
+
+
+@pytest.mark.parametrize("shape,T", [((2816, 128, 8, 704), 4), ((2816, 128, 8, 704), 80),
+                                     ((64, 16, 4, 64), 7)])
+def test_decoder_ff_tail(oracle, shape, T):
+    """apt_moe_decoder_ff: x2 = x1 + post_ff_ln(post_ff_ln_1(hmlp) + post_ff_ln_2(MoE(x1)))."""
+    H, E, K, I = shape
+    d = block_inputs(T, seed=3 * T + H, device=DEV, H=H, E=E, K=K, I=I, nonunit=True)
+    g = torch.Generator(device=DEV).manual_seed(6)
+    ws = [(1 + 0.2 * torch.randn(H, generator=g, device=DEV)).to(torch.bfloat16) for _ in range(4)]
+    pre, ln1, post, lnf = ws
+    hmlp = (0.5 * torch.randn(T, H, generator=g, device=DEV)).to(torch.bfloat16)
+    cfg = A.ESModelConfig(hidden_size=H, num_experts=E, top_k_experts=K, moe_intermediate_size=I,
+                          moe_sparse=True, max_tokens=T)
+    blk = A.MoEBlock(cfg, d["proj"], d["scale"], d["pes"], d["gate_up"], d["down"])
+    x2 = blk.forward_decoder_ff(d["x"], hmlp, pre, ln1, post, lnf)
+    _, tk = blk.forward(d["x"], return_routing=True)
+    torch.cuda.synchronize()
+    ref, idx_ref, _ = oracle.decoder_ff(_np(d["x"]), _np(hmlp), _np(pre), _np(ln1), _np(post),
+                                        _np(lnf), _np(d["proj"]), _np(d["scale"]), _np(d["pes"]),
+                                        _np(d["gate_up"]), _np(d["down"]), K)
+    _, _, aux = oracle.route_topk(_np(d["x"]), _np(d["proj"]), _np(d["scale"]), _np(d["pes"]), K,
+                                  return_scores=True)
+    bad, _ = router_index_check(tk.idx.cpu().numpy(), idx_ref, aux["scores"])
+    assert bad == 0
+    same = np.all(tk.idx.cpu().numpy() == idx_ref, axis=1)
+    got, refv = bf16_to_f32(_np(x2))[same], bf16_to_f32(ref)[same]
+    peak = np.abs(refv).max()
+    ok, ma, cos = block_close(got, refv, max_abs=2.0 ** -6 * peak)
+    assert ok, (ma, cos, peak)
