@@ -17,6 +17,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <string>
+#include <vector>
 
 #include "../../include/apt_moe.h"
 #include "moe_internal.h"
@@ -34,6 +35,21 @@ struct apt_moe_handle {
     // per-stage CUDA-event timing (apt_moe_set_timing / apt_moe_stage_times)
     bool timing = false;
     cudaEvent_t ev[APT_STAGE_COUNT][2] = {};
+
+    // apt_moe_forward_host replays a CUDA graph of (copy in, block, copy out)
+    // per (T, host buffers): one launch instead of a copy, ~5 kernels and a
+    // copy.  Captured on a private stream (the legacy default stream cannot
+    // be captured); any change of weights or settings drops the cache.
+    struct HostGraph {
+        int T;
+        const void *x;
+        void *out;
+        cudaGraphExec_t exec;
+        int launches;
+    };
+    std::vector<HostGraph> graphs;
+    cudaStream_t gstream = nullptr;
+    cudaEvent_t gev_in = nullptr, gev_out = nullptr;
     bool ev_used[APT_STAGE_COUNT] = {};
 
     // router
@@ -159,6 +175,11 @@ struct StageScope {
         StageScope sc_((h), (id), (s));          \
         CUDA_TRY((h), (expr));                   \
     } while (0)
+
+void drop_graphs(apt_moe_handle *h) {
+    for (auto &g : h->graphs) cudaGraphExecDestroy(g.exec);
+    h->graphs.clear();
+}
 
 void begin_call(apt_moe_handle *h) {
     h->launches = 0;
@@ -304,6 +325,10 @@ extern "C" apt_status apt_moe_destroy(apt_moe_handle *h) {
                     h->perm, h->inv, h->active, h->n_active, h->errflag, h->done, h->hsplit, h->rt_cnt, h->xp, h->yp, h->op,
                     h->Wd, h->idx2, h->w2, h->xin, h->xout, h->dq_gu, h->dq_dn, h->gu_sb, h->dn_sb, h->xn};
     for (void *p : ptrs) dfree(p);
+    drop_graphs(h);
+    if (h->gstream) cudaStreamDestroy(h->gstream);
+    if (h->gev_in) cudaEventDestroy(h->gev_in);
+    if (h->gev_out) cudaEventDestroy(h->gev_out);
     for (int i = 0; i < APT_STAGE_COUNT; ++i)
         for (int j = 0; j < 2; ++j)
             if (h->ev[i][j]) cudaEventDestroy(h->ev[i][j]);
@@ -317,18 +342,21 @@ extern "C" const char *apt_moe_last_error(const apt_moe_handle *h) {
 
 extern "C" apt_status apt_moe_set_gemv_max_tokens(apt_moe_handle *h, int t) {
     if (!h) return APT_ERR_INVALID;
+    drop_graphs(h);
     h->gemv_max_tokens = t;
     return APT_OK;
 }
 
 extern "C" apt_status apt_moe_set_gemm_pair(apt_moe_handle *h, int mode) {
     if (!h || mode < -1 || mode > 1) return APT_ERR_INVALID;
+    drop_graphs(h);
     h->gemm_pair = mode;
     return APT_OK;
 }
 
 extern "C" apt_status apt_moe_set_timing(apt_moe_handle *h, int enable) {
     if (!h) return APT_ERR_INVALID;
+    drop_graphs(h);
     h->timing = enable != 0;
     return APT_OK;
 }
@@ -392,6 +420,7 @@ extern "C" apt_status apt_moe_load_router(apt_moe_handle *h, const uint16_t *pro
                                           int on_device) {
     if (!h || !proj || !scale || !pes) return fail(h, APT_ERR_INVALID, "null router weight");
     DeviceGuard g(h->cfg.device);
+    drop_graphs(h);
     const int H = h->cfg.hidden_size, E = h->cfg.num_experts;
     if (!h->proj) {
         CUDA_TRY(h, dalloc(&h->proj, (size_t)E * H));
@@ -409,6 +438,7 @@ extern "C" apt_status apt_moe_load_experts_bf16(apt_moe_handle *h, const uint16_
                                                 const uint16_t *down, int on_device) {
     if (!h || !gate_up || !down) return fail(h, APT_ERR_INVALID, "null expert weight");
     DeviceGuard g(h->cfg.device);
+    drop_graphs(h);
     const size_t H = h->cfg.hidden_size, E = h->cfg.num_experts, I = h->cfg.moe_intermediate_size;
     if (!h->gu) {
         CUDA_TRY(h, dalloc(&h->gu, E * 2 * I * H));
@@ -451,6 +481,7 @@ extern "C" apt_status apt_moe_load_experts_quant(apt_moe_handle *h, const uint32
     if (!((bits == 4 || bits == 8) && gs == 64))
         return fail(h, APT_ERR_UNSUPPORTED, "bits=%d group=%d (need bits 4|8, group 64)", bits, gs);
     DeviceGuard g(h->cfg.device);
+    drop_graphs(h);
     const size_t H = h->cfg.hidden_size, E = h->cfg.num_experts, I = h->cfg.moe_intermediate_size;
     dfree(h->gu_q); dfree(h->dn_q); dfree(h->gu_s); dfree(h->gu_b); dfree(h->dn_s); dfree(h->dn_b);
     h->gu_q = h->dn_q = nullptr;
@@ -905,10 +936,67 @@ extern "C" apt_status apt_moe_forward_host(apt_moe_handle *h, const uint16_t *x_
     DeviceGuard g(h->cfg.device);
     cudaStream_t s = (cudaStream_t)stream;
     const size_t bytes = sizeof(uint16_t) * (size_t)T * h->cfg.hidden_size;
-    CUDA_TRY(h, cudaMemcpyAsync(h->xin, x_host, bytes, cudaMemcpyHostToDevice, s));
-    apt_status st = apt_moe_forward(h, h->xin, h->xin, T, h->xout, nullptr, nullptr, stream);
-    if (st) return st;
-    CUDA_TRY(h, cudaMemcpyAsync(out_host, h->xout, bytes, cudaMemcpyDeviceToHost, s));
-    CUDA_TRY(h, cudaStreamSynchronize(s));
+    static const bool no_graph = [] {
+        const char *v = getenv("APT_NO_GRAPH");
+        return v && atoi(v) != 0;
+    }();
+    auto direct = [&]() -> apt_status {
+        CUDA_TRY(h, cudaMemcpyAsync(h->xin, x_host, bytes, cudaMemcpyHostToDevice, s));
+        apt_status st = apt_moe_forward(h, h->xin, h->xin, T, h->xout, nullptr, nullptr, stream);
+        if (st) return st;
+        CUDA_TRY(h, cudaMemcpyAsync(out_host, h->xout, bytes, cudaMemcpyDeviceToHost, s));
+        CUDA_TRY(h, cudaStreamSynchronize(s));
+        return APT_OK;
+    };
+    if (no_graph || h->timing) return direct();
+    apt_moe_handle::HostGraph *hg = nullptr;
+    for (auto &e : h->graphs)
+        if (e.T == T && e.x == x_host && e.out == out_host) hg = &e;
+    if (!hg) {
+        if (!h->gstream) {
+            CUDA_TRY(h, cudaStreamCreateWithFlags(&h->gstream, cudaStreamNonBlocking));
+            CUDA_TRY(h, cudaEventCreateWithFlags(&h->gev_in, cudaEventDisableTiming));
+            CUDA_TRY(h, cudaEventCreateWithFlags(&h->gev_out, cudaEventDisableTiming));
+        }
+        // capture; anything the capture refuses (pageable host memory, ...)
+        // leaves the graph unset and the call runs the same kernels directly
+        cudaGraph_t graph = nullptr;
+        cudaGraphExec_t exec = nullptr;
+        apt_status st = APT_OK;
+        int launches = 0;
+        if (cudaStreamBeginCapture(h->gstream, cudaStreamCaptureModeRelaxed) == cudaSuccess) {
+            cudaError_t e1 = cudaMemcpyAsync(h->xin, x_host, bytes, cudaMemcpyHostToDevice,
+                                             h->gstream);
+            if (e1 == cudaSuccess) {
+                st = apt_moe_forward(h, h->xin, h->xin, T, h->xout, nullptr, nullptr, h->gstream);
+                launches = h->launches;
+                if (st == APT_OK)
+                    e1 = cudaMemcpyAsync(out_host, h->xout, bytes, cudaMemcpyDeviceToHost,
+                                         h->gstream);
+            }
+            const cudaError_t e2 = cudaStreamEndCapture(h->gstream, &graph);
+            if (st == APT_OK && e1 == cudaSuccess && e2 == cudaSuccess && graph &&
+                cudaGraphInstantiateWithFlags(&exec, graph, 0) != cudaSuccess)
+                exec = nullptr;
+            if (graph) cudaGraphDestroy(graph);
+        }
+        (void)cudaGetLastError();  // clear the (non-sticky) error a refused capture leaves
+        if (st != APT_OK) return st;
+        if (!exec) return direct();
+        if (h->graphs.size() >= 8) {
+            cudaGraphExecDestroy(h->graphs.front().exec);
+            h->graphs.erase(h->graphs.begin());
+        }
+        h->graphs.push_back({T, x_host, out_host, exec, launches});
+        hg = &h->graphs.back();
+    }
+    begin_call(h);
+    CUDA_TRY(h, cudaEventRecord(h->gev_in, s));
+    CUDA_TRY(h, cudaStreamWaitEvent(h->gstream, h->gev_in, 0));
+    CUDA_TRY(h, cudaGraphLaunch(hg->exec, h->gstream));
+    CUDA_TRY(h, cudaEventRecord(h->gev_out, h->gstream));
+    CUDA_TRY(h, cudaStreamWaitEvent(s, h->gev_out, 0));
+    h->launches = hg->launches;
+    CUDA_TRY(h, cudaStreamSynchronize(h->gstream));
     return APT_OK;
 }

@@ -162,108 +162,129 @@ __device__ __forceinline__ void store8(uint16_t *dst, const float (&o)[8]) {
 //   + mlp/ff_w:   out = resid + post_ff_ln( post_ff_ln_1(mlp) + post_ff_ln_2(moe) )
 constexpr int kMaxK = 256;
 
-__global__ void combine_kernel(const uint16_t *__restrict__ op, const int32_t *__restrict__ idx,
-                               const uint16_t *__restrict__ w, const int32_t *__restrict__ inv,
-                               int T, int K, int H, uint16_t *__restrict__ out, CombineTail tail) {
-    __shared__ int s_row[kMaxK];
-    __shared__ float s_w[kMaxK];
+// Persistent over tokens: CTA c handles tokens c, c + grid, ...; the next
+// token's (inv, w) are fetched into the other half of a double buffer while
+// the current token's rows stream, so each token costs one memory round trip.
+__device__ __forceinline__ void combine_meta(const int32_t *__restrict__ idx,
+                                             const uint16_t *__restrict__ w,
+                                             const int32_t *__restrict__ inv, int t, int K,
+                                             int *s_row, float *s_w) {
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        const int p = t * K + k;
+        const int e = idx[p], r = inv[p];
+        const float wk = bf2f(w[p]);
+        s_row[k] = e >= 0 ? r : -1;
+        s_w[k] = e >= 0 ? wk : 0.f;
+    }
+}
+
+__global__ void __launch_bounds__(512, 2)
+combine_kernel(const uint16_t *__restrict__ op, const int32_t *__restrict__ idx,
+               const uint16_t *__restrict__ w, const int32_t *__restrict__ inv, int T, int K,
+               int H, uint16_t *__restrict__ out, CombineTail tail) {
+    __shared__ int s_row[2][kMaxK];
+    __shared__ float s_w[2][kMaxK];
     __shared__ float2 s_red[32];
     extern __shared__ float s_buf[];  // [H] bf16 MoE output before the norm; [H] mlp row
     float *s_moe = s_buf, *s_mlp = s_buf + H;
-    const int t = blockIdx.x;
     pdl_trigger();
     pdl_wait();
-    for (int k = threadIdx.x; k < K; k += blockDim.x) {
-        const int p = t * K + k;
-        const bool live = idx[p] >= 0;
-        s_row[k] = live ? inv[p] : -1;
-        s_w[k] = live ? bf2f(w[p]) : 0.f;
-    }
-    __syncthreads();
     const bool post = tail.post_w != nullptr, full = post && tail.mlp != nullptr;
-    float ss = 0.f, ssd = 0.f;
-    for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
-        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        constexpr int B = 8;  // rows in flight per batch
-        uint4 mv;
-        if (full) mv = *reinterpret_cast<const uint4 *>(tail.mlp + (size_t)t * H + v * 8);
-        for (int k0 = 0; k0 < K; k0 += B) {
-            uint4 o[B];
+    if (blockIdx.x < T) combine_meta(idx, w, inv, blockIdx.x, K, s_row[0], s_w[0]);
+    int buf = 0;
+    for (int t = blockIdx.x; t < T; t += gridDim.x, buf ^= 1) {
+        __syncthreads();  // this token's meta is in s_row[buf]; s_row[buf^1] is free
+        if (t + (int)gridDim.x < T)
+            combine_meta(idx, w, inv, t + gridDim.x, K, s_row[buf ^ 1], s_w[buf ^ 1]);
+        const int *rows = s_row[buf];
+        const float *ws = s_w[buf];
+        float ss = 0.f, ssd = 0.f;
+        for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
+            float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            constexpr int B = 8;  // rows in flight per batch
+            uint4 mv;
+            if (full) mv = *reinterpret_cast<const uint4 *>(tail.mlp + (size_t)t * H + v * 8);
+            for (int k0 = 0; k0 < K; k0 += B) {
+                uint4 o[B];
 #pragma unroll
-            for (int j = 0; j < B; ++j) {
-                const int row = (k0 + j < K) ? s_row[k0 + j] : -1;
-                if (row >= 0) o[j] = *reinterpret_cast<const uint4 *>(op + (size_t)row * H + v * 8);
-            }
+                for (int j = 0; j < B; ++j) {
+                    const int row = (k0 + j < K) ? rows[k0 + j] : -1;
+                    if (row >= 0)
+                        o[j] = *reinterpret_cast<const uint4 *>(op + (size_t)row * H + v * 8);
+                }
 #pragma unroll
-            for (int j = 0; j < B; ++j) {
-                const int row = (k0 + j < K) ? s_row[k0 + j] : -1;
-                if (row < 0) continue;
-                const float wk = s_w[k0 + j];
-                float f[8];
-                unpack8(o[j], f);
+                for (int j = 0; j < B; ++j) {
+                    const int row = (k0 + j < K) ? rows[k0 + j] : -1;
+                    if (row < 0) continue;
+                    const float wk = ws[k0 + j];
+                    float f[8];
+                    unpack8(o[j], f);
 #pragma unroll
-                for (int q = 0; q < 8; ++q) acc[q] = __fadd_rn(acc[q], rbf(__fmul_rn(wk, f[q])));
-            }
-        }
-        if (post) {
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                const float m = rbf(acc[q]);  // the MoE output is bf16 before post_ff_ln_2
-                s_moe[v * 8 + q] = m;
-                ss = fmaf(m, m, ss);
-            }
-            if (full) {
-                float f[8];
-                unpack8(mv, f);
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    s_mlp[v * 8 + q] = f[q];
-                    ssd = fmaf(f[q], f[q], ssd);
+                    for (int q = 0; q < 8; ++q)
+                        acc[q] = __fadd_rn(acc[q], rbf(__fmul_rn(wk, f[q])));
                 }
             }
-        } else {
-            store8(out + (size_t)t * H + v * 8, acc);
-        }
-    }
-    if (!post) return;
-    const float2 sums = block_sum2(ss, ssd, s_red);
-    const float rm = rms_inv(sums.x, H, tail.eps);
-    if (!full) {  // post_ff_ln_2 only
-        for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
-            float wf[8], o[8];
-            unpack8(*reinterpret_cast<const uint4 *>(tail.post_w + v * 8), wf);
+            if (post) {
 #pragma unroll
-            for (int q = 0; q < 8; ++q) o[q] = __fmul_rn(__fmul_rn(s_moe[v * 8 + q], rm), wf[q]);
+                for (int q = 0; q < 8; ++q) {
+                    const float m = rbf(acc[q]);  // the MoE output is bf16 before post_ff_ln_2
+                    s_moe[v * 8 + q] = m;
+                    ss = fmaf(m, m, ss);
+                }
+                if (full) {
+                    float f[8];
+                    unpack8(mv, f);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        s_mlp[v * 8 + q] = f[q];
+                        ssd = fmaf(f[q], f[q], ssd);
+                    }
+                }
+            } else {
+                store8(out + (size_t)t * H + v * 8, acc);
+            }
+        }
+        if (!post) continue;
+        const float2 sums = block_sum2(ss, ssd, s_red);
+        const float rm = rms_inv(sums.x, H, tail.eps);
+        if (!full) {  // post_ff_ln_2 only
+            for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
+                float wf[8], o[8];
+                unpack8(*reinterpret_cast<const uint4 *>(tail.post_w + v * 8), wf);
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    o[q] = __fmul_rn(__fmul_rn(s_moe[v * 8 + q], rm), wf[q]);
+                store8(out + (size_t)t * H + v * 8, o);
+            }
+            continue;
+        }
+        // ff = bf16( bf16(post_ff_ln_1(mlp)) + bf16(post_ff_ln_2(moe)) ), kept in s_moe
+        const float rd = rms_inv(sums.y, H, tail.eps);
+        float ssf = 0.f;
+        for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
+            float w2[8], w1[8];
+            unpack8(*reinterpret_cast<const uint4 *>(tail.post_w + v * 8), w2);
+            unpack8(*reinterpret_cast<const uint4 *>(tail.mlp_w + v * 8), w1);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float m = rbf(__fmul_rn(__fmul_rn(s_moe[v * 8 + q], rm), w2[q]));
+                const float d = rbf(__fmul_rn(__fmul_rn(s_mlp[v * 8 + q], rd), w1[q]));
+                const float f = rbf(__fadd_rn(d, m));
+                s_moe[v * 8 + q] = f;
+                ssf = fmaf(f, f, ssf);
+            }
+        }
+        const float rf = rms_inv(block_sum2(ssf, 0.f, s_red).x, H, tail.eps);
+        // out = bf16( resid + bf16(post_ff_ln(ff)) )
+        for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
+            float wf[8], xr[8], o[8];
+            unpack8(*reinterpret_cast<const uint4 *>(tail.ff_w + v * 8), wf);
+            unpack8(*reinterpret_cast<const uint4 *>(tail.resid + (size_t)t * H + v * 8), xr);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                o[q] = __fadd_rn(xr[q], rbf(__fmul_rn(__fmul_rn(s_moe[v * 8 + q], rf), wf[q])));
             store8(out + (size_t)t * H + v * 8, o);
         }
-        return;
-    }
-    // ff = bf16( bf16(post_ff_ln_1(mlp)) + bf16(post_ff_ln_2(moe)) ), kept in s_moe
-    const float rd = rms_inv(sums.y, H, tail.eps);
-    float ssf = 0.f;
-    for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
-        float w2[8], w1[8];
-        unpack8(*reinterpret_cast<const uint4 *>(tail.post_w + v * 8), w2);
-        unpack8(*reinterpret_cast<const uint4 *>(tail.mlp_w + v * 8), w1);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const float m = rbf(__fmul_rn(__fmul_rn(s_moe[v * 8 + q], rm), w2[q]));
-            const float d = rbf(__fmul_rn(__fmul_rn(s_mlp[v * 8 + q], rd), w1[q]));
-            const float f = rbf(__fadd_rn(d, m));
-            s_moe[v * 8 + q] = f;
-            ssf = fmaf(f, f, ssf);
-        }
-    }
-    const float rf = rms_inv(block_sum2(ssf, 0.f, s_red).x, H, tail.eps);
-    // out = bf16( resid + bf16(post_ff_ln(ff)) )
-    for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
-        float wf[8], xr[8], o[8];
-        unpack8(*reinterpret_cast<const uint4 *>(tail.ff_w + v * 8), wf);
-        unpack8(*reinterpret_cast<const uint4 *>(tail.resid + (size_t)t * H + v * 8), xr);
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-            o[q] = __fadd_rn(xr[q], rbf(__fmul_rn(__fmul_rn(s_moe[v * 8 + q], rf), wf[q])));
-        store8(out + (size_t)t * H + v * 8, o);
     }
 }
 
@@ -401,8 +422,18 @@ cudaError_t launch_combine(const uint16_t *op, const int32_t *idx, const uint16_
     CombineTail tl{};
     if (tail) tl = *tail;
     const size_t smem = tl.post_w ? (size_t)H * sizeof(float) * (tl.mlp ? 2 : 1) : 0;
-    cudaError_t err = launch_ex(combine_kernel, dim3(T), dim3(threads), smem, s, true, op, idx, w,
-                                (const int32_t *)d.inv, T, K, H, out, tl);
+    // persistent: as many CTAs as are resident at once (cached per shape class)
+    static int occ_cache[64][3][17] = {};
+    const int dev = current_device();
+    const int cls = !tl.post_w ? 0 : tl.mlp ? 2 : 1;
+    int &occ = occ_cache[dev & 63][cls][threads / 32];
+    if (!occ) {
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, combine_kernel, threads, smem);
+        if (occ < 1) occ = 1;
+    }
+    const int grid = T < num_sms(dev) * occ ? T : num_sms(dev) * occ;
+    cudaError_t err = launch_ex(combine_kernel, dim3(grid > 0 ? grid : 1), dim3(threads), smem, s,
+                                true, op, idx, w, (const int32_t *)d.inv, T, K, H, out, tl);
     if (launches) ++*launches;
     return err;
 }

@@ -183,7 +183,12 @@ APT_API apt_status apt_moe_decoder_ff(apt_moe_handle *h, const uint16_t *x1, con
 /*
  * Same as apt_moe_forward with HOST buffers: copies x to the device, runs
  * the block, copies out back and synchronises the stream.  x_host [T,H],
- * out_host [T,H] bf16.
+ * out_host [T,H] bf16.  With pinned buffers the sequence is captured once per
+ * (T, x_host, out_host) as a CUDA graph and replayed on later calls, so a
+ * pinned buffer passed here must stay allocated and pinned while the handle
+ * is used with it (a freed buffer's address reused for pageable memory is
+ * not detected).  Loading weights or changing a setting drops the graphs;
+ * environment APT_NO_GRAPH=1 disables them.
  */
 APT_API apt_status apt_moe_forward_host(apt_moe_handle *h, const uint16_t *x_host, int T,
                                 uint16_t *out_host, void *stream);
