@@ -614,7 +614,7 @@ apt_status run_experts(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
                                          &h->launches));
             STAGE(h, APT_STAGE_DOWN, s,
                   launch_gemm_down(h->yp, d, ew, rows_cap, H, I, E, h->op, h->errflag, s,
-                                   &h->launches));
+                                   &h->launches, max_rows));
         }
     } else if (quant && h->gemv_tma && gemv_tma_q_supported(H, I, h->qbits)) {
         STAGE(h, APT_STAGE_GATE_UP, s,

@@ -79,15 +79,20 @@ __device__ __forceinline__ void decode_tile(int t, int NT, const int *mtp, int E
     mloc = mt - mtp[e];
 }
 
-template <int EPI, int BN, int BN2, int STAGES>
+// AROWS: rows of A staged per stage.  128 in general; 64 for decode-sized
+// groups (at most 64 rows per expert), which frees shared memory for more
+// weight stages in flight.  The M = 128 MMA then reads rows 64..127 from
+// whatever follows the stage (never stored rows: D rows are independent).
+template <int EPI, int BN, int BN2, int STAGES, int AROWS = 128>
 __global__ void __launch_bounds__(kThreads, 1)
 moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const int32_t *__restrict__ counts, const int32_t *__restrict__ offsets, int E,
                 int Kdim, int I, int H, uint16_t *__restrict__ out, int out_ld,
                 int32_t *__restrict__ err, const int32_t *__restrict__ g2e,
-                const int32_t *__restrict__ gperm, int gk) {
+                const int32_t *__restrict__ gperm, int gk, int a_rows) {
     constexpr bool GU = (EPI == EPI_GATEUP || EPI == EPI_GATEUP_G);
-    constexpr int A_BYTES = Smem<BN>::A_BYTES, B_BYTES = Smem<BN>::B_BYTES;
+    constexpr int A_BYTES = AROWS * kBK * 2, B_BYTES = Smem<BN>::B_BYTES;
+    constexpr bool STAGE_C = (EPI == EPI_DOWN && AROWS == kBM);  // TMA-store epilogue
     constexpr uint32_t IDESC = idesc_bf16_f32(kBM, BN);
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -95,7 +100,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     uint8_t *sA = smem;
     uint8_t *sB = smem + STAGES * A_BYTES;
     uint8_t *sC = sB + STAGES * B_BYTES;  // down: per-epilogue-warp store staging
-    uint64_t *full = reinterpret_cast<uint64_t *>(sC + (EPI == EPI_DOWN ? kStageC : 0));
+    uint64_t *full = reinterpret_cast<uint64_t *>(sC + (STAGE_C ? kStageC : 0));
     uint64_t *empty = full + STAGES;
     uint64_t *tfull = empty + STAGES;
     uint64_t *tempty = tfull + 2;
@@ -168,7 +173,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             // only the 4-row groups holding valid rows are fetched; the rest of
             // the A stage keeps stale data, which only feeds accumulator rows
             // that are never stored (rows of D are independent)
-            const int nact = min(32, (nvalid + 3) >> 2);
+            const int nact = min(AROWS / 4, (nvalid + 3) >> 2);
             for (int kb = 0; kb < KB; ++kb, ++g) {
                 const int s = g % STAGES;
                 const uint32_t ph = (g / STAGES) & 1;
@@ -208,8 +213,10 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                         record_error(err, 1, t);
                         goto done;
                     }
-                    mbar_arrive_expect_tx(&full[s], GU ? A_BYTES + 2 * wrows * kBK * 2
-                                                       : A_BYTES + B_BYTES);
+                    // a_rows: A box height (decode-sized groups stage fewer rows;
+                    // the rest of the stage is never stored)
+                    mbar_arrive_expect_tx(&full[s], a_rows * kBK * 2 +
+                                                        (GU ? 2 * wrows * kBK * 2 : B_BYTES));
                     tma_load_2d(sA + s * A_BYTES, &tmA, &full[s], kb * kBK, row0);
                     if (EPI == EPI_GATEUP) {
                         // g2e: row group -> expert (grouped entry point); else identity
@@ -297,7 +304,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                                             __uint_as_float(a[6]), __uint_as_float(a[7]));
                     }
                 }
-            } else if (q * 32 + 32 <= nvalid) {
+            } else if (STAGE_C && q * 32 + 32 <= nvalid) {
                 epilogue_bf16_tma<BN>(taddr, sC + q * 8192, bufsel, &tmC, nt * BN, row - lane,
                                       lane);
             } else if (q * 32 < nvalid) {
@@ -306,7 +313,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             tc_fence_before();
             mbar_arrive(&tempty[buf]);
         }
-        if (EPI == EPI_DOWN && lane == 0) bulk_wait<0>();  // stores complete before exit
+        if (STAGE_C && lane == 0) bulk_wait<0>();  // stores complete before exit
     }
 done:
     __syncthreads();
@@ -323,28 +330,30 @@ bool make_map(CUtensorMap *m, const void *base, uint64_t inner, uint64_t rows, u
     return bf16_map_2d(m, base, inner, rows, kBK, box_rows, true);
 }
 
-template <int EPI, int BN, int BN2, int STAGES>
+template <int EPI, int BN, int BN2, int STAGES, int AROWS = 128>
 constexpr size_t smem_bytes() {
-    return 1024 + (size_t)STAGES * (Smem<BN>::A_BYTES + Smem<BN>::B_BYTES) +
-           (EPI == EPI_DOWN ? kStageC : 0) + 8 * (2 * STAGES + 4) + 16 + 4 * (kMaxExperts + 1);
+    return 1024 + (size_t)STAGES * (AROWS * kBK * 2 + Smem<BN>::B_BYTES) +
+           ((EPI == EPI_DOWN && AROWS == kBM) ? kStageC : 0) + 8 * (2 * STAGES + 4) + 16 +
+           4 * (kMaxExperts + 1);
 }
 
-template <int EPI, int BN, int BN2, int STAGES>
+template <int EPI, int BN, int BN2, int STAGES, int AROWS = 128>
 cudaError_t set_attr() {
-    return cudaFuncSetAttribute(moe_gemm_kernel<EPI, BN, BN2, STAGES>,
+    static_assert(smem_bytes<EPI, BN, BN2, STAGES, AROWS>() <= 232448, "shared memory");
+    return cudaFuncSetAttribute(moe_gemm_kernel<EPI, BN, BN2, STAGES, AROWS>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)smem_bytes<EPI, BN, BN2, STAGES>());
+                                (int)smem_bytes<EPI, BN, BN2, STAGES, AROWS>());
 }
 
-template <int EPI, int BN, int BN2, int STAGES>
+template <int EPI, int BN, int BN2, int STAGES, int AROWS = 128>
 cudaError_t launch(const CUtensorMap &a, const CUtensorMap &b, const Dispatch &d, int E, int Kdim,
                    int I, int H, uint16_t *out, int out_ld, int32_t *err, cudaStream_t s,
                    const int32_t *g2e = nullptr, const CUtensorMap *c = nullptr,
-                   const int32_t *gperm = nullptr, int gk = 1) {
+                   const int32_t *gperm = nullptr, int gk = 1, int a_rows = kBM) {
     const int sms = num_sms(current_device());
-    return launch_ex(moe_gemm_kernel<EPI, BN, BN2, STAGES>, dim3(sms), dim3(kThreads),
-                     smem_bytes<EPI, BN, BN2, STAGES>(), s, true, a, b, c ? *c : a, d.counts,
-                     d.offsets, E, Kdim, I, H, out, out_ld, err, g2e, gperm, gk);
+    return launch_ex(moe_gemm_kernel<EPI, BN, BN2, STAGES, AROWS>, dim3(sms), dim3(kThreads),
+                     smem_bytes<EPI, BN, BN2, STAGES, AROWS>(), s, true, a, b, c ? *c : a, d.counts,
+                     d.offsets, E, Kdim, I, H, out, out_ld, err, g2e, gperm, gk, a_rows);
 }
 
 // gate_up tile: BN2 gate + BN2 up rows; down tile: BN rows of W_down.
@@ -359,6 +368,8 @@ cudaError_t gemm_init() {
     if ((e = set_attr<EPI_GATEUP, 256, 128, kDnStages>())) return e;
     if ((e = set_attr<EPI_GATEUP, 128, 64, kGuStages>())) return e;
     if ((e = set_attr<EPI_GATEUP_G, 176, 88, kGuStages>())) return e;
+    if ((e = set_attr<EPI_GATEUP_G, 176, 88, 7, 64>())) return e;
+    if ((e = set_attr<EPI_DOWN, 256, 0, 5, 64>())) return e;
     if ((e = set_attr<EPI_GATEUP_G, 256, 128, kDnStages>())) return e;
     if ((e = set_attr<EPI_GATEUP_G, 128, 64, kGuStages>())) return e;
     if ((e = set_attr<EPI_DOWN, 256, 0, kDnStages>())) return e;
@@ -427,8 +438,11 @@ cudaError_t launch_gemm_gateup_gather(const uint16_t *x, int T, int Kp, const Di
         return cudaErrorInvalidValue;
     const int32_t *perm = d.perm;
     cudaError_t e = (bn2 == 88)
-        ? launch<EPI_GATEUP_G, 176, 88, kGuStages>(a, b, d, E, H, I, H, yp, I, err, s, nullptr,
-                                                  &c, perm, Kp)
+        ? (T <= 64  // at most 64 rows per expert: 64-row A stages, 7 weight stages
+               ? launch<EPI_GATEUP_G, 176, 88, 7, 64>(a, b, d, E, H, I, H, yp, I, err, s,
+                                                      nullptr, &c, perm, Kp)
+               : launch<EPI_GATEUP_G, 176, 88, kGuStages>(a, b, d, E, H, I, H, yp, I, err, s,
+                                                         nullptr, &c, perm, Kp))
         : (bn2 == 128)
         ? launch<EPI_GATEUP_G, 256, 128, kDnStages>(a, b, d, E, H, I, H, yp, I, err, s, nullptr,
                                                    &c, perm, Kp)
@@ -477,16 +491,27 @@ cudaError_t launch_gemm_down_grouped(const uint16_t *yp, const Dispatch &d, cons
 
 cudaError_t launch_gemm_down(const uint16_t *yp, const Dispatch &d, const ExpertWeights &w,
                              int rows_cap, int H, int I, int E, uint16_t *op, int32_t *err,
-                             cudaStream_t s, int *launches) {
+                             cudaStream_t s, int *launches, int max_group_rows) {
     if (E > kMaxExperts) return cudaErrorInvalidValue;
+    // Decode-sized groups (a few rows per expert): A boxes only as tall as the
+    // largest group (rounded to 16); the rest of each A stage is never stored.
+    // (128-column tiles were tried for a finer spread and were slower: half
+    // the bytes in flight per stage.)
+    const bool small = max_group_rows > 0 && max_group_rows <= 64;
+    const int a_rows = small ? ((max_group_rows + 15) / 16) * 16 : kBM;
     const int bn = (H % 256 == 0) ? 256 : 128;
     CUtensorMap a, b, c;
-    if (!make_map(&a, yp, I, rows_cap, kBM) || !make_map(&b, w.dn, I, (uint64_t)E * H, bn) ||
+    if (!make_map(&a, yp, I, rows_cap, a_rows) || !make_map(&b, w.dn, I, (uint64_t)E * H, bn) ||
         !bf16_map_2d(&c, op, H, rows_cap, 64, 32, true))
         return cudaErrorInvalidValue;
     cudaError_t e = (bn == 256)
-        ? launch<EPI_DOWN, 256, 0, kDnStages>(a, b, d, E, I, I, H, op, H, err, s, nullptr, &c)
-        : launch<EPI_DOWN, 128, 0, kDnStages>(a, b, d, E, I, I, H, op, H, err, s, nullptr, &c);
+        ? (small  // 64-row A stages, 5 weight stages, plain-store epilogue
+               ? launch<EPI_DOWN, 256, 0, 5, 64>(a, b, d, E, I, I, H, op, H, err, s, nullptr, &c,
+                                                 nullptr, 1, a_rows)
+               : launch<EPI_DOWN, 256, 0, kDnStages>(a, b, d, E, I, I, H, op, H, err, s, nullptr,
+                                                     &c, nullptr, 1, a_rows))
+        : launch<EPI_DOWN, 128, 0, kDnStages>(a, b, d, E, I, I, H, op, H, err, s, nullptr, &c,
+                                              nullptr, 1, a_rows);
     if (launches) ++*launches;
     return e;
 }

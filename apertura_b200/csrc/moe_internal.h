@@ -134,9 +134,10 @@ cudaError_t launch_gemm_gateup(const uint16_t *xp, const Dispatch &d, const Expe
 cudaError_t launch_gemm_gateup_gather(const uint16_t *x, int T, int Kp, const Dispatch &d,
                                       const ExpertWeights &w, int rows_cap, int H, int I, int E,
                                       uint16_t *yp, int32_t *err, cudaStream_t s, int *launches);
+// max_group_rows: bound on rows per expert for this call (0 = unknown)
 cudaError_t launch_gemm_down(const uint16_t *yp, const Dispatch &d, const ExpertWeights &w,
                              int rows_cap, int H, int I, int E, uint16_t *op, int32_t *err,
-                             cudaStream_t s, int *launches);
+                             cudaStream_t s, int *launches, int max_group_rows = 0);
 
 // Grouped variants: G row groups (counts/offsets in d), group g uses the
 // weights of expert g2e[g]; rows are consumed in place (no gather).
