@@ -107,20 +107,51 @@ dispatch_kernel(const int32_t *__restrict__ idx, int P, int E, const int32_t *__
 }
 
 // One warp per sorted row: xp[row] = x[perm[row] / K].
-__global__ void gather_rows_kernel(const uint16_t *__restrict__ x, int H, int K,
-                                   const int32_t *__restrict__ perm,
-                                   const int32_t *__restrict__ offsets, int E, int max_rows,
-                                   uint16_t *__restrict__ xp) {
+// Warp per pair of rows, all 2 x H/256 16-byte loads of both rows in flight
+// before the stores.  Rows are produced from the last to the first, so the
+// rows gate_up reads first are the most recently written (still in L2).
+constexpr int kGatherVec = 12;  // H <= 12 * 256
+
+__global__ void __launch_bounds__(128)
+gather_rows_kernel(const uint16_t *__restrict__ x, int H, int K, const int32_t *__restrict__ perm,
+                   const int32_t *__restrict__ offsets, int E, int max_rows,
+                   uint16_t *__restrict__ xp) {
     pdl_trigger();
     pdl_wait();
-    const int rows = offsets[E];
+    const int rows = min(offsets[E], max_rows);
     const int lane = threadIdx.x & 31;
-    for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows && row < max_rows;
-         row += (gridDim.x * blockDim.x) >> 5) {
-        const int t = perm[row] / K;
-        const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)t * H);
-        uint4 *dst = reinterpret_cast<uint4 *>(xp + (size_t)row * H);
-        for (int v = lane; v < H / 8; v += 32) dst[v] = src[v];
+    const int nv = H / 256;  // full 32-lane vectors per row
+    const int warps = (gridDim.x * blockDim.x) >> 5;
+    for (int pr = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; 2 * pr < rows; pr += warps) {
+        const int r0 = rows - 1 - 2 * pr, r1 = r0 - 1;  // r1 may be -1
+        const int t0 = perm[r0] / K, t1 = r1 >= 0 ? perm[r1] / K : t0;
+        const uint4 *s0 = reinterpret_cast<const uint4 *>(x + (size_t)t0 * H) + lane;
+        const uint4 *s1 = reinterpret_cast<const uint4 *>(x + (size_t)t1 * H) + lane;
+        uint4 v0[kGatherVec], v1[kGatherVec];
+#pragma unroll
+        for (int i = 0; i < kGatherVec; ++i)
+            if (i < nv) {
+                v0[i] = s0[i * 32];
+                v1[i] = s1[i * 32];
+            }
+        uint4 *d0 = reinterpret_cast<uint4 *>(xp + (size_t)r0 * H) + lane;
+#pragma unroll
+        for (int i = 0; i < kGatherVec; ++i)
+            if (i < nv) d0[i * 32] = v0[i];
+        if (r1 >= 0) {
+            uint4 *d1 = reinterpret_cast<uint4 *>(xp + (size_t)r1 * H) + lane;
+#pragma unroll
+            for (int i = 0; i < kGatherVec; ++i)
+                if (i < nv) d1[i * 32] = v1[i];
+        }
+        // the H % 256 tail (H is a multiple of 8)
+        for (int v = nv * 32 + lane; v < H / 8; v += 32) {
+            reinterpret_cast<uint4 *>(xp + (size_t)r0 * H)[v] =
+                reinterpret_cast<const uint4 *>(x + (size_t)t0 * H)[v];
+            if (r1 >= 0)
+                reinterpret_cast<uint4 *>(xp + (size_t)r1 * H)[v] =
+                    reinterpret_cast<const uint4 *>(x + (size_t)t1 * H)[v];
+        }
     }
 }
 
@@ -407,8 +438,9 @@ cudaError_t launch_dispatch(const int32_t *idx, int P, int E, const Dispatch &d,
 cudaError_t launch_gather_rows(const uint16_t *x, int H, int K, int E, const Dispatch &d,
                                int max_rows, uint16_t *xp, cudaStream_t s, int *launches) {
     const int sms = num_sms(current_device());
-    const int blocks = min(sms * 8, (max_rows + 7) / 8);
-    cudaError_t err = launch_ex(gather_rows_kernel, dim3(blocks > 0 ? blocks : 1), dim3(256), 0, s,
+    const int pairs_per_block = 4;  // 128 threads = 4 warps, a row pair each
+    const int blocks = min(sms * 8, (max_rows + 2 * pairs_per_block - 1) / (2 * pairs_per_block));
+    cudaError_t err = launch_ex(gather_rows_kernel, dim3(blocks > 0 ? blocks : 1), dim3(128), 0, s,
                                 true, x, H, K, (const int32_t *)d.perm,
                                 (const int32_t *)d.offsets, E, max_rows, xp);
     if (launches) ++*launches;
