@@ -23,7 +23,7 @@ EXPORTED = [
     "apt_moe_experts_dense", "apt_moe_forward", "apt_moe_layer_forward", "apt_moe_decoder_ff", "apt_moe_forward_host", "apt_moe_ep_dispatch",
     "apt_moe_ep_combine", "apt_moe_experts_grouped", "apt_moe_sync",
     "apt_moe_last_counts", "apt_moe_last_launches", "apt_moe_set_gemv_max_tokens",
-    "apt_moe_set_gemm_pair",
+    "apt_moe_set_gemm_pair", "apt_moe_set_sm_limit",
     "apt_moe_set_timing", "apt_moe_stage_times", "apt_moe_route_noalloc",
 ]
 
@@ -91,6 +91,7 @@ def lib():
         "apt_moe_last_launches": ([hp], i32),
         "apt_moe_set_gemv_max_tokens": ([hp, i32], i32),
         "apt_moe_set_gemm_pair": ([hp, i32], i32),
+        "apt_moe_set_sm_limit": ([hp, i32], i32),
         "apt_moe_set_timing": ([hp, i32], i32),
         "apt_moe_stage_times": ([hp, P], i32),
         "apt_moe_route_noalloc": ([P, i32, P, P, P, i32, i32, i32, f32, P, P, P], i32),

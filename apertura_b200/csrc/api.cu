@@ -21,6 +21,7 @@
 
 #include "../../include/apt_moe.h"
 #include "moe_internal.h"
+#include "launch_util.h"
 
 using namespace apt;
 
@@ -30,6 +31,7 @@ struct apt_moe_handle {
     int launches = 0;
     int gemv_max_tokens = 8;
     int gemm_pair = -1;    // CTA-pair GEMM: -1 by size, 0 off, 1 on (apt_moe_set_gemm_pair)
+    int sm_limit = 0;      // cap on SMs for persistent grids (0: all)
     bool gemv_tma = true;  // TMA-streamed bf16 GEMV (else the register-prefetch GEMV)
 
     // per-stage CUDA-event timing (apt_moe_set_timing / apt_moe_stage_times)
@@ -183,6 +185,7 @@ void drop_graphs(apt_moe_handle *h) {
 
 void begin_call(apt_moe_handle *h) {
     h->launches = 0;
+    sm_cap() = h->sm_limit;
     for (int i = 0; i < APT_STAGE_COUNT; ++i) h->ev_used[i] = false;
 }
 
@@ -344,6 +347,13 @@ extern "C" apt_status apt_moe_set_gemv_max_tokens(apt_moe_handle *h, int t) {
     if (!h) return APT_ERR_INVALID;
     drop_graphs(h);
     h->gemv_max_tokens = t;
+    return APT_OK;
+}
+
+extern "C" apt_status apt_moe_set_sm_limit(apt_moe_handle *h, int n) {
+    if (!h || n < 0) return APT_ERR_INVALID;
+    drop_graphs(h);
+    h->sm_limit = n;
     return APT_OK;
 }
 

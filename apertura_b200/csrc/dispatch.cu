@@ -463,7 +463,7 @@ cudaError_t launch_combine(const uint16_t *op, const int32_t *idx, const uint16_
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, combine_kernel, threads, smem);
         if (occ < 1) occ = 1;
     }
-    const int grid = T < num_sms(dev) * occ ? T : num_sms(dev) * occ;
+    const int grid = T < grid_sms(dev) * occ ? T : grid_sms(dev) * occ;
     cudaError_t err = launch_ex(combine_kernel, dim3(grid > 0 ? grid : 1), dim3(threads), smem, s,
                                 true, op, idx, w, (const int32_t *)d.inv, T, K, H, out, tl);
     if (launches) ++*launches;

@@ -350,7 +350,7 @@ cudaError_t launch(const CUtensorMap &a, const CUtensorMap &b, const Dispatch &d
                    int I, int H, uint16_t *out, int out_ld, int32_t *err, cudaStream_t s,
                    const int32_t *g2e = nullptr, const CUtensorMap *c = nullptr,
                    const int32_t *gperm = nullptr, int gk = 1, int a_rows = kBM) {
-    const int sms = num_sms(current_device());
+    const int sms = grid_sms(current_device());
     return launch_ex(moe_gemm_kernel<EPI, BN, BN2, STAGES, AROWS>, dim3(sms), dim3(kThreads),
                      smem_bytes<EPI, BN, BN2, STAGES, AROWS>(), s, true, a, b, c ? *c : a, d.counts,
                      d.offsets, E, Kdim, I, H, out, out_ld, err, g2e, gperm, gk, a_rows);

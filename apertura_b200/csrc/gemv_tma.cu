@@ -316,7 +316,7 @@ cudaError_t launch_one(const CUtensorMap &m, const Args &a, int max_items, int l
                                                       kThreads, smem);
         if (occ < 1) occ = 1;
     }
-    int grid = num_sms(dev) * occ;
+    int grid = grid_sms(dev) * occ;
     if (max_items < grid) grid = max_items;
     if (grid < 1) grid = 1;
     return launch_ex(gemv_tma_kernel<EPI, NTMAX, kStages>, dim3(grid), dim3(kThreads), smem, s,

@@ -30,6 +30,20 @@ inline int num_sms(int dev) {
     return cache[dev];
 }
 
+// SMs the persistent kernels of the current call may fill: all of them, or a
+// per-handle cap (apt_moe_set_sm_limit) that leaves room for kernels running
+// beside them, e.g. NCCL's during an expert-parallel exchange.  Set by the
+// entry point at the start of each call on the calling thread.
+inline int &sm_cap() {
+    static thread_local int cap = 0;
+    return cap;
+}
+
+inline int grid_sms(int dev) {
+    const int n = num_sms(dev), c = sm_cap();
+    return (c > 0 && c < n) ? c : n;
+}
+
 // ---------------------------------------------------------------- tensor maps
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,

@@ -125,6 +125,10 @@ class Handle:
     def set_gemv_max_tokens(self, t: int):
         self.check(lib().apt_moe_set_gemv_max_tokens(self.h, int(t)))
 
+    def set_sm_limit(self, n: int):
+        """Cap on the SMs the persistent kernels of this handle fill (0 = all)."""
+        self.check(lib().apt_moe_set_sm_limit(self.h, int(n)))
+
     def set_gemm_pair(self, mode: int):
         """Tensor-core tile form: 1 CTA pairs, 0 single CTAs, -1 by size."""
         self.check(lib().apt_moe_set_gemm_pair(self.h, int(mode)))

@@ -380,14 +380,14 @@ def run_ep(args, dev, world, rank, T=4096, steps=5, warmup=3):
     import torch.distributed as dist
     import apertura_b200 as A
     from apertura_b200.ep import ExpertParallelMoE
-    from apertura_b200.synthetic import block_inputs, expert_bank, zipf_targets
+    from apertura_b200.synthetic import block_inputs, expert_bank
     d = block_inputs(T * world, seed=5, device=dev, routing="zipf", with_experts=False,
                      calib_tokens=4096)
     x = d["x"][rank * T:(rank + 1) * T].contiguous()
     gu, dn = expert_bank(E, H, I, 0, dev)
     cfg = A.ESModelConfig(moe_sparse=True, max_tokens=T, device=dev.index)
     ep = ExpertParallelMoE(cfg, d["proj"], d["scale"], d["pes"], gu, dn,
-                           loads=zipf_targets(E, K).tolist(), max_tokens_per_rank=T)
+                           loads=d["zipf"]["target"].tolist(), max_tokens_per_rank=T)
     del gu, dn
     torch.cuda.empty_cache()
     for _ in range(warmup):
@@ -403,18 +403,32 @@ def run_ep(args, dev, world, rank, T=4096, steps=5, warmup=3):
         b.record(stream)
         torch.cuda.synchronize()
         ms += a.elapsed_time(b) / steps
+    # one more step with per-phase events (not part of the timed steps)
+    ep.timing = True
+    ep(x)
+    ep.timing = False
+    names = list(ep.last_phase_ms)
+    ph = torch.tensor([ep.last_phase_ms[n] for n in names], device=dev)
+    dist.all_reduce(ph, op=dist.ReduceOp.MAX)
+    phases = {n: float(v) for n, v in zip(names, ph.tolist())}
+    hph = torch.tensor([ep.last_host_ms[n] for n in names], device=dev)
+    dist.all_reduce(hph, op=dist.ReduceOp.MAX)
+    host_phases = {n: float(v) for n, v in zip(names, hph.tolist())}
     t = torch.tensor([ms, float(ep.last_recv_rows)], device=dev)
     mx = t.clone()
     dist.all_reduce(mx, op=dist.ReduceOp.MAX)
     loads = [torch.zeros_like(t) for _ in range(world)]
     dist.all_gather(loads, t)
     recv = [int(l[1].item()) for l in loads]
-    return {"config": f"expert parallel, 128/{world} experts per GPU, {T} tokens per GPU, "
-                      f"Zipf s=1.1, LPT placement, NCCL all-to-all",
+    return {"config": f"expert parallel: {ep.n_hot} hottest experts replicated, {ep.n_cold}/{world} "
+                      f"sharded per GPU, {T} tokens per GPU, Zipf s=1.1, LPT placement, "
+                      f"NCCL all-to-all",
             "ms_per_step": float(mx[0].item()),
             "tokens_per_s": world * T / (float(mx[0].item()) / 1e3),
             "recv_rows_per_rank": recv,
-            "load_max_over_mean": max(recv) / (sum(recv) / len(recv))}
+            "load_max_over_mean": max(recv) / (sum(recv) / len(recv)),
+            "phases_ms_max_over_ranks": phases,
+            "host_enqueue_ms_max_over_ranks": host_phases}
 
 
 def run_quant(dev, peaks, flush, bits=4, Ts=(1, 4096), steps=5):

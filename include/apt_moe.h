@@ -255,6 +255,13 @@ APT_API apt_status apt_moe_set_gemv_max_tokens(apt_moe_handle *h, int t);
 APT_API apt_status apt_moe_set_gemm_pair(apt_moe_handle *h, int mode);
 
 /*
+ * Cap on the SMs this handle's persistent kernels fill (0 = all, the
+ * default).  Leaves room for kernels that must run beside them, e.g. NCCL's
+ * all-to-all while the replicated experts of an expert-parallel step run.
+ */
+APT_API apt_status apt_moe_set_sm_limit(apt_moe_handle *h, int n);
+
+/*
  * Per-stage timing for measurement: when enabled, every compute call records
  * a CUDA event pair on its stream around each stage's kernel;
  * apt_moe_stage_times fills ms[APT_STAGE_COUNT] with the last call's

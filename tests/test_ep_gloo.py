@@ -14,7 +14,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from apertura_b200.ep import lpt_placement
+from apertura_b200.ep import hot_cold_placement, lpt_placement
 
 H, E, K, I = 64, 16, 4, 64
 
@@ -40,11 +40,24 @@ def test_lpt_rejects_uneven():
         lpt_placement([1.0] * 10, 4)
 
 
+def test_hot_cold_placement():
+    loads = [1.0 / (e + 1) for e in range(16)]
+    perm = hot_cold_placement(loads, 2, 4)
+    assert sorted(perm) == list(range(16))
+    assert sorted(perm[:4]) == [0, 1, 2, 3]  # the 4 heaviest are replicated
+    assert len(hot_cold_placement(loads, 3, 4)) == 16  # 12 cold over 3 ranks
+    with pytest.raises(ValueError):
+        hot_cold_placement(loads, 3, 3)       # 13 cold experts do not split over 3
+    with pytest.raises(ValueError):
+        hot_cold_placement(loads, 2, 5)       # 11 cold experts do not split over 2
+
+
 class OracleBackend:
     """CPU stand-in for CudaBackend, built on the oracle."""
 
-    def __init__(self, cfg, proj, scale, pes, gu_loc, dn_loc, max_recv):
+    def __init__(self, cfg, proj, scale, pes, gu_loc, dn_loc, max_recv, n_hot=0):
         from oracle import oracle as O
+        self.hot_base = gu_loc.shape[0] - n_hot  # hot bank follows the cold one
         self.O = O
         b = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)
         self.proj, self.scale, self.pes = b(proj), b(scale), b(pes)
@@ -63,15 +76,21 @@ class OracleBackend:
         t = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16)
         return (torch.from_numpy(idx), t(w), t(rows), torch.from_numpy(counts))
 
-    def experts(self, rows, group_counts, group_expert):
-        R = rows.shape[0]
+    def experts(self, rows, group_counts, group_expert, out=None, hot=False):
+        R = int(group_counts.sum())  # rows past the groups are left untouched
         if R == 0:
-            return rows.clone()
+            return rows.clone() if out is None else out
+        rows = rows[:R]
         rb = rows.contiguous().view(torch.int16).numpy().view(np.uint16)
-        ids = np.repeat(group_expert.numpy(), group_counts.numpy()).astype(np.int32).reshape(R, 1)
+        ge = group_expert.numpy() + (self.hot_base if hot else 0)
+        ids = np.repeat(ge, group_counts.numpy()).astype(np.int32).reshape(R, 1)
         ones = self.O.f32_to_bf16(np.ones((R, 1), np.float32))
-        out = self.O.experts_sparse(rb, self.gu, self.dn, ids, ones)
-        return torch.from_numpy(out.view(np.int16)).view(torch.bfloat16)
+        res = torch.from_numpy(self.O.experts_sparse(rb, self.gu, self.dn, ids, ones).view(np.int16))
+        res = res.view(torch.bfloat16)
+        if out is None:
+            return res
+        out[:R].copy_(res)
+        return out
 
     def combine(self, back, idx, w):
         O = self.O
@@ -86,7 +105,7 @@ class OracleBackend:
         return torch.from_numpy(O.f32_to_bf16(acc).view(np.int16)).view(torch.bfloat16)
 
 
-def _worker(rank, world, port, result_q):
+def _worker(rank, world, port, result_q, n_hot):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -107,7 +126,8 @@ def _worker(rank, world, port, result_q):
         cfg = ESModelConfig(hidden_size=H, num_experts=E, top_k_experts=K, moe_intermediate_size=I,
                             moe_sparse=True, max_tokens=64, device=0)
         ep = ExpertParallelMoE(cfg, proj, scale, pes, gu, dn, loads=loads, max_tokens_per_rank=64,
-                               backend=OracleBackend)
+                               backend=OracleBackend, replicate_hot=n_hot)
+        assert ep.n_hot == n_hot
         out = ep(x)
         b = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)
         idx, w = O.route_topk(b(x), b(proj), b(scale), b(pes), K)
@@ -119,13 +139,16 @@ def _worker(rank, world, port, result_q):
         dist.destroy_process_group()
 
 
-def test_ep_exchange_matches_single_device():
+@pytest.mark.parametrize("n_hot", [0, 4])
+def test_ep_exchange_matches_single_device(n_hot):
+    """Pure sharding, and 4 of 16 experts replicated on both ranks (their rows
+    computed at home, the rest exchanged)."""
     from oracle import oracle as O
     O.build()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29500 + os.getpid() % 1000
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    port = 29500 + (os.getpid() + 7 * n_hot) % 1000
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, n_hot)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:

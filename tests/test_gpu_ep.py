@@ -16,7 +16,7 @@ import os, sys, numpy as np, torch, torch.distributed as dist
 sys.path.insert(0, os.environ["APT_ROOT"])
 import apertura_b200 as A
 from apertura_b200.ep import ExpertParallelMoE
-from apertura_b200.synthetic import block_inputs, expert_bank, zipf_targets
+from apertura_b200.synthetic import block_inputs, expert_bank
 rank = int(os.environ["RANK"]); world = int(os.environ["WORLD_SIZE"])
 torch.cuda.set_device(rank); dev = torch.device("cuda", rank)
 dist.init_process_group("nccl", device_id=dev)
@@ -26,7 +26,7 @@ r0 = block_inputs(T * world, seed=1000, device=dev, routing="zipf", with_experts
 d = dict(x=r0["x"][rank * T:(rank + 1) * T].contiguous())
 gu, dn = expert_bank(128, 2816, 704, 7, dev)
 cfg = A.ESModelConfig(moe_sparse=True, max_tokens=T, device=rank)
-loads = zipf_targets(128, 8).tolist()
+loads = r0["zipf"]["target"].tolist()  # the expected loads of this routing
 ep = ExpertParallelMoE(cfg, r0["proj"], r0["scale"], r0["pes"], gu, dn, loads=loads,
                        max_tokens_per_rank=T)
 out = ep(d["x"])
@@ -35,7 +35,7 @@ ref = ref_blk.forward(d["x"])
 torch.cuda.synchronize()
 ma = float((out.float() - ref.float()).abs().max()); peak = float(ref.float().abs().max())
 cos = float(torch.nn.functional.cosine_similarity(out.float().flatten(), ref.float().flatten(), 0))
-print(f"\nRESULT rank={rank} max_abs={ma:.3e} peak={peak:.3e} cos={cos:.6f} recv={ep.last_recv_rows}")
+print(f"\nRESULT rank={rank} max_abs={ma:.3e} peak={peak:.3e} cos={cos:.6f} recv={ep.last_recv_rows} hot={ep.last_hot_rows}")
 ok = ma <= 2e-2 and cos >= 0.9999
 dist.destroy_process_group()
 sys.exit(0 if ok else 3)
