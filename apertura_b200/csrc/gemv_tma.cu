@@ -17,7 +17,9 @@
 //   down:    64 hidden rows, K chunks of 64; a warp owns 16 rows as 4
 //            row-groups of 8 lanes, each lane 4 rows.
 // The expert's tokens are staged as bf16 in shared memory, up to NTMAX per
-// pass (the compile-time bound picked from the call's T).  All mbarrier waits
+// pass (the compile-time bound picked from the call's T), by 1-D bulk copies
+// the producer issues ahead of the compute warps into a double buffer, so
+// consecutive items of a CTA follow without a memory round trip between them.  All mbarrier waits
 // are bounded; on expiry the kernel records an error code and returns.
 #include <cuda.h>
 
@@ -198,9 +200,13 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, Args a) {
     uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~uintptr_t(1023));
     const int LEN = (EPI == GATEUP) ? a.H : a.I;
-    uint16_t *xs = reinterpret_cast<uint16_t *>(ring + STAGES * S::STAGE_BYTES);
-    uint64_t *full = reinterpret_cast<uint64_t *>(xs + NTMAX * LEN);
+    // token rows per unit (item x token pass), double-buffered, fetched by the
+    // producer with 1-D bulk copies ahead of the compute warps
+    uint16_t *xs0 = reinterpret_cast<uint16_t *>(ring + STAGES * S::STAGE_BYTES);
+    uint64_t *full = reinterpret_cast<uint64_t *>(xs0 + 2 * NTMAX * LEN);
     uint64_t *empty = full + STAGES;
+    uint64_t *ufull = empty + STAGES;
+    uint64_t *uempty = ufull + 2;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rows_per_blk = (EPI == GATEUP) ? S::ROWS / 2 : S::ROWS;  // j or h per item
     const int NRB = ((EPI == GATEUP) ? a.I : a.H) / rows_per_blk;
@@ -208,6 +214,10 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, Args a) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kComputeWarps);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&ufull[b], 1);
+            mbar_init(&uempty[b], kComputeWarps);
         }
         fence_barrier_init();
         tma_prefetch(&tmW);
@@ -217,50 +227,70 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, Args a) {
     const int items = *a.n_active * NRB;
     __syncthreads();
     const int NK = LEN / S::KC;
-    int g = 0;
+    int g = 0, u = 0;
     if (warp == kComputeWarps) {
         if (lane != 0) return;
+        // one weight stage of unit (e, blk0) into the ring
+        auto stage = [&](int e, int blk0, int kc, int item) -> bool {
+            const int s = g % STAGES;
+            if (!mbar_wait(&empty[s], ((g / STAGES) & 1) ^ 1, kWaitLimit)) {
+                record_error(a.err, 10, item);
+                return false;
+            }
+            mbar_arrive_expect_tx(&full[s], S::STAGE_BYTES);
+            uint8_t *dst = ring + s * S::STAGE_BYTES;
+            if (EPI == GATEUP) {
+                const int r0 = e * 2 * a.I + blk0;
+                tma_load_2d(dst, &tmW, &full[s], kc * S::KC, r0);
+                tma_load_2d(dst + S::STAGE_BYTES / 2, &tmW, &full[s], kc * S::KC, r0 + a.I);
+            } else {
+                tma_load_2d(dst, &tmW, &full[s], kc * S::KC, e * a.H + blk0);
+            }
+            ++g;
+            return true;
+        };
         for (int item = blockIdx.x; item < items; item += gridDim.x) {
             const int e = a.active[item / NRB], blk0 = (item % NRB) * rows_per_blk;
-            const int n = a.counts[e];
-            for (int tc = 0; tc < n; tc += NTMAX) {
-                for (int kc = 0; kc < NK; ++kc, ++g) {
-                    const int s = g % STAGES;
-                    if (!mbar_wait(&empty[s], ((g / STAGES) & 1) ^ 1, kWaitLimit)) {
-                        record_error(a.err, 10, item);
-                        return;
-                    }
-                    mbar_arrive_expect_tx(&full[s], S::STAGE_BYTES);
-                    uint8_t *dst = ring + s * S::STAGE_BYTES;
-                    if (EPI == GATEUP) {
-                        const int r0 = e * 2 * a.I + blk0;
-                        tma_load_2d(dst, &tmW, &full[s], kc * S::KC, r0);
-                        tma_load_2d(dst + S::STAGE_BYTES / 2, &tmW, &full[s], kc * S::KC, r0 + a.I);
-                    } else {
-                        tma_load_2d(dst, &tmW, &full[s], kc * S::KC, e * a.H + blk0);
-                    }
+            const int n = a.counts[e], base = a.offsets[e];
+            for (int tc = 0; tc < n; tc += NTMAX, ++u) {
+                // the weight stream first (it needs only e); the unit's operands
+                // need the dispatch order, one more dependent load
+                const int lead = NK < STAGES ? NK : STAGES;
+                for (int kc = 0; kc < lead; ++kc)
+                    if (!stage(e, blk0, kc, item)) return;
+                const int b = u & 1;
+                if (!mbar_wait(&uempty[b], ((u >> 1) & 1) ^ 1, kWaitLimit)) {
+                    record_error(a.err, 13, item);
+                    return;
                 }
+                const int nt = min(NTMAX, n - tc);
+                uint16_t *xs = xs0 + b * NTMAX * LEN;
+                mbar_arrive_expect_tx(&ufull[b], nt * LEN * 2);
+                if (EPI == GATEUP) {
+                    for (int r = 0; r < nt; ++r)
+                        bulk_load(xs + r * LEN, a.in + (size_t)(a.perm[base + tc + r] / a.K) * a.H,
+                                  LEN * 2, &ufull[b]);
+                } else {
+                    bulk_load(xs, a.in + (size_t)(base + tc) * a.I, nt * LEN * 2, &ufull[b]);
+                }
+                for (int kc = lead; kc < NK; ++kc)
+                    if (!stage(e, blk0, kc, item)) return;
             }
         }
         return;
     }
-    // compute warps (128 threads): named barrier 1 among themselves
+    // compute warps (128 threads)
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
         const int e = a.active[item / NRB], blk0 = (item % NRB) * rows_per_blk;
         const int n = a.counts[e], base = a.offsets[e];
-        for (int tc = 0; tc < n; tc += NTMAX, g += NK) {
+        for (int tc = 0; tc < n; tc += NTMAX, g += NK, ++u) {
             const int nt = min(NTMAX, n - tc);
-            const int vecs = LEN / 8;
-            asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32));  // previous pass done with xs
-            for (int v = threadIdx.x; v < nt * vecs; v += kComputeWarps * 32) {
-                const int r = v / vecs, k = (v - r * vecs) * 8;
-                const uint16_t *src = (EPI == GATEUP)
-                    ? a.in + (size_t)(a.perm[base + tc + r] / a.K) * a.H
-                    : a.in + (size_t)(base + tc + r) * a.I;
-                *reinterpret_cast<uint4 *>(xs + r * LEN + k) =
-                    *reinterpret_cast<const uint4 *>(src + k);
+            const int b = u & 1;
+            if (!mbar_wait(&ufull[b], (u >> 1) & 1, kWaitLimit)) {
+                record_error(a.err, 14, item);
+                return;
             }
-            asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32));
+            const uint16_t *xs = xs0 + b * NTMAX * LEN;
             bool ok = true;
             if (EPI == GATEUP) {
                 if (nt == 1) ok = gateup_pass<1, STAGES>(ring, full, empty, xs, a, g, warp, lane, blk0, nt, base + tc);
@@ -276,6 +306,8 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, Args a) {
             // A timed-out wait leaves the ring inconsistent: every compute warp
             // waits on the same barriers, so all of them expire; leave at once.
             if (!ok) return;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&uempty[b]);  // this warp is done with the unit's rows
         }
     }
 }
@@ -291,8 +323,8 @@ constexpr int kStages = 4;
 
 template <int EPI, int NTMAX>
 size_t smem_bytes(int len) {
-    return 1024 + (size_t)kStages * Shape<EPI>::STAGE_BYTES + (size_t)NTMAX * len * 2 +
-           16 * kStages + 64;
+    return 1024 + (size_t)kStages * Shape<EPI>::STAGE_BYTES + 2 * (size_t)NTMAX * len * 2 +
+           16 * kStages + 32 + 64;
 }
 
 template <int EPI, int NTMAX>

@@ -12,8 +12,12 @@
 // Same structure as the bf16 TMA GEMV: persistent CTAs over (active expert,
 // row block) items; a producer warp streams the packed rows into a deep
 // shared-memory ring (4-bit rows are a quarter of the bf16 bytes, so the ring
-// has more, smaller stages); the item's scales and biases and its tokens are
-// staged by the compute warps.  Waits are bounded; expiry records an error.
+// has more, smaller stages).  The producer also fetches each unit's operands
+// ahead of the compute warps, into one of two buffers: the item's (scale,
+// bias) pairs by a 2-D TMA copy, its token rows by 1-D bulk copies.  The
+// compute warps never wait on a global load of their own, so a CTA's items
+// follow one another without a memory round trip in between.  Waits are
+// bounded; expiry records an error.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -70,19 +74,20 @@ __device__ __forceinline__ float pick(const float (&acc)[R][NT], int r, int t) {
 struct QArgs {
     const uint16_t *in;
     const int32_t *perm, *offsets, *counts, *active, *n_active;
-    const uint32_t *sb;  // [E*rows, len/64] (scale | bias << 16) pairs
+    const uint32_t *sb;  // [E*rows, gp] (scale | bias << 16) pairs, rows padded to gp
     uint16_t *out;
     int32_t *err;
     int K, H, I;
+    int gp;              // groups per row, rounded up to 4 (16-byte rows)
 };
 
 template <int NT, int BITS>
 __device__ __forceinline__ bool gateup_pass_q(const uint8_t *ring, uint64_t *full,
                                               uint64_t *empty, const uint16_t *xs,
-                                              const float *ss, const float *sb, const QArgs &a,
-                                              int g, int w, int lane, int j0, int nt, int row0) {
+                                              const uint32_t *sbp, const QArgs &a, int g, int w,
+                                              int lane, int j0, int nt, int row0) {
     using S = QShape<GATEUP, BITS>;
-    const int NK = a.H / S::KC, G = a.H / 64;
+    const int NK = a.H / S::KC, G = a.gp;
     float acc[8][NT];
 #pragma unroll
     for (int r = 0; r < 8; ++r)
@@ -105,8 +110,9 @@ __device__ __forceinline__ bool gateup_pass_q(const uint8_t *ring, uint64_t *ful
             for (int k = 0; k < S::LANE_WORDS; ++k)
                 wd[k] = st[row * S::ROW_WORDS + lane * S::LANE_WORDS + k];
             unpack_q8<BITS>(wd, qf[q]);
-            sr[q] = ss[row * G + grp];
-            br[q] = sb[row * G + grp];
+            const uint32_t pv = sbp[row * G + grp];
+            sr[q] = bf_lo(pv);
+            br[q] = bf_hi(pv);
         }
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
@@ -146,11 +152,11 @@ __device__ __forceinline__ bool gateup_pass_q(const uint8_t *ring, uint64_t *ful
 
 template <int NT, int BITS>
 __device__ __forceinline__ bool down_pass_q(const uint8_t *ring, uint64_t *full, uint64_t *empty,
-                                            const uint16_t *xs, const float *ss, const float *sb,
+                                            const uint16_t *xs, const uint32_t *sbp,
                                             const QArgs &a, int g, int w, int lane, int h0, int nt,
                                             int row0) {
     using S = QShape<DOWN, BITS>;
-    const int NK = a.I / S::KC, G = a.I / 64;
+    const int NK = a.I / S::KC, G = a.gp;
     const int gq = lane >> 3, c = lane & 7;
     const int rbase = 16 * w + 4 * gq;
     float acc[4][NT];
@@ -173,8 +179,9 @@ __device__ __forceinline__ bool down_pass_q(const uint8_t *ring, uint64_t *full,
             for (int k = 0; k < S::LANE_WORDS; ++k)
                 wd[k] = st[(rbase + r) * S::ROW_WORDS + c * S::LANE_WORDS + k];
             unpack_q8<BITS>(wd, qf[r]);
-            sr[r] = ss[(rbase + r) * G + kc];
-            br[r] = sb[(rbase + r) * G + kc];
+            const uint32_t pv = sbp[(rbase + r) * G + kc];
+            sr[r] = bf_lo(pv);
+            br[r] = bf_hi(pv);
         }
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
@@ -216,19 +223,22 @@ __device__ __forceinline__ bool down_pass_q(const uint8_t *ring, uint64_t *full,
 
 template <int EPI, int BITS, int NTMAX>
 __global__ void __launch_bounds__(kThreads)
-gemv_tma_q_kernel(const __grid_constant__ CUtensorMap tmQ, QArgs a) {
+gemv_tma_q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmSB,
+                  QArgs a) {
     using S = QShape<EPI, BITS>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~uintptr_t(1023));
     const int LEN = (EPI == GATEUP) ? a.H : a.I;
-    const int G = LEN / 64;
-    uint16_t *xs = reinterpret_cast<uint16_t *>(ring + S::STAGES * S::STAGE_BYTES);
-    float *ss = reinterpret_cast<float *>(xs + NTMAX * LEN);
-    float *sb = ss + S::ROWS * G;
-    uint64_t *full = reinterpret_cast<uint64_t *>(
-        (reinterpret_cast<uintptr_t>(sb + S::ROWS * G) + 7) & ~uintptr_t(7));
+    const int Gp = a.gp;
+    // per unit (item x token pass), double-buffered: token rows, (scale, bias)
+    uint16_t *xs0 = reinterpret_cast<uint16_t *>(ring + S::STAGES * S::STAGE_BYTES);
+    uint32_t *sb0 = reinterpret_cast<uint32_t *>(
+        (reinterpret_cast<uintptr_t>(xs0 + 2 * NTMAX * LEN) + 127) & ~uintptr_t(127));
+    uint64_t *full = reinterpret_cast<uint64_t *>(sb0 + 2 * S::ROWS * Gp);
     uint64_t *empty = full + S::STAGES;
+    uint64_t *ufull = empty + S::STAGES;
+    uint64_t *uempty = ufull + 2;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rows_per_blk = (EPI == GATEUP) ? S::ROWS / 2 : S::ROWS;
     const int NRB = ((EPI == GATEUP) ? a.I : a.H) / rows_per_blk;
@@ -237,101 +247,106 @@ gemv_tma_q_kernel(const __grid_constant__ CUtensorMap tmQ, QArgs a) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kComputeWarps);
         }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&ufull[b], 1);
+            mbar_init(&uempty[b], kComputeWarps);
+        }
         fence_barrier_init();
         tma_prefetch(&tmQ);
+        tma_prefetch(&tmSB);
     }
     pdl_trigger();
     pdl_wait();
     const int items = *a.n_active * NRB;
     __syncthreads();
     const int NK = LEN / S::KC;
-    int g = 0;
     if (warp == kComputeWarps) {
         if (lane != 0) return;
+        int g = 0, u = 0;
+        // one weight stage of unit (e, blk0) into the ring
+        auto stage = [&](int e, int blk0, int kc, int item) -> bool {
+            const int s = g % S::STAGES;
+            if (!mbar_wait(&empty[s], ((g / S::STAGES) & 1) ^ 1, kWaitLimit)) {
+                record_error(a.err, 20, item);
+                return false;
+            }
+            mbar_arrive_expect_tx(&full[s], S::STAGE_BYTES);
+            uint8_t *dst = ring + s * S::STAGE_BYTES;
+            if (EPI == GATEUP) {
+                const int r0 = e * 2 * a.I + blk0;
+                tma_load_2d(dst, &tmQ, &full[s], kc * S::ROW_WORDS, r0);
+                tma_load_2d(dst + S::STAGE_BYTES / 2, &tmQ, &full[s], kc * S::ROW_WORDS, r0 + a.I);
+            } else {
+                tma_load_2d(dst, &tmQ, &full[s], kc * S::ROW_WORDS, e * a.H + blk0);
+            }
+            ++g;
+            return true;
+        };
         for (int item = blockIdx.x; item < items; item += gridDim.x) {
             const int e = a.active[item / NRB], blk0 = (item % NRB) * rows_per_blk;
-            const int n = a.counts[e];
-            for (int tc = 0; tc < n; tc += NTMAX) {
-                for (int kc = 0; kc < NK; ++kc, ++g) {
-                    const int s = g % S::STAGES;
-                    if (!mbar_wait(&empty[s], ((g / S::STAGES) & 1) ^ 1, kWaitLimit)) {
-                        record_error(a.err, 20, item);
-                        return;
-                    }
-                    mbar_arrive_expect_tx(&full[s], S::STAGE_BYTES);
-                    uint8_t *dst = ring + s * S::STAGE_BYTES;
-                    if (EPI == GATEUP) {
-                        const int r0 = e * 2 * a.I + blk0;
-                        tma_load_2d(dst, &tmQ, &full[s], kc * S::ROW_WORDS, r0);
-                        tma_load_2d(dst + S::STAGE_BYTES / 2, &tmQ, &full[s], kc * S::ROW_WORDS,
-                                    r0 + a.I);
-                    } else {
-                        tma_load_2d(dst, &tmQ, &full[s], kc * S::ROW_WORDS, e * a.H + blk0);
-                    }
+            const int n = a.counts[e], base = a.offsets[e];
+            for (int tc = 0; tc < n; tc += NTMAX, ++u) {
+                // the weight stream first (it needs only e); the unit's operands
+                // need the dispatch order, one more dependent load
+                const int lead = NK < S::STAGES ? NK : S::STAGES;
+                for (int kc = 0; kc < lead; ++kc)
+                    if (!stage(e, blk0, kc, item)) return;
+                const int b = u & 1;
+                if (!mbar_wait(&uempty[b], ((u >> 1) & 1) ^ 1, kWaitLimit)) {
+                    record_error(a.err, 23, item);
+                    return;
                 }
+                const int nt = min(NTMAX, n - tc);
+                uint16_t *xs = xs0 + b * NTMAX * LEN;
+                uint32_t *sbp = sb0 + b * S::ROWS * Gp;
+                mbar_arrive_expect_tx(&ufull[b], S::ROWS * Gp * 4 + nt * LEN * 2);
+                if (EPI == GATEUP) {
+                    const int r0 = e * 2 * a.I + blk0;
+                    tma_load_2d(sbp, &tmSB, &ufull[b], 0, r0);
+                    tma_load_2d(sbp + (S::ROWS / 2) * Gp, &tmSB, &ufull[b], 0, r0 + a.I);
+                    for (int r = 0; r < nt; ++r)
+                        bulk_load(xs + r * LEN, a.in + (size_t)(a.perm[base + tc + r] / a.K) * a.H,
+                                  LEN * 2, &ufull[b]);
+                } else {
+                    tma_load_2d(sbp, &tmSB, &ufull[b], 0, e * a.H + blk0);
+                    bulk_load(xs, a.in + (size_t)(base + tc) * a.I, nt * LEN * 2, &ufull[b]);
+                }
+                for (int kc = lead; kc < NK; ++kc)
+                    if (!stage(e, blk0, kc, item)) return;
             }
         }
         return;
     }
+    int g = 0, u = 0;
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
         const int e = a.active[item / NRB], blk0 = (item % NRB) * rows_per_blk;
         const int n = a.counts[e], base = a.offsets[e];
-        bool first = true;
-        for (int tc = 0; tc < n; tc += NTMAX, g += NK) {
+        for (int tc = 0; tc < n; tc += NTMAX, g += NK, ++u) {
             const int nt = min(NTMAX, n - tc);
-            const int vecs = LEN / 8;
-            asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32));
-            if (first && (G & 3)) {  // (scale, bias) pairs, rows not 16-byte aligned
-                for (int v = threadIdx.x; v < S::ROWS * G; v += kComputeWarps * 32) {
-                    const int r = v / G, gi = v - r * G;
-                    const int64_t grow = (EPI == GATEUP)
-                        ? (int64_t)e * 2 * a.I + (r < 16 ? blk0 + r : a.I + blk0 + r - 16)
-                        : (int64_t)e * a.H + blk0 + r;
-                    const uint32_t pv = __ldg(a.sb + grow * G + gi);
-                    ss[v] = bf_lo(pv);
-                    sb[v] = bf_hi(pv);
-                }
-                first = false;
+            const int b = u & 1;
+            if (!mbar_wait(&ufull[b], (u >> 1) & 1, kWaitLimit)) {
+                record_error(a.err, 24, item);
+                return;
             }
-            if (first) {  // the item's (scale, bias) pairs, once per item, 16-byte loads
-                const int G4 = G / 4;  // 4 pairs per 16 bytes
-                for (int v = threadIdx.x; v < S::ROWS * G4; v += kComputeWarps * 32) {
-                    const int r = v / G4, g4 = v - r * G4;
-                    const int64_t grow = (EPI == GATEUP)
-                        ? (int64_t)e * 2 * a.I + (r < 16 ? blk0 + r : a.I + blk0 + r - 16)
-                        : (int64_t)e * a.H + blk0 + r;
-                    const uint4 p4 = __ldg(reinterpret_cast<const uint4 *>(a.sb + grow * G) + g4);
-                    const uint32_t pv[4] = {p4.x, p4.y, p4.z, p4.w};
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        ss[r * G + g4 * 4 + j] = bf_lo(pv[j]);
-                        sb[r * G + g4 * 4 + j] = bf_hi(pv[j]);
-                    }
-                }
-                first = false;
-            }
-            for (int v = threadIdx.x; v < nt * vecs; v += kComputeWarps * 32) {
-                const int r = v / vecs, k = (v - r * vecs) * 8;
-                const uint16_t *src = (EPI == GATEUP)
-                    ? a.in + (size_t)(a.perm[base + tc + r] / a.K) * a.H
-                    : a.in + (size_t)(base + tc + r) * a.I;
-                *reinterpret_cast<uint4 *>(xs + r * LEN + k) =
-                    *reinterpret_cast<const uint4 *>(src + k);
-            }
-            asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32));
+            const uint16_t *xs = xs0 + b * NTMAX * LEN;
+            const uint32_t *sbp = sb0 + b * S::ROWS * Gp;
             bool ok = true;
             if (EPI == GATEUP) {
-                if (nt == 1) ok = gateup_pass_q<1, BITS>(ring, full, empty, xs, ss, sb, a, g, warp, lane, blk0, nt, base + tc);
-                else if (nt == 2) { if constexpr (NTMAX >= 2) ok = gateup_pass_q<2, BITS>(ring, full, empty, xs, ss, sb, a, g, warp, lane, blk0, nt, base + tc); }
-                else if (nt <= 4) { if constexpr (NTMAX >= 4) ok = gateup_pass_q<4, BITS>(ring, full, empty, xs, ss, sb, a, g, warp, lane, blk0, nt, base + tc); }
-                else { if constexpr (NTMAX >= 8) ok = gateup_pass_q<8, BITS>(ring, full, empty, xs, ss, sb, a, g, warp, lane, blk0, nt, base + tc); }
+                if (nt == 1) ok = gateup_pass_q<1, BITS>(ring, full, empty, xs, sbp, a, g, warp, lane, blk0, nt, base + tc);
+                else if (nt == 2) { if constexpr (NTMAX >= 2) ok = gateup_pass_q<2, BITS>(ring, full, empty, xs, sbp, a, g, warp, lane, blk0, nt, base + tc); }
+                else if (nt <= 4) { if constexpr (NTMAX >= 4) ok = gateup_pass_q<4, BITS>(ring, full, empty, xs, sbp, a, g, warp, lane, blk0, nt, base + tc); }
+                else { if constexpr (NTMAX >= 8) ok = gateup_pass_q<8, BITS>(ring, full, empty, xs, sbp, a, g, warp, lane, blk0, nt, base + tc); }
             } else {
-                if (nt == 1) ok = down_pass_q<1, BITS>(ring, full, empty, xs, ss, sb, a, g, warp, lane, blk0, nt, base + tc);
-                else if (nt == 2) { if constexpr (NTMAX >= 2) ok = down_pass_q<2, BITS>(ring, full, empty, xs, ss, sb, a, g, warp, lane, blk0, nt, base + tc); }
-                else if (nt <= 4) { if constexpr (NTMAX >= 4) ok = down_pass_q<4, BITS>(ring, full, empty, xs, ss, sb, a, g, warp, lane, blk0, nt, base + tc); }
-                else { if constexpr (NTMAX >= 8) ok = down_pass_q<8, BITS>(ring, full, empty, xs, ss, sb, a, g, warp, lane, blk0, nt, base + tc); }
+                if (nt == 1) ok = down_pass_q<1, BITS>(ring, full, empty, xs, sbp, a, g, warp, lane, blk0, nt, base + tc);
+                else if (nt == 2) { if constexpr (NTMAX >= 2) ok = down_pass_q<2, BITS>(ring, full, empty, xs, sbp, a, g, warp, lane, blk0, nt, base + tc); }
+                else if (nt <= 4) { if constexpr (NTMAX >= 4) ok = down_pass_q<4, BITS>(ring, full, empty, xs, sbp, a, g, warp, lane, blk0, nt, base + tc); }
+                else { if constexpr (NTMAX >= 8) ok = down_pass_q<8, BITS>(ring, full, empty, xs, sbp, a, g, warp, lane, blk0, nt, base + tc); }
             }
+            // A timed-out wait leaves the rings inconsistent: every compute warp
+            // waits on the same barriers, so all of them expire; leave at once.
             if (!ok) return;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&uempty[b]);  // this warp is done with the unit's operands
         }
     }
 }
@@ -354,16 +369,16 @@ bool make_qmap(CUtensorMap *m, const void *base, uint64_t words, uint64_t rows,
 }
 
 template <int EPI, int BITS, int NTMAX>
-size_t qsmem_bytes(int len) {
+size_t qsmem_bytes(int len, int gp) {
     using S = QShape<EPI, BITS>;
-    return 1024 + (size_t)S::STAGES * S::STAGE_BYTES + (size_t)NTMAX * len * 2 +
-           2 * (size_t)S::ROWS * (len / 64) * 4 + 8 + 16 * S::STAGES + 64;
+    return 1024 + (size_t)S::STAGES * S::STAGE_BYTES + 2 * (size_t)NTMAX * len * 2 + 128 +
+           2 * (size_t)S::ROWS * gp * 4 + 16 * S::STAGES + 32 + 64;
 }
 
 template <int EPI, int BITS, int NTMAX>
-cudaError_t qlaunch_one(const CUtensorMap &m, const QArgs &a, int max_items, int len,
-                        cudaStream_t s) {
-    const size_t smem = qsmem_bytes<EPI, BITS, NTMAX>(len);
+cudaError_t qlaunch_one(const CUtensorMap &m, const CUtensorMap &sbm, const QArgs &a,
+                        int max_items, int len, cudaStream_t s) {
+    const size_t smem = qsmem_bytes<EPI, BITS, NTMAX>(len, a.gp);
     static int occ_cache[64] = {};
     const int dev = current_device();
     int &occ = occ_cache[dev & 63];
@@ -378,16 +393,16 @@ cudaError_t qlaunch_one(const CUtensorMap &m, const QArgs &a, int max_items, int
     if (max_items < grid) grid = max_items;
     if (grid < 1) grid = 1;
     return launch_ex(gemv_tma_q_kernel<EPI, BITS, NTMAX>, dim3(grid), dim3(kThreads), smem, s,
-                     true, m, a);
+                     true, m, sbm, a);
 }
 
 template <int EPI, int BITS>
-cudaError_t qlaunch(const CUtensorMap &m, const QArgs &a, int max_items, int len, int max_rows,
-                    cudaStream_t s) {
-    if (max_rows <= 1) return qlaunch_one<EPI, BITS, 1>(m, a, max_items, len, s);
-    if (max_rows <= 2) return qlaunch_one<EPI, BITS, 2>(m, a, max_items, len, s);
-    if (max_rows <= 4) return qlaunch_one<EPI, BITS, 4>(m, a, max_items, len, s);
-    return qlaunch_one<EPI, BITS, 8>(m, a, max_items, len, s);
+cudaError_t qlaunch(const CUtensorMap &m, const CUtensorMap &sbm, const QArgs &a, int max_items,
+                    int len, int max_rows, cudaStream_t s) {
+    if (max_rows <= 1) return qlaunch_one<EPI, BITS, 1>(m, sbm, a, max_items, len, s);
+    if (max_rows <= 2) return qlaunch_one<EPI, BITS, 2>(m, sbm, a, max_items, len, s);
+    if (max_rows <= 4) return qlaunch_one<EPI, BITS, 4>(m, sbm, a, max_items, len, s);
+    return qlaunch_one<EPI, BITS, 8>(m, sbm, a, max_items, len, s);
 }
 
 }  // namespace
@@ -400,14 +415,16 @@ bool gemv_tma_q_supported(int H, int I, int bits) {
 cudaError_t launch_gemv_tma_q_gateup(const uint16_t *x, int K, const Dispatch &d,
                                      const ExpertWeights &w, int H, int I, int E, int max_rows,
                                      uint16_t *yp, int32_t *err, cudaStream_t s, int *launches) {
-    CUtensorMap m;
+    CUtensorMap m, sbm;
     const uint32_t row_words = 256 * w.bits / 32;
-    if (!make_qmap(&m, w.gu_q, (uint64_t)H * w.bits / 32, (uint64_t)E * 2 * I, row_words, 16))
+    const int gp = sb_row_words(H);
+    if (!make_qmap(&m, w.gu_q, (uint64_t)H * w.bits / 32, (uint64_t)E * 2 * I, row_words, 16) ||
+        !make_qmap(&sbm, w.gu_sb, gp, (uint64_t)E * 2 * I, gp, 16))
         return cudaErrorInvalidValue;
-    QArgs a{x, d.perm, d.offsets, d.counts, d.active, d.n_active, w.gu_sb, yp, err, K, H, I};
+    QArgs a{x, d.perm, d.offsets, d.counts, d.active, d.n_active, w.gu_sb, yp, err, K, H, I, gp};
     const int max_items = min(E, max_rows * K) * (I / 16);
-    cudaError_t e = (w.bits == 4) ? qlaunch<GATEUP, 4>(m, a, max_items, H, max_rows, s)
-                                  : qlaunch<GATEUP, 8>(m, a, max_items, H, max_rows, s);
+    cudaError_t e = (w.bits == 4) ? qlaunch<GATEUP, 4>(m, sbm, a, max_items, H, max_rows, s)
+                                  : qlaunch<GATEUP, 8>(m, sbm, a, max_items, H, max_rows, s);
     if (launches) ++*launches;
     return e;
 }
@@ -415,14 +432,16 @@ cudaError_t launch_gemv_tma_q_gateup(const uint16_t *x, int K, const Dispatch &d
 cudaError_t launch_gemv_tma_q_down(const uint16_t *yp, const Dispatch &d, const ExpertWeights &w,
                                    int H, int I, int E, int max_k, int max_rows, uint16_t *op,
                                    int32_t *err, cudaStream_t s, int *launches) {
-    CUtensorMap m;
+    CUtensorMap m, sbm;
     const uint32_t row_words = 64 * w.bits / 32;
-    if (!make_qmap(&m, w.dn_q, (uint64_t)I * w.bits / 32, (uint64_t)E * H, row_words, 64))
+    const int gp = sb_row_words(I);
+    if (!make_qmap(&m, w.dn_q, (uint64_t)I * w.bits / 32, (uint64_t)E * H, row_words, 64) ||
+        !make_qmap(&sbm, w.dn_sb, gp, (uint64_t)E * H, gp, 64))
         return cudaErrorInvalidValue;
-    QArgs a{yp, d.perm, d.offsets, d.counts, d.active, d.n_active, w.dn_sb, op, err, 0, H, I};
+    QArgs a{yp, d.perm, d.offsets, d.counts, d.active, d.n_active, w.dn_sb, op, err, 0, H, I, gp};
     const int max_items = min(E, max_rows * max_k) * (H / 64);
-    cudaError_t e = (w.bits == 4) ? qlaunch<DOWN, 4>(m, a, max_items, I, max_rows, s)
-                                  : qlaunch<DOWN, 8>(m, a, max_items, I, max_rows, s);
+    cudaError_t e = (w.bits == 4) ? qlaunch<DOWN, 4>(m, sbm, a, max_items, I, max_rows, s)
+                                  : qlaunch<DOWN, 8>(m, sbm, a, max_items, I, max_rows, s);
     if (launches) ++*launches;
     return e;
 }

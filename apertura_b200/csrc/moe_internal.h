@@ -170,8 +170,11 @@ cudaError_t launch_group_offsets(const int32_t *counts, int G, int32_t *offsets,
 cudaError_t launch_quantize_affine(const uint16_t *w, int64_t rows, int cols, int gs, int bits,
                                    uint32_t *q, uint16_t *sc, uint16_t *bi, cudaStream_t s);
 // (scale, bias) pairs interleaved per group: [rows, groups] uint32
-cudaError_t launch_interleave_sb(const uint16_t *sc, const uint16_t *bi, int64_t n, uint32_t *out,
-                                 cudaStream_t s);
+// Interleaved (scale, bias) pairs of `rows` rows of g groups each, rows padded
+// to sb_row_words(g * 64) words (zeros), for the quantised TMA GEMV.
+inline int sb_row_words(int len) { return ((len / 64) + 3) / 4 * 4; }
+cudaError_t launch_interleave_sb(const uint16_t *sc, const uint16_t *bi, int64_t rows, int g,
+                                 uint32_t *out, cudaStream_t s);
 // bf16 copy of the active experts' quantised rows (prefill path)
 cudaError_t launch_dequant_active(const uint32_t *q, const uint16_t *sc, const uint16_t *bi,
                                   int rows, int cols, int bits, const Dispatch &d, int E,

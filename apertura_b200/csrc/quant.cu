@@ -94,19 +94,25 @@ __global__ void dequant_active_kernel(const uint32_t *__restrict__ q, const uint
 // Repack scales/biases [rows, groups] x2 into one [rows, groups] uint32 array
 // of (scale | bias << 16) pairs: a row's pairs are contiguous (groups*4 bytes),
 // so a kernel stages a block of rows with plain 16-byte loads.
+// (scale | bias << 16) per group, rows of g groups padded with zeros to gp
+// (a multiple of 4, so every row starts on 16 bytes for the TMA).
 __global__ void interleave_sb_kernel(const uint16_t *__restrict__ sc,
-                                     const uint16_t *__restrict__ bi, int64_t n,
+                                     const uint16_t *__restrict__ bi, int64_t rows, int g, int gp,
                                      uint32_t *__restrict__ out) {
+    const int64_t n = rows * gp;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * blockDim.x)
-        out[i] = (uint32_t)sc[i] | ((uint32_t)bi[i] << 16);
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / gp;
+        const int c = (int)(i - r * gp);
+        out[i] = c < g ? ((uint32_t)sc[r * g + c] | ((uint32_t)bi[r * g + c] << 16)) : 0u;
+    }
 }
 
 }  // namespace
 
-cudaError_t launch_interleave_sb(const uint16_t *sc, const uint16_t *bi, int64_t n, uint32_t *out,
-                                 cudaStream_t s) {
-    interleave_sb_kernel<<<1024, 256, 0, s>>>(sc, bi, n, out);
+cudaError_t launch_interleave_sb(const uint16_t *sc, const uint16_t *bi, int64_t rows, int g,
+                                 uint32_t *out, cudaStream_t s) {
+    interleave_sb_kernel<<<1024, 256, 0, s>>>(sc, bi, rows, g, sb_row_words(g * 64), out);
     return cudaGetLastError();
 }
 

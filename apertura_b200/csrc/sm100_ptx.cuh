@@ -93,6 +93,17 @@ __device__ __forceinline__ void tma_gather4(void *dst, const CUtensorMap *map, u
         : "memory");
 }
 
+// 1-D bulk copy global -> shared of `bytes` (a multiple of 16; both addresses
+// 16-byte aligned), completing those bytes on `bar`.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
+                                          uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // 2-D tiled store of a shared-memory box to global (bulk-group completion).
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int c0,
                                              int c1) {
