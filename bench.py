@@ -37,7 +37,7 @@ GATEUP_BYTES = 2 * I * H * 2                    # gate_up part of it
 # DRAM bytes read by the four gate_up launches of one sweep step (T=1,4,16,64),
 # from an ncu capture (dram__bytes_read.sum); the command and the per-T figures
 # are in profiles/gate_up_decode_sweep_traffic.txt.
-GATEUP_SWEEP_TRAFFIC = 1999.3e6
+GATEUP_SWEEP_TRAFFIC = 1992.83e6  # dram__bytes_read.sum, profiles/gate_up_decode_sweep_traffic.txt
 ROUTER_BYTES = E * H * 2                        # 720,896 B
 
 
