@@ -221,7 +221,185 @@ __device__ __forceinline__ bool down_pass_q(const uint8_t *ring, uint64_t *full,
     return true;
 }
 
-template <int EPI, int BITS, int NTMAX>
+// ---------------------------------------------------------------- 4-bit on the tensor cores
+//
+// For 4-bit codes the SIMT pass above is issue-bound (about five instructions
+// per weight to unpack and multiply).  This variant turns two codes into a
+// bf16 pair with three integer instructions and lets mma.sync.m16n8k16 do the
+// multiplies for all (up to 8) tokens at once.  A code q becomes the bf16
+// value 128 + q exactly (0x4300 | q: exponent of 128, q in the low mantissa
+// bits), so a 16x16 weight tile times the tokens' x gives
+//   D = sum (128 + q) x = sum q x + 128 sum x
+// with exact products and f32 sums; per 64-element group the affine
+// dequantisation then adds  s * D + (b - 128 s) * sum x,  i.e. the same
+// s * sum q x + b * sum x  as the SIMT pass, in a different summation order.
+// (mma.sync rather than tcgen05: at T <= 8 the multiply is a small part of
+// the work and the operands are built in registers; a tcgen05 MMA would need
+// them written to shared memory first.)
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4],
+                                               uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// The A fragment of one 16x16 tile (rows g and g + 8, k = 2t, 2t+1, 2t+8,
+// 2t+9 of the tile) from the two packed words (k 0..7, k 8..15) of each row.
+__device__ __forceinline__ void q4_pair(uint32_t w0, uint32_t w1, int t, uint32_t &lo,
+                                        uint32_t &hi) {
+    // byte t of w0 (codes k=2t, 2t+1) and byte t of w1 (k=2t+8, 2t+9)
+    const uint32_t x = __byte_perm(w0, w1, (uint32_t)(t | ((4 + t) << 4))) & 0xFFFFu;
+    lo = ((x | (x << 12)) & 0x000F000Fu) | 0x43004300u;         // (128+q0, 128+q1)
+    hi = (((x >> 8) | (x << 4)) & 0x000F000Fu) | 0x43004300u;  // (128+q8, 128+q9)
+}
+
+// gate_up, 32 rows (16 gate + 16 up) x one 256-wide stage per pass step;
+// warp w takes the stage's group w (k = 64w .. 64w+63) for both row halves.
+// Partial sums meet in shared memory at the end of the item.
+template <int NT>
+__device__ __forceinline__ bool gateup_pass_mma(const uint8_t *ring, uint64_t *full,
+                                                uint64_t *empty, const uint16_t *xs,
+                                                const uint32_t *sbp, const float *xsum,
+                                                float *red, const QArgs &a, int g, int w,
+                                                int lane, int j0, int nt, int row0) {
+    using S = QShape<GATEUP, 4>;
+    const int NK = a.H / S::KC, G = a.gp, LEN = a.H;
+    const int gid = lane >> 2, t = lane & 3;
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    for (int kc = 0; kc < NK; ++kc, ++g) {
+        const int s = g % S::STAGES;
+        if (!mbar_wait(&full[s], (g / S::STAGES) & 1, kWaitLimit)) {
+            record_error(a.err, 25, kc);
+            return false;
+        }
+        const uint32_t *st = reinterpret_cast<const uint32_t *>(ring + s * S::STAGE_BYTES);
+        const int grp = kc * (S::KC / 64) + w;  // this warp's group of the row
+        float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {  // 16-wide chunks of the group
+            const int k0 = w * 64 + c * 16;  // within the stage
+            uint32_t b0 = 0u, b1 = 0u;
+            if (gid < nt) {
+                const uint16_t *xr = xs + gid * LEN + kc * S::KC + k0 + 2 * t;
+                b0 = *reinterpret_cast<const uint32_t *>(xr);
+                b1 = *reinterpret_cast<const uint32_t *>(xr + 8);
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {  // gate rows 0..15, up rows 16..31
+                const uint32_t *r0 = st + (h * 16 + gid) * S::ROW_WORDS + k0 / 8;
+                const uint32_t *r1 = r0 + 8 * S::ROW_WORDS;
+                uint32_t af[4];
+                q4_pair(r0[0], r0[1], t, af[0], af[2]);
+                q4_pair(r1[0], r1[1], t, af[1], af[3]);
+                mma_bf16_16816(d[h], af, b0, b1);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        // affine dequantisation of this group: s*D + (b - 128 s)*sum(x)
+        const float xs0 = (2 * t < nt) ? xsum[(2 * t) * G + grp] : 0.f;
+        const float xs1 = (2 * t + 1 < nt) ? xsum[(2 * t + 1) * G + grp] : 0.f;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t p0 = sbp[(h * 16 + gid) * G + grp];
+            const uint32_t p1 = sbp[(h * 16 + gid + 8) * G + grp];
+            const float s0 = bf_lo(p0), c0 = fmaf(-128.f, s0, bf_hi(p0));
+            const float s1 = bf_lo(p1), c1 = fmaf(-128.f, s1, bf_hi(p1));
+            acc[h][0] += fmaf(s0, d[h][0], c0 * xs0);
+            acc[h][1] += fmaf(s0, d[h][1], c0 * xs1);
+            acc[h][2] += fmaf(s1, d[h][2], c1 * xs0);
+            acc[h][3] += fmaf(s1, d[h][3], c1 * xs1);
+        }
+    }
+    // red[w][row 0..31][tok 0..7]
+    float *rw = red + w * 256;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        rw[(h * 16 + gid) * 8 + 2 * t] = acc[h][0];
+        rw[(h * 16 + gid) * 8 + 2 * t + 1] = acc[h][1];
+        rw[(h * 16 + gid + 8) * 8 + 2 * t] = acc[h][2];
+        rw[(h * 16 + gid + 8) * 8 + 2 * t + 1] = acc[h][3];
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32));
+    {
+        const int j = threadIdx.x >> 3, tok = threadIdx.x & 7;  // 16 j x 8 tokens
+        if (tok < nt) {
+            float gsum = 0.f, usum = 0.f;
+#pragma unroll
+            for (int q = 0; q < kComputeWarps; ++q) {
+                gsum += red[q * 256 + j * 8 + tok];
+                usum += red[q * 256 + (16 + j) * 8 + tok];
+            }
+            a.out[(size_t)(row0 + tok) * a.I + j0 + j] = f2bf(geglu_bf16(rbf(gsum), rbf(usum)));
+        }
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32));  // red free for the next item
+    return true;
+}
+
+// down, 64 rows x one 64-wide stage (= one group); warp w owns rows 16w..16w+15.
+template <int NT>
+__device__ __forceinline__ bool down_pass_mma(const uint8_t *ring, uint64_t *full, uint64_t *empty,
+                                              const uint16_t *xs, const uint32_t *sbp,
+                                              const float *xsum, const QArgs &a, int g, int w,
+                                              int lane, int h0, int nt, int row0) {
+    using S = QShape<DOWN, 4>;
+    const int NK = a.I / S::KC, G = a.gp, LEN = a.I;
+    const int gid = lane >> 2, t = lane & 3;
+    const int rb = 16 * w;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int kc = 0; kc < NK; ++kc, ++g) {
+        const int s = g % S::STAGES;
+        if (!mbar_wait(&full[s], (g / S::STAGES) & 1, kWaitLimit)) {
+            record_error(a.err, 26, kc);
+            return false;
+        }
+        const uint32_t *st = reinterpret_cast<const uint32_t *>(ring + s * S::STAGE_BYTES);
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            uint32_t b0 = 0u, b1 = 0u;
+            if (gid < nt) {
+                const uint16_t *xr = xs + gid * LEN + kc * S::KC + c * 16 + 2 * t;
+                b0 = *reinterpret_cast<const uint32_t *>(xr);
+                b1 = *reinterpret_cast<const uint32_t *>(xr + 8);
+            }
+            const uint32_t *r0 = st + (rb + gid) * S::ROW_WORDS + c * 2;
+            const uint32_t *r1 = r0 + 8 * S::ROW_WORDS;
+            uint32_t af[4];
+            q4_pair(r0[0], r0[1], t, af[0], af[2]);
+            q4_pair(r1[0], r1[1], t, af[1], af[3]);
+            mma_bf16_16816(d, af, b0, b1);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        const float xs0 = (2 * t < nt) ? xsum[(2 * t) * G + kc] : 0.f;
+        const float xs1 = (2 * t + 1 < nt) ? xsum[(2 * t + 1) * G + kc] : 0.f;
+        const uint32_t p0 = sbp[(rb + gid) * G + kc];
+        const uint32_t p1 = sbp[(rb + gid + 8) * G + kc];
+        const float s0 = bf_lo(p0), c0 = fmaf(-128.f, s0, bf_hi(p0));
+        const float s1 = bf_lo(p1), c1 = fmaf(-128.f, s1, bf_hi(p1));
+        acc[0] += fmaf(s0, d[0], c0 * xs0);
+        acc[1] += fmaf(s0, d[1], c0 * xs1);
+        acc[2] += fmaf(s1, d[2], c1 * xs0);
+        acc[3] += fmaf(s1, d[3], c1 * xs1);
+    }
+    // rows rb+gid, rb+gid+8; tokens 2t, 2t+1
+    if (2 * t < nt) {
+        a.out[(size_t)(row0 + 2 * t) * a.H + h0 + rb + gid] = f2bf(acc[0]);
+        a.out[(size_t)(row0 + 2 * t) * a.H + h0 + rb + gid + 8] = f2bf(acc[2]);
+    }
+    if (2 * t + 1 < nt) {
+        a.out[(size_t)(row0 + 2 * t + 1) * a.H + h0 + rb + gid] = f2bf(acc[1]);
+        a.out[(size_t)(row0 + 2 * t + 1) * a.H + h0 + rb + gid + 8] = f2bf(acc[3]);
+    }
+    return true;
+}
+
+template <int EPI, int BITS, int NTMAX, bool MMA = false>
 __global__ void __launch_bounds__(kThreads)
 gemv_tma_q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmSB,
                   QArgs a) {
@@ -235,7 +413,13 @@ gemv_tma_q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
     uint16_t *xs0 = reinterpret_cast<uint16_t *>(ring + S::STAGES * S::STAGE_BYTES);
     uint32_t *sb0 = reinterpret_cast<uint32_t *>(
         (reinterpret_cast<uintptr_t>(xs0 + 2 * NTMAX * LEN) + 127) & ~uintptr_t(127));
-    uint64_t *full = reinterpret_cast<uint64_t *>(sb0 + 2 * S::ROWS * Gp);
+    // MMA variant: per-unit sums of x over each group, and gate_up's
+    // cross-warp partial sums
+    float *xsum = reinterpret_cast<float *>(sb0 + 2 * S::ROWS * Gp);
+    float *red = xsum + (MMA ? NTMAX * Gp : 0);
+    uint64_t *full = reinterpret_cast<uint64_t *>(
+        (reinterpret_cast<uintptr_t>(red + (MMA && EPI == GATEUP ? kComputeWarps * 256 : 0)) + 7) &
+        ~uintptr_t(7));
     uint64_t *empty = full + S::STAGES;
     uint64_t *ufull = empty + S::STAGES;
     uint64_t *uempty = ufull + 2;
@@ -331,7 +515,31 @@ gemv_tma_q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
             const uint16_t *xs = xs0 + b * NTMAX * LEN;
             const uint32_t *sbp = sb0 + b * S::ROWS * Gp;
             bool ok = true;
-            if (EPI == GATEUP) {
+            if constexpr (MMA && BITS == 4) {
+                // sum of x over every 64-element group, per token of the unit
+                asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32));  // old sums read
+                const int G = LEN / 64;
+                for (int v = threadIdx.x; v < nt * G; v += kComputeWarps * 32) {
+                    const int tok = v / G, gi = v - tok * G;
+                    const uint4 *xp = reinterpret_cast<const uint4 *>(xs + tok * LEN + gi * 64);
+                    float sum = 0.f;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        float f[8];
+                        unpack8(xp[q], f);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) sum += f[i];
+                    }
+                    xsum[tok * Gp + gi] = sum;
+                }
+                asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32));
+                if (EPI == GATEUP)
+                    ok = gateup_pass_mma<NTMAX>(ring, full, empty, xs, sbp, xsum, red, a, g, warp,
+                                                lane, blk0, nt, base + tc);
+                else
+                    ok = down_pass_mma<NTMAX>(ring, full, empty, xs, sbp, xsum, a, g, warp, lane,
+                                              blk0, nt, base + tc);
+            } else if (EPI == GATEUP) {
                 if (nt == 1) ok = gateup_pass_q<1, BITS>(ring, full, empty, xs, sbp, a, g, warp, lane, blk0, nt, base + tc);
                 else if (nt == 2) { if constexpr (NTMAX >= 2) ok = gateup_pass_q<2, BITS>(ring, full, empty, xs, sbp, a, g, warp, lane, blk0, nt, base + tc); }
                 else if (nt <= 4) { if constexpr (NTMAX >= 4) ok = gateup_pass_q<4, BITS>(ring, full, empty, xs, sbp, a, g, warp, lane, blk0, nt, base + tc); }
@@ -368,41 +576,45 @@ bool make_qmap(CUtensorMap *m, const void *base, uint64_t words, uint64_t rows,
            CUDA_SUCCESS;
 }
 
-template <int EPI, int BITS, int NTMAX>
+template <int EPI, int BITS, int NTMAX, bool MMA>
 size_t qsmem_bytes(int len, int gp) {
     using S = QShape<EPI, BITS>;
     return 1024 + (size_t)S::STAGES * S::STAGE_BYTES + 2 * (size_t)NTMAX * len * 2 + 128 +
-           2 * (size_t)S::ROWS * gp * 4 + 16 * S::STAGES + 32 + 64;
+           2 * (size_t)S::ROWS * gp * 4 + (MMA ? (size_t)NTMAX * gp * 4 : 0) +
+           (MMA && EPI == GATEUP ? (size_t)kComputeWarps * 256 * 4 : 0) + 8 + 16 * S::STAGES +
+           32 + 64;
 }
 
-template <int EPI, int BITS, int NTMAX>
+template <int EPI, int BITS, int NTMAX, bool MMA>
 cudaError_t qlaunch_one(const CUtensorMap &m, const CUtensorMap &sbm, const QArgs &a,
                         int max_items, int len, cudaStream_t s) {
-    const size_t smem = qsmem_bytes<EPI, BITS, NTMAX>(len, a.gp);
+    const size_t smem = qsmem_bytes<EPI, BITS, NTMAX, MMA>(len, a.gp);
     static int occ_cache[64] = {};
     const int dev = current_device();
     int &occ = occ_cache[dev & 63];
     if (!occ) {
-        cudaFuncSetAttribute(gemv_tma_q_kernel<EPI, BITS, NTMAX>,
+        cudaFuncSetAttribute(gemv_tma_q_kernel<EPI, BITS, NTMAX, MMA>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_tma_q_kernel<EPI, BITS, NTMAX>,
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_tma_q_kernel<EPI, BITS, NTMAX, MMA>,
                                                       kThreads, smem);
         if (occ < 1) occ = 1;
     }
     int grid = grid_sms(dev) * occ;
     if (max_items < grid) grid = max_items;
     if (grid < 1) grid = 1;
-    return launch_ex(gemv_tma_q_kernel<EPI, BITS, NTMAX>, dim3(grid), dim3(kThreads), smem, s,
+    return launch_ex(gemv_tma_q_kernel<EPI, BITS, NTMAX, MMA>, dim3(grid), dim3(kThreads), smem, s,
                      true, m, sbm, a);
 }
 
 template <int EPI, int BITS>
 cudaError_t qlaunch(const CUtensorMap &m, const CUtensorMap &sbm, const QArgs &a, int max_items,
                     int len, int max_rows, cudaStream_t s) {
-    if (max_rows <= 1) return qlaunch_one<EPI, BITS, 1>(m, sbm, a, max_items, len, s);
-    if (max_rows <= 2) return qlaunch_one<EPI, BITS, 2>(m, sbm, a, max_items, len, s);
-    if (max_rows <= 4) return qlaunch_one<EPI, BITS, 4>(m, sbm, a, max_items, len, s);
-    return qlaunch_one<EPI, BITS, 8>(m, sbm, a, max_items, len, s);
+    // 4-bit codes on the tensor cores (mma passes), 8-bit on the SIMT passes
+    constexpr bool M = (BITS == 4);
+    if (max_rows <= 1) return qlaunch_one<EPI, BITS, 1, M>(m, sbm, a, max_items, len, s);
+    if (max_rows <= 2) return qlaunch_one<EPI, BITS, 2, M>(m, sbm, a, max_items, len, s);
+    if (max_rows <= 4) return qlaunch_one<EPI, BITS, 4, M>(m, sbm, a, max_items, len, s);
+    return qlaunch_one<EPI, BITS, 8, M>(m, sbm, a, max_items, len, s);
 }
 
 }  // namespace
