@@ -17,7 +17,7 @@ STATUS_NAMES = {0: "APT_OK", 1: "APT_ERR_INVALID", 2: "APT_ERR_UNSUPPORTED", 3: 
 
 # Every symbol include/apt_moe.h declares, in header order.
 EXPORTED = [
-    "apt_moe_config_from_json", "apt_moe_create", "apt_moe_destroy", "apt_moe_last_error",
+    "apt_moe_config_from_json", "apt_moe_create", "apt_moe_destroy", "apt_moe_clone_shared", "apt_moe_last_error",
     "apt_moe_version", "apt_moe_load_router", "apt_moe_load_experts_bf16",
     "apt_moe_load_experts_quant", "apt_moe_route", "apt_moe_route_weights", "apt_moe_experts",
     "apt_moe_experts_dense", "apt_moe_forward", "apt_moe_layer_forward", "apt_moe_decoder_ff", "apt_moe_forward_host", "apt_moe_ep_dispatch",
@@ -70,6 +70,7 @@ def lib():
         "apt_moe_config_from_json": ([ctypes.c_char_p, cfgp], i32),
         "apt_moe_create": ([cfgp, ctypes.POINTER(ctypes.c_void_p)], i32),
         "apt_moe_destroy": ([hp], i32),
+        "apt_moe_clone_shared": ([hp, cfgp, ctypes.POINTER(ctypes.c_void_p)], i32),
         "apt_moe_last_error": ([hp], ctypes.c_char_p),
         "apt_moe_version": ([], ctypes.c_char_p),
         "apt_moe_load_router": ([hp, P, P, P, i32], i32),

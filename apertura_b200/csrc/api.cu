@@ -17,6 +17,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <string>
+#include <memory>
 #include <vector>
 
 #include "../../include/apt_moe.h"
@@ -24,6 +25,20 @@
 #include "launch_util.h"
 
 using namespace apt;
+
+// Device weight buffers shared by handles made with apt_moe_clone_shared: freed
+// when the last handle holding them is destroyed.
+struct WeightOwner {
+    int device = 0;
+    std::vector<void *> ptrs;
+    ~WeightOwner() {
+        int prev = -1;
+        cudaGetDevice(&prev);
+        cudaSetDevice(device);
+        for (void *p : ptrs) cudaFree(p);
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
 
 struct apt_moe_handle {
     apt_moe_config cfg{};
@@ -67,6 +82,8 @@ struct apt_moe_handle {
     uint16_t *gu_s = nullptr, *gu_b = nullptr, *dn_s = nullptr, *dn_b = nullptr;
     uint32_t *gu_sb = nullptr, *dn_sb = nullptr;  // (scale, bias) pairs, per-row contiguous
     int qbits = 0, qgs = 64;
+    // set when the weights above are shared with other handles (read-only then)
+    std::shared_ptr<WeightOwner> wowner;
 
     // workspace
     int Tm = 0, Pcap = 0;
@@ -179,6 +196,18 @@ struct StageScope {
         StageScope sc_((h), (id), (s));          \
         CUDA_TRY((h), (expr));                   \
     } while (0)
+
+// The handle's weight buffers (what apt_moe_clone_shared shares).
+std::vector<void **> weight_fields(apt_moe_handle *h) {
+    return {reinterpret_cast<void **>(&h->proj),  reinterpret_cast<void **>(&h->scale),
+            reinterpret_cast<void **>(&h->pes),   reinterpret_cast<void **>(&h->gu),
+            reinterpret_cast<void **>(&h->dn),    reinterpret_cast<void **>(&h->gu_q),
+            reinterpret_cast<void **>(&h->dn_q),  reinterpret_cast<void **>(&h->gu_s),
+            reinterpret_cast<void **>(&h->gu_b),  reinterpret_cast<void **>(&h->dn_s),
+            reinterpret_cast<void **>(&h->dn_b),  reinterpret_cast<void **>(&h->gu_sb),
+            reinterpret_cast<void **>(&h->dn_sb), reinterpret_cast<void **>(&h->dq_gu),
+            reinterpret_cast<void **>(&h->dq_dn), reinterpret_cast<void **>(&h->dq_ids)};
+}
 
 void drop_graphs(apt_moe_handle *h) {
     for (auto &g : h->graphs) cudaGraphExecDestroy(g.exec);
@@ -325,6 +354,12 @@ extern "C" apt_status apt_moe_create(const apt_moe_config *cfg, apt_moe_handle *
 extern "C" apt_status apt_moe_destroy(apt_moe_handle *h) {
     if (!h) return APT_OK;
     DeviceGuard g(h->cfg.device);
+    if (h->wowner) {  // shared weights: freed by their owner with the last handle
+        for (void **f : weight_fields(h))
+            for (void *p : h->wowner->ptrs)
+                if (*f == p) *f = nullptr;
+        h->wowner.reset();
+    }
     void *ptrs[] = {h->proj, h->scale, h->pes, h->gu, h->dn, h->gu_q, h->dn_q, h->gu_s, h->gu_b,
                     h->dn_s, h->dn_b, h->scores, h->idx_i, h->w_i, h->counts, h->offsets,
                     h->perm, h->inv, h->active, h->n_active, h->errflag, h->done, h->hsplit, h->rt_cnt, h->xp, h->yp, h->op,
@@ -338,6 +373,45 @@ extern "C" apt_status apt_moe_destroy(apt_moe_handle *h) {
         for (int j = 0; j < 2; ++j)
             if (h->ev[i][j]) cudaEventDestroy(h->ev[i][j]);
     delete h;
+    return APT_OK;
+}
+
+extern "C" apt_status apt_moe_clone_shared(apt_moe_handle *src, const apt_moe_config *cfg,
+                                           apt_moe_handle **out) {
+    if (!src || !out) return APT_ERR_INVALID;
+    *out = nullptr;
+    if (!src->proj) return fail(src, APT_ERR_STATE, "router weights not loaded");
+    apt_moe_config c = src->cfg;
+    if (cfg) {  // the clone may differ in workspace size and sparse/dense switch only
+        if (cfg->hidden_size != c.hidden_size || cfg->num_experts != c.num_experts ||
+            cfg->top_k_experts != c.top_k_experts ||
+            cfg->moe_intermediate_size != c.moe_intermediate_size ||
+            cfg->quant_bits != c.quant_bits || cfg->device != c.device)
+            return fail(src, APT_ERR_INVALID, "clone config differs in shape, format or device");
+        c.max_tokens = cfg->max_tokens;
+        c.moe_sparse = cfg->moe_sparse;
+        c.rms_norm_eps = cfg->rms_norm_eps;
+        c.enable_moe_block = cfg->enable_moe_block;
+    }
+    apt_moe_handle *h = nullptr;
+    if (apt_status st = apt_moe_create(&c, &h)) return st;
+    DeviceGuard g(src->cfg.device);
+    if (!src->wowner) {  // hand the source's weight buffers to a shared owner
+        src->wowner = std::make_shared<WeightOwner>();
+        src->wowner->device = src->cfg.device;
+        for (void **f : weight_fields(src))
+            if (*f) src->wowner->ptrs.push_back(*f);
+    }
+    h->wowner = src->wowner;
+    std::vector<void **> to = weight_fields(h), from = weight_fields(src);
+    for (size_t i = 0; i < to.size(); ++i) {
+        bool shared = false;
+        for (void *p : src->wowner->ptrs) shared |= (*from[i] == p);
+        *to[i] = shared ? *from[i] : nullptr;  // the dequantised cache stays per handle
+    }
+    h->qbits = src->qbits;
+    h->qgs = src->qgs;
+    *out = h;
     return APT_OK;
 }
 
@@ -434,6 +508,8 @@ extern "C" apt_status apt_moe_load_router(apt_moe_handle *h, const uint16_t *pro
     if (!h || !proj || !scale || !pes) return fail(h, APT_ERR_INVALID, "null router weight");
     DeviceGuard g(h->cfg.device);
     drop_graphs(h);
+    if (h->wowner)
+        return fail(h, APT_ERR_STATE, "weights are shared with another handle (read-only)");
     const int H = h->cfg.hidden_size, E = h->cfg.num_experts;
     if (!h->proj) {
         CUDA_TRY(h, dalloc(&h->proj, (size_t)E * H));
@@ -452,6 +528,8 @@ extern "C" apt_status apt_moe_load_experts_bf16(apt_moe_handle *h, const uint16_
     if (!h || !gate_up || !down) return fail(h, APT_ERR_INVALID, "null expert weight");
     DeviceGuard g(h->cfg.device);
     drop_graphs(h);
+    if (h->wowner)
+        return fail(h, APT_ERR_STATE, "weights are shared with another handle (read-only)");
     const size_t H = h->cfg.hidden_size, E = h->cfg.num_experts, I = h->cfg.moe_intermediate_size;
     if (!h->gu) {
         CUDA_TRY(h, dalloc(&h->gu, E * 2 * I * H));
@@ -495,6 +573,8 @@ extern "C" apt_status apt_moe_load_experts_quant(apt_moe_handle *h, const uint32
         return fail(h, APT_ERR_UNSUPPORTED, "bits=%d group=%d (need bits 4|8, group 64)", bits, gs);
     DeviceGuard g(h->cfg.device);
     drop_graphs(h);
+    if (h->wowner)
+        return fail(h, APT_ERR_STATE, "weights are shared with another handle (read-only)");
     const size_t H = h->cfg.hidden_size, E = h->cfg.num_experts, I = h->cfg.moe_intermediate_size;
     dfree(h->gu_q); dfree(h->dn_q); dfree(h->gu_s); dfree(h->gu_b); dfree(h->dn_s); dfree(h->dn_b);
     h->gu_q = h->dn_q = nullptr;

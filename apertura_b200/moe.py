@@ -108,6 +108,20 @@ class Handle:
         check(lib().apt_moe_create(ctypes.byref(c), ctypes.byref(h)))
         self.h = h
 
+    def clone_shared(self, cfg: Optional[ESModelConfig] = None) -> "Handle":
+        """A second handle on the same device weights (own workspace and
+        settings; the shared weights are read-only).  cfg may change only
+        max_tokens, moe_sparse, rms_norm_eps and enable_moe_block."""
+        out = Handle.__new__(Handle)
+        out.cfg = cfg or self.cfg
+        out.device = self.device
+        h = ctypes.c_void_p()
+        c = out.cfg.to_c() if cfg is not None else None
+        self.check(lib().apt_moe_clone_shared(self.h, ctypes.byref(c) if c is not None else None,
+                                              ctypes.byref(h)))
+        out.h = h
+        return out
+
     def close(self):
         if getattr(self, "h", None):
             lib().apt_moe_destroy(self.h)

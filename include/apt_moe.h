@@ -76,6 +76,18 @@ APT_API apt_status apt_moe_config_from_json(const char *json_text, apt_moe_confi
  * max_tokens on cfg->device.  No weights yet. */
 APT_API apt_status apt_moe_create(const apt_moe_config *cfg, apt_moe_handle **out);
 APT_API apt_status apt_moe_destroy(apt_moe_handle *h);
+
+/*
+ * A second handle on the same device weights (ESExperts / ESRouter instances
+ * sharing mx::arrays, as several sessions of one model do): its own
+ * workspace, streams, settings and error state, the weights shared and
+ * read-only.  cfg may be NULL (same config) or differ from the source's only
+ * in max_tokens, moe_sparse, rms_norm_eps and enable_moe_block.  Loading
+ * weights into either handle afterwards returns APT_ERR_STATE.  The weights
+ * are freed with the last handle that holds them; destroy order is free.
+ */
+APT_API apt_status apt_moe_clone_shared(apt_moe_handle *src, const apt_moe_config *cfg,
+                                        apt_moe_handle **out);
 APT_API const char *apt_moe_last_error(const apt_moe_handle *h);
 /* Library version string (static). */
 APT_API const char *apt_moe_version(void);
