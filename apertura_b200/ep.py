@@ -41,6 +41,7 @@ exchange logic on gloo ranks.
 """
 from __future__ import annotations
 
+import ctypes
 import time
 from typing import List, Optional, Sequence, Tuple
 
@@ -288,3 +289,66 @@ class ExpertParallelMoE:
         return out
 
     __call__ = forward
+
+
+class NativeExpertParallelMoE:
+    """The same expert-parallel block with the whole step inside the library
+    (apt_moe_create_ep: C++ host flow, NCCL resolved by the library): what a
+    C or C++ host would call.  Construction is collective over `group` (its
+    NCCL communicator is made from an id that rank 0 creates and the group
+    broadcasts).  Parameters as ExpertParallelMoE."""
+
+    def __init__(self, cfg: ESModelConfig, proj, scale, pes, gate_up, down, group=None,
+                 loads: Optional[Sequence[float]] = None, max_tokens_per_rank: int = 4096,
+                 replicate_hot: int = 24):
+        import numpy as np
+        from ._lib import check as _check
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.cfg = cfg
+        idbuf = ctypes.create_string_buffer(128)
+        if self.rank == 0:
+            _check(lib().apt_moe_nccl_unique_id(idbuf))
+        obj = [idbuf.raw if self.rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0, group=group)
+        idbuf = ctypes.create_string_buffer(obj[0], 128)
+        self._loads = None if loads is None else np.asarray(loads, dtype=np.float32)
+        c = ESModelConfig(**{**cfg.__dict__, "moe_sparse": True,
+                             "max_tokens": max_tokens_per_rank}).to_c()
+        ep = ctypes.c_void_p()
+        lp = None if self._loads is None else ctypes.c_void_p(self._loads.ctypes.data)
+        _check(lib().apt_moe_create_ep(ctypes.byref(c), idbuf, self.rank, self.world, lp,
+                                       int(replicate_hot), ctypes.byref(ep)))
+        self.ep = ep
+        self._check(lib().apt_moe_ep_load_router(ep, _ptr(proj), _ptr(scale), _ptr(pes), 1))
+        self._check(lib().apt_moe_ep_load_experts_bf16(ep, _ptr(gate_up), _ptr(down), 1))
+
+    def _check(self, status):
+        if status != 0:
+            msg = lib().apt_moe_ep_last_error(self.ep)
+            raise RuntimeError(f"apt_moe_ep: status {status}: {msg.decode() if msg else ''}")
+
+    def stats(self):
+        r, h = ctypes.c_int(), ctypes.c_int()
+        self._check(lib().apt_moe_ep_stats(self.ep, ctypes.byref(r), ctypes.byref(h)))
+        return r.value, h.value
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        T, H = x.shape
+        out = torch.empty_like(x)
+        self._check(lib().apt_moe_ep_forward(self.ep, _ptr(x), T, _ptr(out), _stream(x.device)))
+        return out
+
+    __call__ = forward
+
+    def close(self):
+        if getattr(self, "ep", None):
+            lib().apt_moe_ep_destroy(self.ep)
+            self.ep = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+

@@ -388,8 +388,7 @@ def run_ep(args, dev, world, rank, T=4096, steps=5, warmup=3):
     cfg = A.ESModelConfig(moe_sparse=True, max_tokens=T, device=dev.index)
     ep = ExpertParallelMoE(cfg, d["proj"], d["scale"], d["pes"], gu, dn,
                            loads=d["zipf"]["target"].tolist(), max_tokens_per_rank=T)
-    del gu, dn
-    torch.cuda.empty_cache()
+    gu_full, dn_full = gu, dn  # kept for the C-ABI form below
     for _ in range(warmup):
         ep(x)
     stream = torch.cuda.current_stream(dev)
@@ -414,6 +413,29 @@ def run_ep(args, dev, world, rank, T=4096, steps=5, warmup=3):
     hph = torch.tensor([ep.last_host_ms[n] for n in names], device=dev)
     dist.all_reduce(hph, op=dist.ReduceOp.MAX)
     host_phases = {n: float(v) for n, v in zip(names, hph.tolist())}
+    # the same step with the host flow inside the library (apt_moe_create_ep)
+    from apertura_b200.ep import NativeExpertParallelMoE
+    nep = NativeExpertParallelMoE(cfg, d["proj"], d["scale"], d["pes"], gu_full, dn_full,
+                                  loads=d["zipf"]["target"].tolist(), max_tokens_per_rank=T)
+    for _ in range(warmup):
+        nep(x)
+    nms = 0.0
+    for _ in range(steps):
+        dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        nep(x)
+        b.record(stream)
+        torch.cuda.synchronize()
+        nms += a.elapsed_time(b) / steps
+    nt = torch.tensor([nms], device=dev)
+    dist.all_reduce(nt, op=dist.ReduceOp.MAX)
+    native = {"ms_per_step": float(nt.item()),
+              "tokens_per_s": world * T / (float(nt.item()) / 1e3)}
+    nep.close()
+    del gu_full, dn_full, gu, dn
+    torch.cuda.empty_cache()
     t = torch.tensor([ms, float(ep.last_recv_rows)], device=dev)
     mx = t.clone()
     dist.all_reduce(mx, op=dist.ReduceOp.MAX)
@@ -428,7 +450,8 @@ def run_ep(args, dev, world, rank, T=4096, steps=5, warmup=3):
             "recv_rows_per_rank": recv,
             "load_max_over_mean": max(recv) / (sum(recv) / len(recv)),
             "phases_ms_max_over_ranks": phases,
-            "host_enqueue_ms_max_over_ranks": host_phases}
+            "host_enqueue_ms_max_over_ranks": host_phases,
+            "native_c_abi": native}
 
 
 def run_quant(dev, peaks, flush, bits=4, Ts=(1, 4096), steps=5):

@@ -321,6 +321,45 @@ APT_API apt_status apt_moe_route_noalloc(const uint16_t *x, int T, const uint16_
                                          int hidden_size, int num_experts, int top_k, float eps,
                                          int32_t *idx, uint16_t *w, void *stream);
 
+/*
+ * Expert parallelism as one C-ABI handle per GPU over NCCL (no reference
+ * counterpart): the hottest `replicate_hot` experts (by expected_loads, [E]
+ * tokens per expert; NULL = uniform) are held by every rank, the others are
+ * spread over the ranks by longest-processing-time placement; each forward
+ * routes the rank's tokens, computes the replicated experts at home beside
+ * the NCCL exchange of the other rows, computes the rank's own experts on
+ * the rows it receives, sends the results back and combines in k order.
+ * The result equals the single-GPU block on the same tokens.  NCCL is
+ * resolved at run time (libnccl.so.2).  bf16 experts only.
+ *
+ *   apt_moe_nccl_unique_id: 128-byte id for the ranks' communicator (rank 0
+ *     makes it, the host distributes it)
+ *   apt_moe_create_ep: cfg.max_tokens = tokens per rank per call; the
+ *     communicator is created from nccl_id (collective over the ranks)
+ *   apt_moe_ep_load_router / _experts_bf16: the FULL router and expert banks
+ *     (every rank passes the same tensors; each keeps what it needs)
+ *   apt_moe_ep_forward: x, out [T, H] bf16 on this rank's device
+ *   apt_moe_ep_placement: the placement alone, perm[new id] = original id
+ *   apt_moe_ep_stats: rows received / computed at home in the last forward
+ */
+typedef struct apt_moe_ep apt_moe_ep;
+APT_API apt_status apt_moe_nccl_unique_id(void *id_out);
+APT_API apt_status apt_moe_create_ep(const apt_moe_config *cfg, const void *nccl_id, int rank,
+                                     int nranks, const float *expected_loads, int replicate_hot,
+                                     apt_moe_ep **out);
+APT_API apt_status apt_moe_ep_destroy(apt_moe_ep *ep);
+APT_API const char *apt_moe_ep_last_error(const apt_moe_ep *ep);
+APT_API apt_status apt_moe_ep_load_router(apt_moe_ep *ep, const uint16_t *proj,
+                                          const uint16_t *scale, const uint16_t *pes,
+                                          int on_device);
+APT_API apt_status apt_moe_ep_load_experts_bf16(apt_moe_ep *ep, const uint16_t *gate_up,
+                                                const uint16_t *down, int on_device);
+APT_API apt_status apt_moe_ep_forward(apt_moe_ep *ep, const uint16_t *x, int T, uint16_t *out,
+                                      void *stream);
+APT_API apt_status apt_moe_ep_placement(const float *loads, int E, int nranks, int n_hot,
+                                        int32_t *perm_out);
+APT_API apt_status apt_moe_ep_stats(const apt_moe_ep *ep, int *recv_rows, int *hot_rows);
+
 #ifdef __cplusplus
 }
 #endif

@@ -52,6 +52,21 @@ def test_hot_cold_placement():
         hot_cold_placement(loads, 2, 5)       # 11 cold experts do not split over 2
 
 
+def test_native_placement_matches_python():
+    """apt_moe_ep_placement (the C-ABI EP's placement) = hot_cold_placement."""
+    import ctypes
+    from apertura_b200._lib import lib
+    rng = np.random.default_rng(3)
+    for E, N, R in ((128, 2, 24), (128, 8, 24), (128, 4, 0), (16, 2, 4)):
+        loads = rng.pareto(1.1, E).astype(np.float32)
+        loads[5] = loads[6]  # a tie
+        out = np.zeros(E, np.int32)
+        st = lib().apt_moe_ep_placement(ctypes.c_void_p(loads.ctypes.data), E, N, R,
+                                        ctypes.c_void_p(out.ctypes.data))
+        assert st == 0
+        assert out.tolist() == hot_cold_placement([float(v) for v in loads], N, R)
+
+
 class OracleBackend:
     """CPU stand-in for CudaBackend, built on the oracle."""
 
