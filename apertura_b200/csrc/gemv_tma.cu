@@ -319,17 +319,24 @@ bool make_map(CUtensorMap *m, const void *base, uint64_t inner, uint64_t rows, u
     return bf16_map_2d(m, base, inner, rows, kc, box_rows, false);
 }
 
-constexpr int kStages = 4;
+// Ring depth: about 64-96 KB of weights in flight per CTA (a CTA's stream is
+// bounded by bytes in flight over the load latency), within the shared memory
+// that still lets two CTAs share an SM at small token counts.
+template <int EPI, int NTMAX>
+constexpr int stages_for() {
+    return EPI == DOWN ? 8 : (NTMAX <= 2 ? 6 : 4);
+}
 
 template <int EPI, int NTMAX>
 size_t smem_bytes(int len) {
+    constexpr int kStages = stages_for<EPI, NTMAX>();
     return 1024 + (size_t)kStages * Shape<EPI>::STAGE_BYTES + 2 * (size_t)NTMAX * len * 2 +
            16 * kStages + 32 + 64;
 }
 
 template <int EPI, int NTMAX>
 cudaError_t set_attr() {
-    return cudaFuncSetAttribute(gemv_tma_kernel<EPI, NTMAX, kStages>,
+    return cudaFuncSetAttribute(gemv_tma_kernel<EPI, NTMAX, stages_for<EPI, NTMAX>()>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
 }
 
@@ -344,14 +351,16 @@ cudaError_t launch_one(const CUtensorMap &m, const Args &a, int max_items, int l
     const int slot = len >= 2048 ? 0 : len >= 1024 ? 1 : len >= 512 ? 2 : 3;
     int &occ = occ_cache[dev & 63][slot];
     if (!occ) {
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_tma_kernel<EPI, NTMAX, kStages>,
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ,
+                                                      gemv_tma_kernel<EPI, NTMAX, stages_for<EPI, NTMAX>()>,
                                                       kThreads, smem);
         if (occ < 1) occ = 1;
     }
     int grid = grid_sms(dev) * occ;
     if (max_items < grid) grid = max_items;
     if (grid < 1) grid = 1;
-    return launch_ex(gemv_tma_kernel<EPI, NTMAX, kStages>, dim3(grid), dim3(kThreads), smem, s,
+    return launch_ex(gemv_tma_kernel<EPI, NTMAX, stages_for<EPI, NTMAX>()>, dim3(grid),
+                     dim3(kThreads), smem, s,
                      true, m, a);
 }
 

@@ -42,7 +42,10 @@ struct QShape {
     static constexpr int KC = EPI == GATEUP ? 256 : 64;    // elements per row per stage
     static constexpr int ROW_WORDS = KC * BITS / 32;       // packed words per row per stage
     static constexpr int STAGE_BYTES = ROWS * ROW_WORDS * 4;
-    static constexpr int STAGES = STAGE_BYTES <= 2048 ? 16 : 8;
+    // ~64 KB of packed weights in flight per CTA (a CTA's stream is bounded by
+    // bytes in flight over the load latency)
+    static constexpr int STAGES = (65536 / STAGE_BYTES) < 4 ? 4 : (65536 / STAGE_BYTES) > 32 ? 32
+                                                                 : (65536 / STAGE_BYTES);
     static constexpr int LANE_WORDS = 8 * BITS / 32;       // words holding a lane's 8 elements
 };
 

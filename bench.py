@@ -51,27 +51,84 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks + throttle reasons polled every ~200 ms from a thread."""
+    """SM clock, max clock and clock-event (throttle) reasons of one GPU, read
+    every ~10 ms from a thread while the timed region runs: through NVML when
+    the bindings are importable, else nvidia-smi every ~200 ms.  Read-only."""
 
+    # NVML clocks-event reason bits
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+            "hw_thermal_slowdown": 0x40}
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index):
         self.index = index
-        self.lines = []
+        self.sm, self.mx, self.reasons = [], None, set()
         self.stop = threading.Event()
 
-    def _poll(self):
+    def _poll_nvml(self, nv):
+        # the CUDA device's own GPU (NVML numbers all GPUs of the machine)
+        h = None
+        try:
+            import torch
+            uuid = getattr(torch.cuda.get_device_properties(self.index), "uuid", None)
+            if uuid is not None:
+                h = nv.nvmlDeviceGetHandleByUUID(f"GPU-{uuid}")
+        except Exception:
+            h = None
+        if h is None:
+            h = nv.nvmlDeviceGetHandleByIndex(self.index)
+        self.mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
+        while not self.stop.is_set():
+            self.sm.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+            bits = get_reasons(h)
+            for n, b in self.BITS.items():
+                if bits & b:
+                    self.reasons.add(n)
+            self.stop.wait(0.01)
+
+    def _poll_smi(self):
         cmd = ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
                "--format=csv,noheader,nounits"]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         while not self.stop.is_set():
             try:
                 r = subprocess.run(cmd, capture_output=True, text=True, timeout=5)
-                self.lines.extend(l.strip() for l in r.stdout.splitlines() if l.strip())
             except Exception:
                 return
+            for ln in r.stdout.splitlines():
+                f = [x.strip() for x in ln.split(",")]
+                if len(f) < 8:
+                    continue
+                try:
+                    self.sm.append(float(f[1]))
+                    self.mx = float(f[2])
+                except ValueError:
+                    continue
+                for n, v in zip(names, f[4:8]):
+                    if v.lower().startswith("active"):
+                        self.reasons.add(n)
             self.stop.wait(0.2)
+
+    def _poll(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+        except Exception:
+            return self._poll_smi()
+        try:
+            self._poll_nvml(nv)
+        except Exception:
+            if not self.sm:
+                self._poll_smi()
+        finally:
+            try:
+                nv.nvmlShutdown()
+            except Exception:
+                pass
 
     def __enter__(self):
         self.t = threading.Thread(target=self._poll, daemon=True)
@@ -83,24 +140,10 @@ class ClockSampler:
         self.t.join(timeout=10)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 8:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[4:8]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
-        sm.sort()
-        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons),
+        if not self.sm:
+            return {"sm_mhz": None, "sm_max_mhz": self.mx, "reasons": [], "samples": 0}
+        sm = sorted(self.sm)
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": self.mx, "reasons": sorted(self.reasons),
                 "samples": len(sm)}
 
 
