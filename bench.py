@@ -170,7 +170,7 @@ def oracle_sweep_inputs(d_by_T, gate_up, down):
                 gate_up=nb(gate_up), down=nb(down))
 
 
-def time_oracle_sweep(o, budget_s=12.0, max_passes=50):
+def time_oracle_sweep(o, budget_s=12.0, max_passes=400):
     """Oracle (route + sparse experts) over the sweep until `budget_s` elapses.
     Returns (tokens/s, passes, seconds, threads)."""
     from oracle import oracle as O
