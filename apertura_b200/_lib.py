@@ -27,7 +27,7 @@ EXPORTED = [
     "apt_moe_set_timing", "apt_moe_stage_times", "apt_moe_route_noalloc",
     "apt_moe_nccl_unique_id", "apt_moe_create_ep", "apt_moe_ep_destroy", "apt_moe_ep_last_error",
     "apt_moe_ep_load_router", "apt_moe_ep_load_experts_bf16", "apt_moe_ep_forward",
-    "apt_moe_ep_placement", "apt_moe_ep_stats",
+    "apt_moe_ep_placement", "apt_moe_ep_stats", "apt_moe_selftest_wait",
 ]
 
 STAGES = ["router_scores", "router_select", "dispatch_count", "dispatch", "gather", "gate_up",
@@ -100,6 +100,7 @@ def lib():
         "apt_moe_stage_times": ([hp, P], i32),
         "apt_moe_route_noalloc": ([P, i32, P, P, P, i32, i32, i32, f32, P, P, P], i32),
         "apt_moe_nccl_unique_id": ([P], i32),
+        "apt_moe_selftest_wait": ([hp, i32, P], i32),
         "apt_moe_create_ep": ([cfgp, P, i32, i32, P, i32, ctypes.POINTER(ctypes.c_void_p)], i32),
         "apt_moe_ep_destroy": ([P], i32),
         "apt_moe_ep_last_error": ([P], ctypes.c_char_p),

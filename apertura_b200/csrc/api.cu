@@ -483,6 +483,16 @@ extern "C" apt_status apt_moe_sync(apt_moe_handle *h) {
     return APT_OK;
 }
 
+extern "C" apt_status apt_moe_selftest_wait(apt_moe_handle *h, int microseconds, void *stream) {
+    if (!h || microseconds <= 0 || microseconds > 10000000) return APT_ERR_INVALID;
+    DeviceGuard g(h->cfg.device);
+    int khz = 0;
+    CUDA_TRY(h, cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, h->cfg.device));
+    const long long cycles = (long long)khz * microseconds / 1000;  // at the rated clock
+    CUDA_TRY(h, launch_selftest_wait(cycles, h->errflag, (cudaStream_t)stream));
+    return APT_OK;
+}
+
 // ------------------------------------------------------------------ weights
 
 namespace {

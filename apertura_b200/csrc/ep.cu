@@ -110,7 +110,7 @@ apt_status ep_fail(apt_moe_ep *ep, apt_status st, const char *fmt, ...) {
     do {                                                                                    \
         ncclResult_t r_ = (call);                                                           \
         if (r_ != ncclSuccess)                                                              \
-            return ep_fail(ep, APT_ERR_CUDA, "%s: %s", #call, nccl().error_string(r_));      \
+            return ep_fail(ep, APT_ERR_NCCL, "%s: %s", #call, nccl().error_string(r_));      \
     } while (0)
 
 #define EP_APT(ep, h, call)                                                                 \
@@ -190,7 +190,7 @@ extern "C" apt_status apt_moe_nccl_unique_id(void *id_out) {
     if (!id_out) return APT_ERR_INVALID;
     if (!nccl().ok) return APT_ERR_UNSUPPORTED;
     ncclUniqueId id;
-    if (nccl().get_unique_id(&id) != ncclSuccess) return APT_ERR_CUDA;
+    if (nccl().get_unique_id(&id) != ncclSuccess) return APT_ERR_NCCL;
     memcpy(id_out, &id, sizeof id);
     return APT_OK;
 }
@@ -251,7 +251,7 @@ extern "C" apt_status apt_moe_create_ep(const apt_moe_config *cfg, const void *n
     if (apt_moe_ep_placement(expected_loads, E, nranks, R, ep->perm.data())) return bail(APT_ERR_INVALID);
     ncclUniqueId id;
     memcpy(&id, nccl_id, sizeof id);
-    if (nccl().comm_init_rank(&ep->comm, nranks, id, rank) != ncclSuccess) return bail(APT_ERR_CUDA);
+    if (nccl().comm_init_rank(&ep->comm, nranks, id, rank) != ncclSuccess) return bail(APT_ERR_NCCL);
     // handles: router over all experts, replicated bank, owned bank
     apt_moe_config c = ep->cfg;
     if (apt_moe_create(&c, &ep->router)) return bail(APT_ERR_CUDA);

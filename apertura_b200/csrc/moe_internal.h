@@ -170,6 +170,10 @@ cudaError_t launch_group_offsets(const int32_t *counts, int G, int32_t *offsets,
 cudaError_t launch_quantize_affine(const uint16_t *w, int64_t rows, int cols, int gs, int bits,
                                    uint32_t *q, uint16_t *sc, uint16_t *bi, cudaStream_t s);
 // (scale, bias) pairs interleaved per group: [rows, groups] uint32
+// Self-test of the bounded device wait: expires after limit_cycles and records
+// error code 99 (quant.cu).
+cudaError_t launch_selftest_wait(long long limit_cycles, int32_t *err, cudaStream_t s);
+
 // Interleaved (scale, bias) pairs of `rows` rows of g groups each, rows padded
 // to sb_row_words(g * 64) words (zeros), for the quantised TMA GEMV.
 inline int sb_row_words(int len) { return ((len / 64) + 3) / 4 * 4; }

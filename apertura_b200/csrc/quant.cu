@@ -11,6 +11,7 @@
 #include "common.cuh"
 #include "launch_util.h"
 #include "moe_internal.h"
+#include "sm100_ptx.cuh"
 
 namespace apt {
 
@@ -133,6 +134,31 @@ cudaError_t launch_quantize_affine(const uint16_t *w, int64_t rows, int cols, in
     const int threads = 256;
     const int64_t blocks = (groups + threads - 1) / threads;
     quantize_affine_kernel<<<(unsigned)blocks, threads, 0, s>>>(w, rows, cols, gs, bits, q, sc, bi);
+    return cudaGetLastError();
+}
+
+}  // namespace apt
+
+namespace apt {
+
+namespace {
+
+// One thread waits on an mbarrier nothing arrives on, through the same bounded
+// wait every pipeline of the library uses; on expiry it records `code` in the
+// error word and returns (the context stays usable).
+__global__ void selftest_wait_kernel(long long limit_cycles, int32_t *err, int code) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        sm100::mbar_init(&bar, 1);
+        sm100::fence_barrier_init();
+        if (!sm100::mbar_wait(&bar, 0, limit_cycles) && atomicCAS(err, 0, code) == 0) err[1] = -1;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_selftest_wait(long long limit_cycles, int32_t *err, cudaStream_t s) {
+    selftest_wait_kernel<<<1, 32, 0, s>>>(limit_cycles, err, 99);
     return cudaGetLastError();
 }
 

@@ -242,6 +242,15 @@ APT_API apt_status apt_moe_experts_grouped(apt_moe_handle *h, const uint16_t *ro
 APT_API apt_status apt_moe_sync(apt_moe_handle *h);
 
 /*
+ * Self-test of the failure path: launches one thread that waits on a device
+ * barrier nothing signals, through the same bounded wait the kernels use,
+ * for about `microseconds`; it then records a timeout in the handle's error
+ * word and returns.  The next apt_moe_sync reports APT_ERR_TIMEOUT (and clears
+ * it); the context stays usable.
+ */
+APT_API apt_status apt_moe_selftest_wait(apt_moe_handle *h, int microseconds, void *stream);
+
+/*
  * Introspection for tests and the bench: per-expert token counts of the last
  * dispatch (device -> host copy, synchronous), and kernel launch count of the
  * last compute call.

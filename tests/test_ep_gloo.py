@@ -173,3 +173,62 @@ def test_ep_exchange_matches_single_device(n_hot):
     for rank, ma, peak in res:
         # same arithmetic, same order: identical up to relabelled tie-breaking
         assert ma <= 2.0 ** -7 * peak, (rank, ma, peak)
+
+
+def _failing_worker(rank, world, port, result_q):
+    """Rank 1 leaves between steps (no exchange in flight); rank 0's next
+    exchange must end with an error from the process-group timeout, not hang."""
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=8))
+    from apertura_b200.moe import ESModelConfig
+    from apertura_b200.ep import ExpertParallelMoE
+    g = torch.Generator().manual_seed(0)
+    bf = lambda t: t.to(torch.bfloat16)
+    proj = bf(torch.randn(E, H, generator=g) / H ** 0.5)
+    scale, pes = bf(torch.ones(H)), bf(torch.ones(E))
+    gu = bf(0.02 * torch.randn(E, 2 * I, H, generator=g))
+    dn = bf(0.02 * torch.randn(E, H, I, generator=g))
+    cfg = ESModelConfig(hidden_size=H, num_experts=E, top_k_experts=K, moe_intermediate_size=I,
+                        moe_sparse=True, max_tokens=64, device=0)
+    ep = ExpertParallelMoE(cfg, proj, scale, pes, gu, dn, max_tokens_per_rank=64,
+                           backend=OracleBackend, replicate_hot=0)
+    x = bf(torch.randn(8, H, generator=g))
+    ep(x)  # one good step on both ranks
+    if rank == 1:
+        result_q.put((rank, "left"))
+        result_q.close()
+        result_q.join_thread()
+        os._exit(0)  # leaves without a goodbye, between steps
+    import time
+    t0 = time.time()
+    try:
+        ep(x)
+        result_q.put((rank, "no error"))
+    except Exception as e:  # gloo reports the lost peer or the timeout
+        result_q.put((rank, f"error after {time.time() - t0:.1f}s: {type(e).__name__}"))
+    result_q.close()
+    result_q.join_thread()
+    os._exit(0)
+
+
+def test_ep_lost_rank_is_detected():
+    from oracle import oracle as O
+    O.build()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + (os.getpid() + 311) % 1000
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    alive = [p.is_alive() for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert not any(alive), "a rank hung instead of failing"
+    res = dict(q.get(timeout=5) for _ in range(2))
+    assert res[1] == "left"
+    assert res[0].startswith("error after"), res[0]
