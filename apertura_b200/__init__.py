@@ -5,7 +5,8 @@ csrc/).  This package builds it and mirrors the reference's ESRouter /
 ESExperts interface over torch device tensors.
 """
 from ._lib import AptError, lib  # noqa: F401
-from .moe import ESExperts, ESModelConfig, ESRouter, Handle, MoEBlock, TopK, make_experts  # noqa: F401
+from .moe import (ESExperts, ESModelConfig, ESRouter, Handle, MLPBlock, MoEBlock, TopK,  # noqa: F401
+                  make_experts)
 
-__all__ = ["AptError", "ESExperts", "ESModelConfig", "ESRouter", "Handle", "MoEBlock", "TopK",
+__all__ = ["AptError", "ESExperts", "ESModelConfig", "ESRouter", "Handle", "MLPBlock", "MoEBlock", "TopK",
            "make_experts", "lib"]

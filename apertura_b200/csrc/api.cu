@@ -1045,6 +1045,52 @@ extern "C" apt_status apt_moe_experts_grouped(apt_moe_handle *h, const uint16_t 
     return APT_OK;
 }
 
+extern "C" apt_status apt_moe_mlp_forward(apt_moe_handle *h, const uint16_t *x, int T,
+                                          uint16_t *out, void *stream) {
+    if (!h) return APT_ERR_INVALID;
+    if (check_T(h, T)) return APT_ERR_INVALID;
+    if (T == 0) return APT_OK;
+    if (!x || !out) return fail(h, APT_ERR_INVALID, "null pointer");
+    if (h->cfg.num_experts != 1 || h->cfg.top_k_experts != 1)
+        return fail(h, APT_ERR_STATE, "an MLP handle has num_experts = top_k_experts = 1");
+    DeviceGuard g(h->cfg.device);
+    cudaStream_t s = (cudaStream_t)stream;
+    begin_call(h);
+    // down(gelu(gate(x)) * up(x)) = the expert pipeline with one expert and
+    // weight 1 (the combine's bf16(1 * y) is exact)
+    CUDA_TRY(h, launch_fill_mlp_routing(h->idx_i, h->w_i, T, s, &h->launches));
+    return experts_sparse(h, x, h->idx_i, h->w_i, T, out, s, false);
+}
+
+extern "C" apt_status apt_moe_decoder_ff_full(apt_moe_handle *moe, apt_moe_handle *mlp,
+                                              const uint16_t *x1, const uint16_t *pre_ff_ln_w,
+                                              const uint16_t *pre_ff_ln_2_w,
+                                              const uint16_t *post_ff_ln_1_w,
+                                              const uint16_t *post_ff_ln_2_w,
+                                              const uint16_t *post_ff_ln_w, int T, uint16_t *x2,
+                                              void *stream) {
+    if (!moe || !mlp) return APT_ERR_INVALID;
+    if (check_T(mlp, T)) return APT_ERR_INVALID;
+    if (T == 0) return APT_OK;
+    if (!x1 || !x2 || !pre_ff_ln_w) return fail(moe, APT_ERR_INVALID, "null pointer");
+    if (mlp->cfg.device != moe->cfg.device || mlp->cfg.hidden_size != moe->cfg.hidden_size)
+        return fail(moe, APT_ERR_INVALID, "MLP and MoE handles differ in device or hidden size");
+    {
+        DeviceGuard g(mlp->cfg.device);
+        cudaStream_t s = (cudaStream_t)stream;
+        begin_call(mlp);
+        // hmlp = mlp(pre_ff_ln(x1)) in the MLP handle's workspace
+        CUDA_TRY(mlp, launch_rmsnorm(x1, pre_ff_ln_w, T, mlp->cfg.hidden_size,
+                                     mlp->cfg.rms_norm_eps, mlp->xn, s, &mlp->launches));
+        CUDA_TRY(mlp, launch_fill_mlp_routing(mlp->idx_i, mlp->w_i, T, s, &mlp->launches));
+        if (apt_status st = experts_sparse(mlp, mlp->xn, mlp->idx_i, mlp->w_i, T, mlp->xout, s,
+                                           false))
+            return st;
+    }
+    return apt_moe_decoder_ff(moe, x1, mlp->xout, pre_ff_ln_2_w, post_ff_ln_1_w, post_ff_ln_2_w,
+                              post_ff_ln_w, T, x2, stream);
+}
+
 extern "C" apt_status apt_moe_forward_host(apt_moe_handle *h, const uint16_t *x_host, int T,
                                            uint16_t *out_host, void *stream) {
     if (!h) return APT_ERR_INVALID;

@@ -471,3 +471,30 @@ cudaError_t launch_combine(const uint16_t *op, const int32_t *idx, const uint16_
 }
 
 }  // namespace apt
+
+namespace apt {
+
+namespace {
+
+__global__ void fill_mlp_routing_kernel(int32_t *__restrict__ idx, uint16_t *__restrict__ w,
+                                        int n) {
+    pdl_trigger();
+    pdl_wait();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        idx[i] = 0;
+        w[i] = 0x3F80;  // bf16 1.0
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_fill_mlp_routing(int32_t *idx, uint16_t *w, int n, cudaStream_t s,
+                                    int *launches) {
+    const int blocks = (n + 255) / 256 < 148 ? (n + 255) / 256 : 148;
+    cudaError_t e = launch_ex(fill_mlp_routing_kernel, dim3(blocks > 0 ? blocks : 1), dim3(256), 0,
+                              s, true, idx, w, n);
+    if (launches) ++*launches;
+    return e;
+}
+
+}  // namespace apt

@@ -47,6 +47,10 @@ cudaError_t launch_router_norm_split(const uint16_t *x, const uint16_t *scale, i
                                      int *launches, const uint16_t *pre_w = nullptr,
                                      uint16_t *xn = nullptr);
 // out = RMSNorm(x) * w (ESRMSNorm.mm:14-28), one warp per row
+// idx[i] = 0, w[i] = bf16 1.0 for i < n: every row to the single "expert"
+// of a dense GeGLU MLP handle
+cudaError_t launch_fill_mlp_routing(int32_t *idx, uint16_t *w, int n, cudaStream_t s,
+                                    int *launches);
 cudaError_t launch_rmsnorm(const uint16_t *x, const uint16_t *w, int T, int H, float eps,
                           uint16_t *out, cudaStream_t s, int *launches);
 cudaError_t launch_gemm_router(const uint16_t *hs, const uint16_t *proj, const int32_t *cnt_off,

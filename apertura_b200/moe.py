@@ -369,6 +369,26 @@ class MoEBlock:
             _ptr(post_ff_ln_2_w), _ptr(post_ff_ln_w), T, _ptr(x2), _stream(x1.device)))
         return x2
 
+    def forward_decoder_ff_full(self, x1: torch.Tensor, mlp: "MLPBlock", pre_ff_ln_w,
+                                pre_ff_ln_2_w, post_ff_ln_1_w, post_ff_ln_2_w,
+                                post_ff_ln_w) -> torch.Tensor:
+        """The whole feed-forward half of an MoE ESDecoderLayer (ESDecoderLayer.mm:
+        61-78), dense MLP included: x2 = x1 + post_ff_ln(post_ff_ln_1(mlp(
+        pre_ff_ln(x1))) + post_ff_ln_2(MoE(x1)))."""
+        _need_cuda_bf16("x1", x1)
+        H = self.cfg.hidden_size
+        T = x1.shape[0]
+        for name, t in (("pre_ff_ln_w", pre_ff_ln_w), ("pre_ff_ln_2_w", pre_ff_ln_2_w),
+                        ("post_ff_ln_1_w", post_ff_ln_1_w), ("post_ff_ln_2_w", post_ff_ln_2_w),
+                        ("post_ff_ln_w", post_ff_ln_w)):
+            _need_cuda_bf16(name, t, (H,))
+        x2 = torch.empty(T, H, dtype=torch.bfloat16, device=x1.device)
+        self.handle.check(lib().apt_moe_decoder_ff_full(
+            self.handle.h, mlp.handle.h, _ptr(x1), _ptr(pre_ff_ln_w), _ptr(pre_ff_ln_2_w),
+            _ptr(post_ff_ln_1_w), _ptr(post_ff_ln_2_w), _ptr(post_ff_ln_w), T, _ptr(x2),
+            _stream(x1.device)))
+        return x2
+
     def forward_host(self, x_host: torch.Tensor, out_host: Optional[torch.Tensor] = None):
         """End-to-end call with host buffers (pinned for speed)."""
         if x_host.is_cuda or x_host.dtype != torch.bfloat16:
@@ -380,3 +400,36 @@ class MoEBlock:
         self.handle.check(lib().apt_moe_forward_host(self.handle.h, _ptr(x_host), T,
                                                      _ptr(out_host), _stream(self.handle.device)))
         return out_host
+
+
+class MLPBlock:
+    """ESMLPBlock (ESMLPBlock.mm:11-15): down(gelu(gate(x)) * up(x)), the dense
+    GeGLU MLP that an MoE layer adds to the expert output.  Runs on the
+    expert kernels as a one-expert handle; gate/up/down are the [I, H], [I, H]
+    and [H, I] bf16 Linear weights (quantised at load when quant_bits > 0)."""
+
+    def __init__(self, gate, up, down, hidden_size: int = 2816, intermediate_size: int = 2112,
+                 rms_norm_eps: float = 1e-6, quant_bits: int = 0, max_tokens: int = 8192,
+                 device: int = 0):
+        I, H = intermediate_size, hidden_size
+        for name, t, shp in (("gate", gate, (I, H)), ("up", up, (I, H)), ("down", down, (H, I))):
+            _need_cuda_bf16(name, t, shp)
+        self.cfg = ESModelConfig(hidden_size=H, num_experts=1, top_k_experts=1,
+                                 moe_intermediate_size=I, rms_norm_eps=rms_norm_eps,
+                                 moe_sparse=True, quant_bits=quant_bits, max_tokens=max_tokens,
+                                 device=device)
+        self.handle = Handle(self.cfg)
+        gu = torch.cat([gate, up], 0).unsqueeze(0).contiguous()
+        dn = down.unsqueeze(0).contiguous()
+        self.handle.check(lib().apt_moe_load_experts_bf16(self.handle.h, _ptr(gu), _ptr(dn), 1))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        _need_cuda_bf16("x", x)
+        T = x.shape[0]
+        out = torch.empty_like(x)
+        self.handle.check(lib().apt_moe_mlp_forward(self.handle.h, _ptr(x), T, _ptr(out),
+                                                    _stream(x.device)))
+        return out
+
+    __call__ = forward
+

@@ -193,6 +193,32 @@ APT_API apt_status apt_moe_decoder_ff(apt_moe_handle *h, const uint16_t *x1, con
                                       void *stream);
 
 /*
+ * The dense GeGLU MLP of the same layer (ESMLPBlock::forward, ESMLPBlock.mm:
+ * 11-15): down(gelu(gate(x)) * up(x)) with the same rounding points as an
+ * expert.  The handle is made with num_experts = top_k_experts = 1 and
+ * moe_intermediate_size = the MLP's intermediate_size, and loaded with
+ * apt_moe_load_experts_bf16 / _quant using gate_up = [gate_proj ; up_proj]
+ * ([1, 2I, H]) and down = down_proj ([1, H, I]).  x, out [T, H] bf16 (device).
+ */
+APT_API apt_status apt_moe_mlp_forward(apt_moe_handle *h, const uint16_t *x, int T,
+                                       uint16_t *out, void *stream);
+
+/*
+ * The whole feed-forward half of an MoE decoder layer (ESDecoderLayer.mm:
+ * 61-78) with the dense MLP computed too:
+ *   x2 = x1 + post_ff_ln( post_ff_ln_1(mlp(pre_ff_ln(x1)))
+ *                         + post_ff_ln_2(MoE(pre_ff_ln_2(x1), router(x1))) )
+ * `mlp` is an MLP handle (see apt_moe_mlp_forward) on the same device.
+ */
+APT_API apt_status apt_moe_decoder_ff_full(apt_moe_handle *moe, apt_moe_handle *mlp,
+                                           const uint16_t *x1, const uint16_t *pre_ff_ln_w,
+                                           const uint16_t *pre_ff_ln_2_w,
+                                           const uint16_t *post_ff_ln_1_w,
+                                           const uint16_t *post_ff_ln_2_w,
+                                           const uint16_t *post_ff_ln_w, int T, uint16_t *x2,
+                                           void *stream);
+
+/*
  * Same as apt_moe_forward with HOST buffers: copies x to the device, runs
  * the block, copies out back and synchronises the stream.  x_host [T,H],
  * out_host [T,H] bf16.  With pinned buffers the sequence is captured once per

@@ -69,6 +69,16 @@ public:
                                  stream),
               "decoder_ff");
     }
+    // the whole feed-forward half with the dense MLP too (see ESMLPCuda)
+    void decoderFFFull(apt_moe_handle *mlp, const uint16_t *x1, const uint16_t *preFFLN,
+                       const uint16_t *preFFLN2, const uint16_t *postFFLN1,
+                       const uint16_t *postFFLN2, const uint16_t *postFFLN, int T, uint16_t *x2,
+                       void *stream = nullptr) {
+        check(apt_moe_decoder_ff_full(h_, mlp, x1, preFFLN, preFFLN2, postFFLN1, postFFLN2,
+                                      postFFLN, T, x2, stream),
+              "decoder_ff_full");
+    }
+    apt_moe_handle *raw() { return h_; }
     // host buffers in and out (copies included)
     void forwardHost(const uint16_t *x_host, int T, uint16_t *out_host) {
         check(apt_moe_forward_host(h_, x_host, T, out_host, nullptr), "forward_host");
@@ -82,6 +92,43 @@ private:
     }
     apt_moe_handle *h_ = nullptr;
     apt_moe_config cfg_{};
+};
+
+// ESMLPBlock (ESMLPBlock.mm:11-15) on the expert kernels: one-expert handle.
+class ESMLPCuda {
+public:
+    ESMLPCuda(int hidden_size, int intermediate_size, int max_tokens, float rms_norm_eps = 1e-6f,
+              int quant_bits = 0, int device = 0) {
+        apt_moe_config cfg{};
+        cfg.hidden_size = hidden_size;
+        cfg.num_experts = 1;
+        cfg.top_k_experts = 1;
+        cfg.moe_intermediate_size = intermediate_size;
+        cfg.rms_norm_eps = rms_norm_eps;
+        cfg.enable_moe_block = 1;
+        cfg.moe_sparse = 1;
+        cfg.quant_bits = quant_bits;
+        cfg.quant_group_size = 64;
+        cfg.max_tokens = max_tokens;
+        cfg.device = device;
+        if (apt_moe_create(&cfg, &h_) != APT_OK) throw std::runtime_error("apt_moe mlp: create");
+    }
+    ESMLPCuda(const ESMLPCuda &) = delete;
+    ESMLPCuda &operator=(const ESMLPCuda &) = delete;
+    ~ESMLPCuda() { apt_moe_destroy(h_); }
+    // gate_up = [gate_proj ; up_proj] as [1, 2I, H], down = down_proj as [1, H, I]
+    void load(const uint16_t *gate_up, const uint16_t *down, bool on_device = false) {
+        if (apt_moe_load_experts_bf16(h_, gate_up, down, on_device) != APT_OK)
+            throw std::runtime_error(std::string("apt_moe mlp: ") + apt_moe_last_error(h_));
+    }
+    void forward(const uint16_t *x, int T, uint16_t *out, void *stream = nullptr) {
+        if (apt_moe_mlp_forward(h_, x, T, out, stream) != APT_OK)
+            throw std::runtime_error(std::string("apt_moe mlp: ") + apt_moe_last_error(h_));
+    }
+    apt_moe_handle *raw() { return h_; }
+
+private:
+    apt_moe_handle *h_ = nullptr;
 };
 
 }  // namespace es

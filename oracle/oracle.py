@@ -237,3 +237,23 @@ def decoder_ff(x1, hmlp, pre_w, ln1_w, post_w, ff_w, proj, scale, pes, gate_up, 
     ff = bf16_add(dense, moe)
     return bf16_add(x1, rms_norm(ff, ff_w, eps)), idx, w
 
+
+def mlp(x, gate, up, down):
+    """ESMLPBlock::forward (ESMLPBlock.mm:11-15): down(bf16(gelu(bf16 gate(x))) *
+    bf16 up(x)) -- the expert arithmetic with one expert of weight 1."""
+    gu = np.concatenate([_c(gate, np.uint16), _c(up, np.uint16)], 0)[None]
+    dn = _c(down, np.uint16)[None]
+    T = np.asarray(x).shape[0]
+    idx = np.zeros((T, 1), np.int32)
+    w = f32_to_bf16(np.ones((T, 1), np.float32))
+    return experts_sparse(x, gu, dn, idx, w)
+
+
+def decoder_ff_full(x1, pre_ff_w, gate, up, down, pre_w, ln1_w, post_w, ff_w, proj, scale, pes,
+                    gate_up, down_e, top_k, eps=1e-6):
+    """ESDecoderLayer.mm:61-78 from x1: the dense MLP on pre_ff_ln(x1) plus the
+    MoE, with the trailing norms and the residual add."""
+    hmlp = mlp(rms_norm(x1, pre_ff_w, eps), gate, up, down)
+    return decoder_ff(x1, hmlp, pre_w, ln1_w, post_w, ff_w, proj, scale, pes, gate_up, down_e,
+                      top_k, eps)
+

@@ -81,3 +81,55 @@ def test_decoder_ff_tail(oracle, shape, T):
     peak = np.abs(refv).max()
     ok, ma, cos = block_close(got, refv, max_abs=2.0 ** -6 * peak)
     assert ok, (ma, cos, peak)
+
+
+@pytest.mark.parametrize("T", [1, 5, 96])
+def test_dense_mlp(oracle, T):
+    """MLPBlock (ESMLPBlock): GEMV path for small T, tensor-core path above."""
+    H, I = 2816, 2112
+    g = torch.Generator(device=DEV).manual_seed(7 + T)
+    gate = (0.02 * torch.randn(I, H, generator=g, device=DEV)).to(torch.bfloat16)
+    up = (0.02 * torch.randn(I, H, generator=g, device=DEV)).to(torch.bfloat16)
+    down = (0.02 * torch.randn(H, I, generator=g, device=DEV)).to(torch.bfloat16)
+    x = torch.randn(T, H, generator=g, device=DEV).to(torch.bfloat16)
+    mlp = A.MLPBlock(gate, up, down, hidden_size=H, intermediate_size=I, max_tokens=128)
+    out = mlp(x)
+    torch.cuda.synchronize()
+    mlp.handle.sync()
+    ref = oracle.mlp(_np(x), _np(gate), _np(up), _np(down))
+    got, refv = bf16_to_f32(_np(out)), bf16_to_f32(ref)
+    ok, ma, cos = block_close(got, refv)
+    assert ok and ma <= 2.0 ** -6 * np.abs(refv).max(), (ma, cos)
+
+
+@pytest.mark.parametrize("T", [4, 80])
+def test_decoder_ff_full(oracle, T):
+    """apt_moe_decoder_ff_full: the layer's whole feed-forward half from x1."""
+    H, E, K, I, Id = 2816, 128, 8, 704, 2112
+    d = block_inputs(T, seed=11 * T, device=DEV, H=H, E=E, K=K, I=I, nonunit=True)
+    g = torch.Generator(device=DEV).manual_seed(9)
+    ws = [(1 + 0.2 * torch.randn(H, generator=g, device=DEV)).to(torch.bfloat16) for _ in range(5)]
+    pre_ff, pre2, ln1, post, lnf = ws
+    gate = (0.02 * torch.randn(Id, H, generator=g, device=DEV)).to(torch.bfloat16)
+    up = (0.02 * torch.randn(Id, H, generator=g, device=DEV)).to(torch.bfloat16)
+    down = (0.02 * torch.randn(H, Id, generator=g, device=DEV)).to(torch.bfloat16)
+    cfg = A.ESModelConfig(hidden_size=H, num_experts=E, top_k_experts=K, moe_intermediate_size=I,
+                          moe_sparse=True, max_tokens=T)
+    blk = A.MoEBlock(cfg, d["proj"], d["scale"], d["pes"], d["gate_up"], d["down"])
+    mlp = A.MLPBlock(gate, up, down, hidden_size=H, intermediate_size=Id, max_tokens=T)
+    x2 = blk.forward_decoder_ff_full(d["x"], mlp, pre_ff, pre2, ln1, post, lnf)
+    _, tk = blk.forward(d["x"], return_routing=True)
+    torch.cuda.synchronize()
+    ref, idx_ref, _ = oracle.decoder_ff_full(_np(d["x"]), _np(pre_ff), _np(gate), _np(up),
+                                             _np(down), _np(pre2), _np(ln1), _np(post), _np(lnf),
+                                             _np(d["proj"]), _np(d["scale"]), _np(d["pes"]),
+                                             _np(d["gate_up"]), _np(d["down"]), K)
+    _, _, aux = oracle.route_topk(_np(d["x"]), _np(d["proj"]), _np(d["scale"]), _np(d["pes"]), K,
+                                  return_scores=True)
+    bad, _ = router_index_check(tk.idx.cpu().numpy(), idx_ref, aux["scores"])
+    assert bad == 0
+    same = np.all(tk.idx.cpu().numpy() == idx_ref, axis=1)
+    got, refv = bf16_to_f32(_np(x2))[same], bf16_to_f32(ref)[same]
+    peak = np.abs(refv).max()
+    ok, ma, cos = block_close(got, refv, max_abs=2.0 ** -6 * peak)
+    assert ok, (ma, cos, peak)
