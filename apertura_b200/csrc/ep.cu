@@ -5,8 +5,9 @@
 // the host flow in apertura_b200/ep.py (same placement, same steps), for hosts
 // that drive the library from C or C++:
 //   1. route + top-K + dispatch + row gather        (router handle, all experts)
-//   2. replicated experts on a side stream, straight into the return buffer
-//   3. NCCL exchange of per-expert counts, one host sync for the splits
+//   2. NCCL exchange of per-expert counts
+//   3. replicated experts on a side stream, straight into the return buffer;
+//      one host sync for the splits
 //   4. NCCL exchange of the cold rows to their owners
 //   5. owned experts on the received rows, grouped by (source rank, expert)
 //   6. NCCL exchange of the result rows back
@@ -382,7 +383,15 @@ extern "C" apt_status apt_moe_ep_forward(apt_moe_ep *ep, const uint16_t *x, int 
     // 1. route, dispatch, gather: rows sorted [hot | cold by destination rank]
     EP_APT(ep, ep->router,
            apt_moe_ep_dispatch(ep->router, x, T, ep->idx, ep->w, ep->rows, ep->counts, stream));
-    // 2. replicated experts beside the exchange (hot rows open the buffer)
+    // 2. counts of the cold experts, exchanged first (a small NCCL op that must
+    //    not queue behind the replicated experts for SMs)
+    EP_NCCL(ep, nc.group_start());
+    for (int r = 0; r < N; ++r) {
+        EP_NCCL(ep, nc.send(ep->counts + R + r * C, C, ncclInt32, r, ep->comm, s));
+        EP_NCCL(ep, nc.recv(ep->recv_counts + r * C, C, ncclInt32, r, ep->comm, s));
+    }
+    EP_NCCL(ep, nc.group_end());
+    // 3. replicated experts beside the exchange (hot rows open the buffer)
     if (R) {
         EP_CUDA(ep, cudaEventRecord(ep->ev_fork, s));
         EP_CUDA(ep, cudaStreamWaitEvent(ep->side, ep->ev_fork, 0));
@@ -390,13 +399,7 @@ extern "C" apt_status apt_moe_ep_forward(apt_moe_ep *ep, const uint16_t *x, int 
                apt_moe_experts_grouped(ep->hot, ep->rows, T * K, ep->counts, ep->hot_ge, R,
                                        ep->back, ep->side));
     }
-    // 3. counts of the cold experts, exchanged; one host sync for the splits
-    EP_NCCL(ep, nc.group_start());
-    for (int r = 0; r < N; ++r) {
-        EP_NCCL(ep, nc.send(ep->counts + R + r * C, C, ncclInt32, r, ep->comm, s));
-        EP_NCCL(ep, nc.recv(ep->recv_counts + r * C, C, ncclInt32, r, ep->comm, s));
-    }
-    EP_NCCL(ep, nc.group_end());
+    // one host sync for the splits
     EP_CUDA(ep, cudaMemcpyAsync(ep->h_counts, ep->counts, sizeof(int32_t) * E,
                                 cudaMemcpyDeviceToHost, s));
     EP_CUDA(ep, cudaMemcpyAsync(ep->h_recv, ep->recv_counts, sizeof(int32_t) * N * C,

@@ -27,9 +27,9 @@ send buffer.
 
 Per step (one process per GPU, torch.distributed over NCCL for the plumbing):
   1. apt_moe_ep_dispatch: route, top-K, dispatch, gather rows
-  2. hot rows: apt_moe_experts_grouped on a side stream, straight into the
-     return buffer, overlapping 3-6
-  3. all_to_all of the per-expert cold counts, one host sync for the splits
+  2. all_to_all of the per-expert cold counts
+  3. hot rows: apt_moe_experts_grouped on a side stream, straight into the
+     return buffer, overlapping 4-6; then one host sync for the splits
   4. all_to_all of the cold rows to their owners
   5. apt_moe_experts_grouped on the received rows, grouped by (source rank,
      local expert), in place -> unweighted expert rows
@@ -232,8 +232,13 @@ class ExpertParallelMoE:
         mark("dispatch")
         Rh = self.n_hot
         back = torch.empty_like(rows)
-        # 1. replicated experts: their rows open the sorted buffer and their group
-        #    sizes are on the device, so this is queued before any host sync and
+        # 1. per-(destination rank, local cold expert) counts, exchanged first:
+        #    a small NCCL op that must not queue behind the replicated experts
+        cold_counts = counts[Rh:].contiguous()
+        recv_counts = torch.empty_like(cold_counts)
+        dist.all_to_all_single(recv_counts, cold_counts, group=self.group)
+        # 2. replicated experts: their rows open the sorted buffer and their group
+        #    sizes are on the device, so this is queued before the host sync and
         #    runs beside the exchange below
         hot_side = Rh > 0 and self._side is not None
         if Rh:
@@ -247,10 +252,6 @@ class ExpertParallelMoE:
                 hot_counts.record_stream(self._side)
             else:
                 self.backend.experts(rows, hot_counts, self.hot_expert, out=back, hot=True)
-        # 2. per-(destination rank, local cold expert) counts, exchanged
-        cold_counts = counts[Rh:].contiguous()
-        recv_counts = torch.empty_like(cold_counts)
-        dist.all_to_all_single(recv_counts, cold_counts, group=self.group)
         both = torch.cat([cold_counts.view(N, C_loc).sum(1), recv_counts.view(N, C_loc).sum(1),
                           counts[:Rh].sum().view(1)]).cpu()  # one host sync for the splits
         mark("counts")
