@@ -367,7 +367,12 @@ def run_ours(args):
            "h2d_bytes_per_step": sum(SWEEP) * H * 2, "d2h_bytes_per_step": sum(SWEEP) * H * 2}
 
     prefill = run_prefill(blk, dev, peaks, flush) if args.prefill else None
-    ep = run_ep(args, dev, world, rank) if (world > 1 and args.ep) else None
+    ep = None
+    if world > 1 and args.ep:
+        try:
+            ep = run_ep(args, dev, world, rank)
+        except Exception as e:  # the EP extra must not cost the headline line
+            ep = {"error": f"{type(e).__name__}: {e}"[:300]}
     quant = run_quant(dev, peaks, flush) if args.quant else None
 
     cpu = None
