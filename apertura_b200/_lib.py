@@ -20,7 +20,7 @@ EXPORTED = [
     "apt_moe_config_from_json", "apt_moe_create", "apt_moe_destroy", "apt_moe_clone_shared", "apt_moe_last_error",
     "apt_moe_version", "apt_moe_load_router", "apt_moe_load_experts_bf16",
     "apt_moe_load_experts_quant", "apt_moe_route", "apt_moe_route_weights", "apt_moe_experts",
-    "apt_moe_experts_dense", "apt_moe_forward", "apt_moe_layer_forward", "apt_moe_decoder_ff", "apt_moe_mlp_forward", "apt_moe_decoder_ff_full", "apt_moe_forward_host", "apt_moe_ep_dispatch",
+    "apt_moe_experts_dense", "apt_moe_forward", "apt_moe_layer_forward", "apt_moe_decoder_ff", "apt_moe_mlp_forward", "apt_moe_decoder_ff_full", "apt_moe_forward_host", "apt_moe_forward_host_async", "apt_moe_ep_dispatch",
     "apt_moe_ep_combine", "apt_moe_experts_grouped", "apt_moe_sync",
     "apt_moe_last_counts", "apt_moe_last_launches", "apt_moe_set_gemv_max_tokens",
     "apt_moe_set_gemm_pair", "apt_moe_set_sm_limit",
@@ -85,6 +85,7 @@ def lib():
         "apt_moe_experts_dense": ([hp, P, P, i32, P, P], i32),
         "apt_moe_forward": ([hp, P, P, i32, P, P, P, P], i32),
         "apt_moe_forward_host": ([hp, P, i32, P, P], i32),
+        "apt_moe_forward_host_async": ([hp, P, i32, P, P], i32),
         "apt_moe_layer_forward": ([hp, P, P, P, i32, P, P], i32),
         "apt_moe_decoder_ff": ([hp, P, P, P, P, P, P, i32, P, P], i32),
         "apt_moe_mlp_forward": ([hp, P, i32, P, P], i32),

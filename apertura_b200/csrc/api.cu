@@ -56,7 +56,8 @@ struct apt_moe_handle {
     // apt_moe_forward_host replays a CUDA graph of (copy in, block, copy out)
     // per (T, host buffers): one launch instead of a copy, ~5 kernels and a
     // copy.  Captured on a private stream (the legacy default stream cannot
-    // be captured); any change of weights or settings drops the cache.
+    // be captured) and launched on the caller's; any change of weights or
+    // settings drops the cache.
     struct HostGraph {
         int T;
         const void *x;
@@ -66,7 +67,6 @@ struct apt_moe_handle {
     };
     std::vector<HostGraph> graphs;
     cudaStream_t gstream = nullptr;
-    cudaEvent_t gev_in = nullptr, gev_out = nullptr;
     bool ev_used[APT_STAGE_COUNT] = {};
 
     // router
@@ -367,8 +367,6 @@ extern "C" apt_status apt_moe_destroy(apt_moe_handle *h) {
     for (void *p : ptrs) dfree(p);
     drop_graphs(h);
     if (h->gstream) cudaStreamDestroy(h->gstream);
-    if (h->gev_in) cudaEventDestroy(h->gev_in);
-    if (h->gev_out) cudaEventDestroy(h->gev_out);
     for (int i = 0; i < APT_STAGE_COUNT; ++i)
         for (int j = 0; j < 2; ++j)
             if (h->ev[i][j]) cudaEventDestroy(h->ev[i][j]);
@@ -1091,8 +1089,10 @@ extern "C" apt_status apt_moe_decoder_ff_full(apt_moe_handle *moe, apt_moe_handl
                               post_ff_ln_w, T, x2, stream);
 }
 
-extern "C" apt_status apt_moe_forward_host(apt_moe_handle *h, const uint16_t *x_host, int T,
-                                           uint16_t *out_host, void *stream) {
+namespace {
+
+apt_status forward_host_impl(apt_moe_handle *h, const uint16_t *x_host, int T,
+                             uint16_t *out_host, void *stream, bool sync) {
     if (!h) return APT_ERR_INVALID;
     if (check_T(h, T)) return APT_ERR_INVALID;
     if (T == 0) return APT_OK;
@@ -1109,7 +1109,7 @@ extern "C" apt_status apt_moe_forward_host(apt_moe_handle *h, const uint16_t *x_
         apt_status st = apt_moe_forward(h, h->xin, h->xin, T, h->xout, nullptr, nullptr, stream);
         if (st) return st;
         CUDA_TRY(h, cudaMemcpyAsync(out_host, h->xout, bytes, cudaMemcpyDeviceToHost, s));
-        CUDA_TRY(h, cudaStreamSynchronize(s));
+        if (sync) CUDA_TRY(h, cudaStreamSynchronize(s));
         return APT_OK;
     };
     if (no_graph || h->timing) return direct();
@@ -1119,8 +1119,6 @@ extern "C" apt_status apt_moe_forward_host(apt_moe_handle *h, const uint16_t *x_
     if (!hg) {
         if (!h->gstream) {
             CUDA_TRY(h, cudaStreamCreateWithFlags(&h->gstream, cudaStreamNonBlocking));
-            CUDA_TRY(h, cudaEventCreateWithFlags(&h->gev_in, cudaEventDisableTiming));
-            CUDA_TRY(h, cudaEventCreateWithFlags(&h->gev_out, cudaEventDisableTiming));
         }
         // capture; anything the capture refuses (pageable host memory, ...)
         // leaves the graph unset and the call runs the same kernels directly
@@ -1155,12 +1153,22 @@ extern "C" apt_status apt_moe_forward_host(apt_moe_handle *h, const uint16_t *x_
         hg = &h->graphs.back();
     }
     begin_call(h);
-    CUDA_TRY(h, cudaEventRecord(h->gev_in, s));
-    CUDA_TRY(h, cudaStreamWaitEvent(h->gstream, h->gev_in, 0));
-    CUDA_TRY(h, cudaGraphLaunch(hg->exec, h->gstream));
-    CUDA_TRY(h, cudaEventRecord(h->gev_out, h->gstream));
-    CUDA_TRY(h, cudaStreamWaitEvent(s, h->gev_out, 0));
+    // captured on the private stream, replayed on the caller's (any stream,
+    // the legacy default one included, may launch a graph)
+    CUDA_TRY(h, cudaGraphLaunch(hg->exec, s));
     h->launches = hg->launches;
-    CUDA_TRY(h, cudaStreamSynchronize(h->gstream));
+    if (sync) CUDA_TRY(h, cudaStreamSynchronize(s));
     return APT_OK;
+}
+
+}  // namespace
+
+extern "C" apt_status apt_moe_forward_host(apt_moe_handle *h, const uint16_t *x_host, int T,
+                                           uint16_t *out_host, void *stream) {
+    return forward_host_impl(h, x_host, T, out_host, stream, true);
+}
+
+extern "C" apt_status apt_moe_forward_host_async(apt_moe_handle *h, const uint16_t *x_host, int T,
+                                                 uint16_t *out_host, void *stream) {
+    return forward_host_impl(h, x_host, T, out_host, stream, false);
 }

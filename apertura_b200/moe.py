@@ -389,16 +389,21 @@ class MoEBlock:
             _stream(x1.device)))
         return x2
 
-    def forward_host(self, x_host: torch.Tensor, out_host: Optional[torch.Tensor] = None):
-        """End-to-end call with host buffers (pinned for speed)."""
+    def forward_host(self, x_host: torch.Tensor, out_host: Optional[torch.Tensor] = None,
+                     asynchronous: bool = False):
+        """End-to-end call with host buffers (pinned for speed).  With
+        asynchronous=True the copies and the block are only queued on the
+        current stream (apt_moe_forward_host_async): synchronise before reading
+        out_host or reusing x_host."""
         if x_host.is_cuda or x_host.dtype != torch.bfloat16:
             raise ValueError("x_host must be a CPU bfloat16 tensor")
         T = x_host.shape[0]
         if out_host is None:
             out_host = torch.empty(T, self.cfg.hidden_size, dtype=torch.bfloat16,
                                    pin_memory=x_host.is_pinned())
-        self.handle.check(lib().apt_moe_forward_host(self.handle.h, _ptr(x_host), T,
-                                                     _ptr(out_host), _stream(self.handle.device)))
+        fn = lib().apt_moe_forward_host_async if asynchronous else lib().apt_moe_forward_host
+        self.handle.check(fn(self.handle.h, _ptr(x_host), T, _ptr(out_host),
+                             _stream(self.handle.device)))
         return out_host
 
 

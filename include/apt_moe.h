@@ -232,6 +232,16 @@ APT_API apt_status apt_moe_forward_host(apt_moe_handle *h, const uint16_t *x_hos
                                 uint16_t *out_host, void *stream);
 
 /*
+ * apt_moe_forward_host without the final synchronisation: the copy in, the
+ * block and the copy out are queued on `stream` (x_host must stay unchanged
+ * and out_host unread until the stream reaches that point, e.g. after
+ * cudaStreamSynchronize or an event).  Consecutive calls on one handle are
+ * ordered; a decode engine can queue several and wait once.
+ */
+APT_API apt_status apt_moe_forward_host_async(apt_moe_handle *h, const uint16_t *x_host, int T,
+                                              uint16_t *out_host, void *stream);
+
+/*
  * Expert parallelism (no reference counterpart: the reference is one device).
  * The block splits at the token exchange:
  *   apt_moe_ep_dispatch: router + top-K + dispatch on this rank's tokens, and the

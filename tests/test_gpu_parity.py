@@ -258,3 +258,23 @@ def test_golden_hf_through_cuda(oracle, case):
     assert bad == 0
     ok, ma, cos = block_close(_f32(out), g["hf_out"])
     assert ok, (ma, cos)
+
+
+def test_forward_host_async_matches_device_path():
+    """apt_moe_forward_host_async: several queued calls on one handle (graph
+    replay and direct), one synchronisation, same results as the device call."""
+    cfg = A.ESModelConfig(moe_sparse=True, max_tokens=16)
+    ds = [block_inputs(T, seed=40 + T, device=DEV) for T in (1, 4, 16)]
+    d0 = ds[0]
+    blk = A.MoEBlock(cfg, d0["proj"], d0["scale"], d0["pes"], d0["gate_up"], d0["down"])
+    refs = [blk.forward(d["x"]).cpu() for d in ds]
+    xs = [d["x"].cpu().pin_memory() for d in ds]
+    outs = [torch.empty_like(x).pin_memory() for x in xs]
+    for _ in range(2):  # first pass captures the graphs, second replays them
+        for x, o in zip(xs, outs):
+            o.zero_()
+            blk.forward_host(x, o, asynchronous=True)
+        torch.cuda.synchronize()
+        for o, r in zip(outs, refs):
+            assert torch.equal(o, r)
+
