@@ -750,7 +750,7 @@ apt_status run_experts(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
     }
     STAGE(h, APT_STAGE_COMBINE, s,
           launch_combine(h->op, idx, w, d, T, Kp, H, out, s, &h->launches,
-                         h->cur_tail.post_w ? &h->cur_tail : nullptr));
+                         h->cur_tail.post_w ? &h->cur_tail : nullptr, h->errflag));
     return APT_OK;
 }
 
@@ -998,7 +998,7 @@ extern "C" apt_status apt_moe_ep_combine(apt_moe_handle *h, const uint16_t *rows
     cudaStream_t s = (cudaStream_t)stream;
     STAGE(h, APT_STAGE_COMBINE, s,
           launch_combine(rows, idx, w, h->disp(), T, h->cfg.top_k_experts, h->cfg.hidden_size,
-                         out, s, &h->launches));
+                         out, s, &h->launches, nullptr, h->errflag));
     return APT_OK;
 }
 

@@ -87,10 +87,12 @@ struct CombineTail {
     const uint16_t *resid;   // x1 [T,H]
     float eps;
 };
-// out[t] = bf16( sum_k f32(bf16(w[t,k] * op[inv[t*K+k]])) ), then the tail
+// out[t] = bf16( sum_k f32(bf16(w[t,k] * op[inv[t*K+k]])) ), then the tail.  With
+// err (bounded-wait error sink) and T >= 2 x SMs the bulk-copy form runs.
 cudaError_t launch_combine(const uint16_t *op, const int32_t *idx, const uint16_t *w,
                            const Dispatch &d, int T, int K, int H, uint16_t *out,
-                           cudaStream_t s, int *launches, const CombineTail *tail = nullptr);
+                           cudaStream_t s, int *launches, const CombineTail *tail = nullptr,
+                           int32_t *err = nullptr);
 
 // ---- decode GEMV (gemv.cu).  Weight formats: bits == 0 -> bf16, else affine.
 struct ExpertWeights {

@@ -63,6 +63,27 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, long l
     return true;
 }
 
+// Bounded wait that parks the thread in hardware between polls
+// (mbarrier.try_wait with a suspend-time hint of `hint_ns`): for many warps
+// waiting on one barrier, without a polling loop taking issue slots from the
+// warps that do work.  Gives up after `limit` clock cycles.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t hint_ns,
+                                                long long limit) {
+    const long long t0 = clock64();
+    while (true) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+            : "memory");
+        if (ok) return true;
+        if (clock64() - t0 > limit) return false;
+    }
+}
+
 // ---------------------------------------------------------------- TMA
 
 __device__ __forceinline__ void tma_prefetch(const CUtensorMap *map) {

@@ -22,6 +22,7 @@ DEV = torch.device("cuda", 0)
 @pytest.mark.parametrize("shape,T,sparse", [((2816, 128, 8, 704), 3, True),
                                             ((2816, 128, 8, 704), 100, True),
                                             ((2816, 128, 8, 704), 5, False),
+                                            ((2816, 128, 8, 704), 400, True),
                                             ((64, 16, 4, 64), 7, True)])
 def test_layer_forward_with_norms(oracle, shape, T, sparse):
     H, E, K, I = shape
@@ -54,7 +55,7 @@ def test_layer_forward_with_norms(oracle, shape, T, sparse):
 
 
 @pytest.mark.parametrize("shape,T", [((2816, 128, 8, 704), 4), ((2816, 128, 8, 704), 80),
-                                     ((64, 16, 4, 64), 7)])
+                                     ((2816, 128, 8, 704), 400), ((64, 16, 4, 64), 7)])
 def test_decoder_ff_tail(oracle, shape, T):
     """apt_moe_decoder_ff: x2 = x1 + post_ff_ln(post_ff_ln_1(hmlp) + post_ff_ln_2(MoE(x1)))."""
     H, E, K, I = shape
@@ -102,7 +103,7 @@ def test_dense_mlp(oracle, T):
     assert ok and ma <= 2.0 ** -6 * np.abs(refv).max(), (ma, cos)
 
 
-@pytest.mark.parametrize("T", [4, 80])
+@pytest.mark.parametrize("T", [4, 80, 320])
 def test_decoder_ff_full(oracle, T):
     """apt_moe_decoder_ff_full: the layer's whole feed-forward half from x1."""
     H, E, K, I, Id = 2816, 128, 8, 704, 2112
