@@ -711,7 +711,8 @@ apt_status run_experts(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
         const bool gather_in_gemm = !pair && rows_cap <= kGatherInGemmRows;
         if (!gather_in_gemm)
             STAGE(h, APT_STAGE_GATHER, s,
-                  launch_gather_rows(x, H, Kp, E, d, rows_cap, h->xp, s, &h->launches));
+                  launch_gather_rows(x, H, Kp, E, d, rows_cap, h->xp, s, &h->launches, idx, T,
+                                     h->errflag));
         if (pair) {
             STAGE(h, APT_STAGE_GATE_UP, s,
                   launch_gemm_pair_gateup(h->xp, d, nullptr, ew, rows_cap, H, I, E, E, h->yp,
@@ -981,7 +982,8 @@ extern "C" apt_status apt_moe_ep_dispatch(apt_moe_handle *h, const uint16_t *x, 
         STAGE(h, APT_STAGE_DISPATCH, s, launch_place(idx, h->idx2, T * K, E, d, s, &h->launches));
     }
     STAGE(h, APT_STAGE_GATHER, s,
-          launch_gather_rows(x, H, K, E, d, T * K, rows_out, s, &h->launches));
+          launch_gather_rows(x, H, K, E, d, T * K, rows_out, s, &h->launches, idx, T,
+                             h->errflag));
     CUDA_TRY(h, cudaMemcpyAsync(counts_out, h->counts, sizeof(int32_t) * E,
                                 cudaMemcpyDeviceToDevice, s));
     return APT_OK;

@@ -19,6 +19,10 @@ namespace apt {
 
 namespace {
 
+__device__ __forceinline__ void record_error(int32_t *err, int code, int where) {
+    if (atomicCAS(err, 0, code) == 0) err[1] = where;
+}
+
 __global__ void count_kernel(const int32_t *__restrict__ idx, int P, int E,
                              int32_t *__restrict__ counts) {
     for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < P; p += gridDim.x * blockDim.x) {
@@ -154,6 +158,98 @@ gather_rows_kernel(const uint16_t *__restrict__ x, int H, int K, const int32_t *
                     reinterpret_cast<const uint4 *>(x + (size_t)t1 * H)[v];
         }
     }
+}
+
+// Prefill-sized gather, token-major: each x row is read once into shared
+// memory by a bulk copy and written to its K routed rows of xp by bulk
+// stores, so x crosses HBM once instead of once per pair.  One warp per CTA,
+// several CTAs per SM; a ring of kGatherSlots rows, loads kGatherAhead tokens
+// ahead of the stores.  Measured at T = 8192 (8 pairs per token): 75 us
+// against 87 us for gather_rows_kernel.  Lane j*K+k looks up pair (token j of a batch, k).
+// Waits are bounded (error code 42 in err).
+constexpr int kGatherSlots = 8, kGatherAhead = 6;
+constexpr long long kGatherWaitLimit = 4000000000LL;
+
+struct GatherBulkArgs {
+    const uint16_t *x;
+    const int32_t *idx, *inv, *offsets;
+    int T, K, H, E, max_rows;
+    uint16_t *xp;
+    int32_t *err;
+};
+
+__device__ __forceinline__ void bulk_store(void *dst, const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+                 "r"(sm100::smem_u32(src)), "r"(bytes)
+                 : "memory");
+}
+
+template <int S, int L>
+__global__ void __launch_bounds__(32)
+gather_bulk_kernel(GatherBulkArgs a) {
+    using namespace sm100;
+    extern __shared__ __align__(128) uint8_t gb_smem[];
+    __shared__ uint64_t fullb[S];
+    const int K = a.K, H = a.H, lane = threadIdx.x;
+    const uint32_t row_bytes = (uint32_t)H * 2;
+    uint16_t *ring = reinterpret_cast<uint16_t *>(gb_smem);
+    if (lane == 0) {
+        for (int s = 0; s < S; ++s) mbar_init(&fullb[s], 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+    pdl_trigger();
+    pdl_wait();  // the dispatch this kernel reads is complete
+    const int rows = min(a.offsets[a.E], a.max_rows);
+    const int TPB = 32 / K, j_me = lane / K, k_me = lane % K;
+    const int n = a.T > (int)blockIdx.x ? (a.T - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    auto token = [&](int g) { return blockIdx.x + g * gridDim.x; };
+    auto fetch = [&](int g0) {  // destination row of pair (token g0 + j_me, k_me), or -1
+        const int g = g0 + j_me;
+        if (j_me >= TPB || g >= n) return -1;
+        const int p = token(g) * K + k_me;
+        const int e = a.idx[p], r = a.inv[p];
+        return (e >= 0 && r < rows) ? r : -1;
+    };
+    auto load = [&](int g) {
+        const int s = g % S;
+        mbar_arrive_expect_tx(&fullb[s], row_bytes);
+        bulk_load(ring + (size_t)s * H, a.x + (size_t)token(g) * H, row_bytes, &fullb[s]);
+    };
+    constexpr int kDepth = 3;  // batches of pair lookups in flight ahead of use
+    int dst[kDepth];
+#pragma unroll
+    for (int q = 0; q < kDepth; ++q) dst[q] = fetch(q * TPB);
+    if (lane == 0)
+        for (int g = 0; g < L && g < n; ++g) load(g);
+    for (int g0 = 0; g0 < n; g0 += TPB) {
+        const int d0 = dst[0];
+#pragma unroll
+        for (int q = 0; q + 1 < kDepth; ++q) dst[q] = dst[q + 1];
+        dst[kDepth - 1] = fetch(g0 + kDepth * TPB);
+        for (int j = 0; j < TPB && g0 + j < n; ++j) {
+            const int g = g0 + j;
+            if (g + L < n) {
+                // the slot of token g + L last held token g + L - S, whose
+                // stores were committed S - L - 1 groups ago
+                bulk_wait_read<S - L - 1>();
+                __syncwarp();
+                if (lane == 0) load(g + L);
+            }
+            // every lane observes the phase (the lanes' stores read the row)
+            const bool ok = __all_sync(
+                0xffffffffu, mbar_wait(&fullb[g % S], (g / S) & 1, kGatherWaitLimit));
+            if (!ok) {
+                if (lane == 0) record_error(a.err, 42, token(g));
+                bulk_wait<0>();
+                return;
+            }
+            if (j_me == j && d0 >= 0)
+                bulk_store(a.xp + (size_t)d0 * H, ring + (size_t)(g % S) * H, row_bytes);
+            bulk_commit();  // one group per token on every lane, empty or not
+        }
+    }
+    bulk_wait<0>();
 }
 
 // Block-wide sum of two values (all threads get both results).
@@ -342,9 +438,6 @@ struct CombineBulkArgs {
 
 constexpr long long kCombineWaitLimit = 4000000000LL;
 
-__device__ __forceinline__ void record_error(int32_t *err, int code, int where) {
-    if (atomicCAS(err, 0, code) == 0) err[1] = where;
-}
 
 __device__ __forceinline__ void consumer_bar(int nthreads) {
     asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
@@ -687,15 +780,31 @@ cudaError_t launch_dispatch(const int32_t *idx, int P, int E, const Dispatch &d,
 }
 
 cudaError_t launch_gather_rows(const uint16_t *x, int H, int K, int E, const Dispatch &d,
-                               int max_rows, uint16_t *xp, cudaStream_t s, int *launches) {
+                               int max_rows, uint16_t *xp, cudaStream_t s, int *launches,
+                               const int32_t *idx, int T, int32_t *err) {
     const int sms = num_sms(current_device());
+    if (idx && err && T >= 2 * sms && K <= 32 && H % 8 == 0 &&
+        !((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(xp)) & 15)) {
+        void (*kern)(GatherBulkArgs) = gather_bulk_kernel<kGatherSlots, kGatherAhead>;
+        const size_t smem = (size_t)kGatherSlots * H * 2;
+        if (smem <= 48 * 1024) {
+            // as many one-warp CTAs as fit, up to one token each
+            int occ = 0;
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 32, smem);
+            const int grid = min(T, grid_sms(current_device()) * (occ > 0 ? occ : 1));
+            GatherBulkArgs a{x, idx, d.inv, d.offsets, T, K, H, E, max_rows, xp, err};
+            cudaError_t r = launch_ex(kern, dim3(grid), dim3(32), smem, s, true, a);
+            if (launches) ++*launches;
+            return r;
+        }
+    }
     const int pairs_per_block = 4;  // 128 threads = 4 warps, a row pair each
     const int blocks = min(sms * 8, (max_rows + 2 * pairs_per_block - 1) / (2 * pairs_per_block));
-    cudaError_t err = launch_ex(gather_rows_kernel, dim3(blocks > 0 ? blocks : 1), dim3(128), 0, s,
-                                true, x, H, K, (const int32_t *)d.perm,
-                                (const int32_t *)d.offsets, E, max_rows, xp);
+    cudaError_t r = launch_ex(gather_rows_kernel, dim3(blocks > 0 ? blocks : 1), dim3(128), 0, s,
+                              true, x, H, K, (const int32_t *)d.perm,
+                              (const int32_t *)d.offsets, E, max_rows, xp);
     if (launches) ++*launches;
-    return err;
+    return r;
 }
 
 // Shared memory of combine_bulk_kernel at `stages` ring stages.

@@ -72,9 +72,12 @@ cudaError_t launch_dispatch(const int32_t *idx, int P, int E, const Dispatch &d,
 // active list, perm and inv in one launch
 cudaError_t launch_place(const int32_t *idx, const int32_t *rank, int P, int E, const Dispatch &d,
                          cudaStream_t s, int *launches);
-// xp[row] = x[perm[row] / K] for row < offsets[E]
+// xp[row] = x[perm[row] / K] for row < offsets[E].  With the routing (idx, T)
+// and a bounded-wait error sink, prefill-sized calls run token-major on bulk
+// copies (each x row read once).
 cudaError_t launch_gather_rows(const uint16_t *x, int H, int K, int E, const Dispatch &d,
-                               int max_rows, uint16_t *xp, cudaStream_t s, int *launches);
+                               int max_rows, uint16_t *xp, cudaStream_t s, int *launches,
+                               const int32_t *idx = nullptr, int T = 0, int32_t *err = nullptr);
 // Optional norms around the MoE output, applied by the combine
 // (ESDecoderLayer.mm:66-78).  post_w alone: out = post_ff_ln_2(moe).  With
 // mlp (+ mlp_w, ff_w, resid): out = resid + post_ff_ln(post_ff_ln_1(mlp) +

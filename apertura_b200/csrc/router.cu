@@ -283,22 +283,24 @@ __device__ __forceinline__ float fkey_inv(unsigned k) {
     return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
-__device__ __forceinline__ void select_core(float (&p)[kMaxPerLane], int E, int K, int lane,
+// NP = scores per lane (E <= 32 NP); E <= 128 scans 4 slots per lane per round.
+template <int NP>
+__device__ __forceinline__ void select_core(float (&p)[NP], int E, int K, int lane,
                                             int &sel_e, float &sel_p, float &sum) {
     float m = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < kMaxPerLane; ++j) m = fmaxf(m, p[j]);
+    for (int j = 0; j < NP; ++j) m = fmaxf(m, p[j]);
     m = fkey_inv(__reduce_max_sync(0xffffffffu, fkey(m)));
     float den = 0.f;
 #pragma unroll
-    for (int j = 0; j < kMaxPerLane; ++j) {
+    for (int j = 0; j < NP; ++j) {
         const int e = lane + 32 * j;
         p[j] = (e < E) ? expf(__fsub_rn(p[j], m)) : 0.f;
         den += p[j];
     }
     den = warp_sum(den);
 #pragma unroll
-    for (int j = 0; j < kMaxPerLane; ++j) {
+    for (int j = 0; j < NP; ++j) {
         const int e = lane + 32 * j;
         p[j] = (e < E) ? __fdiv_rn(p[j], den) : -1.f;  // -1: never selected
     }
@@ -310,7 +312,7 @@ __device__ __forceinline__ void select_core(float (&p)[kMaxPerLane], int E, int 
         float bp = -2.f;  // lane-local best among untaken (lowest id on ties)
         int be = 0x7fffffff;
 #pragma unroll
-        for (int j = 0; j < kMaxPerLane; ++j) {
+        for (int j = 0; j < NP; ++j) {
             const int e = lane + 32 * j;
             if (!((taken >> j) & 1u) && (p[j] > bp)) {
                 bp = p[j];
@@ -334,18 +336,26 @@ __device__ __forceinline__ void select_core(float (&p)[kMaxPerLane], int E, int 
 // Softmax, top-K (descending prob, lower id on ties), renormalise and
 // per-expert scale for one token, by one warp.  Lanes k < K return the k-th
 // choice in (sel_e, wk); other lanes return sel_e = -1.
-__device__ __forceinline__ void select_token(const float *__restrict__ sr,
-                                             const uint16_t *__restrict__ pes, int E, int K,
-                                             int lane, int &sel_e_out, float &wk_out) {
-    float p[kMaxPerLane];
+// One token's scores row into p (lane + 32 j), -inf past E.
+template <int NP>
+__device__ __forceinline__ void load_scores(const float *__restrict__ sr, int E, int lane,
+                                            float (&p)[NP]) {
 #pragma unroll
-    for (int j = 0; j < kMaxPerLane; ++j) {
+    for (int j = 0; j < NP; ++j) {
         const int e = lane + 32 * j;
         p[j] = (e < E) ? __ldcg(sr + e) : -INFINITY;  // written by other CTAs
     }
+}
+
+template <int NP>
+__device__ __forceinline__ void select_token(const float *__restrict__ sr,
+                                             const uint16_t *__restrict__ pes, int E, int K,
+                                             int lane, int &sel_e_out, float &wk_out) {
+    float p[NP];
+    load_scores<NP>(sr, E, lane, p);
     int sel_e;
     float sel_p, sum;
-    select_core(p, E, K, lane, sel_e, sel_p, sum);
+    select_core<NP>(p, E, K, lane, sel_e, sel_p, sum);
     wk_out = 0.f;
     sel_e_out = -1;
     if (lane < K) {
@@ -354,26 +364,42 @@ __device__ __forceinline__ void select_token(const float *__restrict__ sr,
     }
 }
 
-// One warp per token.
-__global__ void router_select(const float *__restrict__ scores, const uint16_t *__restrict__ pes,
-                              int T, int E, int K, int32_t *__restrict__ idx,
-                              uint16_t *__restrict__ w, int32_t *__restrict__ counts,
-                              int32_t *__restrict__ rank) {
+// One warp per token.  Slots in the experts' groups are claimed per block:
+// shared-memory atomics give each pair its place among the block's pairs of
+// the same expert, then one global atomic per (block, expert) reserves the
+// block's range -- under skewed routing most pairs go to a few experts, and
+// one global atomic per pair would serialise on those counters.
+constexpr int kSelectWarps = 32;
+
+template <int NP>
+__global__ void __launch_bounds__(kSelectWarps * 32)
+router_select(const float *__restrict__ scores, const uint16_t *__restrict__ pes, int T, int E,
+              int K, int32_t *__restrict__ idx, uint16_t *__restrict__ w,
+              int32_t *__restrict__ counts, int32_t *__restrict__ rank) {
+    __shared__ int s_cnt[kMaxPerLane * 32];
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
     pdl_trigger();
     pdl_wait();
-    if (warp >= T) return;
-    int e;
-    float wk;
-    select_token(scores + (size_t)warp * E, pes, E, K, lane, e, wk);
-    if (lane < K) {
-        idx[(size_t)warp * K + lane] = e;
-        w[(size_t)warp * K + lane] = f2bf(wk);
-        if (counts) {
-            const int r = atomicAdd(counts + e, 1);  // slot of this pair in its expert's group
-            if (rank) rank[(size_t)warp * K + lane] = r;
+    int e = -1, local = 0;
+    float wk = 0.f;
+    if (warp < T) {
+        select_token<NP>(scores + (size_t)warp * E, pes, E, K, lane, e, wk);
+        if (lane < K) {
+            idx[(size_t)warp * K + lane] = e;
+            w[(size_t)warp * K + lane] = f2bf(wk);
         }
     }
+    if (!counts) return;  // uniform over the block
+    __syncthreads();  // s_cnt zeroed
+    if (e >= 0) local = atomicAdd(&s_cnt[e], 1);
+    __syncthreads();
+    for (int x = threadIdx.x; x < E; x += blockDim.x) {
+        const int c = s_cnt[x];
+        s_cnt[x] = c > 0 ? atomicAdd(counts + x, c) : 0;  // base of this block's range
+    }
+    __syncthreads();
+    if (e >= 0 && rank) rank[(size_t)warp * K + lane] = s_cnt[e] + local;
 }
 
 // Decode-sized fused routing: the scores of router_scores_small; the last CTA
@@ -421,15 +447,17 @@ router_dispatch_small(const uint16_t *__restrict__ x, const uint16_t *__restrict
     {
         const int t = blockIdx.y * kSmallTok + warp;  // 8 warps, 8 tokens per chunk
         if (t < T) {
-            float p[kMaxPerLane];
-#pragma unroll
-            for (int j = 0; j < kMaxPerLane; ++j) {
-                const int e = lane + 32 * j;
-                p[j] = (e < E) ? __ldcg(scores + (size_t)t * E + e) : -INFINITY;
-            }
             int e;
             float sel_p, sum;
-            select_core(p, E, K, lane, e, sel_p, sum);
+            if (E <= 128) {
+                float p[4];
+                load_scores<4>(scores + (size_t)t * E, E, lane, p);
+                select_core<4>(p, E, K, lane, e, sel_p, sum);
+            } else {
+                float p[kMaxPerLane];
+                load_scores<kMaxPerLane>(scores + (size_t)t * E, E, lane, p);
+                select_core<kMaxPerLane>(p, E, K, lane, e, sel_p, sum);
+            }
             if (lane < K) {
                 idx[(size_t)t * K + lane] = e;
                 w[(size_t)t * K + lane] = f2bf(__fmul_rn(__fdiv_rn(sel_p, sum), s_pes[e]));
@@ -534,20 +562,44 @@ __global__ void router_norm_split(const uint16_t *__restrict__ x,
     }
     if (warp >= T) return;
     const uint16_t *xr = x + (size_t)warp * H;
+    // the row stays in registers (all of its loads in flight at once) when
+    // H <= 32 * 8 * kNormVec; longer rows are read twice
+    constexpr int kNormVec = 12;
+    const int nv = (H + 255) / 256;
+    const bool in_regs = nv <= kNormVec;
+    uint4 xv[kNormVec];
     float ss = 0.f;
-    for (int i = lane * 8; i < H; i += 256) {
-        float f[8];
-        unpack8(*reinterpret_cast<const uint4 *>(xr + i), f);
+    if (in_regs) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+        for (int q = 0; q < kNormVec; ++q) {
+            const int i = lane * 8 + q * 256;
+            if (q < nv && i < H) xv[q] = *reinterpret_cast<const uint4 *>(xr + i);
+        }
+#pragma unroll
+        for (int q = 0; q < kNormVec; ++q) {
+            const int i = lane * 8 + q * 256;
+            if (q < nv && i < H) {
+                float f[8];
+                unpack8(xv[q], f);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+            }
+        }
+    } else {
+        for (int i = lane * 8; i < H; i += 256) {
+            float f[8];
+            unpack8(*reinterpret_cast<const uint4 *>(xr + i), f);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+        }
     }
     ss = warp_sum(ss);
     const float r = 1.0f / sqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / (float)H), eps));
     uint16_t *d1 = hs + (size_t)warp * 2 * H;
     uint16_t *d2 = d1 + H;
-    for (int i = lane * 8; i < H; i += 256) {
+    auto emit = [&](int i, const uint4 &xq) {
         float f[8], sf[8];
-        unpack8(*reinterpret_cast<const uint4 *>(xr + i), f);
+        unpack8(xq, f);
         unpack8(*reinterpret_cast<const uint4 *>(scale + i), sf);
         float h1[8], h2[8];
 #pragma unroll
@@ -573,6 +625,15 @@ __global__ void router_norm_split(const uint16_t *__restrict__ x,
             v.z = pack_bf2(o[4], o[5]); v.w = pack_bf2(o[6], o[7]);
             *reinterpret_cast<uint4 *>(xn + (size_t)warp * H + i) = v;
         }
+    };
+    if (in_regs) {
+#pragma unroll
+        for (int q = 0; q < kNormVec; ++q) {
+            const int i = lane * 8 + q * 256;
+            if (q < nv && i < H) emit(i, xv[q]);
+        }
+    } else {
+        for (int i = lane * 8; i < H; i += 256) emit(i, *reinterpret_cast<const uint4 *>(xr + i));
     }
 }
 
@@ -710,9 +771,9 @@ cudaError_t launch_router_norm_split(const uint16_t *x, const uint16_t *scale, i
 cudaError_t launch_router_select(const float *scores, const uint16_t *pes, int T, int E, int K,
                                  int32_t *idx, uint16_t *w, int32_t *counts, cudaStream_t s,
                                  int *launches, int32_t *rank) {
-    const int warps_per_block = 8;
-    dim3 grid((T + warps_per_block - 1) / warps_per_block);
-    cudaError_t err = launch_ex(router_select, grid, dim3(warps_per_block * 32), 0, s, true,
+    dim3 grid((T + kSelectWarps - 1) / kSelectWarps);
+    cudaError_t err = launch_ex(E <= 128 ? router_select<4> : router_select<kMaxPerLane>, grid,
+                                dim3(kSelectWarps * 32), 0, s, true,
                                 (const float *)scores, pes, T, E, K, idx, w, counts, rank);
     if (launches) ++*launches;
     return err;
