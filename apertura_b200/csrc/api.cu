@@ -1093,6 +1093,18 @@ extern "C" apt_status apt_moe_decoder_ff_full(apt_moe_handle *moe, apt_moe_handl
 
 namespace {
 
+// Device address of a pinned host buffer, or null for pageable memory: under
+// unified addressing page-locked host memory is mapped into the device's
+// address space, so kernels may read and write it directly.
+void *mapped_host_ptr(const void *p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return nullptr;
+    }
+    return a.type == cudaMemoryTypeHost ? a.devicePointer : nullptr;
+}
+
 apt_status forward_host_impl(apt_moe_handle *h, const uint16_t *x_host, int T,
                              uint16_t *out_host, void *stream, bool sync) {
     if (!h) return APT_ERR_INVALID;
@@ -1106,11 +1118,37 @@ apt_status forward_host_impl(apt_moe_handle *h, const uint16_t *x_host, int T,
         const char *v = getenv("APT_NO_GRAPH");
         return v && atoi(v) != 0;
     }();
-    auto direct = [&]() -> apt_status {
-        CUDA_TRY(h, cudaMemcpyAsync(h->xin, x_host, bytes, cudaMemcpyHostToDevice, s));
-        apt_status st = apt_moe_forward(h, h->xin, h->xin, T, h->xout, nullptr, nullptr, stream);
+    // Pinned buffers (sparse path, 16-byte aligned): x is staged in by a kernel
+    // that reads the host buffer and the combine writes the result straight
+    // into out_host, so no copy-engine transfer sits between the step's
+    // kernels.  Pageable buffers go through cudaMemcpyAsync.
+    const uint16_t *x_map = nullptr;
+    uint16_t *out_map = nullptr;
+    if (h->cfg.moe_sparse && h->cfg.hidden_size % 8 == 0) {
+        x_map = static_cast<const uint16_t *>(mapped_host_ptr(x_host));
+        out_map = static_cast<uint16_t *>(mapped_host_ptr(out_host));
+        if (!x_map || !out_map ||
+            ((reinterpret_cast<uintptr_t>(x_map) | reinterpret_cast<uintptr_t>(out_map)) & 15))
+            x_map = nullptr, out_map = nullptr;
+    }
+    // the whole step on stream `cs`: copy in, block, copy out
+    auto enqueue = [&](cudaStream_t cs, int *launches) -> apt_status {
+        if (x_map) {
+            CUDA_TRY(h, launch_copy16(x_map, h->xin, bytes, cs, nullptr));
+            apt_status st = apt_moe_forward(h, h->xin, h->xin, T, out_map, nullptr, nullptr, cs);
+            h->launches += 1;  // the staging kernel (the call's counter starts in the forward)
+            if (launches) *launches = h->launches;
+            return st;
+        }
+        CUDA_TRY(h, cudaMemcpyAsync(h->xin, x_host, bytes, cudaMemcpyHostToDevice, cs));
+        apt_status st = apt_moe_forward(h, h->xin, h->xin, T, h->xout, nullptr, nullptr, cs);
+        if (launches) *launches = h->launches;
         if (st) return st;
-        CUDA_TRY(h, cudaMemcpyAsync(out_host, h->xout, bytes, cudaMemcpyDeviceToHost, s));
+        CUDA_TRY(h, cudaMemcpyAsync(out_host, h->xout, bytes, cudaMemcpyDeviceToHost, cs));
+        return APT_OK;
+    };
+    auto direct = [&]() -> apt_status {
+        if (apt_status st = enqueue(s, nullptr)) return st;
         if (sync) CUDA_TRY(h, cudaStreamSynchronize(s));
         return APT_OK;
     };
@@ -1129,17 +1167,9 @@ apt_status forward_host_impl(apt_moe_handle *h, const uint16_t *x_host, int T,
         apt_status st = APT_OK;
         int launches = 0;
         if (cudaStreamBeginCapture(h->gstream, cudaStreamCaptureModeRelaxed) == cudaSuccess) {
-            cudaError_t e1 = cudaMemcpyAsync(h->xin, x_host, bytes, cudaMemcpyHostToDevice,
-                                             h->gstream);
-            if (e1 == cudaSuccess) {
-                st = apt_moe_forward(h, h->xin, h->xin, T, h->xout, nullptr, nullptr, h->gstream);
-                launches = h->launches;
-                if (st == APT_OK)
-                    e1 = cudaMemcpyAsync(out_host, h->xout, bytes, cudaMemcpyDeviceToHost,
-                                         h->gstream);
-            }
+            st = enqueue(h->gstream, &launches);
             const cudaError_t e2 = cudaStreamEndCapture(h->gstream, &graph);
-            if (st == APT_OK && e1 == cudaSuccess && e2 == cudaSuccess && graph &&
+            if (st == APT_OK && e2 == cudaSuccess && graph &&
                 cudaGraphInstantiateWithFlags(&exec, graph, 0) != cudaSuccess)
                 exec = nullptr;
             if (graph) cudaGraphDestroy(graph);

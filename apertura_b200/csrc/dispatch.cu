@@ -903,4 +903,34 @@ cudaError_t launch_fill_mlp_routing(int32_t *idx, uint16_t *w, int n, cudaStream
     return e;
 }
 
+namespace {
+
+// 16-byte copy by SM loads and stores: moves a host buffer (pinned and mapped,
+// read over the host link) into device memory as a kernel, so the step's next
+// kernel follows it by programmatic dependent launch instead of waiting on a
+// copy-engine transfer.
+__global__ void __launch_bounds__(256) copy16_kernel(const uint4 *__restrict__ src,
+                                                     uint4 *__restrict__ dst, size_t n) {
+    pdl_trigger();
+    pdl_wait();  // dst may still be read by the stream's previous kernels
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x)
+        dst[i] = src[i];
+}
+
+}  // namespace
+
+cudaError_t launch_copy16(const void *src, void *dst, size_t bytes, cudaStream_t s,
+                          int *launches) {
+    const size_t n = bytes / 16;
+    const size_t want = (n + 255) / 256;
+    const int cap = 4 * num_sms(current_device());
+    const int blocks = want < (size_t)cap ? (int)(want > 0 ? want : 1) : cap;
+    cudaError_t e = launch_ex(copy16_kernel, dim3(blocks), dim3(256), 0, s, true,
+                              reinterpret_cast<const uint4 *>(src), reinterpret_cast<uint4 *>(dst),
+                              n);
+    if (launches) ++*launches;
+    return e;
+}
+
 }  // namespace apt

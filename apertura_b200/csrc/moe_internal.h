@@ -78,6 +78,10 @@ cudaError_t launch_place(const int32_t *idx, const int32_t *rank, int P, int E, 
 cudaError_t launch_gather_rows(const uint16_t *x, int H, int K, int E, const Dispatch &d,
                                int max_rows, uint16_t *xp, cudaStream_t s, int *launches,
                                const int32_t *idx = nullptr, int T = 0, int32_t *err = nullptr);
+// dst[0, bytes) = src[0, bytes) by a kernel (bytes % 16 == 0, both 16-byte
+// aligned; src may be mapped pinned host memory)
+cudaError_t launch_copy16(const void *src, void *dst, size_t bytes, cudaStream_t s,
+                          int *launches);
 // Optional norms around the MoE output, applied by the combine
 // (ESDecoderLayer.mm:66-78).  post_w alone: out = post_ff_ln_2(moe).  With
 // mlp (+ mlp_w, ff_w, resid): out = resid + post_ff_ln(post_ff_ln_1(mlp) +

@@ -427,6 +427,7 @@ router_dispatch_small(const uint16_t *__restrict__ x, const uint16_t *__restrict
     __shared__ float s_pes[256];
     RT_STAMP(0);
     pdl_trigger();
+    pdl_wait();  // launched early behind the stream's previous kernel; x may be its output
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // per_expert_scale for the select phase, fetched while the scores run
     for (int e = tid; e < E; e += blockDim.x) s_pes[e] = bf2f(pes[e]);
@@ -724,11 +725,11 @@ cudaError_t launch_router_dispatch(const uint16_t *x, const uint16_t *proj, cons
     const float root = (float)(1.0 / sqrt((double)H));
     const size_t smem = (size_t)(T < kSmallTok ? T : kSmallTok) * H * sizeof(float) + H * 2;
     dim3 grid((E + kSmallWarps - 1) / kSmallWarps, (T + kSmallTok - 1) / kSmallTok);
-    router_dispatch_small<<<grid, kSmallThreads, smem, s>>>(x, proj, scale, pes, T, H, E, K,
-                                                               eps, root, scores, idx, w, d, done,
-                                                               pre_w, xn);
+    cudaError_t err = launch_ex(router_dispatch_small, grid, dim3(kSmallThreads), smem, s, true,
+                                x, proj, scale, pes, T, H, E, K, eps, root, scores, idx, w, d,
+                                done, pre_w, xn);
     if (launches) ++*launches;
-    return cudaGetLastError();
+    return err;
 }
 
 cudaError_t launch_router_scores(const uint16_t *x, const uint16_t *proj, const uint16_t *scale,

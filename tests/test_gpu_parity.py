@@ -214,12 +214,33 @@ def test_deterministic(gemma16):
     assert torch.equal(a.view(torch.int16), b.view(torch.int16))
 
 
-def test_forward_host_matches_device(gemma16):
+@pytest.mark.parametrize("pinned", [True, False])
+def test_forward_host_matches_device(gemma16, pinned):
+    """Pinned buffers: x staged in by a kernel reading host memory, the combine
+    writing out_host directly.  Pageable buffers: copy-engine transfers."""
     d = gemma16
     blk = make_block(d, sparse=True)
     dev_out = blk.forward(d["x"]).cpu()
-    host_out = blk.forward_host(d["x"].cpu().pin_memory())
+    xh = d["x"].cpu()
+    host_out = blk.forward_host(xh.pin_memory() if pinned else xh)
+    assert host_out.is_pinned() == pinned
     assert torch.equal(dev_out.view(torch.int16), host_out.view(torch.int16))
+
+
+def test_forward_host_prefill_size():
+    """A prefill-sized call through the host entry point (bulk-copy gather and
+    combine, the combine storing into the pinned output)."""
+    T = 400
+    cfg = A.ESModelConfig(moe_sparse=True, max_tokens=T)
+    d = block_inputs(T, seed=77, device=DEV)
+    blk = A.MoEBlock(cfg, d["proj"], d["scale"], d["pes"], d["gate_up"], d["down"])
+    ref = blk.forward(d["x"]).cpu()
+    out = torch.empty(T, 2816, dtype=torch.bfloat16).pin_memory()
+    for _ in range(2):
+        out.zero_()
+        blk.forward_host(d["x"].cpu().pin_memory(), out, asynchronous=True)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
 
 
 def test_errors_are_reported():
