@@ -221,7 +221,11 @@ APT_API apt_status apt_moe_decoder_ff_full(apt_moe_handle *moe, apt_moe_handle *
 /*
  * Same as apt_moe_forward with HOST buffers: copies x to the device, runs
  * the block, copies out back and synchronises the stream.  x_host [T,H],
- * out_host [T,H] bf16.  With pinned buffers the sequence is captured once per
+ * out_host [T,H] bf16.  Pinned (page-locked, hence device-mapped) 16-byte
+ * aligned buffers are moved by kernels: x is read from the host buffer by a
+ * staging kernel and the combine stores the result directly into out_host
+ * (sparse configurations); other buffers go through cudaMemcpyAsync.  With
+ * pinned buffers the sequence is captured once per
  * (T, x_host, out_host) as a CUDA graph and replayed on later calls, so a
  * pinned buffer passed here must stay allocated and pinned while the handle
  * is used with it (a freed buffer's address reused for pageable memory is
