@@ -222,33 +222,55 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, Args a) {
         fence_barrier_init();
         tma_prefetch(&tmW);
     }
-    pdl_trigger();
-    pdl_wait();  // the dispatch / gate_up output this kernel reads is complete
-    const int items = *a.n_active * NRB;
-    __syncthreads();
+    __syncthreads();  // barriers initialised
     const int NK = LEN / S::KC;
     int g = 0, u = 0;
+    // one weight stage of unit (e, blk0) into the ring (producer lane only)
+    auto stage = [&](int e, int blk0, int kc, int item) -> bool {
+        const int s = g % STAGES;
+        if (!mbar_wait(&empty[s], ((g / STAGES) & 1) ^ 1, kWaitLimit)) {
+            record_error(a.err, 10, item);
+            return false;
+        }
+        mbar_arrive_expect_tx(&full[s], S::STAGE_BYTES);
+        uint8_t *dst = ring + s * S::STAGE_BYTES;
+        if (EPI == GATEUP) {
+            const int r0 = e * 2 * a.I + blk0;
+            tma_load_2d(dst, &tmW, &full[s], kc * S::KC, r0);
+            tma_load_2d(dst + S::STAGE_BYTES / 2, &tmW, &full[s], kc * S::KC, r0 + a.I);
+        } else {
+            tma_load_2d(dst, &tmW, &full[s], kc * S::KC, e * a.H + blk0);
+        }
+        ++g;
+        return true;
+    };
+    // Launch order: gate_up lets its dependent (this kernel's DOWN form) start
+    // only after its own wait, i.e. once the routing and dispatch are
+    // complete.  DOWN may then read the dispatch and stream the first weight
+    // stages of its first item while gate_up is still running; it waits for
+    // gate_up's output (its token rows) before loading any of them.
+    int items, pre = 0;  // pre: weight stages of the first unit already issued
+    if constexpr (EPI == GATEUP) {
+        pdl_wait();  // the dispatch this kernel reads is complete
+        pdl_trigger();
+        items = *a.n_active * NRB;
+    } else {
+        pdl_trigger();
+        items = *a.n_active * NRB;
+        if (warp == kComputeWarps && lane == 0 && (int)blockIdx.x < items) {
+            const int item = blockIdx.x;
+            const int e = a.active[item / NRB], blk0 = (item % NRB) * rows_per_blk;
+            const int lead = NK < STAGES ? NK : STAGES;
+            for (; pre < lead; ++pre)
+                if (!stage(e, blk0, pre, item)) {
+                    pre = -1;
+                    break;
+                }
+        }
+        pdl_wait();  // gate_up's rows (this kernel's operands) are complete
+    }
     if (warp == kComputeWarps) {
-        if (lane != 0) return;
-        // one weight stage of unit (e, blk0) into the ring
-        auto stage = [&](int e, int blk0, int kc, int item) -> bool {
-            const int s = g % STAGES;
-            if (!mbar_wait(&empty[s], ((g / STAGES) & 1) ^ 1, kWaitLimit)) {
-                record_error(a.err, 10, item);
-                return false;
-            }
-            mbar_arrive_expect_tx(&full[s], S::STAGE_BYTES);
-            uint8_t *dst = ring + s * S::STAGE_BYTES;
-            if (EPI == GATEUP) {
-                const int r0 = e * 2 * a.I + blk0;
-                tma_load_2d(dst, &tmW, &full[s], kc * S::KC, r0);
-                tma_load_2d(dst + S::STAGE_BYTES / 2, &tmW, &full[s], kc * S::KC, r0 + a.I);
-            } else {
-                tma_load_2d(dst, &tmW, &full[s], kc * S::KC, e * a.H + blk0);
-            }
-            ++g;
-            return true;
-        };
+        if (lane != 0 || pre < 0) return;
         for (int item = blockIdx.x; item < items; item += gridDim.x) {
             const int e = a.active[item / NRB], blk0 = (item % NRB) * rows_per_blk;
             const int n = a.counts[e], base = a.offsets[e];
@@ -256,8 +278,9 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, Args a) {
                 // the weight stream first (it needs only e); the unit's operands
                 // need the dispatch order, one more dependent load
                 const int lead = NK < STAGES ? NK : STAGES;
-                for (int kc = 0; kc < lead; ++kc)
+                for (int kc = pre; kc < lead; ++kc)
                     if (!stage(e, blk0, kc, item)) return;
+                pre = 0;  // only the first unit was started early
                 const int b = u & 1;
                 if (!mbar_wait(&uempty[b], ((u >> 1) & 1) ^ 1, kWaitLimit)) {
                     record_error(a.err, 13, item);
