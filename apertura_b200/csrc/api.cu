@@ -881,7 +881,8 @@ apt_status forward_impl(apt_moe_handle *h, const uint16_t *x_router, const uint1
         STAGE(h, APT_STAGE_ROUTER_SCORES, s,
               launch_router_dispatch(x_router, h->proj, h->scale, h->pes, T, H, E, K,
                                      h->cfg.rms_norm_eps, h->scores, idx, w, h->disp(), h->done,
-                                     s, &h->launches, pre_w, pre_w ? h->xn : nullptr));
+                                     s, &h->launches, pre_w, pre_w ? h->xn : nullptr,
+                                     h->errflag));
         return run_experts(h, x_experts, idx, w, T, K, quant, out, s, true);
     }
     if (apt_status st = router_scores(h, x_router, T, s, pre_w)) return st;
@@ -972,7 +973,7 @@ extern "C" apt_status apt_moe_ep_dispatch(apt_moe_handle *h, const uint16_t *x, 
         STAGE(h, APT_STAGE_ROUTER_SCORES, s,
               launch_router_dispatch(x, h->proj, h->scale, h->pes, T, H, E, K,
                                      h->cfg.rms_norm_eps, h->scores, idx, w, d, h->done, s,
-                                     &h->launches));
+                                     &h->launches, nullptr, nullptr, h->errflag));
     } else {
         if (apt_status st = router_scores(h, x, T, s)) return st;
         CUDA_TRY(h, cudaMemsetAsync(h->counts, 0, sizeof(int32_t) * E, s));

@@ -38,7 +38,8 @@ cudaError_t launch_router_dispatch(const uint16_t *x, const uint16_t *proj, cons
                                    const uint16_t *pes, int T, int H, int E, int K, float eps,
                                    float *scores, int32_t *idx, uint16_t *w, const Dispatch &d,
                                    int32_t *done, cudaStream_t s, int *launches,
-                                   const uint16_t *pre_w = nullptr, uint16_t *xn = nullptr);
+                                   const uint16_t *pre_w = nullptr, uint16_t *xn = nullptr,
+                                   int32_t *err = nullptr);
 // Tensor-core router path: two-term bf16 split of the f32 router input, then
 // an f32-output tcgen05 GEMM against proj (gemm_sm100.cu).
 // pre_w/xn (optional): also write xn = RMSNorm(x) * pre_w (pre_ff_ln_2)

@@ -15,6 +15,7 @@
 #include "common.cuh"
 #include "launch_util.h"
 #include "moe_internal.h"
+#include "sm100_ptx.cuh"
 
 namespace apt {
 
@@ -22,7 +23,7 @@ namespace {
 
 constexpr int kSmallTok = 8;     // tokens staged per CTA in the decode kernel
 constexpr int kSmallWarps = 4;   // experts per CTA in the decode kernel
-constexpr int kSmallThreads = 256;  // 8 warps: 4 experts x 2 token groups
+constexpr int kSmallThreads = 256;  // 8 warps per decode router CTA
 
 // Phase timestamps (%globaltimer, thread 0 of each CTA) for tuning builds
 // compiled with -DAPT_ROUTER_TRACE; absent from the library build.
@@ -64,126 +65,121 @@ __device__ __forceinline__ float router_h(float x, float r, float sc, float root
     return __fmul_rn(__fmul_rn(__fmul_rn(x, r), sc), root);
 }
 
-// Scores of experts [blockIdx.x*4, +4) for tokens [blockIdx.y*8, +8).  All
-// global reads the phase needs (the warp's proj row, the scale vector and its
-// tokens' rows) are issued before any is consumed, so the phase costs one
-// memory round trip; h is then staged in shared memory for the dot products.
+// Scores of experts [blockIdx.x*4, +4) for tokens [blockIdx.y*8, +8).  The
+// chunk's token rows, the CTA's 4 proj rows and the scale vector arrive in
+// shared memory by bulk copies issued at entry (one memory round trip).  Each
+// thread then owns 8-element slices of the hidden axis: it reads every staged
+// row once (16-byte, conflict-free), forms h = ((x r) scale) root for the
+// chunk's tokens in registers and keeps all 4 x 8 partial dot products; a warp
+// sum and a sum over the 8 warps finish them.  Shared-memory reads are one
+// pass over 13 rows, where a warp-per-(expert, token-group) mapping re-reads
+// every staged h row once per expert.
+// Dynamic shared memory: (min(T, 8) + kSmallWarps + 1) rows of H bf16.
 constexpr int kMaxVec = 12;  // H <= 12 * 256
+constexpr long long kRouterWaitLimit = 4000000000LL;
+
+__host__ __device__ constexpr size_t scores_small_smem(int T, int H) {
+    return (size_t)((T < kSmallTok ? T : kSmallTok) + kSmallWarps + 1) * H * 2;
+}
 
 __device__ __forceinline__ void scores_small_block(const uint16_t *__restrict__ x,
                                                    const uint16_t *__restrict__ proj,
                                                    const uint16_t *__restrict__ scale, int T,
                                                    int H, int E, float eps, float root,
-                                                   float *__restrict__ scores, float *hs,
+                                                   float *__restrict__ scores, uint16_t *sm,
                                                    const uint16_t *__restrict__ pre_w = nullptr,
-                                                   uint16_t *__restrict__ xn = nullptr) {
+                                                   uint16_t *__restrict__ xn = nullptr,
+                                                   int32_t *__restrict__ err = nullptr) {
+    __shared__ __align__(8) uint64_t s_bar;
+    __shared__ float s_part[kSmallThreads / 32][kSmallWarps * kSmallTok];
+    __shared__ float s_r[kSmallTok];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int e = blockIdx.x * kSmallWarps + (warp & (kSmallWarps - 1));
-    const int tg = warp / kSmallWarps;  // token group of this warp in the dot phase
+    const int e0 = blockIdx.x * kSmallWarps;
+    const int ne = min(kSmallWarps, E - e0);
     const int t0 = blockIdx.y * kSmallTok;
     const int nt = min(kSmallTok, T - t0);
-    const int nv = H / 256;
-    // the scale vector into shared memory, the token row (its sum of squares
-    // is on the critical path) and the warp's proj row into registers: all
-    // issued before any is consumed
-    uint16_t *s_scale = reinterpret_cast<uint16_t *>(hs + min(T, kSmallTok) * H);
-    for (int v = threadIdx.x; v < H / 8; v += blockDim.x)
-        reinterpret_cast<uint4 *>(s_scale)[v] = __ldg(reinterpret_cast<const uint4 *>(scale) + v);
-    uint4 xv[kMaxVec];
-    if (warp < nt) {  // warp w stages token w
-        const uint16_t *xr = x + (size_t)(t0 + warp) * H + lane * 8;
-#pragma unroll
-        for (int i = 0; i < kMaxVec; ++i)
-            if (i < nv) xv[i] = __ldg(reinterpret_cast<const uint4 *>(xr + i * 256));
+    const int nts = min(T, kSmallTok);  // staged token rows
+    uint16_t *s_x = sm;                      // [nts][H]
+    uint16_t *s_p = sm + (size_t)nts * H;    // [kSmallWarps][H]
+    uint16_t *s_scale = s_p + (size_t)kSmallWarps * H;
+    if (threadIdx.x == 0) {
+        sm100::mbar_init(&s_bar, 1);
+        sm100::fence_barrier_init();
+        const uint32_t row_bytes = (uint32_t)H * 2;
+        sm100::mbar_arrive_expect_tx(&s_bar, (uint32_t)(nt + ne + 1) * row_bytes);
+        sm100::bulk_load(s_scale, scale, row_bytes, &s_bar);
+        sm100::bulk_load(s_p, proj + (size_t)e0 * H, (uint32_t)ne * row_bytes, &s_bar);
+        sm100::bulk_load(s_x, x + (size_t)t0 * H, (uint32_t)nt * row_bytes, &s_bar);
     }
-    uint4 pv[kMaxVec];
-    const uint16_t *pr = proj + (size_t)(e < E ? e : 0) * H + lane * 8;
-#pragma unroll
-    for (int i = 0; i < kMaxVec; ++i)
-        if (i < nv) pv[i] = __ldg(reinterpret_cast<const uint4 *>(pr + i * 256));
-    __syncthreads();  // s_scale complete
+    __syncthreads();  // barrier initialised
+    if (!sm100::mbar_wait(&s_bar, 0, kRouterWaitLimit) && err && threadIdx.x == 0)
+        atomicCAS(err, 0, 30);  // rows never arrived: the scores of this call are invalid
     RT_STAMP(7);
+    const int nch = H / 8;  // 8-element slices
+    // r_t = 1/sqrt(mean(x_t^2) + eps): warp w sums token w
     if (warp < nt) {
         float ss = 0.f;
+        for (int c = lane; c < nch; c += 32) {
+            float f[8];
+            unpack8(*reinterpret_cast<const uint4 *>(s_x + (size_t)warp * H + c * 8), f);
 #pragma unroll
-        for (int i = 0; i < kMaxVec; ++i)
-            if (i < nv) {
-                float f[8];
-                unpack8(xv[i], f);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
-            }
-        ss = warp_sum(ss);
-        const float r = 1.0f / sqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / (float)H), eps));
-        float *dst = hs + warp * H + lane * 8;
-#pragma unroll
-        for (int i = 0; i < kMaxVec; ++i)
-            if (i < nv) {
-                float f[8], sf[8], hv[8];
-                unpack8(xv[i], f);
-                unpack8(*reinterpret_cast<const uint4 *>(s_scale + i * 256 + lane * 8), sf);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) hv[j] = router_h(f[j], r, sf[j], root);
-                *reinterpret_cast<float4 *>(dst + i * 256) = make_float4(hv[0], hv[1], hv[2], hv[3]);
-                *reinterpret_cast<float4 *>(dst + i * 256 + 4) = make_float4(hv[4], hv[5], hv[6], hv[7]);
-            }
-        // pre_ff_ln_2(x1) as a by-product: the same r, times the norm weight
-        // (ESRMSNorm.mm:21-26), written once per token (expert group 0)
-        if (xn && blockIdx.x == 0) {
-            uint16_t *xo = xn + (size_t)(t0 + warp) * H + lane * 8;
-#pragma unroll
-            for (int i = 0; i < kMaxVec; ++i)
-                if (i < nv) {
-                    float f[8], wf[8];
-                    unpack8(xv[i], f);
-                    unpack8(__ldg(reinterpret_cast<const uint4 *>(pre_w + i * 256 + lane * 8)), wf);
-                    uint4 o;
-                    o.x = pack_bf2(__fmul_rn(__fmul_rn(f[0], r), wf[0]), __fmul_rn(__fmul_rn(f[1], r), wf[1]));
-                    o.y = pack_bf2(__fmul_rn(__fmul_rn(f[2], r), wf[2]), __fmul_rn(__fmul_rn(f[3], r), wf[3]));
-                    o.z = pack_bf2(__fmul_rn(__fmul_rn(f[4], r), wf[4]), __fmul_rn(__fmul_rn(f[5], r), wf[5]));
-                    o.w = pack_bf2(__fmul_rn(__fmul_rn(f[6], r), wf[6]), __fmul_rn(__fmul_rn(f[7], r), wf[7]));
-                    *reinterpret_cast<uint4 *>(xo + i * 256) = o;
-                }
+            for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
         }
+        ss = warp_sum(ss);
+        if (lane == 0) s_r[warp] = 1.0f / sqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / (float)H), eps));
     }
     __syncthreads();
-    RT_STAMP(8);
-    constexpr int TPW = kSmallTok / (kSmallThreads / 32 / kSmallWarps);  // tokens per warp
-    if (e < E) {
-        float acc[TPW];
+    float acc[kSmallWarps][kSmallTok];
 #pragma unroll
-        for (int q = 0; q < TPW; ++q) acc[q] = 0.f;
+    for (int q = 0; q < kSmallWarps; ++q)
 #pragma unroll
-        for (int i = 0; i < kMaxVec; ++i)
-            if (i < nv) {
-                float p[8];
-                unpack8(pv[i], p);
+        for (int t = 0; t < kSmallTok; ++t) acc[q][t] = 0.f;
+    const bool wxn = xn && blockIdx.x == 0;  // pre_ff_ln_2(x1), once per token
+    for (int c = threadIdx.x; c < nch; c += blockDim.x) {
+        float sf[8], p[kSmallWarps][8];
+        unpack8(*reinterpret_cast<const uint4 *>(s_scale + c * 8), sf);
 #pragma unroll
-                for (int q = 0; q < TPW; ++q) {
-                    const int t = tg + q * (kSmallThreads / 32 / kSmallWarps);
-                    if (t < nt) {
-                        const float *hr = hs + t * H + i * 256 + lane * 8;
-                        const float4 a4 = *reinterpret_cast<const float4 *>(hr);
-                        const float4 b4 = *reinterpret_cast<const float4 *>(hr + 4);
-                        float s2 = acc[q];
-                        s2 = fmaf(p[0], a4.x, s2);
-                        s2 = fmaf(p[1], a4.y, s2);
-                        s2 = fmaf(p[2], a4.z, s2);
-                        s2 = fmaf(p[3], a4.w, s2);
-                        s2 = fmaf(p[4], b4.x, s2);
-                        s2 = fmaf(p[5], b4.y, s2);
-                        s2 = fmaf(p[6], b4.z, s2);
-                        s2 = fmaf(p[7], b4.w, s2);
-                        acc[q] = s2;
-                    }
-                }
+        for (int q = 0; q < kSmallWarps; ++q)
+            if (q < ne) unpack8(*reinterpret_cast<const uint4 *>(s_p + (size_t)q * H + c * 8), p[q]);
+#pragma unroll
+        for (int t = 0; t < kSmallTok; ++t) {
+            if (t >= nt) break;
+            float f[8], hv[8];
+            unpack8(*reinterpret_cast<const uint4 *>(s_x + (size_t)t * H + c * 8), f);
+            const float r = s_r[t];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) hv[j] = router_h(f[j], r, sf[j], root);
+#pragma unroll
+            for (int q = 0; q < kSmallWarps; ++q)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[q][t] = fmaf(p[q][j], hv[j], acc[q][t]);
+            if (wxn) {
+                float wf[8];
+                unpack8(__ldg(reinterpret_cast<const uint4 *>(pre_w + c * 8)), wf);
+                uint4 o;
+                o.x = pack_bf2(__fmul_rn(__fmul_rn(f[0], r), wf[0]), __fmul_rn(__fmul_rn(f[1], r), wf[1]));
+                o.y = pack_bf2(__fmul_rn(__fmul_rn(f[2], r), wf[2]), __fmul_rn(__fmul_rn(f[3], r), wf[3]));
+                o.z = pack_bf2(__fmul_rn(__fmul_rn(f[4], r), wf[4]), __fmul_rn(__fmul_rn(f[5], r), wf[5]));
+                o.w = pack_bf2(__fmul_rn(__fmul_rn(f[6], r), wf[6]), __fmul_rn(__fmul_rn(f[7], r), wf[7]));
+                *reinterpret_cast<uint4 *>(xn + (size_t)(t0 + t) * H + c * 8) = o;
             }
-#pragma unroll
-        for (int q = 0; q < TPW; ++q) {
-            const int t = tg + q * (kSmallThreads / 32 / kSmallWarps);
-            const float v = warp_sum(acc[q]);
-            if (lane == 0 && t < nt) scores[(size_t)(t0 + t) * E + e] = v;
         }
+    }
+    // sum the partials: over the warp's lanes, then over the 8 warps
+#pragma unroll
+    for (int q = 0; q < kSmallWarps; ++q)
+#pragma unroll
+        for (int t = 0; t < kSmallTok; ++t) {
+            const float v = warp_sum(acc[q][t]);
+            if (lane == 0) s_part[warp][q * kSmallTok + t] = v;
+        }
+    __syncthreads();
+    if (threadIdx.x < kSmallWarps * kSmallTok) {
+        const int q = threadIdx.x / kSmallTok, t = threadIdx.x % kSmallTok;
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kSmallThreads / 32; ++w) v += s_part[w][threadIdx.x];
+        if (q < ne && t < nt) scores[(size_t)(t0 + t) * E + e0 + q] = v;
     }
 }
 
@@ -191,8 +187,8 @@ __global__ void __launch_bounds__(kSmallThreads)
 router_scores_small(const uint16_t *__restrict__ x, const uint16_t *__restrict__ proj,
                     const uint16_t *__restrict__ scale, int T, int H, int E, float eps,
                     float root, float *__restrict__ scores) {
-    extern __shared__ float hs[];  // [kSmallTok][H]
-    scores_small_block(x, proj, scale, T, H, E, eps, root, scores, hs);
+    extern __shared__ __align__(16) uint16_t rs_smem[];
+    scores_small_block(x, proj, scale, T, H, E, eps, root, scores, rs_smem);
 }
 
 // Register-tiled f32 GEMM: CTA = 64 tokens x 64 experts, 256 threads, each
@@ -418,8 +414,8 @@ router_dispatch_small(const uint16_t *__restrict__ x, const uint16_t *__restrict
                       int H, int E, int K, float eps, float root, float *__restrict__ scores,
                       int32_t *__restrict__ idx, uint16_t *__restrict__ w, Dispatch d,
                       int32_t *__restrict__ done, const uint16_t *__restrict__ pre_w,
-                      uint16_t *__restrict__ xn) {
-    extern __shared__ float hs[];
+                      uint16_t *__restrict__ xn, int32_t *__restrict__ err) {
+    extern __shared__ __align__(16) uint16_t rs_smem[];
     __shared__ int s_last;
     __shared__ int s_idx[kFusedMaxPairs];
     __shared__ int s_cnt[256];
@@ -431,7 +427,7 @@ router_dispatch_small(const uint16_t *__restrict__ x, const uint16_t *__restrict
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // per_expert_scale for the select phase, fetched while the scores run
     for (int e = tid; e < E; e += blockDim.x) s_pes[e] = bf2f(pes[e]);
-    scores_small_block(x, proj, scale, T, H, E, eps, root, scores, hs, pre_w, xn);
+    scores_small_block(x, proj, scale, T, H, E, eps, root, scores, rs_smem, pre_w, xn, err);
     RT_STAMP(1);
     // level 1: the last CTA of this token chunk selects the chunk's tokens
     __threadfence();
@@ -721,15 +717,15 @@ cudaError_t launch_router_dispatch(const uint16_t *x, const uint16_t *proj, cons
                                    const uint16_t *pes, int T, int H, int E, int K, float eps,
                                    float *scores, int32_t *idx, uint16_t *w, const Dispatch &d,
                                    int32_t *done, cudaStream_t s, int *launches,
-                                   const uint16_t *pre_w, uint16_t *xn) {
+                                   const uint16_t *pre_w, uint16_t *xn, int32_t *err) {
     const float root = (float)(1.0 / sqrt((double)H));
-    const size_t smem = (size_t)(T < kSmallTok ? T : kSmallTok) * H * sizeof(float) + H * 2;
+    const size_t smem = scores_small_smem(T, H);
     dim3 grid((E + kSmallWarps - 1) / kSmallWarps, (T + kSmallTok - 1) / kSmallTok);
-    cudaError_t err = launch_ex(router_dispatch_small, grid, dim3(kSmallThreads), smem, s, true,
-                                x, proj, scale, pes, T, H, E, K, eps, root, scores, idx, w, d,
-                                done, pre_w, xn);
+    cudaError_t r = launch_ex(router_dispatch_small, grid, dim3(kSmallThreads), smem, s, true,
+                              x, proj, scale, pes, T, H, E, K, eps, root, scores, idx, w, d,
+                              done, pre_w, xn, err);
     if (launches) ++*launches;
-    return err;
+    return r;
 }
 
 cudaError_t launch_router_scores(const uint16_t *x, const uint16_t *proj, const uint16_t *scale,
@@ -737,7 +733,7 @@ cudaError_t launch_router_scores(const uint16_t *x, const uint16_t *proj, const 
                                  int *launches) {
     const float root = (float)(1.0 / sqrt((double)H));
     if (T <= 64 && H % 256 == 0 && H <= 256 * kMaxVec) {
-        const size_t smem = (size_t)(T < kSmallTok ? T : kSmallTok) * H * sizeof(float) + H * 2;
+        const size_t smem = scores_small_smem(T, H);
         dim3 grid((E + kSmallWarps - 1) / kSmallWarps, (T + kSmallTok - 1) / kSmallTok);
         router_scores_small<<<grid, kSmallThreads, smem, s>>>(x, proj, scale, T, H, E, eps,
                                                                  root, scores);
