@@ -18,6 +18,7 @@
 #include <cstring>
 #include <string>
 #include <memory>
+#include <initializer_list>
 #include <vector>
 
 #include "../../include/apt_moe.h"
@@ -213,6 +214,21 @@ void drop_graphs(apt_moe_handle *h) {
     for (auto &g : h->graphs) cudaGraphExecDestroy(g.exec);
     h->graphs.clear();
 }
+
+// Activations and norm weights are read and written with 16-byte vector
+// accesses and bulk copies, so each such device pointer must be 16-byte
+// aligned (what any allocator returns).  Checked at the entry points.
+bool aligned16(std::initializer_list<const void *> ps) {
+    for (const void *p : ps)
+        if (reinterpret_cast<uintptr_t>(p) & 15) return false;
+    return true;
+}
+
+#define CHECK_ALIGNED(h, ...)                                                                \
+    do {                                                                                     \
+        if (!aligned16({__VA_ARGS__}))                                                       \
+            return fail((h), APT_ERR_INVALID, "activation / norm buffers must be 16-byte aligned"); \
+    } while (0)
 
 void begin_call(apt_moe_handle *h) {
     h->launches = 0;
@@ -798,6 +814,7 @@ extern "C" apt_status apt_moe_route(apt_moe_handle *h, const uint16_t *x, int T,
     if (!h->proj) return fail(h, APT_ERR_STATE, "router weights not loaded");
     if (T == 0) return APT_OK;
     if (!x || !idx || !w) return fail(h, APT_ERR_INVALID, "null pointer");
+    CHECK_ALIGNED(h, x);
     DeviceGuard g(h->cfg.device);
     cudaStream_t s = (cudaStream_t)stream;
     begin_call(h);
@@ -830,6 +847,7 @@ extern "C" apt_status apt_moe_experts(apt_moe_handle *h, const uint16_t *x, cons
     if (check_T(h, T)) return APT_ERR_INVALID;
     if (T == 0) return APT_OK;
     if (!x || !idx || !w || !out) return fail(h, APT_ERR_INVALID, "null pointer");
+    CHECK_ALIGNED(h, x, out);
     DeviceGuard g(h->cfg.device);
     begin_call(h);
     return experts_sparse(h, x, idx, w, T, out, (cudaStream_t)stream, false);
@@ -842,6 +860,7 @@ extern "C" apt_status apt_moe_experts_dense(apt_moe_handle *h, const uint16_t *x
     if (check_T(h, T)) return APT_ERR_INVALID;
     if (T == 0) return APT_OK;
     if (!x || !W || !out) return fail(h, APT_ERR_INVALID, "null pointer");
+    CHECK_ALIGNED(h, x, out);
     DeviceGuard g(h->cfg.device);
     begin_call(h);
     return experts_dense(h, x, W, T, out, (cudaStream_t)stream);
@@ -860,6 +879,7 @@ apt_status forward_impl(apt_moe_handle *h, const uint16_t *x_router, const uint1
     if (T == 0) return APT_OK;
     if (!x_router || !out) return fail(h, APT_ERR_INVALID, "null pointer");
     if (!x_experts) x_experts = x_router;
+    CHECK_ALIGNED(h, x_router, x_experts, out, pre_w);
     if (!h->proj) return fail(h, APT_ERR_STATE, "router weights not loaded");
     DeviceGuard g(h->cfg.device);
     cudaStream_t s = (cudaStream_t)stream;
@@ -922,6 +942,7 @@ extern "C" apt_status apt_moe_layer_forward(apt_moe_handle *h, const uint16_t *x
     if (!h) return APT_ERR_INVALID;
     if (!pre_ff_ln_2_w || !post_ff_ln_2_w) return fail(h, APT_ERR_INVALID, "null norm weight");
     if (h->cfg.hidden_size % 8) return fail(h, APT_ERR_UNSUPPORTED, "hidden_size % 8");
+    CHECK_ALIGNED(h, pre_ff_ln_2_w, post_ff_ln_2_w);
     CombineTail tail{};
     tail.post_w = post_ff_ln_2_w;
     tail.eps = h->cfg.rms_norm_eps;
@@ -938,6 +959,7 @@ extern "C" apt_status apt_moe_decoder_ff(apt_moe_handle *h, const uint16_t *x1,
     if (!x1 || !hmlp || !x2) return fail(h, APT_ERR_INVALID, "null pointer");
     if (!pre_ff_ln_2_w || !post_ff_ln_1_w || !post_ff_ln_2_w || !post_ff_ln_w)
         return fail(h, APT_ERR_INVALID, "null norm weight");
+    CHECK_ALIGNED(h, x1, hmlp, x2, pre_ff_ln_2_w, post_ff_ln_1_w, post_ff_ln_2_w, post_ff_ln_w);
     if (h->cfg.hidden_size % 8) return fail(h, APT_ERR_UNSUPPORTED, "hidden_size % 8");
     if (x2 == x1 || x2 == hmlp)
         return fail(h, APT_ERR_INVALID, "x2 must not alias x1 or hmlp");
@@ -963,6 +985,7 @@ extern "C" apt_status apt_moe_ep_dispatch(apt_moe_handle *h, const uint16_t *x, 
     if (T == 0) return APT_OK;
     if (!x || !idx || !w || !rows_out || !counts_out)
         return fail(h, APT_ERR_INVALID, "null pointer");
+    CHECK_ALIGNED(h, x, rows_out);
     if (!h->proj) return fail(h, APT_ERR_STATE, "router weights not loaded");
     DeviceGuard g(h->cfg.device);
     cudaStream_t s = (cudaStream_t)stream;
@@ -997,6 +1020,7 @@ extern "C" apt_status apt_moe_ep_combine(apt_moe_handle *h, const uint16_t *rows
     if (check_T(h, T)) return APT_ERR_INVALID;
     if (T == 0) return APT_OK;
     if (!rows || !idx || !w || !out) return fail(h, APT_ERR_INVALID, "null pointer");
+    CHECK_ALIGNED(h, rows, out);
     DeviceGuard g(h->cfg.device);
     cudaStream_t s = (cudaStream_t)stream;
     STAGE(h, APT_STAGE_COMBINE, s,
@@ -1015,6 +1039,7 @@ extern "C" apt_status apt_moe_experts_grouped(apt_moe_handle *h, const uint16_t 
     if (R == 0) return APT_OK;
     if (!rows || !group_counts || !group_expert || !out || G <= 0 || G > 256)
         return fail(h, APT_ERR_INVALID, "bad grouped-experts arguments");
+    CHECK_ALIGNED(h, rows, out);
     if (!h->gu) return fail(h, APT_ERR_STATE, "bf16 expert weights not loaded");
     const int H = h->cfg.hidden_size, I = h->cfg.moe_intermediate_size, E = h->cfg.num_experts;
     if (!gemm_supported(H, I)) return fail(h, APT_ERR_UNSUPPORTED, "shape not covered by the GEMM");
@@ -1052,6 +1077,7 @@ extern "C" apt_status apt_moe_mlp_forward(apt_moe_handle *h, const uint16_t *x, 
     if (check_T(h, T)) return APT_ERR_INVALID;
     if (T == 0) return APT_OK;
     if (!x || !out) return fail(h, APT_ERR_INVALID, "null pointer");
+    CHECK_ALIGNED(h, x, out);
     if (h->cfg.num_experts != 1 || h->cfg.top_k_experts != 1)
         return fail(h, APT_ERR_STATE, "an MLP handle has num_experts = top_k_experts = 1");
     DeviceGuard g(h->cfg.device);
@@ -1074,6 +1100,7 @@ extern "C" apt_status apt_moe_decoder_ff_full(apt_moe_handle *moe, apt_moe_handl
     if (check_T(mlp, T)) return APT_ERR_INVALID;
     if (T == 0) return APT_OK;
     if (!x1 || !x2 || !pre_ff_ln_w) return fail(moe, APT_ERR_INVALID, "null pointer");
+    CHECK_ALIGNED(moe, x1, x2, pre_ff_ln_w);
     if (mlp->cfg.device != moe->cfg.device || mlp->cfg.hidden_size != moe->cfg.hidden_size)
         return fail(moe, APT_ERR_INVALID, "MLP and MoE handles differ in device or hidden size");
     {

@@ -13,6 +13,10 @@
  *   - bf16 tensors are passed as uint16_t* holding raw bf16 bits, row-major.
  *   - Pointers marked "device" are CUDA device pointers on the handle's
  *     device; "host" pointers are ordinary host memory (pinned for speed).
+ *   - Activation buffers ([T,H] / [rows,H] inputs and outputs) and norm
+ *     weights must be 16-byte aligned (any CUDA allocation is); a misaligned
+ *     one is refused with APT_ERR_INVALID.  Weights given to the loaders are
+ *     copied and have no such requirement.
  *   - `stream` is a cudaStream_t passed as void* (NULL = legacy stream).  All
  *     compute entry points are stream-ordered and asynchronous.
  *   - A handle is not re-entrant: callers serialise calls per handle.

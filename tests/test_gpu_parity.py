@@ -256,6 +256,12 @@ def test_errors_are_reported():
         h.check(A.lib().apt_moe_experts(h.h, x.data_ptr(), idx.data_ptr(), w.data_ptr(), 8,
                                         x.data_ptr(), None))
     assert ei.value.status == 1
+    # a misaligned activation pointer is refused at the boundary (nothing launches)
+    h2 = A.Handle(A.ESModelConfig(max_tokens=4))
+    with pytest.raises(A.AptError) as ei:
+        h2.check(A.lib().apt_moe_forward(h2.h, x.data_ptr() + 2, None, 2, x.data_ptr(), None,
+                                         None, None))
+    assert ei.value.status == 1 and "aligned" in str(ei.value)
 
 
 # ------------------------------------------------------------------ golden
