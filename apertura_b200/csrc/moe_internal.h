@@ -23,14 +23,18 @@ cudaError_t gemm_init();
 
 // ---- router (router.cu)
 // scores [T,E] f32 = (((x*rsqrt(mean(x^2)+eps))*scale)*H^-1/2) . proj^T
+// err (optional): set to 30 by the T <= 64 kernel when its staged rows never arrive
 cudaError_t launch_router_scores(const uint16_t *x, const uint16_t *proj, const uint16_t *scale,
                                  int T, int H, int E, float eps, float *scores,
-                                 cudaStream_t s, int *launches);
+                                 cudaStream_t s, int *launches, int32_t *err = nullptr);
 // softmax + top-K + renorm + per-expert scale; optional per-expert counts
 // rank (optional, needs counts): each pair's slot in its expert group (atomic)
+// err (optional): when the word is non-zero (the score kernel's bounded wait
+// gave up), every idx of the call is written as -1 and every w as 0
 cudaError_t launch_router_select(const float *scores, const uint16_t *pes, int T, int E, int K,
                                  int32_t *idx, uint16_t *w, int32_t *counts, cudaStream_t s,
-                                 int *launches, int32_t *rank = nullptr);
+                                 int *launches, int32_t *rank = nullptr,
+                                 const int32_t *err = nullptr);
 // Decode-sized fused router + dispatch (one launch): writes idx/w and the full
 // Dispatch.  `done` is a zero-initialised device counter the kernel resets.
 bool router_dispatch_fusable(int T, int H, int E, int K);

@@ -2,12 +2,15 @@
 //
 // The reference quantises the bf16 expert banks once at load when quantBits > 0
 // (aptransformer/ESExperts.mm:13-18, via mx::quantize, ml-explore/mlx @ 057cdc9ec).
-// This kernel applies MLX's published affine scheme per group of `gs` values
-// along the input axis:
-//   scale = (max - min) / (2^bits - 1)  (clamped below at 1e-7), bias = min,
-//   both stored as bf16; q = clamp(rint((w - bias) / scale), 0, 2^bits - 1)
-//   computed against the stored bf16 scale and bias; 32/bits values per uint32,
-//   element i at bit (i*bits) % 32 of word i*bits/32 (low bits first).
+// This kernel applies MLX's affine rule (mlx/fast.cpp `affine_quantize` at that
+// commit) per group of `gs` values along the input axis, in f32:
+//   n = 2^bits - 1; mask = |min| > |max|
+//   scale = max((max - min) / n, 1e-7), negated when !mask
+//   edge = mask ? min : max;  q0 = rint(edge / scale)
+//   if q0 != 0: scale = edge / q0 (zero becomes a code);  bias = q0 ? edge : 0
+//   q = clamp(rint((w - bias) / scale), 0, n) with the f32 scale and bias,
+// then scale and bias are stored as bf16; 32/bits values per uint32, element i
+// at bit (i*bits) % 32 of word i*bits/32 (low bits first).
 #include "common.cuh"
 #include "launch_util.h"
 #include "moe_internal.h"
@@ -33,12 +36,17 @@ __global__ void quantize_affine_kernel(const uint16_t *__restrict__ w, int64_t r
         mx = fmaxf(mx, v);
     }
     const int qmax = (1 << bits) - 1;
+    const bool mask = fabsf(mn) > fabsf(mx);
     float s = __fdiv_rn(__fsub_rn(mx, mn), (float)qmax);
     if (s < 1e-7f) s = 1e-7f;
-    const uint16_t sb = f2bf(s), bb = f2bf(mn);
-    sc[r * ng + g] = sb;
-    bi[r * ng + g] = bb;
-    const float sq = bf2f(sb), bq = bf2f(bb);
+    if (!mask) s = -s;
+    const float edge = mask ? mn : mx;
+    const float q0 = rintf(__fdiv_rn(edge, s));
+    if (q0 != 0.f) s = __fdiv_rn(edge, q0);
+    const float bq = q0 == 0.f ? 0.f : edge;
+    const float sq = s;
+    sc[r * ng + g] = f2bf(sq);
+    bi[r * ng + g] = f2bf(bq);
     const int per_word = 32 / bits;
     uint32_t *dst = q + (r * cols + (int64_t)g * gs) / per_word;
     for (int i = 0; i < gs; i += per_word) {

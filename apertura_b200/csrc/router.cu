@@ -186,9 +186,9 @@ __device__ __forceinline__ void scores_small_block(const uint16_t *__restrict__ 
 __global__ void __launch_bounds__(kSmallThreads)
 router_scores_small(const uint16_t *__restrict__ x, const uint16_t *__restrict__ proj,
                     const uint16_t *__restrict__ scale, int T, int H, int E, float eps,
-                    float root, float *__restrict__ scores) {
+                    float root, float *__restrict__ scores, int32_t *__restrict__ err) {
     extern __shared__ __align__(16) uint16_t rs_smem[];
-    scores_small_block(x, proj, scale, T, H, E, eps, root, scores, rs_smem);
+    scores_small_block(x, proj, scale, T, H, E, eps, root, scores, rs_smem, nullptr, nullptr, err);
 }
 
 // Register-tiled f32 GEMM: CTA = 64 tokens x 64 experts, 256 threads, each
@@ -371,7 +371,8 @@ template <int NP>
 __global__ void __launch_bounds__(kSelectWarps * 32)
 router_select(const float *__restrict__ scores, const uint16_t *__restrict__ pes, int T, int E,
               int K, int32_t *__restrict__ idx, uint16_t *__restrict__ w,
-              int32_t *__restrict__ counts, int32_t *__restrict__ rank) {
+              int32_t *__restrict__ counts, int32_t *__restrict__ rank,
+              const int32_t *__restrict__ err) {
     __shared__ int s_cnt[kMaxPerLane * 32];
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
@@ -379,6 +380,13 @@ router_select(const float *__restrict__ scores, const uint16_t *__restrict__ pes
     pdl_wait();
     int e = -1, local = 0;
     float wk = 0.f;
+    if (err && __ldcg(err) != 0) {  // the scores of this call never arrived: mark it invalid
+        if (warp < T && lane < K) {
+            idx[(size_t)warp * K + lane] = -1;
+            w[(size_t)warp * K + lane] = 0;
+        }
+        return;
+    }
     if (warp < T) {
         select_token<NP>(scores + (size_t)warp * E, pes, E, K, lane, e, wk);
         if (lane < K) {
@@ -730,13 +738,13 @@ cudaError_t launch_router_dispatch(const uint16_t *x, const uint16_t *proj, cons
 
 cudaError_t launch_router_scores(const uint16_t *x, const uint16_t *proj, const uint16_t *scale,
                                  int T, int H, int E, float eps, float *scores, cudaStream_t s,
-                                 int *launches) {
+                                 int *launches, int32_t *err) {
     const float root = (float)(1.0 / sqrt((double)H));
     if (T <= 64 && H % 256 == 0 && H <= 256 * kMaxVec) {
         const size_t smem = scores_small_smem(T, H);
         dim3 grid((E + kSmallWarps - 1) / kSmallWarps, (T + kSmallTok - 1) / kSmallTok);
         router_scores_small<<<grid, kSmallThreads, smem, s>>>(x, proj, scale, T, H, E, eps,
-                                                                 root, scores);
+                                                                 root, scores, err);
     } else {
         dim3 grid((E + kEB - 1) / kEB, (T + kTT - 1) / kTT);
         router_scores_tiled<<<grid, 256, 0, s>>>(x, proj, scale, T, H, E, eps, root, scores);
@@ -767,13 +775,13 @@ cudaError_t launch_router_norm_split(const uint16_t *x, const uint16_t *scale, i
 
 cudaError_t launch_router_select(const float *scores, const uint16_t *pes, int T, int E, int K,
                                  int32_t *idx, uint16_t *w, int32_t *counts, cudaStream_t s,
-                                 int *launches, int32_t *rank) {
+                                 int *launches, int32_t *rank, const int32_t *err) {
     dim3 grid((T + kSelectWarps - 1) / kSelectWarps);
-    cudaError_t err = launch_ex(E <= 128 ? router_select<4> : router_select<kMaxPerLane>, grid,
-                                dim3(kSelectWarps * 32), 0, s, true,
-                                (const float *)scores, pes, T, E, K, idx, w, counts, rank);
+    cudaError_t r = launch_ex(E <= 128 ? router_select<4> : router_select<kMaxPerLane>, grid,
+                              dim3(kSelectWarps * 32), 0, s, true,
+                              (const float *)scores, pes, T, E, K, idx, w, counts, rank, err);
     if (launches) ++*launches;
-    return err;
+    return r;
 }
 
 cudaError_t launch_scatter_dense(const int32_t *idx, const uint16_t *w, int T, int E, int K,

@@ -366,6 +366,10 @@ APT_API apt_status apt_moe_stage_times(apt_moe_handle *h, float *ms);
  * device address (no allocation); make that first call outside any stream
  * capture.  Every call shares the array, so two calls that overlap on the GPU
  * (different streams, or different host threads) race; serialise them.
+ * x, proj and scale must be 16-byte aligned (else APT_ERR_INVALID, nothing
+ * launched).  If the score kernel's bounded wait for its staged rows runs
+ * out, every idx of the call is written as -1 and every w as 0.  Calls made
+ * after a cudaDeviceReset of the device are not supported.
  * Requires hidden_size % 64 == 0, num_experts <= 256, top_k <= min(32, E).
  */
 #define APT_NOALLOC_MAX_SCORES 16384

@@ -207,14 +207,39 @@ void oracle_route_weights(const int32_t *idx, const uint16_t *w, int T, int E, i
 /* ---------------- affine quantisation (mx::quantize, affine mode) ---------------- */
 
 /*
- * MLX's published affine scheme, per group of `gs` consecutive elements along
- * the last (input) axis:  scale = (max - min) / (2^bits - 1), bias = min,
- * q = clamp(round((w - bias) / scale), 0, 2^bits - 1); scale and bias are
- * stored in bf16 (the weight dtype) and q is computed against the stored
- * values.  Packing: 32/bits values per uint32, element i of a row at word
- * i*bits/32, bit offset (i*bits) % 32 (low bits first).
+ * mx::quantize, affine mode (called at ESExperts.mm:14,16 and
+ * ESWeightLoader.mm:221), restated from MLX's published source at the pinned
+ * commit ml-explore/mlx @ 057cdc9ec (mlx/fast.cpp `affine_quantize`, the CPU
+ * fallback; the Metal kernel `affine_quantize` in
+ * mlx/backend/metal/kernels/quantized.h computes the same per-group values).
+ * Per group of `gs` consecutive elements along the last (input) axis, in f32:
+ *   n = 2^bits - 1;  mask = |min| > |max|
+ *   scale = max((max - min) / n, 1e-7), negated when !mask
+ *   edge  = mask ? min : max         (the larger-magnitude end)
+ *   q0 = rint(edge / scale);  if q0 != 0: scale = edge / q0  (zero lands on a code)
+ *   bias = q0 == 0 ? 0 : edge
+ *   q = clip(rint((w - bias) / scale), 0, n)   with the f32 scale and bias
+ * and only then are scale and bias stored as bf16 (the weight dtype).  The
+ * scale is negative when the group's larger-magnitude end is its maximum.
+ * Packing: 32/bits values per uint32, element i of a row at word i*bits/32,
+ * bit offset (i*bits) % 32 (low bits first), as MLX's power-of-two shifts.
  * w [rows, cols] bf16 -> q [rows, cols*bits/32] u32, s, b [rows, cols/gs] bf16.
+ * Dequantisation (mx::dequantize, gather_qmm): w = scale*q + bias with the
+ * stored bf16 scale and bias.
  */
+void oracle_affine_params(float mn, float mx, int bits, float *scale, float *bias) {
+    const float n = (float)((1 << bits) - 1);
+    const int mask = fabsf(mn) > fabsf(mx);
+    float sc = (mx - mn) / n;
+    if (sc < 1e-7f) sc = 1e-7f;
+    if (!mask) sc = -sc;
+    const float edge = mask ? mn : mx;
+    const float q0 = nearbyintf(edge / sc);
+    if (q0 != 0.0f) sc = edge / q0;
+    *scale = sc;
+    *bias = q0 == 0.0f ? 0.0f : edge;
+}
+
 int oracle_quantize_affine(const uint16_t *w, int64_t rows, int cols, int gs, int bits,
                            uint32_t *q, uint16_t *s, uint16_t *b) {
     if (bits != 4 && bits != 8) return 1;
@@ -234,16 +259,14 @@ int oracle_quantize_affine(const uint16_t *w, int64_t rows, int cols, int gs, in
                 mn = v < mn ? v : mn;
                 mx = v > mx ? v : mx;
             }
-            float sc = (mx - mn) / (float)qmax;
-            if (sc < 1e-7f) sc = 1e-7f;
-            uint16_t sb = f2bf(sc), bb = f2bf(mn);
-            s[r * ng + g] = sb;
-            b[r * ng + g] = bb;
-            float scq = bf2f(sb), biq = bf2f(bb);
+            float sc, bi;
+            oracle_affine_params(mn, mx, bits, &sc, &bi);
+            s[r * ng + g] = f2bf(sc);
+            b[r * ng + g] = f2bf(bi);
             for (int i = 0; i < gs; i += per_word) {
                 uint32_t word = 0;
                 for (int l = 0; l < per_word; ++l) {
-                    float v = (bf2f(wr[g * gs + i + l]) - biq) / scq;
+                    float v = (bf2f(wr[g * gs + i + l]) - bi) / sc;
                     int qi = (int)nearbyintf(v);
                     qi = qi < 0 ? 0 : (qi > qmax ? qmax : qi);
                     word |= ((uint32_t)qi) << (l * bits);

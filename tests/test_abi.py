@@ -79,3 +79,13 @@ def test_null_arguments(L):
     assert L.apt_moe_create(None, None) == 1
     assert L.apt_moe_destroy(None) == 0
     assert L.apt_moe_route(None, None, 0, None, None, None) == 1
+
+
+def test_route_noalloc_rejects_misaligned_pointer(L):
+    """A pointer off the 16-byte grid is refused before anything is launched
+    (the values are never dereferenced: validation runs on the host only)."""
+    good, odd = ctypes.c_void_p(0x10000), ctypes.c_void_p(0x10002)
+    for x, proj, scale in ((odd, good, good), (good, odd, good), (good, good, odd)):
+        st = L.apt_moe_route_noalloc(x, 16, proj, scale, good, 2816, 128, 8, 1e-6, good, good,
+                                     None)
+        assert st == 1  # APT_ERR_INVALID

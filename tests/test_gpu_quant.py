@@ -113,3 +113,32 @@ def test_quant_prefill_tensor_core_path(oracle, bits):
     got, refv = bf16_to_f32(_np(out))[rows], bf16_to_f32(ref)
     ok, ma, cos = block_close(got, refv)
     assert ok and ma <= TIGHT_REL * np.abs(refv).max(), (ma, cos)
+
+
+def test_quant4_prefill_T4096_zipf_vs_oracle(oracle):
+    """BASELINE config 4 at T=4096: 4-bit MLX-affine experts (group 64),
+    Zipf-skewed routing, the block's prefill path against the oracle's
+    gather_qmm restatement on 128 sampled tokens with the oracle's routing
+    (indices first checked on every token)."""
+    from tests.helpers import router_index_check
+    H, E, K, I, T = 2816, 128, 8, 704, 4096
+    d = block_inputs(T, seed=4096, device=DEV, routing="zipf", H=H, E=E, K=K, I=I)
+    gq, dq = _quantize(oracle, d, 4)
+    cfg = A.ESModelConfig(moe_sparse=True, max_tokens=T)
+    q = dict(gu_q=_dev(gq[0]), gu_s=_dev(gq[1]), gu_b=_dev(gq[2]), dn_q=_dev(dq[0]),
+             dn_s=_dev(dq[1]), dn_b=_dev(dq[2]), bits=4, group_size=64)
+    blk = A.MoEBlock(cfg, d["proj"], d["scale"], d["pes"], quantized=q)
+    out, tk = blk.forward(d["x"], return_routing=True)
+    torch.cuda.synchronize()
+    blk.handle.sync()
+    idx = tk.idx.cpu().numpy()
+    idx_o, w_o, aux = oracle.route_topk(_np(d["x"]), _np(d["proj"]), _np(d["scale"]),
+                                        _np(d["pes"]), K, return_scores=True)
+    bad, exempt = router_index_check(idx, idx_o, aux["scores"])
+    assert bad == 0, f"{bad} non-tie index mismatches (exempt {exempt})"
+    same = np.nonzero(np.all(idx == idx_o, axis=1))[0]
+    rows = np.sort(np.random.default_rng(2).choice(same, 128, replace=False))
+    ref = oracle.experts_sparse_q(_np(d["x"][rows]), *gq, *dq, 4, 64, idx_o[rows], w_o[rows], I)
+    got, refv = bf16_to_f32(_np(out))[rows], bf16_to_f32(ref)
+    ok, ma, cos = block_close(got, refv)
+    assert ok and ma <= TIGHT_REL * np.abs(refv).max(), (ma, cos)

@@ -118,6 +118,47 @@ def test_dense_equals_sparse(oracle):
     assert np.all(diff <= np.abs(sp) * 2.0 ** -7 + 1e-6)
 
 
+def _mlx_affine_py(wf, gs, bits):
+    """MLX's affine_quantize rule (mlx/fast.cpp at ml-explore/mlx @ 057cdc9ec,
+    the call behind mx::quantize at ESExperts.mm:14,16), restated in numpy
+    float32 independently of the C oracle."""
+    f = np.float32
+    n = f((1 << bits) - 1)
+    g = wf.reshape(wf.shape[0], -1, gs).astype(f)
+    mx, mn = g.max(-1), g.min(-1)
+    mask = np.abs(mn) > np.abs(mx)
+    sc = np.maximum((mx - mn) / n, f(1e-7)).astype(f)
+    sc = np.where(mask, sc, -sc).astype(f)
+    edge = np.where(mask, mn, mx).astype(f)
+    q0 = np.rint(edge / sc).astype(f)
+    sc = np.where(q0 != 0, edge / np.where(q0 != 0, q0, f(1)), sc).astype(f)
+    bi = np.where(q0 == 0, f(0), edge).astype(f)
+    q = np.clip(np.rint((g - bi[..., None]) / sc[..., None]), 0, n).astype(np.uint32)
+    return q.reshape(wf.shape), sc, bi
+
+
+def test_quantize_matches_mlx_rule(oracle):
+    rng = np.random.default_rng(5)
+    w = oracle.f32_to_bf16(rng.standard_normal((64, 256), dtype=np.float32) * 0.02)
+    w[3, :64] = oracle.f32_to_bf16(np.abs(rng.standard_normal(64, dtype=np.float32)))  # all > 0
+    w[4, :64] = 0  # a constant group: scale 1e-7 path
+    wf = oracle.bf16_to_f32(w)
+    for bits in (4, 8):
+        q, s, b = oracle.quantize_affine(w, 64, bits)
+        qr, sr, br = _mlx_affine_py(wf, 64, bits)
+        per = 32 // bits
+        codes = np.stack([(q >> (bits * l)) & ((1 << bits) - 1) for l in range(per)], -1)
+        codes = codes.reshape(q.shape[0], -1)  # low bits first
+        np.testing.assert_array_equal(codes, qr)
+        np.testing.assert_array_equal(s, oracle.f32_to_bf16(sr))
+        np.testing.assert_array_equal(b, oracle.f32_to_bf16(br))
+        # the scale is negative exactly where the group's max has the larger magnitude
+        g = wf.reshape(64, -1, 64)
+        neg = np.abs(g.min(-1)) <= np.abs(g.max(-1))
+        sf = oracle.bf16_to_f32(s)
+        assert np.all((sf < 0)[neg & (sf != 0)]) and np.all((sf > 0)[~neg])
+
+
 def test_quantize_roundtrip(oracle):
     rng = np.random.default_rng(5)
     w = oracle.f32_to_bf16(rng.standard_normal((8, 256), dtype=np.float32) * 0.02)
@@ -126,24 +167,27 @@ def test_quantize_roundtrip(oracle):
         assert q.shape == (8, 256 * bits // 32) and s.shape == (8, 4)
         deq = oracle.dequantize_affine(q, s, b, 64, bits)
         wf = oracle.bf16_to_f32(w)
-        step = oracle.bf16_to_f32(s).repeat(64, axis=1)
-        # every element within half a step (+ bf16 rounding of scale/bias)
-        assert np.all(np.abs(deq - wf) <= 0.5 * step + 2e-4)
+        step = np.abs(oracle.bf16_to_f32(s)).repeat(64, axis=1)
+        # within one step (half a step, plus the clip at the far end after the
+        # scale was moved so that zero falls on a code) + bf16 rounding
+        assert np.all(np.abs(deq - wf) <= step + 2e-4)
+        assert np.mean(np.abs(deq - wf) <= 0.5 * step + 2e-4) > 0.99
         # packing: element 0 of row 0 sits in the low bits of word 0
         q0 = int(q[0, 0]) & ((1 << bits) - 1)
         ref = (wf[0, 0] - oracle.bf16_to_f32(b)[0, 0]) / oracle.bf16_to_f32(s)[0, 0]
-        assert abs(q0 - ref) <= 0.5 + 1e-3
+        assert abs(q0 - ref) <= 0.5 + 2e-2
 
 
 def test_quantized_experts_close_to_bf16(oracle):
     """testQuantizedLinearCloseToBf16 (ESPrimitivesTests.mm:157-169) for experts:
     the quantised block stays within 5 % of peak of the bf16 block (8-bit)
-    and 15 % (4-bit)."""
+    and 20 % (4-bit: MLX moves each group's scale so that zero is a code, which
+    clips the far end of some groups by up to ~0.7 of a step)."""
     d = load("small")
     idx, w = oracle.route_topk(d["x"], d["proj"], d["scale"], d["pes"], int(d["K"]))
     ref = oracle.bf16_to_f32(oracle.experts_sparse(d["x"], d["gate_up"], d["down"], idx, w))
     peak = np.abs(ref).max()
-    for bits, tol in ((8, 0.05), (4, 0.15)):
+    for bits, tol in ((8, 0.05), (4, 0.20)):
         gq = oracle.quantize_affine(d["gate_up"], 64, bits)
         dq = oracle.quantize_affine(d["down"], 64, bits)
         got = oracle.bf16_to_f32(oracle.experts_sparse_q(d["x"], *gq, *dq, bits, 64, idx, w,
