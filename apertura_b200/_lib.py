@@ -28,6 +28,7 @@ EXPORTED = [
     "apt_moe_nccl_unique_id", "apt_moe_create_ep", "apt_moe_ep_destroy", "apt_moe_ep_last_error",
     "apt_moe_ep_load_router", "apt_moe_ep_load_experts_bf16", "apt_moe_ep_forward",
     "apt_moe_ep_placement", "apt_moe_ep_stats", "apt_moe_selftest_wait",
+    "apt_moe_ep_set_transport", "apt_moe_ep_get_transport", "apt_moe_ep_sync",
 ]
 
 STAGES = ["router_scores", "router_select", "dispatch_count", "dispatch", "gather", "gate_up",
@@ -112,6 +113,9 @@ def lib():
         "apt_moe_ep_forward": ([P, P, i32, P, P], i32),
         "apt_moe_ep_placement": ([P, i32, i32, i32, P], i32),
         "apt_moe_ep_stats": ([P, ctypes.POINTER(i32), ctypes.POINTER(i32)], i32),
+        "apt_moe_ep_set_transport": ([P, i32], i32),
+        "apt_moe_ep_get_transport": ([P, ctypes.POINTER(i32)], i32),
+        "apt_moe_ep_sync": ([P], i32),
     }
     for name, (argtypes, restype) in sig.items():
         fn = getattr(L, name)

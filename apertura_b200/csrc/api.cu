@@ -973,6 +973,10 @@ extern "C" apt_status apt_moe_decoder_ff(apt_moe_handle *h, const uint16_t *x1,
     return forward_impl(h, x1, nullptr, T, x2, nullptr, nullptr, stream, pre_ff_ln_2_w, &tail);
 }
 
+namespace apt {
+Dispatch handle_dispatch(apt_moe_handle *h) { return h->disp(); }
+}  // namespace apt
+
 // ---- expert-parallel halves: the routing + dispatch before the all-to-all,
 // and the combine after it (the remote expert compute is apt_moe_experts on a
 // handle holding the rank's local experts).

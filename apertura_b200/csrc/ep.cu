@@ -26,6 +26,7 @@
 #include <vector>
 
 #include "../../include/apt_moe.h"
+#include "moe_internal.h"
 
 namespace {
 
@@ -37,6 +38,7 @@ struct NcclApi {
     decltype(&ncclGroupEnd) group_end = nullptr;
     decltype(&ncclSend) send = nullptr;
     decltype(&ncclRecv) recv = nullptr;
+    decltype(&ncclAllGather) all_gather = nullptr;
     decltype(&ncclGetErrorString) error_string = nullptr;
     bool ok = false;
 };
@@ -55,10 +57,11 @@ const NcclApi &nccl() {
         APT_NCCL_SYM(group_end, "ncclGroupEnd");
         APT_NCCL_SYM(send, "ncclSend");
         APT_NCCL_SYM(recv, "ncclRecv");
+        APT_NCCL_SYM(all_gather, "ncclAllGather");
         APT_NCCL_SYM(error_string, "ncclGetErrorString");
 #undef APT_NCCL_SYM
         a.ok = a.get_unique_id && a.comm_init_rank && a.comm_destroy && a.group_start &&
-               a.group_end && a.send && a.recv && a.error_string;
+               a.group_end && a.send && a.recv && a.all_gather && a.error_string;
         return a;
     }();
     return api;
@@ -83,6 +86,18 @@ struct apt_moe_ep {
     // pinned host copies of the counts
     int32_t *h_counts = nullptr, *h_recv = nullptr;
     int last_recv = 0, last_hot = 0;
+    // NVLink peer-memory transport (ep_p2p.cu): this rank's shared region,
+    // the IPC mappings of the others', and the per-step epoch
+    int transport = 0;  // APT_EP_NCCL or APT_EP_P2P
+    bool p2p_ready = false;
+    uint8_t *region = nullptr;
+    size_t region_bytes = 0;
+    std::vector<void *> mapped;  // peer regions opened through CUDA IPC
+    apt::EpPeer *d_peers = nullptr;
+    const uint16_t **rowptr = nullptr;
+    int32_t *grp = nullptr, *grp_ge = nullptr;
+    uint32_t epoch = 0;
+    int sms = 148;
     std::string err;
 };
 
@@ -196,10 +211,26 @@ extern "C" apt_status apt_moe_nccl_unique_id(void *id_out) {
     return APT_OK;
 }
 
+namespace {
+apt_status ep_barrier(apt_moe_ep *ep);
+}
+
 extern "C" apt_status apt_moe_ep_destroy(apt_moe_ep *ep) {
     if (!ep) return APT_OK;
     DevGuard g(ep->cfg.device);
     if (ep->side) cudaStreamSynchronize(ep->side);
+    if (ep->p2p_ready) {
+        // peers may still read this rank's region until they are done too
+        cudaDeviceSynchronize();
+        ep_barrier(ep);
+        for (void *m : ep->mapped)
+            if (m) cudaIpcCloseMemHandle(m);
+    }
+    if (ep->region) cudaFree(ep->region);
+    if (ep->d_peers) cudaFree(ep->d_peers);
+    if (ep->rowptr) cudaFree(ep->rowptr);
+    if (ep->grp) cudaFree(ep->grp);
+    if (ep->grp_ge) cudaFree(ep->grp_ge);
     apt_moe_destroy(ep->router);
     apt_moe_destroy(ep->hot);
     apt_moe_destroy(ep->cold);
@@ -220,6 +251,113 @@ extern "C" apt_status apt_moe_ep_destroy(apt_moe_ep *ep) {
 extern "C" const char *apt_moe_ep_last_error(const apt_moe_ep *ep) {
     return ep ? ep->err.c_str() : "null handle";
 }
+
+namespace {
+
+size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+
+// All ranks reach this point before any returns (one tiny NCCL all-gather).
+apt_status ep_barrier(apt_moe_ep *ep) {
+    uint8_t *b = nullptr;
+    EP_CUDA(ep, cudaMalloc(&b, 16 * (size_t)ep->nranks));
+    ncclResult_t r = nccl().all_gather(b + 16 * ep->rank, b, 16, ncclChar, ep->comm, 0);
+    cudaError_t e = cudaStreamSynchronize(0);
+    cudaFree(b);
+    if (r != ncclSuccess) return ep_fail(ep, APT_ERR_NCCL, "barrier: %s", nccl().error_string(r));
+    if (e != cudaSuccess) return ep_fail(ep, APT_ERR_CUDA, "barrier: %s", cudaGetErrorString(e));
+    return APT_OK;
+}
+
+// The peer-memory transport: one region per rank, mapped by every other rank
+// through CUDA IPC (handles exchanged with one NCCL all-gather).  Collective.
+// Any failure leaves the NCCL transport in place.
+apt_status setup_p2p(apt_moe_ep *ep) {
+    const int N = ep->nranks, E = ep->cfg.num_experts, H = ep->cfg.hidden_size;
+    const int K = ep->cfg.top_k_experts;
+    if (N > apt::kEpMaxRanks || E > apt::kEpMaxExperts || K > apt::kEpMaxK || H % 8)
+        return APT_ERR_UNSUPPORTED;
+    const size_t flags_b = align256(sizeof(uint32_t) * (3 * N + 2));
+    const size_t table_b = align256(sizeof(int32_t) * 2 * N * E);
+    const size_t rows_b = align256((size_t)2 * ep->max_recv * H * 2);
+    ep->region_bytes = flags_b + table_b + 2 * rows_b;
+    EP_CUDA(ep, cudaMalloc(&ep->region, ep->region_bytes));
+    EP_CUDA(ep, cudaMemset(ep->region, 0, flags_b + table_b));
+    EP_CUDA(ep, dalloc(&ep->rowptr, (size_t)ep->Tm * K));
+    EP_CUDA(ep, dalloc(&ep->grp, (size_t)ep->c_loc));
+    EP_CUDA(ep, dalloc(&ep->grp_ge, (size_t)ep->c_loc));
+    std::vector<int32_t> ge(ep->c_loc);
+    for (int j = 0; j < ep->c_loc; ++j) ge[j] = j;
+    EP_CUDA(ep, cudaMemcpy(ep->grp_ge, ge.data(), sizeof(int32_t) * ep->c_loc,
+                           cudaMemcpyHostToDevice));
+    EP_CUDA(ep, cudaDeviceSynchronize());
+    // exchange the IPC handles
+    cudaIpcMemHandle_t mine;
+    cudaError_t ie = cudaIpcGetMemHandle(&mine, ep->region);
+    uint8_t *hb = nullptr;
+    EP_CUDA(ep, cudaMalloc(&hb, sizeof(cudaIpcMemHandle_t) * N + 16));
+    // a rank that could not export its region sends zeros; every rank then
+    // sees the failure and stays on NCCL
+    std::vector<uint8_t> h(sizeof(cudaIpcMemHandle_t) * N, 0);
+    if (ie == cudaSuccess) memcpy(h.data() + sizeof mine * ep->rank, &mine, sizeof mine);
+    cudaMemcpy(hb, h.data(), h.size(), cudaMemcpyHostToDevice);
+    ncclResult_t r = nccl().all_gather(hb + sizeof mine * ep->rank, hb, sizeof mine, ncclChar,
+                                       ep->comm, 0);
+    cudaStreamSynchronize(0);
+    cudaMemcpy(h.data(), hb, h.size(), cudaMemcpyDeviceToHost);
+    cudaFree(hb);
+    if (r != ncclSuccess) return ep_fail(ep, APT_ERR_NCCL, "handle exchange failed");
+    bool ok = true;
+    for (int d = 0; d < N; ++d) {
+        bool zero = true;
+        for (size_t i = 0; i < sizeof mine; ++i) zero &= h[sizeof mine * d + i] == 0;
+        ok &= !zero;
+    }
+    std::vector<apt::EpPeer> peers(N);
+    ep->mapped.assign(N, nullptr);
+    for (int d = 0; d < N && ok; ++d) {
+        uint8_t *base = ep->region;
+        if (d != ep->rank) {
+            cudaIpcMemHandle_t hd;
+            memcpy(&hd, h.data() + sizeof hd * d, sizeof hd);
+            void *p = nullptr;
+            if (cudaIpcOpenMemHandle(&p, hd, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                ok = false;
+                break;
+            }
+            ep->mapped[d] = p;
+            base = static_cast<uint8_t *>(p);
+        }
+        peers[d].flags = reinterpret_cast<uint32_t *>(base);
+        peers[d].table = reinterpret_cast<int32_t *>(base + flags_b);
+        peers[d].recv = reinterpret_cast<uint16_t *>(base + flags_b + table_b);
+        peers[d].out = reinterpret_cast<uint16_t *>(base + flags_b + table_b + rows_b);
+    }
+    // every rank must have mapped every other rank's region
+    int32_t *okb = nullptr;
+    EP_CUDA(ep, dalloc(&okb, (size_t)N * 4));
+    std::vector<int32_t> oks(N * 4, 0);
+    oks[ep->rank * 4] = ok ? 1 : 0;
+    cudaMemcpy(okb, oks.data(), sizeof(int32_t) * N * 4, cudaMemcpyHostToDevice);
+    r = nccl().all_gather(okb + ep->rank * 4, okb, 4, ncclInt32, ep->comm, 0);
+    cudaStreamSynchronize(0);
+    cudaMemcpy(oks.data(), okb, sizeof(int32_t) * N * 4, cudaMemcpyDeviceToHost);
+    cudaFree(okb);
+    for (int d = 0; d < N; ++d) ok &= oks[d * 4] == 1;
+    if (r != ncclSuccess || !ok) {
+        for (void *m : ep->mapped)
+            if (m) cudaIpcCloseMemHandle(m);
+        ep->mapped.clear();
+        return ep_fail(ep, APT_ERR_UNSUPPORTED, "peer-memory transport unavailable; using NCCL");
+    }
+    EP_CUDA(ep, dalloc(&ep->d_peers, (size_t)N));
+    EP_CUDA(ep, cudaMemcpy(ep->d_peers, peers.data(), sizeof(apt::EpPeer) * N,
+                           cudaMemcpyHostToDevice));
+    ep->p2p_ready = true;
+    return APT_OK;
+}
+
+}  // namespace
 
 extern "C" apt_status apt_moe_create_ep(const apt_moe_config *cfg, const void *nccl_id, int rank,
                                         int nranks, const float *expected_loads, int replicate_hot,
@@ -299,6 +437,9 @@ extern "C" apt_status apt_moe_create_ep(const apt_moe_config *cfg, const void *n
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cfg->device);
     if (ep->hot) apt_moe_set_sm_limit(ep->hot, sms > 32 ? sms - 24 : sms);
+    ep->sms = sms;
+    ep->transport = APT_EP_NCCL;
+    if (setup_p2p(ep) == APT_OK) ep->transport = APT_EP_P2P;
     *out = ep;
     return APT_OK;
 }
@@ -368,13 +509,78 @@ extern "C" apt_status apt_moe_ep_load_experts_bf16(apt_moe_ep *ep, const uint16_
     return load(ep->cold, ep->perm.data() + R + ep->rank * C, C);
 }
 
+namespace {
+
+// One step over the peer-memory transport (ep_p2p.cu): no host
+// synchronisation; every exchange is a kernel.
+apt_status ep_forward_p2p(apt_moe_ep *ep, const uint16_t *x, int T, uint16_t *out, void *stream) {
+    cudaStream_t s = (cudaStream_t)stream;
+    const int N = ep->nranks, C = ep->c_loc, R = ep->n_hot, K = ep->cfg.top_k_experts;
+    const int E = ep->cfg.num_experts, H = ep->cfg.hidden_size;
+    EP_APT(ep, ep->router,
+           apt_moe_ep_dispatch(ep->router, x, T, ep->idx, ep->w, ep->rows, ep->counts, stream));
+    const apt::Dispatch d = apt::handle_dispatch(ep->router);
+    ++ep->epoch;
+    if (ep->epoch == 0) ep->epoch = 1;  // flags start at 0
+    apt::EpP2PArgs a{};
+    a.peers = ep->d_peers;
+    a.N = N;
+    a.me = ep->rank;
+    a.R = R;
+    a.C = C;
+    a.E = E;
+    a.H = H;
+    a.max_recv = ep->max_recv;
+    a.parity = (int)(ep->epoch & 1);
+    a.epoch = ep->epoch;
+    a.counts = d.counts;
+    a.offsets = d.offsets;
+    a.perm = d.perm;
+    a.rows = ep->rows;
+    a.back = ep->back;
+    a.rowptr = ep->rowptr;
+    a.grp = ep->grp;
+    if (R) {  // replicated experts beside the exchange
+        EP_CUDA(ep, cudaEventRecord(ep->ev_fork, s));
+        EP_CUDA(ep, cudaStreamWaitEvent(ep->side, ep->ev_fork, 0));
+        EP_APT(ep, ep->hot,
+               apt_moe_experts_grouped(ep->hot, ep->rows, T * K, ep->counts, ep->hot_ge, R,
+                                       ep->back, ep->side));
+    }
+    EP_CUDA(ep, apt::launch_ep_push(a, 2 * ep->sms, s));
+    EP_CUDA(ep, apt::launch_ep_wait_recv(a, s));
+    const size_t slot = (size_t)a.parity * ep->max_recv * H;
+    const size_t flags_b = align256(sizeof(uint32_t) * (3 * N + 2));
+    const size_t table_b = align256(sizeof(int32_t) * 2 * N * E);
+    const size_t rows_b = align256((size_t)2 * ep->max_recv * H * 2);
+    uint16_t *recv = reinterpret_cast<uint16_t *>(ep->region + flags_b + table_b) + slot;
+    uint16_t *res = reinterpret_cast<uint16_t *>(ep->region + flags_b + table_b + rows_b) + slot;
+    EP_APT(ep, ep->cold,
+           apt_moe_experts_grouped(ep->cold, recv, ep->max_recv, ep->grp, ep->grp_ge, C, res,
+                                   stream));
+    EP_CUDA(ep, apt::launch_ep_done(a, s));
+    if (R) {
+        EP_CUDA(ep, cudaEventRecord(ep->ev_join, ep->side));
+        EP_CUDA(ep, cudaStreamWaitEvent(s, ep->ev_join, 0));
+    }
+    EP_CUDA(ep, apt::launch_ep_combine(a, ep->w, T, K, out, std::min(T, 4 * ep->sms), s));
+    ep->last_recv = -1;  // counted on demand (apt_moe_ep_stats)
+    ep->last_hot = -1;
+    return APT_OK;
+}
+
+}  // namespace
+
 extern "C" apt_status apt_moe_ep_forward(apt_moe_ep *ep, const uint16_t *x, int T, uint16_t *out,
                                          void *stream) {
     if (!ep) return APT_ERR_INVALID;
     if (T < 0 || T > ep->Tm) return ep_fail(ep, APT_ERR_INVALID, "T=%d outside [0, %d]", T, ep->Tm);
     if (T == 0) return APT_OK;
     if (!x || !out) return ep_fail(ep, APT_ERR_INVALID, "null pointer");
+    if (((uintptr_t)x | (uintptr_t)out) & 15)
+        return ep_fail(ep, APT_ERR_INVALID, "x and out must be 16-byte aligned");
     DevGuard g(ep->cfg.device);
+    if (ep->transport == APT_EP_P2P) return ep_forward_p2p(ep, x, T, out, stream);
     cudaStream_t s = (cudaStream_t)stream;
     const NcclApi &nc = nccl();
     const int N = ep->nranks, C = ep->c_loc, R = ep->n_hot, K = ep->cfg.top_k_experts;
@@ -456,9 +662,60 @@ extern "C" apt_status apt_moe_ep_forward(apt_moe_ep *ep, const uint16_t *x, int 
     return APT_OK;
 }
 
-extern "C" apt_status apt_moe_ep_stats(const apt_moe_ep *ep, int *recv_rows, int *hot_rows) {
+extern "C" apt_status apt_moe_ep_stats(apt_moe_ep *ep, int *recv_rows, int *hot_rows) {
     if (!ep) return APT_ERR_INVALID;
+    if (ep->last_recv < 0) {  // peer-memory step: read the group counts back
+        DevGuard g(ep->cfg.device);
+        std::vector<int32_t> grp(ep->c_loc), cnt(ep->cfg.num_experts);
+        EP_CUDA(ep, cudaDeviceSynchronize());
+        EP_CUDA(ep, cudaMemcpy(grp.data(), ep->grp, sizeof(int32_t) * ep->c_loc,
+                               cudaMemcpyDeviceToHost));
+        EP_CUDA(ep, cudaMemcpy(cnt.data(), ep->counts, sizeof(int32_t) * cnt.size(),
+                               cudaMemcpyDeviceToHost));
+        ep->last_recv = 0;
+        for (int v : grp) ep->last_recv += v;
+        ep->last_hot = 0;
+        for (int e = 0; e < ep->n_hot; ++e) ep->last_hot += cnt[e];
+    }
     if (recv_rows) *recv_rows = ep->last_recv;
     if (hot_rows) *hot_rows = ep->last_hot;
     return APT_OK;
+}
+
+extern "C" apt_status apt_moe_ep_set_transport(apt_moe_ep *ep, int transport) {
+    if (!ep || (transport != APT_EP_NCCL && transport != APT_EP_P2P)) return APT_ERR_INVALID;
+    if (transport == APT_EP_P2P && !ep->p2p_ready)
+        return ep_fail(ep, APT_ERR_UNSUPPORTED, "peer-memory transport was not set up");
+    ep->transport = transport;
+    return APT_OK;
+}
+
+extern "C" apt_status apt_moe_ep_get_transport(const apt_moe_ep *ep, int *transport) {
+    if (!ep || !transport) return APT_ERR_INVALID;
+    *transport = ep->transport;
+    return APT_OK;
+}
+
+extern "C" apt_status apt_moe_ep_sync(apt_moe_ep *ep) {
+    if (!ep) return APT_ERR_INVALID;
+    DevGuard g(ep->cfg.device);
+    EP_CUDA(ep, cudaDeviceSynchronize());
+    apt_status st = APT_OK;
+    if (ep->p2p_ready) {
+        const int N = ep->nranks;
+        uint32_t *errw = reinterpret_cast<uint32_t *>(ep->region) + 3 * N + 1;
+        uint32_t code = 0;
+        EP_CUDA(ep, cudaMemcpy(&code, errw, sizeof code, cudaMemcpyDeviceToHost));
+        if (code) {
+            EP_CUDA(ep, cudaMemset(errw, 0, sizeof code));
+            st = ep_fail(ep, APT_ERR_TIMEOUT, "peer-memory exchange: error code %u", code);
+        }
+    }
+    apt_moe_handle *hs[] = {ep->router, ep->hot, ep->cold};
+    for (apt_moe_handle *h : hs) {
+        if (!h) continue;
+        apt_status hs_st = apt_moe_sync(h);
+        if (hs_st && !st) st = ep_fail(ep, hs_st, "%s", apt_moe_last_error(h));
+    }
+    return st;
 }

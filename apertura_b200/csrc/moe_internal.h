@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+struct apt_moe_handle;
+
 namespace apt {
 
 // Routing / dispatch state of one call, all device pointers.
@@ -201,5 +203,39 @@ cudaError_t launch_interleave_sb(const uint16_t *sc, const uint16_t *bi, int64_t
 cudaError_t launch_dequant_active(const uint32_t *q, const uint16_t *sc, const uint16_t *bi,
                                   int rows, int cols, int bits, const Dispatch &d, int E,
                                   uint16_t *out, cudaStream_t s, int *launches);
+
+// ---- expert parallelism over NVLink peer memory (ep_p2p.cu)
+constexpr int kEpMaxExperts = 256;
+constexpr int kEpMaxK = 32;
+constexpr int kEpMaxRanks = 16;
+// One rank's shared region as seen from this process (own or IPC-mapped).
+struct EpPeer {
+    uint32_t *flags;  // [3N+2]
+    int32_t *table;   // [2][N][E]
+    uint16_t *recv;   // [2][max_recv][H]
+    uint16_t *out;    // [2][max_recv][H]
+};
+struct EpP2PArgs {
+    const EpPeer *peers;  // device array [N]
+    int N, me, R, C, E, H, max_recv, parity;
+    uint32_t epoch;
+    const int32_t *counts, *offsets, *perm;  // this rank's dispatch (new expert ids)
+    const uint16_t *rows;                    // sorted routed rows [P, H]
+    uint16_t *back;                          // hot-expert outputs [P, H] (sorted rows)
+    const uint16_t **rowptr;                 // [P] pair -> address of its expert output
+    int32_t *grp;                            // [C] group counts of this rank's experts
+    __host__ __device__ int CNT() const { return 0; }
+    __host__ __device__ int PUSH() const { return N; }
+    __host__ __device__ int DONE() const { return 2 * N; }
+    __host__ __device__ int CTR() const { return 3 * N; }
+    __host__ __device__ int ERR() const { return 3 * N + 1; }
+};
+cudaError_t launch_ep_push(const EpP2PArgs &a, int grid, cudaStream_t s);
+cudaError_t launch_ep_wait_recv(const EpP2PArgs &a, cudaStream_t s);
+cudaError_t launch_ep_done(const EpP2PArgs &a, cudaStream_t s);
+cudaError_t launch_ep_combine(const EpP2PArgs &a, const uint16_t *w, int T, int K, uint16_t *out,
+                              int grid, cudaStream_t s);
+// The dispatch (counts, offsets, perm, inv) of the last routing call on h.
+Dispatch handle_dispatch(apt_moe_handle *h);
 
 }  // namespace apt

@@ -299,20 +299,24 @@ class NativeExpertParallelMoE:
     NCCL communicator is made from an id that rank 0 creates and the group
     broadcasts).  Parameters as ExpertParallelMoE."""
 
+    TRANSPORTS = {"nccl": 0, "p2p": 1}
+
     def __init__(self, cfg: ESModelConfig, proj, scale, pes, gate_up, down, group=None,
                  loads: Optional[Sequence[float]] = None, max_tokens_per_rank: int = 4096,
-                 replicate_hot: int = 24):
+                 replicate_hot: int = 24, transport: Optional[str] = None):
         import numpy as np
         from ._lib import check as _check
-        self.rank = dist.get_rank(group)
-        self.world = dist.get_world_size(group)
+        single = not (dist.is_available() and dist.is_initialized())
+        self.rank = 0 if single else dist.get_rank(group)
+        self.world = 1 if single else dist.get_world_size(group)
         self.cfg = cfg
         idbuf = ctypes.create_string_buffer(128)
         if self.rank == 0:
             _check(lib().apt_moe_nccl_unique_id(idbuf))
-        obj = [idbuf.raw if self.rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0, group=group)
-        idbuf = ctypes.create_string_buffer(obj[0], 128)
+        if self.world > 1:
+            obj = [idbuf.raw if self.rank == 0 else None]
+            dist.broadcast_object_list(obj, src=0, group=group)
+            idbuf = ctypes.create_string_buffer(obj[0], 128)
         self._loads = None if loads is None else np.asarray(loads, dtype=np.float32)
         c = ESModelConfig(**{**cfg.__dict__, "moe_sparse": True,
                              "max_tokens": max_tokens_per_rank}).to_c()
@@ -323,6 +327,18 @@ class NativeExpertParallelMoE:
         self.ep = ep
         self._check(lib().apt_moe_ep_load_router(ep, _ptr(proj), _ptr(scale), _ptr(pes), 1))
         self._check(lib().apt_moe_ep_load_experts_bf16(ep, _ptr(gate_up), _ptr(down), 1))
+        if transport is not None:
+            self._check(lib().apt_moe_ep_set_transport(ep, self.TRANSPORTS[transport]))
+
+    @property
+    def transport(self) -> str:
+        t = ctypes.c_int()
+        self._check(lib().apt_moe_ep_get_transport(self.ep, ctypes.byref(t)))
+        return {v: k for k, v in self.TRANSPORTS.items()}[t.value]
+
+    def sync(self):
+        """Wait for the device; raises if a bounded wait of the exchange gave up."""
+        self._check(lib().apt_moe_ep_sync(self.ep))
 
     def _check(self, status):
         if status != 0:
@@ -347,9 +363,7 @@ class NativeExpertParallelMoE:
             lib().apt_moe_ep_destroy(self.ep)
             self.ep = None
 
-    def __del__(self):
-        try:
-            self.close()
-        except Exception:
-            pass
+    # No __del__: destroying the handle is collective (its buffers stay mapped
+    # by the other ranks until all of them destroy), so it happens only in an
+    # explicit close() that every rank calls.
 

@@ -139,3 +139,17 @@ def _fold_zipf(x, proj, scale, K, s, seed, device, calib_tokens=None, iters=80):
 def to_numpy_bits(t: torch.Tensor):
     """bf16 tensor -> numpy uint16 bits (CPU copy) for the oracle."""
     return t.detach().contiguous().view(torch.int16).cpu().numpy().view("uint16")
+
+
+def router_tie_tokens(x, proj, scale, K, eps=1e-6):
+    """Tokens whose K-th and (K+1)-th router scores lie within one bf16 ulp
+    of each other (f32 restatement of ESRouter.mm:14-24 in torch): their
+    selected set may differ between two correct implementations, e.g. when
+    the expert ids are relabelled for expert parallelism.  For checks only."""
+    xf = x.float()
+    h = xf * torch.rsqrt((xf * xf).mean(-1, keepdim=True) + eps)
+    h = h * scale.float() * (x.shape[1] ** -0.5)
+    s = torch.sort(h @ proj.float().t(), dim=-1, descending=True).values
+    a, b = s[:, K - 1], s[:, K]
+    ulp = torch.exp2(torch.floor(torch.log2(a.abs().clamp_min(1e-30))) - 7)
+    return (a - b) <= ulp

@@ -379,15 +379,24 @@ APT_API apt_status apt_moe_route_noalloc(const uint16_t *x, int T, const uint16_
                                          int32_t *idx, uint16_t *w, void *stream);
 
 /*
- * Expert parallelism as one C-ABI handle per GPU over NCCL (no reference
+ * Expert parallelism as one C-ABI handle per GPU (no reference
  * counterpart): the hottest `replicate_hot` experts (by expected_loads, [E]
  * tokens per expert; NULL = uniform) are held by every rank, the others are
  * spread over the ranks by longest-processing-time placement; each forward
  * routes the rank's tokens, computes the replicated experts at home beside
- * the NCCL exchange of the other rows, computes the rank's own experts on
- * the rows it receives, sends the results back and combines in k order.
- * The result equals the single-GPU block on the same tokens.  NCCL is
- * resolved at run time (libnccl.so.2).  bf16 experts only.
+ * the exchange of the other rows, computes the rank's own experts on the
+ * rows it receives, returns the results and combines in k order.  The result
+ * equals the single-GPU block on the same tokens (up to router ties, which
+ * the relabelled expert ids may break the other way).  bf16 experts only.
+ *
+ * Two transports.  APT_EP_P2P (the default when every rank could map every
+ * other rank's buffers through CUDA IPC at create): the library's own kernels
+ * store the routed rows straight into their owners' memory over NVLink and
+ * the combine loads the results straight from there, synchronised by
+ * per-step flags in device memory -- no host synchronisation inside a step.
+ * APT_EP_NCCL: NCCL send/recv with one host synchronisation per step for the
+ * split sizes.  NCCL (resolved at run time, libnccl.so.2) also makes the
+ * communicator that create and destroy use in both modes.
  *
  *   apt_moe_nccl_unique_id: 128-byte id for the ranks' communicator (rank 0
  *     makes it, the host distributes it)
@@ -398,7 +407,16 @@ APT_API apt_status apt_moe_route_noalloc(const uint16_t *x, int T, const uint16_
  *   apt_moe_ep_forward: x, out [T, H] bf16 on this rank's device
  *   apt_moe_ep_placement: the placement alone, perm[new id] = original id
  *   apt_moe_ep_stats: rows received / computed at home in the last forward
+ *     (synchronises the device)
+ *   apt_moe_ep_set_transport / _get_transport: APT_EP_P2P or APT_EP_NCCL
+ *   apt_moe_ep_sync: synchronises the device; APT_ERR_TIMEOUT when a bounded
+ *     wait of the peer-memory exchange (about 1 s) gave up -- that step's
+ *     output is invalid (the error is then cleared)
+ * apt_moe_ep_destroy is collective with the P2P transport (a rank's buffers
+ * stay mapped by the others until all ranks destroy).
  */
+#define APT_EP_NCCL 0
+#define APT_EP_P2P 1
 typedef struct apt_moe_ep apt_moe_ep;
 APT_API apt_status apt_moe_nccl_unique_id(void *id_out);
 APT_API apt_status apt_moe_create_ep(const apt_moe_config *cfg, const void *nccl_id, int rank,
@@ -415,7 +433,10 @@ APT_API apt_status apt_moe_ep_forward(apt_moe_ep *ep, const uint16_t *x, int T, 
                                       void *stream);
 APT_API apt_status apt_moe_ep_placement(const float *loads, int E, int nranks, int n_hot,
                                         int32_t *perm_out);
-APT_API apt_status apt_moe_ep_stats(const apt_moe_ep *ep, int *recv_rows, int *hot_rows);
+APT_API apt_status apt_moe_ep_stats(apt_moe_ep *ep, int *recv_rows, int *hot_rows);
+APT_API apt_status apt_moe_ep_set_transport(apt_moe_ep *ep, int transport);
+APT_API apt_status apt_moe_ep_get_transport(const apt_moe_ep *ep, int *transport);
+APT_API apt_status apt_moe_ep_sync(apt_moe_ep *ep);
 
 #ifdef __cplusplus
 }
