@@ -49,6 +49,7 @@ struct apt_moe_handle {
     int gemm_pair = -1;    // CTA-pair GEMM: -1 by size, 0 off, 1 on (apt_moe_set_gemm_pair)
     int sm_limit = 0;      // cap on SMs for persistent grids (0: all)
     bool gemv_tma = true;  // TMA-streamed bf16 GEMV (else the register-prefetch GEMV)
+    bool fused_decode = true;  // whole decode block in one kernel (decode_fused.cu)
 
     // per-stage CUDA-event timing (apt_moe_set_timing / apt_moe_stage_times)
     bool timing = false;
@@ -94,6 +95,7 @@ struct apt_moe_handle {
     int32_t *counts = nullptr, *offsets = nullptr, *perm = nullptr, *inv = nullptr;
     int32_t *active = nullptr, *n_active = nullptr, *errflag = nullptr;
     int32_t *done = nullptr;    // fused decode router's completion counter (self-resetting)
+    int32_t *fsync = nullptr;   // one-kernel decode block's counters (self re-arming)
     uint16_t *hsplit = nullptr; // tensor-core router input [Tm, 2H]
     int32_t *rt_cnt = nullptr;  // its single-group {count, offset, end}
     uint16_t *xp = nullptr, *yp = nullptr, *op = nullptr;
@@ -349,12 +351,16 @@ extern "C" apt_status apt_moe_create(const apt_moe_config *cfg, apt_moe_handle *
     ALLOC(xin, (size_t)h->Tm * H);
     ALLOC(xout, (size_t)h->Tm * H);
     ALLOC(xn, (size_t)h->Tm * H);
+    ALLOC(fsync, decode_fused_sync_words(E, H));
 #undef ALLOC
     if (e1 == cudaSuccess) e1 = router_init();
     if (e1 == cudaSuccess) e1 = gemv_init();
     if (e1 == cudaSuccess) e1 = gemm_init();
     if (e1 == cudaSuccess) e1 = gemm_pair_init();
     if (e1 == cudaSuccess) e1 = gemv_tma_init();
+    if (e1 == cudaSuccess) e1 = decode_fused_init();
+    if (e1 == cudaSuccess)
+        e1 = cudaMemset(h->fsync, 0, sizeof(int32_t) * decode_fused_sync_words(E, H));
     if (e1 == cudaSuccess) e1 = cudaMemset(h->errflag, 0, 16);
     if (e1 == cudaSuccess) e1 = cudaMemset(h->done, 0, 16 * sizeof(int32_t));
     for (int i = 0; i < APT_STAGE_COUNT && e1 == cudaSuccess; ++i)
@@ -379,7 +385,7 @@ extern "C" apt_status apt_moe_destroy(apt_moe_handle *h) {
     void *ptrs[] = {h->proj, h->scale, h->pes, h->gu, h->dn, h->gu_q, h->dn_q, h->gu_s, h->gu_b,
                     h->dn_s, h->dn_b, h->scores, h->idx_i, h->w_i, h->counts, h->offsets,
                     h->perm, h->inv, h->active, h->n_active, h->errflag, h->done, h->hsplit, h->rt_cnt, h->xp, h->yp, h->op,
-                    h->Wd, h->idx2, h->w2, h->xin, h->xout, h->dq_gu, h->dq_dn, h->gu_sb, h->dn_sb, h->xn, h->dq_ids};
+                    h->Wd, h->idx2, h->w2, h->xin, h->xout, h->dq_gu, h->dq_dn, h->gu_sb, h->dn_sb, h->xn, h->dq_ids, h->fsync};
     for (void *p : ptrs) dfree(p);
     drop_graphs(h);
     if (h->gstream) cudaStreamDestroy(h->gstream);
@@ -444,6 +450,13 @@ extern "C" apt_status apt_moe_set_sm_limit(apt_moe_handle *h, int n) {
     if (!h || n < 0) return APT_ERR_INVALID;
     drop_graphs(h);
     h->sm_limit = n;
+    return APT_OK;
+}
+
+extern "C" apt_status apt_moe_set_fused_decode(apt_moe_handle *h, int on) {
+    if (!h || on < 0 || on > 1) return APT_ERR_INVALID;
+    drop_graphs(h);
+    h->fused_decode = on != 0;
     return APT_OK;
 }
 
@@ -893,6 +906,17 @@ apt_status forward_impl(apt_moe_handle *h, const uint16_t *x_router, const uint1
         apt_moe_handle *h;
         ~ClearPost() { h->cur_tail = CombineTail{}; }
     } clear_post{h};
+    if (h->cfg.moe_sparse && h->fused_decode && !pre_w && !tail && h->qbits == 0 && h->gu &&
+        T <= h->gemv_max_tokens &&
+        decode_fused_supported(T, H, h->cfg.moe_intermediate_size, E, K, x_router == x_experts)) {
+        // decode: the whole block (router .. combine) in one persistent kernel
+        STAGE(h, APT_STAGE_GATE_UP, s,
+              launch_decode_fused(x_router, x_experts, h->proj, h->scale, h->pes, T, H, E, K,
+                                  h->cfg.moe_intermediate_size, h->cfg.rms_norm_eps, h->scores,
+                                  idx, w, h->disp(), weights_for(h, false), h->yp, h->op, out,
+                                  h->fsync, h->errflag, s, &h->launches));
+        return APT_OK;
+    }
     if (h->cfg.moe_sparse && router_dispatch_fusable(T, H, E, K)) {
         // decode: router + top-k + dispatch in one launch
         const bool quant = h->qbits > 0;

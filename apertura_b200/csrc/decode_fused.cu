@@ -1,0 +1,830 @@
+// decode_fused.cu -- the whole MoE block for decode-sized calls (T <= 8, bf16
+// experts) as ONE persistent kernel: ESRouter::routeTopK
+// (aptransformer/ESRouter.mm:14-32), ESExperts::sparseForward's gate_up /
+// GeGLU / down (ESExperts.mm:44-57) and the weighted k-order combine
+// (ESExperts.mm:58-59), with the reference's rounding points.
+//
+// Why one kernel: at T = 1 the block moves ~96 MB of expert weights, 15 us of
+// HBM time, but as a chain of launches (router -> gate_up -> down ->
+// combine) every hand-over drains the weight stream and the GEMVs run only
+// 2-3 work items per SM.  Here one CTA per SM does:
+//   1. router: CTA e computes expert e's scores for all T tokens (its proj
+//      row, the token rows and scale arrive by bulk copies); the last CTA to
+//      finish (atomic ticket) selects the top-K of every token (one warp per
+//      token), builds the dispatch and bumps a generation word the others
+//      wait on.  The counters are re-armed by that CTA, so the kernel can be
+//      replayed (CUDA graphs) without host resets.
+//   2. experts: equal-size work items, 32 gate_up rows x H (16 intermediate
+//      columns) or 128 down rows x I, both 11 x 16 KB weight stages; all
+//      gate_up items first, then all down items, spread round-robin over G
+//      CTAs with G chosen so every CTA gets the same number of items.  A
+//      producer warp streams each item's weights through a TMA ring without
+//      waiting on anything but ring slots, so a down item's weights are in
+//      flight while its expert's gate_up items finish elsewhere; a stager
+//      warp waits on the expert's gate_up completion count and copies its
+//      GeGLU rows (L2) into a double buffer; compute warps do the dot
+//      products (f32 accumulate).
+//   3. combine: each down item publishes its rows, then counts in
+//      (token, 128-row block) counters; the item that completes a block's K
+//      contributions sums bf16(w * row) in k order (f32) and stores the
+//      output slice, rounded once.
+// Every wait is bounded; on expiry the kernel records an error code in the
+// handle's error word and returns (apt_moe_sync reports APT_ERR_TIMEOUT).
+#include <cuda.h>
+
+#include "common.cuh"
+#include "launch_util.h"
+#include "moe_internal.h"
+#include "router_select.cuh"
+#include "sm100_ptx.cuh"
+
+namespace apt {
+
+namespace {
+
+using namespace sm100;
+
+constexpr int kCW = 8;                 // compute warps
+constexpr int kProdWarp = kCW;         // TMA producer warp
+constexpr int kStagerWarp = kCW + 1;   // GeGLU-row stager warp
+constexpr int kSignalWarp = kCW + 2;   // completion counts and the combine
+constexpr int kThreads = (kCW + 3) * 32;
+constexpr int kStageBytes = 16384;
+// ring depth by the call's largest per-expert token count: the smaller the
+// staged token rows, the more 16 KB weight stages fit (bytes in flight per SM)
+template <int NTMAX>
+constexpr int stages_for() { return NTMAX <= 2 ? 12 : NTMAX <= 4 ? 10 : 8; }
+constexpr int kMaxT = 8;
+constexpr int kMaxPairs = 64;          // T * K
+constexpr int kGuCols = 16;            // intermediate columns per gate_up item
+constexpr int kDnRows = 128;           // hidden rows per down item
+constexpr int kQ = 8;                  // claimed-item queue between the producer and the rest
+constexpr long long kWait = 4000000000LL;
+// dynamic shared memory cap: 227 KB per CTA less the kernel's static arrays
+constexpr int kMaxDynSmem = 214 * 1024;
+
+// Phase timestamps (%globaltimer, one thread per CTA) for tuning builds
+// compiled with -DAPT_FUSED_TRACE; absent from the library build.
+#ifdef APT_FUSED_TRACE
+__device__ unsigned long long g_ftrace[1024][8];
+#define FT_STAMP(i)                                                        \
+    do {                                                                   \
+        unsigned long long t_;                                             \
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));             \
+        g_ftrace[blockIdx.x][i] = t_;                                      \
+    } while (0)
+#else
+#define FT_STAMP(i) \
+    do {            \
+    } while (0)
+#endif
+
+struct FusedArgs {
+    const uint16_t *xr, *xe;            // router input, expert input [T, H]
+    const uint16_t *scale, *pes, *proj; // router weights
+    int T, H, E, K, I;
+    float eps, root;
+    float *scores;                      // [T, E] scratch
+    int32_t *idx;                       // [T, K]
+    uint16_t *w;                        // [T, K]
+    Dispatch d;
+    uint16_t *yp;                       // [P, I] GeGLU rows, sorted order
+    uint16_t *op;                       // [P, H] down rows, sorted order
+    uint16_t *out;                      // [T, H]
+    int32_t *sync;                      // [0] ticket [1] generation [2] next work item
+                                        // [3, 3+E) gate_up done, then [T][H/128] combine
+                                        // counters
+    int32_t *err;
+};
+
+__device__ __forceinline__ void record_error(int32_t *err, int code, int where) {
+    if (atomicCAS(err, 0, code) == 0) err[1] = where;
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int32_t *p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ int atom_add_acqrel_gpu(int32_t *p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+__device__ __forceinline__ void red_add_release_gpu(int32_t *p, int v) {
+    asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_cta_shared(const int *p) {
+    int v;
+    asm volatile("ld.acquire.cta.shared.s32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void red_add_release_cta_shared(int *p, int v) {
+    asm volatile("red.release.cta.shared.add.s32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ float dot8(const float (&w)[8], const float (&x)[8]) {
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s = fmaf(w[j], x[j], s);
+    return s;
+}
+
+template <int NT, int R>
+__device__ __forceinline__ float pick(const float (&acc)[R][NT], int r, int t) {
+    float v = 0.f;
+#pragma unroll
+    for (int tt = 0; tt < NT; ++tt)
+        if (tt == t) v = acc[r][tt];
+    return v;
+}
+
+// gate_up item: 16 intermediate columns = 16 gate + 16 up rows x H; warp w
+// owns columns j0+2w, j0+2w+1 (2 gate and 2 up rows), lanes split each
+// 256-column stage; tokens read from the staged rows.
+template <int NT, int S>
+__device__ bool gateup_item(const uint8_t *ring, uint64_t *full, uint64_t *empty,
+                            const uint16_t *xs, const int *toks, int nt, const FusedArgs &a,
+                            int &g, int w, int lane, uint16_t *ydst) {
+    const int NK = a.H / 256;
+    int toff[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) toff[t] = (t < nt ? toks[t] : toks[0]) * a.H + lane * 8;
+    float acc[4][NT];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[r][t] = 0.f;
+    for (int kc = 0; kc < NK; ++kc, ++g) {
+        const int s = g % S;
+        if (!mbar_wait(&full[s], (g / S) & 1, kWait)) {
+            record_error(a.err, 71, kc);
+            return false;
+        }
+        const uint8_t *st = ring + s * kStageBytes;
+        float wf[4][8];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            unpack8(*reinterpret_cast<const uint4 *>(st + (2 * w + q) * 512 + lane * 16), wf[q]);
+            unpack8(*reinterpret_cast<const uint4 *>(st + (kGuCols + 2 * w + q) * 512 + lane * 16),
+                    wf[2 + q]);
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            float xf[8];
+            unpack8(*reinterpret_cast<const uint4 *>(xs + toff[t] + kc * 256), xf);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) acc[r][t] += dot8(wf[r], xf);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[r][t] = warp_sum(acc[r][t]);
+    if (lane < nt) {
+        const float y0 = geglu_bf16(rbf(pick<NT, 4>(acc, 0, lane)), rbf(pick<NT, 4>(acc, 2, lane)));
+        const float y1 = geglu_bf16(rbf(pick<NT, 4>(acc, 1, lane)), rbf(pick<NT, 4>(acc, 3, lane)));
+        *reinterpret_cast<uint32_t *>(ydst + (size_t)lane * a.I + 2 * w) = pack_bf2(y0, y1);
+    }
+    return true;
+}
+
+// down item: 128 hidden rows; warp w owns rows 16w..16w+15 as 4 groups of 8
+// lanes, each lane 4 rows x 8 columns of every 64-column stage.
+template <int NT, int S>
+__device__ bool down_item(const uint8_t *ring, uint64_t *full, uint64_t *empty,
+                          const uint16_t *ys, int nt, const FusedArgs &a, int &g, int w, int lane,
+                          uint16_t *odst) {
+    const int NK = a.I / 64;
+    const int gq = lane >> 3, c = lane & 7;
+    const int rbase = 16 * w + 4 * gq;
+    float acc[4][NT];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[r][t] = 0.f;
+    for (int kc = 0; kc < NK; ++kc, ++g) {
+        const int s = g % S;
+        if (!mbar_wait(&full[s], (g / S) & 1, kWait)) {
+            record_error(a.err, 72, kc);
+            return false;
+        }
+        const uint8_t *st = ring + s * kStageBytes;
+        float wf[4][8];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+            unpack8(*reinterpret_cast<const uint4 *>(st + (rbase + r) * 128 + c * 16), wf[r]);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            float yf[8];
+            unpack8(*reinterpret_cast<const uint4 *>(ys + t * a.I + kc * 64 + c * 8), yf);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) acc[r][t] += dot8(wf[r], yf);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            float v = acc[r][t];
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            acc[r][t] = v;
+        }
+    if (c < nt) {
+        uint2 v;
+        v.x = pack_bf2(pick<NT, 4>(acc, 0, c), pick<NT, 4>(acc, 1, c));
+        v.y = pack_bf2(pick<NT, 4>(acc, 2, c), pick<NT, 4>(acc, 3, c));
+        *reinterpret_cast<uint2 *>(odst + (size_t)c * a.H + rbase) = v;
+    }
+    return true;
+}
+
+template <int NTMAX, int S>
+__device__ bool run_gateup(const uint8_t *ring, uint64_t *full, uint64_t *empty,
+                           const uint16_t *xs, const int *toks, int nt, const FusedArgs &a,
+                           int &g, int w, int lane, uint16_t *ydst) {
+    if (nt == 1) return gateup_item<1, S>(ring, full, empty, xs, toks, nt, a, g, w, lane, ydst);
+    if constexpr (NTMAX >= 2)
+        if (nt == 2) return gateup_item<2, S>(ring, full, empty, xs, toks, nt, a, g, w, lane, ydst);
+    if constexpr (NTMAX >= 4)
+        if (nt <= 4) return gateup_item<4, S>(ring, full, empty, xs, toks, nt, a, g, w, lane, ydst);
+    if constexpr (NTMAX >= 8)
+        return gateup_item<8, S>(ring, full, empty, xs, toks, nt, a, g, w, lane, ydst);
+    return false;
+}
+
+template <int NTMAX, int S>
+__device__ bool run_down(const uint8_t *ring, uint64_t *full, uint64_t *empty, const uint16_t *ys,
+                         int nt, const FusedArgs &a, int &g, int w, int lane, uint16_t *odst) {
+    if (nt == 1) return down_item<1, S>(ring, full, empty, ys, nt, a, g, w, lane, odst);
+    if constexpr (NTMAX >= 2)
+        if (nt == 2) return down_item<2, S>(ring, full, empty, ys, nt, a, g, w, lane, odst);
+    if constexpr (NTMAX >= 4)
+        if (nt <= 4) return down_item<4, S>(ring, full, empty, ys, nt, a, g, w, lane, odst);
+    if constexpr (NTMAX >= 8) return down_item<8, S>(ring, full, empty, ys, nt, a, g, w, lane, odst);
+    return false;
+}
+
+template <int NTMAX>
+__global__ void __launch_bounds__(kThreads, 1)
+decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
+                    const __grid_constant__ CUtensorMap tmDN, FusedArgs a) {
+    constexpr int S = stages_for<NTMAX>();
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                ~uintptr_t(1023));
+    uint16_t *xs = reinterpret_cast<uint16_t *>(ring + S * kStageBytes);  // [T][H]
+    uint16_t *ys = xs + (size_t)a.T * a.H;                                       // [2][NTMAX][I]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(ys + 2 * NTMAX * a.I);
+    uint64_t *full = bars, *empty = bars + S;
+    uint64_t *yfull = bars + 2 * S, *yempty = yfull + 2, *xbar = yempty + 2;
+    __shared__ float s_r[kMaxT];
+    __shared__ float s_part[kThreads / 32][kMaxT];
+    __shared__ int s_U, s_skip, s_last, s_gen0;
+    __shared__ int s_idx[kMaxPairs];
+    __shared__ int s_ecnt[kEpMaxExperts], s_eoff[kEpMaxExperts + 1];
+    __shared__ int s_act[kMaxPairs], s_n[kMaxPairs], s_off[kMaxPairs];
+    __shared__ int s_tok[kMaxPairs][kMaxT];
+    __shared__ int s_idone;
+    __shared__ int s_q[kQ];
+    __shared__ __align__(8) uint64_t s_qfull[kQ], s_qempty[kQ];
+    __shared__ int s_inv[kMaxPairs];
+    __shared__ float s_wsel[kMaxPairs];
+    __shared__ int s_slot[kEpMaxExperts];
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int T = a.T, H = a.H, E = a.E, K = a.K, I = a.I;
+    const int P = T * K;
+    const bool has_e = (int)blockIdx.x < E;
+    const bool same_x = a.xr == a.xe;
+    // router staging in the ring (dead once the dispatch is built): x_router
+    // rows (when distinct from the expert input), this CTA's proj row, scale,
+    // per_expert_scale, then all the scores [T][E] f32
+    uint16_t *xr_s = same_x ? xs : reinterpret_cast<uint16_t *>(ring);
+    uint16_t *p_s = reinterpret_cast<uint16_t *>(ring) + (same_x ? 0 : (size_t)T * H);
+    uint16_t *sc_s = p_s + H;
+    uint16_t *pes_s = sc_s + H;
+    float *s_all = reinterpret_cast<float *>(pes_s + ((E + 7) / 8) * 8);
+    int32_t *exit_ctr = a.sync;
+    int32_t *gen = a.sync + 1;
+    int32_t *ticket = a.sync + 3 + E + kMaxT * (H / kDnRows);
+    int32_t *work = a.sync + 2;
+    int32_t *gu_done = a.sync + 3;
+    int32_t *cmb = a.sync + 3 + E;
+    const int NDN = H / kDnRows;
+
+    // ---- 1. router: CTA e computes expert e's scores for all T tokens
+    if (tid == 0) FT_STAMP(0);
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kCW);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&yfull[b], 1);
+            mbar_init(&yempty[b], kCW);
+        }
+        mbar_init(xbar, 1);
+        for (int q = 0; q < kQ; ++q) {
+            mbar_init(&s_qfull[q], 1);
+            mbar_init(&s_qempty[q], kCW + 2);  // compute warps, stager, signal warp
+        }
+        fence_barrier_init();
+        s_idone = 0;
+        s_skip = 0;
+        s_gen0 = *reinterpret_cast<volatile int32_t *>(gen);  // before the ticket
+        const uint32_t row = (uint32_t)H * 2;
+        uint32_t bytes = (uint32_t)T * row + (uint32_t)E * 2;
+        if (!same_x) bytes += (uint32_t)T * row;
+        if (has_e) bytes += 2 * row;
+        mbar_arrive_expect_tx(xbar, bytes);
+        bulk_load(xs, a.xe, (uint32_t)T * row, xbar);
+        if (!same_x) bulk_load(xr_s, a.xr, (uint32_t)T * row, xbar);
+        if (has_e) {
+            bulk_load(p_s, a.proj + (size_t)blockIdx.x * H, row, xbar);
+            bulk_load(sc_s, a.scale, row, xbar);
+        }
+        bulk_load(pes_s, a.pes, (uint32_t)E * 2, xbar);
+        tma_prefetch(&tmGU);
+        tma_prefetch(&tmDN);
+    }
+    __syncthreads();
+    if (!mbar_wait(xbar, 0, kWait) && tid == 0) {
+        record_error(a.err, 70, blockIdx.x);
+        s_skip = 1;
+    }
+    if (tid == 0) FT_STAMP(1);
+    if (has_e) {
+        for (int t = warp; t < T; t += kThreads / 32) {
+            float ss = 0.f;
+            for (int c = lane; c < H / 8; c += 32) {
+                float f[8];
+                unpack8(*reinterpret_cast<const uint4 *>(xr_s + (size_t)t * H + c * 8), f);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) s_r[t] = 1.0f / sqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / (float)H), a.eps));
+        }
+        __syncthreads();
+        float acc[NTMAX];
+#pragma unroll
+        for (int t = 0; t < NTMAX; ++t) acc[t] = 0.f;
+        for (int c = tid; c < H / 8; c += kThreads) {
+            float sf[8], pf[8];
+            unpack8(*reinterpret_cast<const uint4 *>(sc_s + c * 8), sf);
+            unpack8(*reinterpret_cast<const uint4 *>(p_s + c * 8), pf);
+#pragma unroll
+            for (int t = 0; t < NTMAX; ++t) {
+                if (t >= T) break;
+                float f[8];
+                unpack8(*reinterpret_cast<const uint4 *>(xr_s + (size_t)t * H + c * 8), f);
+                const float r = s_r[t];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[t] = fmaf(pf[j], router_h(f[j], r, sf[j], a.root), acc[t]);
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < NTMAX; ++t) {
+            const float v = warp_sum(acc[t]);
+            if (lane == 0) s_part[warp][t] = v;
+        }
+        __syncthreads();
+        if (tid < T) {
+            float v = 0.f;
+#pragma unroll
+            for (int q = 0; q < kThreads / 32; ++q) v += s_part[q][tid];
+            a.scores[(size_t)tid * E + blockIdx.x] = v;
+        }
+    }
+    if (tid == 0) FT_STAMP(2);
+    // ---- ticket: the last CTA to finish its scores bumps the generation
+    __syncthreads();
+    if (tid == 0) {
+        const int prev = atom_add_acqrel_gpu(ticket, 1);  // publishes this CTA's scores
+        s_last = prev == (int)gridDim.x - 1;
+        if (s_last) {
+            *ticket = 0;
+            red_add_release_gpu(gen, 1);  // releases every CTA
+        }
+        const long long t0 = clock64();
+        while (ld_acquire_gpu(gen) == s_gen0) {
+            if (clock64() - t0 > kWait) {
+                record_error(a.err, 73, blockIdx.x);
+                s_skip = 1;
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    for (int i = tid; i < T * E; i += kThreads) s_all[i] = __ldcg(a.scores + i);
+    __syncthreads();
+    if (tid == 0) FT_STAMP(3);
+    // ---- every CTA selects the top-K and builds the dispatch itself, in
+    // shared memory (same inputs and arithmetic, so the same result in every
+    // CTA); CTA 0 also writes idx, w and the dispatch out for the caller.
+    for (int t = warp; t < T; t += kThreads / 32) {
+        int e;
+        float sel_p, sum;
+        if (E <= 128) {
+            float p[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int ee = lane + 32 * j;
+                p[j] = ee < E ? s_all[t * E + ee] : -INFINITY;
+            }
+            select_core<4>(p, E, K, lane, e, sel_p, sum);
+        } else {
+            float p[kMaxPerLane];
+#pragma unroll
+            for (int j = 0; j < kMaxPerLane; ++j) {
+                const int ee = lane + 32 * j;
+                p[j] = ee < E ? s_all[t * E + ee] : -INFINITY;
+            }
+            select_core<kMaxPerLane>(p, E, K, lane, e, sel_p, sum);
+        }
+        if (lane < K) {
+            const uint16_t wb = f2bf(__fmul_rn(__fdiv_rn(sel_p, sum), bf2f(pes_s[e])));
+            s_idx[t * K + lane] = e;
+            s_wsel[t * K + lane] = bf2f(wb);
+            if (blockIdx.x == 0) {
+                a.idx[(size_t)t * K + lane] = e;
+                a.w[(size_t)t * K + lane] = wb;
+            }
+        }
+    }
+    if (tid == 0) FT_STAMP(7);
+    for (int e = tid; e < E; e += kThreads) s_ecnt[e] = 0;
+    __syncthreads();
+    for (int p = tid; p < P; p += kThreads) atomicAdd(&s_ecnt[s_idx[p]], 1);
+    __syncthreads();
+    if (warp == 0) {  // exclusive scan of the counts (E <= 256: 8 per lane) and the active list
+        int loc[8], sum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = lane * 8 + j;
+            loc[j] = e < E ? s_ecnt[e] : 0;
+            sum += loc[j];
+        }
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        int run = incl - sum;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = lane * 8 + j;
+            if (e < E) {
+                s_eoff[e] = run;
+                if (blockIdx.x == 0) {
+                    a.d.counts[e] = loc[j];
+                    a.d.offsets[e] = run;
+                }
+            }
+            run += loc[j];
+        }
+        if (lane == 31) {
+            s_eoff[E] = run;
+            if (blockIdx.x == 0) a.d.offsets[E] = run;
+        }
+        int base = 0;
+        for (int c0 = 0; c0 < E; c0 += 32) {
+            const int e = c0 + lane;
+            const bool has = e < E && s_ecnt[e] > 0;
+            const unsigned m = __ballot_sync(0xffffffffu, has);
+            if (has) {
+                const int u = base + __popc(m & ((1u << lane) - 1u));
+                s_slot[e] = u;
+                s_act[u] = e;
+                s_n[u] = s_ecnt[e];
+                s_off[u] = s_eoff[e];
+                if (blockIdx.x == 0) a.d.active[u] = e;
+            }
+            base += __popc(m);
+        }
+        if (lane == 0) {
+            s_U = base;
+            if (blockIdx.x == 0) *a.d.n_active = base;
+        }
+    }
+    __syncthreads();
+    for (int p = tid; p < P; p += kThreads) {  // stable order within each expert
+        const int e = s_idx[p];
+        int rank = 0;
+        for (int q = 0; q < p; ++q) rank += s_idx[q] == e;
+        const int pos = s_eoff[e] + rank;
+        s_inv[p] = pos;
+        s_tok[s_slot[e]][rank] = p / K;
+        if (blockIdx.x == 0) {
+            a.d.perm[pos] = p;
+            a.d.inv[p] = pos;
+        }
+    }
+    const int U = s_U;
+    __syncthreads();  // the router's staging in the ring is dead from here on
+    if (tid == 0) FT_STAMP(4);
+
+    // ---- 2. expert items
+    const int NGU = I / kGuCols;
+    const int Ngu = U * NGU, N = U * (NGU + NDN);
+    auto producer = [&]() {
+        int g = 0, qi = 0;
+        for (;;) {
+            // claim the next item (global order: every gate_up item before any
+            // down item, so a down item only waits on items already claimed)
+            int i = atomicAdd(work, 1);
+            if (i >= N) i = -1;
+            const int slot = qi % kQ;
+            if (!mbar_wait(&s_qempty[slot], ((qi / kQ) & 1) ^ 1, kWait)) {
+                record_error(a.err, 79, qi);
+                return;
+            }
+            s_q[slot] = i;
+            mbar_arrive(&s_qfull[slot]);
+            ++qi;
+            if (i < 0) break;
+            int r0, nk;
+            const bool gu = i < Ngu;
+            if (gu) {
+                const int u = i / NGU, blk = i - u * NGU;
+                r0 = s_act[u] * 2 * I + blk * kGuCols;
+                nk = H / 256;
+            } else {
+                const int j = i - Ngu, u = j / NDN, hb = j - u * NDN;
+                r0 = s_act[u] * H + hb * kDnRows;
+                nk = I / 64;
+            }
+            for (int kc = 0; kc < nk; ++kc, ++g) {
+                const int s = g % S;
+                if (!mbar_wait(&empty[s], ((g / S) & 1) ^ 1, kWait)) {
+                    record_error(a.err, 74, i);
+                    return;
+                }
+                mbar_arrive_expect_tx(&full[s], kStageBytes);
+                uint8_t *dst = ring + s * kStageBytes;
+                if (gu) {
+                    tma_load_2d(dst, &tmGU, &full[s], kc * 256, r0);
+                    tma_load_2d(dst + kStageBytes / 2, &tmGU, &full[s], kc * 256, r0 + I);
+                } else {
+                    tma_load_2d(dst, &tmDN, &full[s], kc * 64, r0);
+                }
+            }
+        }
+    };
+    int qi = 0;
+    auto next = [&]() -> int {  // the next claimed item, -1 at the end, -2 on a timeout
+        const int slot = qi % kQ;
+        if (!mbar_wait(&s_qfull[slot], (qi / kQ) & 1, kWait)) {
+            if (lane == 0) record_error(a.err, 80, qi);
+            return -2;
+        }
+        const int i = s_q[slot];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_qempty[slot]);
+        ++qi;
+        return i;
+    };
+    auto stager = [&]() {
+        int ub = 0;
+        for (int i = next(); i >= 0; i = next()) {
+            if (i < Ngu) continue;
+            const int u = (i - Ngu) / NDN;
+            if (lane == 0) {
+                const long long t0 = clock64();
+                while (ld_acquire_gpu(gu_done + u) < NGU) {
+                    if (clock64() - t0 > kWait) {
+                        record_error(a.err, 75, u);
+                        break;
+                    }
+                    __nanosleep(32);
+                }
+            }
+            __syncwarp();
+            const int b = ub & 1;
+            if (!mbar_wait(&yempty[b], ((ub >> 1) & 1) ^ 1, kWait)) {
+                if (lane == 0) record_error(a.err, 76, i);
+                return;
+            }
+            const int nv = s_n[u] * I / 8;
+            const uint4 *src = reinterpret_cast<const uint4 *>(a.yp + (size_t)s_off[u] * I);
+            uint4 *dst = reinterpret_cast<uint4 *>(ys + (size_t)b * NTMAX * I);
+            for (int v = lane; v < nv; v += 32) dst[v] = __ldcg(src + v);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&yfull[b]);
+            ++ub;
+        }
+    };
+    auto signal = [&]() {
+        // Global signalling off the compute warps' path: after each item the
+        // four compute warps bump s_idone (release, CTA scope); this warp then
+        // publishes a gate_up item to its expert's count, or counts a down
+        // item into the (token, row block) combine counters and, for every
+        // block the item completes, sums bf16(w * row) in k order (f32) over
+        // the block's K rows and stores the output slice, rounded once.
+        int j = 0;
+        for (int i = next(); i >= 0; i = next(), ++j) {
+            {  // every lane acquires the compute warps' stores of this item
+                const long long t0 = clock64();
+                while (ld_acquire_cta_shared(&s_idone) < kCW * (j + 1)) {
+                    if (clock64() - t0 > kWait) {
+                        if (lane == 0) record_error(a.err, 78, i);
+                        break;
+                    }
+                }
+            }
+            __syncwarp();
+            if (i < Ngu) {
+                if (lane == 0) red_add_release_gpu(gu_done + i / NGU, 1);
+                continue;
+            }
+            const int jj = i - Ngu, u = jj / NDN, hb = jj - u * NDN;
+            const int n = s_n[u];
+            int t = -1;
+            if (lane < n) {
+                t = s_tok[u][lane];
+                if (atom_add_acqrel_gpu(cmb + t * NDN + hb, 1) != K - 1) t = -1;
+            }
+            unsigned fin = __ballot_sync(0xffffffffu, t >= 0);
+            if (fin) __threadfence();
+            while (fin) {
+                const int r = __ffs(fin) - 1;
+                fin &= fin - 1;
+                const int tt = __shfl_sync(0xffffffffu, t, r);
+                if (lane < kDnRows / 8) {
+                    const int h0 = hb * kDnRows + lane * 8;
+                    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                    for (int k = 0; k < K; ++k) {
+                        const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(
+                            a.op + (size_t)s_inv[tt * K + k] * H + h0));
+                        float f[8];
+                        unpack8(v, f);
+                        const float wk = s_wsel[tt * K + k];
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) acc[q] = __fadd_rn(acc[q], rbf(__fmul_rn(wk, f[q])));
+                    }
+                    uint4 o;
+                    o.x = pack_bf2(acc[0], acc[1]);
+                    o.y = pack_bf2(acc[2], acc[3]);
+                    o.z = pack_bf2(acc[4], acc[5]);
+                    o.w = pack_bf2(acc[6], acc[7]);
+                    *reinterpret_cast<uint4 *>(a.out + (size_t)tt * H + h0) = o;
+                }
+            }
+        }
+        if (lane == 0) FT_STAMP(6);
+    };
+    auto compute = [&]() {
+    int g = 0, ub = 0;
+    for (int i = next(); i >= 0; i = next()) {
+        if (i < Ngu) {
+            const int u = i / NGU, blk = i - u * NGU;
+            uint16_t *ydst = a.yp + (size_t)s_off[u] * I + blk * kGuCols;  // + 4 w inside
+            if (!run_gateup<NTMAX, S>(ring, full, empty, xs, s_tok[u], s_n[u], a, g, warp, lane, ydst))
+                return;
+        } else {
+            const int jj = i - Ngu, u = jj / NDN, hb = jj - u * NDN;
+            const int b = ub & 1;
+            if (!mbar_wait(&yfull[b], (ub >> 1) & 1, kWait)) {
+                if (lane == 0) record_error(a.err, 77, i);
+                return;
+            }
+            uint16_t *odst = a.op + (size_t)s_off[u] * H + hb * kDnRows;
+            if (!run_down<NTMAX, S>(ring, full, empty, ys + (size_t)b * NTMAX * I, s_n[u], a, g,
+                                    warp, lane, odst))
+                return;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&yempty[b]);
+            ++ub;
+        }
+        __syncwarp();  // the warp's stores of this item, then one release
+        if (lane == 0) red_add_release_cta_shared(&s_idone, 1);
+    }
+    if (tid == 0) FT_STAMP(5);
+    };
+    if (!s_skip) {
+        if (warp == kProdWarp) {
+            if (lane == 0) producer();
+        } else if (warp == kStagerWarp) {
+            stager();
+        } else if (warp == kSignalWarp) {
+            signal();
+        } else {
+            compute();
+        }
+    }
+    // ---- re-arm the counters for the next call: the last CTA to get here
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        if (atomicAdd(exit_ctr, 1) == (int)gridDim.x - 1) {
+            __threadfence();
+            *work = 0;
+            for (int e = 0; e < E; ++e) gu_done[e] = 0;
+            for (int i = 0; i < T * NDN; ++i) cmb[i] = 0;
+            *exit_ctr = 0;
+        }
+    }
+}
+
+template <int NTMAX>
+size_t fused_smem(int T, int H, int I) {
+    constexpr int S = stages_for<NTMAX>();
+    return 1024 + (size_t)S * kStageBytes + (size_t)T * H * 2 + 2 * (size_t)NTMAX * I * 2 +
+           8 * (2 * S + 5) + 64;
+}
+
+template <int NTMAX>
+cudaError_t fused_attr() {
+    return cudaFuncSetAttribute(decode_fused_kernel<NTMAX>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+}
+
+template <int NTMAX>
+cudaError_t launch_fused_nt(const CUtensorMap &gu, const CUtensorMap &dn, const FusedArgs &a,
+                            cudaStream_t s) {
+    const int dev = current_device();
+    static int occ_cache[64][4] = {};
+    const int slot = NTMAX == 1 ? 0 : NTMAX == 2 ? 1 : NTMAX == 4 ? 2 : 3;
+    int &occ = occ_cache[dev & 63][slot];
+    if (!occ) {
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_fused_kernel<NTMAX>, kThreads,
+                                                      fused_smem<NTMAX>(NTMAX, a.H, a.I));
+        if (occ < 1) return cudaErrorInvalidConfiguration;
+    }
+    // every CTA waits on the router's last CTA: the grid must be resident at
+    // once, one CTA per SM
+    const int grid = grid_sms(dev);
+    if (grid < a.E) return cudaErrorInvalidConfiguration;
+    return launch_ex(decode_fused_kernel<NTMAX>, dim3(grid), dim3(kThreads),
+                     fused_smem<NTMAX>(a.T, a.H, a.I), s, false, gu, dn, a);
+}
+
+size_t fused_smem_T(int T, int H, int I) {
+    return T <= 1 ? fused_smem<1>(T, H, I) : T <= 2 ? fused_smem<2>(T, H, I)
+         : T <= 4 ? fused_smem<4>(T, H, I) : fused_smem<8>(T, H, I);
+}
+
+}  // namespace
+
+cudaError_t decode_fused_init() {
+    cudaError_t e;
+    if ((e = fused_attr<1>()) || (e = fused_attr<2>()) || (e = fused_attr<4>()) ||
+        (e = fused_attr<8>()))
+        return e;
+    return cudaSuccess;
+}
+
+bool decode_fused_supported(int T, int H, int I, int E, int K, bool same_x) {
+    if (T < 1 || T > kMaxT) return false;
+    const int S = T <= 2 ? stages_for<2>() : T <= 4 ? stages_for<4>() : stages_for<8>();
+    const size_t router = (same_x ? 0 : (size_t)T * H * 2) + (size_t)H * 4 +
+                          (size_t)(E + 7) / 8 * 16 + (size_t)T * E * 4;
+    return T * K <= kMaxPairs && K <= 32 && E <= kEpMaxExperts && E % 8 == 0 &&
+           E <= grid_sms(current_device()) && router <= (size_t)S * kStageBytes &&
+           H % 256 == 0 && H % kDnRows == 0 && I % 64 == 0 && I % kGuCols == 0 &&
+           fused_smem_T(T, H, I) <= kMaxDynSmem && encode_tiled_fn() != nullptr;
+}
+
+size_t decode_fused_sync_words(int E, int H) { return 4 + (size_t)E + (size_t)kMaxT * (H / kDnRows); }
+
+cudaError_t launch_decode_fused(const uint16_t *xr, const uint16_t *xe, const uint16_t *proj,
+                                const uint16_t *scale, const uint16_t *pes, int T, int H, int E,
+                                int K, int I, float eps, float *scores, int32_t *idx, uint16_t *w,
+                                const Dispatch &d, const ExpertWeights &wt, uint16_t *yp,
+                                uint16_t *op, uint16_t *out, int32_t *sync, int32_t *err,
+                                cudaStream_t s, int *launches) {
+    CUtensorMap gu, dn;
+    if (!bf16_map_2d(&gu, wt.gu, H, (uint64_t)E * 2 * I, 256, kGuCols, false) ||
+        !bf16_map_2d(&dn, wt.dn, I, (uint64_t)E * H, 64, kDnRows, false))
+        return cudaErrorInvalidValue;
+    FusedArgs a{xr, xe, scale, pes, proj, T, H, E, K, I, eps, (float)(1.0 / sqrt((double)H)),
+                scores, idx, w, d, yp, op, out, sync, err};
+    // the largest per-expert token count is at most T
+    const int nt = T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8;
+    cudaError_t e = nt == 1   ? launch_fused_nt<1>(gu, dn, a, s)
+                    : nt == 2 ? launch_fused_nt<2>(gu, dn, a, s)
+                    : nt == 4 ? launch_fused_nt<4>(gu, dn, a, s)
+                              : launch_fused_nt<8>(gu, dn, a, s);
+    if (launches) ++*launches;
+    return e;
+}
+
+}  // namespace apt
+
+#ifdef APT_FUSED_TRACE
+extern "C" int apt_fused_trace_read(unsigned long long *host) {
+    return (int)cudaMemcpyFromSymbol(host, apt::g_ftrace, sizeof(apt::g_ftrace));
+}
+#endif

@@ -15,6 +15,7 @@
 #include "common.cuh"
 #include "launch_util.h"
 #include "moe_internal.h"
+#include "router_select.cuh"
 #include "sm100_ptx.cuh"
 
 namespace apt {
@@ -60,10 +61,6 @@ __device__ __forceinline__ float token_rrms(const uint16_t *xr, int H, float eps
     return 1.0f / sqrtf(__fadd_rn(ms, eps));
 }
 
-// h = ((x * r) * scale) * root, element-wise, f32 rounding at every step.
-__device__ __forceinline__ float router_h(float x, float r, float sc, float root) {
-    return __fmul_rn(__fmul_rn(__fmul_rn(x, r), sc), root);
-}
 
 // Scores of experts [blockIdx.x*4, +4) for tokens [blockIdx.y*8, +8).  The
 // chunk's token rows, the CTA's 4 proj rows and the scale vector arrive in
@@ -260,71 +257,6 @@ router_scores_tiled(const uint16_t *__restrict__ x, const uint16_t *__restrict__
         for (int j = 0; j < 4; ++j) {
             const int e = e0 + tx * 4 + j;
             if (e < E) scores[(size_t)t * E + e] = acc[i][j];
-        }
-    }
-}
-
-constexpr int kMaxPerLane = 8;  // E <= 256
-
-// Softmax and top-K (descending prob, lower id on ties) of one token's scores
-// p[j] = score of expert lane + 32 j (-inf past E), by one warp.  Lane k < K
-// returns the k-th choice (sel_e, sel_p); every lane returns the k-order sum
-// of the K chosen probabilities.
-// Order-preserving map of f32 to u32 (for single-instruction warp max).
-__device__ __forceinline__ unsigned fkey(float f) {
-    const unsigned b = __float_as_uint(f);
-    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-}
-__device__ __forceinline__ float fkey_inv(unsigned k) {
-    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
-}
-
-// NP = scores per lane (E <= 32 NP); E <= 128 scans 4 slots per lane per round.
-template <int NP>
-__device__ __forceinline__ void select_core(float (&p)[NP], int E, int K, int lane,
-                                            int &sel_e, float &sel_p, float &sum) {
-    float m = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < NP; ++j) m = fmaxf(m, p[j]);
-    m = fkey_inv(__reduce_max_sync(0xffffffffu, fkey(m)));
-    float den = 0.f;
-#pragma unroll
-    for (int j = 0; j < NP; ++j) {
-        const int e = lane + 32 * j;
-        p[j] = (e < E) ? expf(__fsub_rn(p[j], m)) : 0.f;
-        den += p[j];
-    }
-    den = warp_sum(den);
-#pragma unroll
-    for (int j = 0; j < NP; ++j) {
-        const int e = lane + 32 * j;
-        p[j] = (e < E) ? __fdiv_rn(p[j], den) : -1.f;  // -1: never selected
-    }
-    sum = 0.f;
-    sel_p = 0.f;
-    sel_e = -1;
-    unsigned taken = 0;
-    for (int k = 0; k < K; ++k) {
-        float bp = -2.f;  // lane-local best among untaken (lowest id on ties)
-        int be = 0x7fffffff;
-#pragma unroll
-        for (int j = 0; j < NP; ++j) {
-            const int e = lane + 32 * j;
-            if (!((taken >> j) & 1u) && (p[j] > bp)) {
-                bp = p[j];
-                be = e;
-            }
-        }
-        // warp-wide: the largest probability, then the lowest id holding it
-        const unsigned kb = fkey(bp);
-        const unsigned mk = __reduce_max_sync(0xffffffffu, kb);
-        const int we = (int)__reduce_min_sync(0xffffffffu, kb == mk ? (unsigned)be : 0xffffffffu);
-        const float wp = fkey_inv(mk);
-        if ((we & 31) == lane) taken |= 1u << (we >> 5);
-        sum = __fadd_rn(sum, wp);  // sequential in k order, every lane the same
-        if (lane == k) {
-            sel_p = wp;
-            sel_e = we;
         }
     }
 }

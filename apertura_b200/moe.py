@@ -143,6 +143,10 @@ class Handle:
         """Cap on the SMs the persistent kernels of this handle fill (0 = all)."""
         self.check(lib().apt_moe_set_sm_limit(self.h, int(n)))
 
+    def set_fused_decode(self, on: bool):
+        """Decode (T <= 8) as one persistent kernel (default) or the kernel chain."""
+        self.check(lib().apt_moe_set_fused_decode(self.h, int(bool(on))))
+
     def set_gemm_pair(self, mode: int):
         """Tensor-core tile form: 1 CTA pairs, 0 single CTAs, -1 by size."""
         self.check(lib().apt_moe_set_gemm_pair(self.h, int(mode)))

@@ -311,6 +311,15 @@ APT_API int apt_moe_last_launches(const apt_moe_handle *h);
 APT_API apt_status apt_moe_set_gemv_max_tokens(apt_moe_handle *h, int t);
 
 /*
+ * Decode form for T <= gemv_max_tokens (<= 8) with bf16 experts: 1 (default)
+ * = the whole block -- router, dispatch, gate_up, down and the k-order
+ * combine -- in one persistent kernel; 0 = the chain of router, GEMV and
+ * combine kernels.  Same rounding points either way.  Calls with the layer
+ * norms (apt_moe_layer_forward / decoder_ff) use the chain.
+ */
+APT_API apt_status apt_moe_set_fused_decode(apt_moe_handle *h, int on);
+
+/*
  * Tensor-core tile form: 1 = CTA pairs (one M=256 tcgen05.mma over two SMs,
  * each SM staging half the weight tile), 0 = one CTA per 128-row tile,
  * -1 (default) = chosen by size (environment APT_GEMM_PAIR=0/1 overrides the
