@@ -34,10 +34,10 @@ SWEEP = (1, 4, 16, 64)
 H, E, K, I = 2816, 128, 8, 704
 EXPERT_BYTES = (2 * I * H + H * I) * 2          # 11,894,784 B per touched expert
 GATEUP_BYTES = 2 * I * H * 2                    # gate_up part of it
-# DRAM bytes read by the four gate_up launches of one sweep step (T=1,4,16,64),
+# DRAM bytes read by the four expert-stage launches of one sweep step (T=1,4,16,64),
 # from an ncu capture (dram__bytes_read.sum); the command and the per-T figures
-# are in profiles/gate_up_decode_sweep_traffic.txt.
-GATEUP_SWEEP_TRAFFIC = 1992.83e6  # dram__bytes_read.sum, profiles/gate_up_decode_sweep_traffic.txt
+# are in profiles/decode_sweep_traffic.txt.
+GATEUP_SWEEP_TRAFFIC = 2149.07e6  # dram__bytes_read.sum, profiles/decode_sweep_traffic.txt
 ROUTER_BYTES = E * H * 2                        # 720,896 B
 
 
@@ -425,8 +425,8 @@ def run_ours(args):
                          "traffic": args.traffic if args.traffic else GATEUP_SWEEP_TRAFFIC,
                          "traffic_source": ("--traffic argument" if args.traffic else
                                             "fixed figure from one ncu capture (dram__bytes_read"
-                                            ".sum) of the earlier GEMV gate_up launches, "
-                                            "profiles/gate_up_decode_sweep_traffic.txt; not "
+                                            ".sum) of the expert-stage launches, "
+                                            "profiles/decode_sweep_traffic.txt; not "
                                             "measured by this run"),
                          "scope": "sums over the 4 gate_up launches of one sweep step",
                          "algorithmic_bytes": gu_bytes},
