@@ -75,10 +75,9 @@ struct apt_moe_handle {
     uint16_t *proj = nullptr, *scale = nullptr, *pes = nullptr;
     // experts, bf16 (kept when quantised from bf16 so the dense path works)
     uint16_t *gu = nullptr, *dn = nullptr;
-    // bf16 expansion of the quantised experts for the tensor-core path (lazy)
+    // per-call bf16 expansion of the touched quantised experts for the
+    // tensor-core path (scratch of this handle, allocated at first use)
     uint16_t *dq_gu = nullptr, *dq_dn = nullptr;
-    int32_t *dq_ids = nullptr;  // 0..E-1 and E: the "every expert" active list
-    bool dq_ready = false;      // dq_gu / dq_dn hold the current quantised bank
     // experts, affine quantised
     uint32_t *gu_q = nullptr, *dn_q = nullptr;
     uint16_t *gu_s = nullptr, *gu_b = nullptr, *dn_s = nullptr, *dn_b = nullptr;
@@ -208,8 +207,7 @@ std::vector<void **> weight_fields(apt_moe_handle *h) {
             reinterpret_cast<void **>(&h->dn_q),  reinterpret_cast<void **>(&h->gu_s),
             reinterpret_cast<void **>(&h->gu_b),  reinterpret_cast<void **>(&h->dn_s),
             reinterpret_cast<void **>(&h->dn_b),  reinterpret_cast<void **>(&h->gu_sb),
-            reinterpret_cast<void **>(&h->dn_sb), reinterpret_cast<void **>(&h->dq_gu),
-            reinterpret_cast<void **>(&h->dq_dn), reinterpret_cast<void **>(&h->dq_ids)};
+            reinterpret_cast<void **>(&h->dn_sb)};
 }
 
 void drop_graphs(apt_moe_handle *h) {
@@ -385,7 +383,7 @@ extern "C" apt_status apt_moe_destroy(apt_moe_handle *h) {
     void *ptrs[] = {h->proj, h->scale, h->pes, h->gu, h->dn, h->gu_q, h->dn_q, h->gu_s, h->gu_b,
                     h->dn_s, h->dn_b, h->scores, h->idx_i, h->w_i, h->counts, h->offsets,
                     h->perm, h->inv, h->active, h->n_active, h->errflag, h->done, h->hsplit, h->rt_cnt, h->xp, h->yp, h->op,
-                    h->Wd, h->idx2, h->w2, h->xin, h->xout, h->dq_gu, h->dq_dn, h->gu_sb, h->dn_sb, h->xn, h->dq_ids, h->fsync};
+                    h->Wd, h->idx2, h->w2, h->xin, h->xout, h->dq_gu, h->dq_dn, h->gu_sb, h->dn_sb, h->xn, h->fsync};
     for (void *p : ptrs) dfree(p);
     drop_graphs(h);
     if (h->gstream) cudaStreamDestroy(h->gstream);
@@ -524,7 +522,6 @@ extern "C" apt_status apt_moe_selftest_wait(apt_moe_handle *h, int microseconds,
 
 namespace {
 apt_status build_sb(apt_moe_handle *h) {
-    h->dq_ready = false;  // the dequantised copy no longer matches
     const size_t H = h->cfg.hidden_size, E = h->cfg.num_experts, I = h->cfg.moe_intermediate_size;
     const size_t gu_rows = E * 2 * I, dn_rows = E * H;
     dfree(h->gu_sb);
@@ -704,31 +701,21 @@ apt_status run_experts(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
     const bool gemm = T > h->gemv_max_tokens && gemm_supported(H, I);
     if (gemm && quant) {
         // The bf16 GEMM on the dequantised experts (w = scale*q + bias, rounded
-        // to bf16 as MLX's dequantise does).  The expansion of the whole bank is
-        // done once, on the first tensor-core-sized call, and kept until the
-        // quantised weights change: 1.5 GB of HBM at the Gemma-4 shape.
+        // to bf16 as MLX's dequantise does).  Every call expands the experts
+        // it touches (the dispatch's active list) into a scratch bank laid out
+        // like the bf16 weights, then runs the bf16 GEMM on it; the scratch is
+        // allocated at the first tensor-core-sized call (1.5 GB at the
+        // Gemma-4 shape) and nothing of it is reused between calls.
         if (!h->dq_gu) {
             CUDA_TRY(h, dalloc(&h->dq_gu, (size_t)E * 2 * I * H));
             CUDA_TRY(h, dalloc(&h->dq_dn, (size_t)E * H * I));
-            CUDA_TRY(h, dalloc(&h->dq_ids, (size_t)E + 1));
-            std::vector<int32_t> ids(E + 1);
-            for (int e = 0; e < E; ++e) ids[e] = e;
-            ids[E] = E;
-            CUDA_TRY(h, cudaMemcpy(h->dq_ids, ids.data(), sizeof(int32_t) * (E + 1),
-                                   cudaMemcpyHostToDevice));
         }
-        if (!h->dq_ready) {
-            Dispatch all = d;
-            all.active = h->dq_ids;       // every expert
-            all.n_active = h->dq_ids + E;  // = E
-            STAGE(h, APT_STAGE_GATHER, s,
-                  launch_dequant_active(h->gu_q, h->gu_s, h->gu_b, 2 * I, H, h->qbits, all, E,
-                                        h->dq_gu, s, &h->launches));
-            STAGE(h, APT_STAGE_GATHER, s,
-                  launch_dequant_active(h->dn_q, h->dn_s, h->dn_b, H, I, h->qbits, all, E,
-                                        h->dq_dn, s, &h->launches));
-            h->dq_ready = true;
-        }
+        STAGE(h, APT_STAGE_GATHER, s,
+              launch_dequant_active(h->gu_q, h->gu_s, h->gu_b, 2 * I, H, h->qbits, d, E,
+                                    h->dq_gu, s, &h->launches));
+        STAGE(h, APT_STAGE_GATHER, s,
+              launch_dequant_active(h->dn_q, h->dn_s, h->dn_b, H, I, h->qbits, d, E,
+                                    h->dq_dn, s, &h->launches));
         ew.gu = h->dq_gu;
         ew.dn = h->dq_dn;
     }
