@@ -290,11 +290,19 @@ class ESExperts:
 def make_experts(weights: dict, gate_up_name: str, down_name: str, quant_bits: int = 0,
                  group_size: int = 64, **kw) -> ESExperts:
     """esMakeExperts: adopt `<name>.scales/.biases` triples when present, else
-    build from bf16 (quantising at load when quant_bits > 0)."""
+    build from bf16 (quantising at load when quant_bits > 0).  The width of
+    adopted codes is the bundle's (`bundle_bits`, ESWeightLoader::bundleBits,
+    as ESWeightLoader.mm:149-150 passes it); when not given it follows from
+    the triple's shapes: in = groups x group_size, bits = 32 x words / in."""
     if gate_up_name + ".scales" in weights:
         g = gate_up_name
         d = down_name
-        bits = kw.pop("bundle_bits", quant_bits or 4)
+        bits = kw.pop("bundle_bits", None)
+        if bits is None:
+            words, groups = weights[g].shape[-1], weights[g + ".scales"].shape[-1]
+            if (32 * words) % (groups * group_size):
+                raise ValueError(f"{g}: {words} code words for {groups} groups of {group_size}")
+            bits = 32 * words // (groups * group_size)
         return ESExperts.from_quantized(weights[g], weights[g + ".scales"], weights[g + ".biases"],
                                         weights[d], weights[d + ".scales"], weights[d + ".biases"],
                                         bits, group_size, **kw)

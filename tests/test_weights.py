@@ -114,3 +114,24 @@ def test_block_from_checkpoint_matches_direct(tmp_path):
     a, b = blk.forward(d["x"]), ref.forward(d["x"])
     torch.cuda.synchronize()
     assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
+def test_make_experts_bits_from_triple_shapes(monkeypatch):
+    """esMakeExperts adopts a bundle's triples at the bundle's width; without
+    an explicit bundle_bits it follows from the shapes (4-bit and 8-bit)."""
+    import apertura_b200.moe as M
+    seen = {}
+    monkeypatch.setattr(M.ESExperts, "from_quantized",
+                        classmethod(lambda cls, *a, **kw: seen.setdefault("bits", a[6])))
+    for bits in (4, 8):
+        seen.clear()
+        w = {"g": torch.zeros(2, 8, 256 * bits // 32, dtype=torch.int32),
+             "g.scales": torch.zeros(2, 8, 4, dtype=torch.bfloat16),
+             "g.biases": torch.zeros(2, 8, 4, dtype=torch.bfloat16),
+             "d": torch.zeros(2, 256, 4 * bits // 32 * 8, dtype=torch.int32),
+             "d.scales": torch.zeros(2, 256, 1), "d.biases": torch.zeros(2, 256, 1)}
+        M.make_experts(w, "g", "d")
+        assert seen["bits"] == bits
+    seen.clear()
+    M.make_experts(w, "g", "d", bundle_bits=8)
+    assert seen["bits"] == 8
