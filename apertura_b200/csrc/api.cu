@@ -46,7 +46,6 @@ struct apt_moe_handle {
     std::string err;
     int launches = 0;
     int gemv_max_tokens = 8;
-    int gemm_pair = -1;    // CTA-pair GEMM: -1 by size, 0 off, 1 on (apt_moe_set_gemm_pair)
     int sm_limit = 0;      // cap on SMs for persistent grids (0: all)
     bool gemv_tma = true;  // TMA-streamed bf16 GEMV (else the register-prefetch GEMV)
     bool fused_decode = true;  // whole decode block in one kernel (decode_fused.cu)
@@ -354,7 +353,6 @@ extern "C" apt_status apt_moe_create(const apt_moe_config *cfg, apt_moe_handle *
     if (e1 == cudaSuccess) e1 = router_init();
     if (e1 == cudaSuccess) e1 = gemv_init();
     if (e1 == cudaSuccess) e1 = gemm_init();
-    if (e1 == cudaSuccess) e1 = gemm_pair_init();
     if (e1 == cudaSuccess) e1 = gemv_tma_init();
     if (e1 == cudaSuccess) e1 = decode_fused_init();
     if (e1 == cudaSuccess)
@@ -455,13 +453,6 @@ extern "C" apt_status apt_moe_set_fused_decode(apt_moe_handle *h, int on) {
     if (!h || on < 0 || on > 1) return APT_ERR_INVALID;
     drop_graphs(h);
     h->fused_decode = on != 0;
-    return APT_OK;
-}
-
-extern "C" apt_status apt_moe_set_gemm_pair(apt_moe_handle *h, int mode) {
-    if (!h || mode < -1 || mode > 1) return APT_ERR_INVALID;
-    drop_graphs(h);
-    h->gemm_pair = mode;
     return APT_OK;
 }
 
@@ -642,20 +633,6 @@ namespace {
 // Routed rows (T*K) up to which gate_up gathers its A rows itself.
 constexpr int kGatherInGemmRows = 4096;
 
-// CTA-pair GEMM selection: the handle's setting, else APT_GEMM_PAIR (0/1),
-// else by size.
-bool use_pair_gemm(const apt_moe_handle *h, int H, int I, int rows) {
-    static const int env = [] {
-        const char *v = getenv("APT_GEMM_PAIR");
-        return v ? atoi(v) : -1;
-    }();
-    if (!gemm_pair_supported(H, I)) return false;
-    const int mode = h->gemm_pair >= 0 ? h->gemm_pair : env;
-    if (mode >= 0) return mode != 0;
-    (void)rows;
-    return false;
-}
-
 apt_status check_T(apt_moe_handle *h, int T) {
     if (T < 0 || T > h->Tm)
         return fail(h, APT_ERR_INVALID, "T=%d outside [0, max_tokens=%d]", T, h->Tm);
@@ -723,32 +700,22 @@ apt_status run_experts(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
         const int rows_cap = P < h->Pcap ? P : h->Pcap;
         // Few rows per expert: A rows gathered inside the GEMM (tile::gather4);
         // prefill-sized groups: one gather pass, then full-tile TMA copies.
-        const bool pair = use_pair_gemm(h, H, I, rows_cap);
-        const bool gather_in_gemm = !pair && rows_cap <= kGatherInGemmRows;
+        const bool gather_in_gemm = rows_cap <= kGatherInGemmRows;
         if (!gather_in_gemm)
             STAGE(h, APT_STAGE_GATHER, s,
                   launch_gather_rows(x, H, Kp, E, d, rows_cap, h->xp, s, &h->launches, idx, T,
                                      h->errflag));
-        if (pair) {
+        if (gather_in_gemm)
             STAGE(h, APT_STAGE_GATE_UP, s,
-                  launch_gemm_pair_gateup(h->xp, d, nullptr, ew, rows_cap, H, I, E, E, h->yp,
-                                          h->errflag, s, &h->launches));
-            STAGE(h, APT_STAGE_DOWN, s,
-                  launch_gemm_pair_down(h->yp, d, nullptr, ew, rows_cap, H, I, E, E, h->op,
-                                        h->errflag, s, &h->launches));
-        } else {
-            if (gather_in_gemm)
-                STAGE(h, APT_STAGE_GATE_UP, s,
-                      launch_gemm_gateup_gather(x, T, Kp, d, ew, rows_cap, H, I, E, h->yp,
-                                                h->errflag, s, &h->launches));
-            else
-                STAGE(h, APT_STAGE_GATE_UP, s,
-                      launch_gemm_gateup(h->xp, d, ew, rows_cap, H, I, E, h->yp, h->errflag, s,
-                                         &h->launches));
-            STAGE(h, APT_STAGE_DOWN, s,
-                  launch_gemm_down(h->yp, d, ew, rows_cap, H, I, E, h->op, h->errflag, s,
-                                   &h->launches, max_rows));
-        }
+                  launch_gemm_gateup_gather(x, T, Kp, d, ew, rows_cap, H, I, E, h->yp,
+                                            h->errflag, s, &h->launches));
+        else
+            STAGE(h, APT_STAGE_GATE_UP, s,
+                  launch_gemm_gateup(h->xp, d, ew, rows_cap, H, I, E, h->yp, h->errflag, s,
+                                     &h->launches));
+        STAGE(h, APT_STAGE_DOWN, s,
+              launch_gemm_down(h->yp, d, ew, rows_cap, H, I, E, h->op, h->errflag, s,
+                               &h->launches, max_rows));
     } else if (quant && h->gemv_tma && gemv_tma_q_supported(H, I, h->qbits)) {
         STAGE(h, APT_STAGE_GATE_UP, s,
               launch_gemv_tma_q_gateup(x, Kp, d, ew, H, I, E, max_rows, h->yp, h->errflag, s,
@@ -1068,21 +1035,12 @@ extern "C" apt_status apt_moe_experts_grouped(apt_moe_handle *h, const uint16_t 
     d.offsets = (G > E) ? h->perm : h->offsets;
     ExpertWeights ew = weights_for(h, false);
     CUDA_TRY(h, launch_group_offsets(group_counts, G, d.offsets, s, &h->launches));
-    if (use_pair_gemm(h, H, I, R)) {
-        STAGE(h, APT_STAGE_GATE_UP, s,
-              launch_gemm_pair_gateup(rows, d, group_expert, ew, R, H, I, E, G, h->yp, h->errflag,
-                                      s, &h->launches));
-        STAGE(h, APT_STAGE_DOWN, s,
-              launch_gemm_pair_down(h->yp, d, group_expert, ew, R, H, I, E, G, out, h->errflag, s,
-                                    &h->launches));
-    } else {
-        STAGE(h, APT_STAGE_GATE_UP, s,
-              launch_gemm_gateup_grouped(rows, d, group_expert, ew, R, H, I, E, G, h->yp,
-                                         h->errflag, s, &h->launches));
-        STAGE(h, APT_STAGE_DOWN, s,
-              launch_gemm_down_grouped(h->yp, d, group_expert, ew, R, H, I, E, G, out, h->errflag,
-                                       s, &h->launches));
-    }
+    STAGE(h, APT_STAGE_GATE_UP, s,
+          launch_gemm_gateup_grouped(rows, d, group_expert, ew, R, H, I, E, G, h->yp,
+                                     h->errflag, s, &h->launches));
+    STAGE(h, APT_STAGE_DOWN, s,
+          launch_gemm_down_grouped(h->yp, d, group_expert, ew, R, H, I, E, G, out, h->errflag,
+                                   s, &h->launches));
     return APT_OK;
 }
 

@@ -170,18 +170,6 @@ cudaError_t launch_gemm_down_grouped(const uint16_t *yp, const Dispatch &d, cons
                                      int G, uint16_t *out, int32_t *err, cudaStream_t s,
                                      int *launches);
 
-// ---- CTA-pair (cta_group::2, M=256) grouped GEMM (gemm_sm100_pair.cu);
-// g2e may be null (group g = expert g)
-cudaError_t gemm_pair_init();
-bool gemm_pair_supported(int H, int I);
-cudaError_t launch_gemm_pair_gateup(const uint16_t *xp, const Dispatch &d, const int32_t *g2e,
-                                    const ExpertWeights &w, int rows_cap, int H, int I, int E_w,
-                                    int G, uint16_t *yp, int32_t *err, cudaStream_t s,
-                                    int *launches);
-cudaError_t launch_gemm_pair_down(const uint16_t *yp, const Dispatch &d, const int32_t *g2e,
-                                  const ExpertWeights &w, int rows_cap, int H, int I, int E_w,
-                                  int G, uint16_t *out, int32_t *err, cudaStream_t s,
-                                  int *launches);
 // offsets = exclusive scan of G group counts (one CTA); offsets[G] = total
 cudaError_t launch_group_offsets(const int32_t *counts, int G, int32_t *offsets, cudaStream_t s,
                                  int *launches);

@@ -237,111 +237,5 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
 }
 
 
-// ---------------------------------------------------------------- CTA pair
-// Primitives of the two-SM (cta_group::2) form: one tcgen05.mma spans the
-// shared memory and TMEM of both CTAs of an even/odd cluster pair.  Every
-// tcgen05 instruction of a kernel must use the same cta_group, so a pair
-// kernel uses only the *_pair forms below.
-
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-
-// All threads of both CTAs; release/acquire at cluster scope.
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
-                 "barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// shared::cluster address of the variable at `p`'s offset in CTA `rank`.
-__device__ __forceinline__ uint32_t cluster_addr(const void *p, uint32_t rank) {
-    uint32_t out;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
-    return out;
-}
-
-// Arrive (release, cluster scope) on an mbarrier given by its cluster address.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster)
-                 : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// Bounded wait, acquire at cluster scope (arrivals come from the peer CTA).
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, long long limit) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    const long long t0 = clock64();
-    while (!mbar_try_wait_cluster(bar, parity)) {
-        if (clock64() - t0 > limit) return false;
-    }
-    return true;
-}
-
-// Pair form of the tiled load: the tile lands in this CTA's shared memory,
-// the transaction bytes are credited to the mbarrier at cluster address
-// `bar_cluster` (the leader CTA's barrier).  A plain load of this GPU's memory.
-__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map,
-                                                 uint32_t bar_cluster, int c0, int c1) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar_cluster)
-        : "memory");
-}
-
-// TMEM allocation for the pair: the same warp of both CTAs, same slot offset.
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst_smem, uint32_t cols) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(dst_smem)),
-                 "r"(cols)
-                 : "memory");
-}
-
-__device__ __forceinline__ void tmem_relinquish_pair() {
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t cols) {
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols)
-                 : "memory");
-}
-
-// M=256 MMA over the pair, issued by the leader: A rows 0..127 from the
-// leader's shared memory and 128..255 from the peer's (same offsets), B rows
-// 0..N/2-1 from the leader and N/2..N-1 from the peer; each CTA's TMEM gets
-// its 128 rows of D.
-__device__ __forceinline__ void mma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                              uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-// Arrive on the barrier at `bar`'s offset in every CTA of `cta_mask` once the
-// leader's issued MMAs complete.
-__device__ __forceinline__ void mma_commit_pair(uint64_t *bar, uint16_t cta_mask) {
-    asm volatile(
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-        " [%0], %1;" ::"r"(smem_u32(bar)),
-        "h"(cta_mask)
-        : "memory");
-}
-
 }  // namespace sm100
 }  // namespace apt

@@ -147,10 +147,6 @@ class Handle:
         """Decode (T <= 8) as one persistent kernel (default) or the kernel chain."""
         self.check(lib().apt_moe_set_fused_decode(self.h, int(bool(on))))
 
-    def set_gemm_pair(self, mode: int):
-        """Tensor-core tile form: 1 CTA pairs, 0 single CTAs, -1 by size."""
-        self.check(lib().apt_moe_set_gemm_pair(self.h, int(mode)))
-
     def last_counts(self) -> torch.Tensor:
         out = torch.zeros(self.cfg.num_experts, dtype=torch.int32)
         self.check(lib().apt_moe_last_counts(self.h, ctypes.c_void_p(out.data_ptr())))

@@ -320,15 +320,6 @@ APT_API apt_status apt_moe_set_gemv_max_tokens(apt_moe_handle *h, int t);
 APT_API apt_status apt_moe_set_fused_decode(apt_moe_handle *h, int on);
 
 /*
- * Tensor-core tile form: 1 = CTA pairs (one M=256 tcgen05.mma over two SMs,
- * each SM staging half the weight tile), 0 = one CTA per 128-row tile,
- * -1 (default) = chosen by size (environment APT_GEMM_PAIR=0/1 overrides the
- * default).  Both forms accumulate in the same k order with the same
- * rounding points.
- */
-APT_API apt_status apt_moe_set_gemm_pair(apt_moe_handle *h, int mode);
-
-/*
  * Cap on the SMs this handle's persistent kernels fill (0 = all, the
  * default).  Leaves room for kernels that must run beside them, e.g. NCCL's
  * all-to-all while the replicated experts of an expert-parallel step run.
