@@ -63,40 +63,46 @@ __global__ void quantize_affine_kernel(const uint16_t *__restrict__ w, int64_t r
 // Dequantise the rows of every active expert into a bf16 bank with the same
 // [E, rows, cols] layout as the original weights: w = bf16(scale*q + bias).
 // The prefill path runs the bf16 tensor-core GEMM on this bank.  Each thread
-// expands 8 consecutive elements (one 16-byte store).
-__global__ void dequant_active_kernel(const uint32_t *__restrict__ q, const uint16_t *__restrict__ sc,
-                                      const uint16_t *__restrict__ bi, int rows, int cols, int bits,
-                                      const int32_t *__restrict__ active,
-                                      const int32_t *__restrict__ n_active,
-                                      uint16_t *__restrict__ out) {
+// expands 8 consecutive elements: one code word (4-bit) or two (8-bit), one
+// (scale, bias) pair, one 16-byte store; 32-bit index arithmetic (an
+// expert's rows * cols / 8 fits easily).
+__global__ void __launch_bounds__(256)
+dequant_active_kernel(const uint32_t *__restrict__ q, const uint16_t *__restrict__ sc,
+                      const uint16_t *__restrict__ bi, int rows, int cols, int bits,
+                      const int32_t *__restrict__ active, const int32_t *__restrict__ n_active,
+                      uint16_t *__restrict__ out) {
     pdl_trigger();
     pdl_wait();
     if ((int)blockIdx.y >= *n_active) return;
     const int e = active[blockIdx.y];
-    const int per_row = cols / 8;
-    const int64_t nvec = (int64_t)rows * per_row;
-    const int per_word = 32 / bits;
-    const uint32_t mask = (1u << bits) - 1u;
-    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec;
-         v += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r = (int64_t)e * rows + v / per_row;
-        const int c0 = (int)(v % per_row) * 8;
-        const float s = bf2f(sc[r * (cols / 64) + c0 / 64]);
-        const float b = bf2f(bi[r * (cols / 64) + c0 / 64]);
-        const uint32_t *qr = q + r * (cols / per_word);
+    const int nvec = rows * (cols / 8);  // 8-element vectors of this expert
+    const int gpr = cols / 64;           // groups per row
+    const size_t ebase = (size_t)e * rows * cols;
+    const uint32_t *qe = q + ebase * bits / 32;
+    const uint16_t *se = sc + (size_t)e * rows * gpr, *be = bi + (size_t)e * rows * gpr;
+    uint4 *oe = reinterpret_cast<uint4 *>(out + ebase);
+    for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += gridDim.x * blockDim.x) {
+        const int g = v >> 3;  // row-major 64-element groups: 8 vectors each
+        const float s = bf2f(__ldg(se + g)), b = bf2f(__ldg(be + g));
         float f[8];
+        if (bits == 4) {
+            const uint32_t w = __ldg(qe + v);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int c = c0 + i;
-            const uint32_t qi = (qr[c / per_word] >> ((c % per_word) * bits)) & mask;
-            f[i] = fmaf(s, (float)qi, b);
+            for (int i = 0; i < 8; ++i) f[i] = fmaf(s, (float)((w >> (4 * i)) & 15u), b);
+        } else {
+            const uint2 w = __ldg(reinterpret_cast<const uint2 *>(qe) + v);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                f[i] = fmaf(s, (float)((w.x >> (8 * i)) & 255u), b);
+                f[4 + i] = fmaf(s, (float)((w.y >> (8 * i)) & 255u), b);
+            }
         }
         uint4 o;
         o.x = pack_bf2(f[0], f[1]);
         o.y = pack_bf2(f[2], f[3]);
         o.z = pack_bf2(f[4], f[5]);
         o.w = pack_bf2(f[6], f[7]);
-        *reinterpret_cast<uint4 *>(out + r * cols + c0) = o;
+        oe[v] = o;
     }
 }
 
