@@ -49,6 +49,11 @@ struct apt_moe_handle {
     int sm_limit = 0;      // cap on SMs for persistent grids (0: all)
     bool gemv_tma = true;  // TMA-streamed bf16 GEMV (else the register-prefetch GEMV)
     bool fused_decode = true;  // whole decode block in one kernel (decode_fused.cu)
+    // moe_intermediate_size as given when it is not a multiple of 64: the
+    // handle then runs I rounded up to 64, the extra gate / up rows and down
+    // columns zero (GeGLU of a zero row is exactly 0, and a zero column adds
+    // exactly 0), so the outputs are those of the given I
+    int I_user = 0;
 
     // per-stage CUDA-event timing (apt_moe_set_timing / apt_moe_stage_times)
     bool timing = false;
@@ -311,12 +316,18 @@ extern "C" apt_status apt_moe_create(const apt_moe_config *cfg, apt_moe_handle *
     const int H = cfg->hidden_size, E = cfg->num_experts, K = cfg->top_k_experts,
               I = cfg->moe_intermediate_size;
     if (H <= 0 || E <= 0 || K <= 0 || I <= 0 || cfg->max_tokens <= 0) return APT_ERR_INVALID;
-    if (H % 64 || I % 64 || E > 256 || K > 32 || K > E) return APT_ERR_UNSUPPORTED;
+    const bool pad_i = I % 64 != 0;
+    if (H % 64 || (pad_i && (I % 8 || cfg->quant_bits)) || E > 256 || K > 32 || K > E)
+        return APT_ERR_UNSUPPORTED;
     if (cfg->quant_bits && !((cfg->quant_bits == 4 || cfg->quant_bits == 8) &&
                              cfg->quant_group_size == 64))
         return APT_ERR_UNSUPPORTED;
     apt_moe_handle *h = new apt_moe_handle();
     h->cfg = *cfg;
+    if (pad_i) {
+        h->I_user = I;
+        h->cfg.moe_intermediate_size = (I + 63) / 64 * 64;
+    }
     if (cfg->max_tokens > (1 << 24) / K) {
         delete h;
         return APT_ERR_UNSUPPORTED;
@@ -561,8 +572,23 @@ extern "C" apt_status apt_moe_load_experts_bf16(apt_moe_handle *h, const uint16_
         CUDA_TRY(h, dalloc(&h->dn, E * H * I));
     }
     apt_status st;
-    if ((st = copy_in(h, h->gu, gate_up, sizeof(uint16_t) * E * 2 * I * H, on_device))) return st;
-    if ((st = copy_in(h, h->dn, down, sizeof(uint16_t) * E * H * I, on_device))) return st;
+    if (h->I_user) {
+        // [E, 2*Iu, H] and [E, H, Iu] into the zero-padded [E, 2*I, H], [E, H, I]
+        const size_t Iu = h->I_user;
+        CUDA_TRY(h, cudaMemset(h->gu, 0, sizeof(uint16_t) * E * 2 * I * H));
+        CUDA_TRY(h, cudaMemset(h->dn, 0, sizeof(uint16_t) * E * H * I));
+        for (size_t e = 0; e < E; ++e)
+            for (size_t half = 0; half < 2; ++half)
+                CUDA_TRY(h, cudaMemcpy(h->gu + (e * 2 * I + half * I) * H,
+                                       gate_up + (e * 2 * Iu + half * Iu) * H,
+                                       sizeof(uint16_t) * Iu * H, cudaMemcpyDefault));
+        CUDA_TRY(h, cudaMemcpy2D(h->dn, I * 2, down, Iu * 2, Iu * 2, E * H, cudaMemcpyDefault));
+        CUDA_TRY(h, cudaDeviceSynchronize());
+    } else {
+        if ((st = copy_in(h, h->gu, gate_up, sizeof(uint16_t) * E * 2 * I * H, on_device)))
+            return st;
+        if ((st = copy_in(h, h->dn, down, sizeof(uint16_t) * E * H * I, on_device))) return st;
+    }
     if (h->cfg.quant_bits) {
         // ESExperts ctor with quantBits > 0 (ESExperts.mm:13-18): quantise at load,
         // keep bf16 for the dense path.
@@ -594,6 +620,8 @@ extern "C" apt_status apt_moe_load_experts_quant(apt_moe_handle *h, const uint32
                                                  int on_device) {
     if (!h || !gu_q || !gu_s || !gu_b || !dn_q || !dn_s || !dn_b)
         return fail(h, APT_ERR_INVALID, "null quantised expert weight");
+    if (h->I_user)
+        return fail(h, APT_ERR_UNSUPPORTED, "quantised experts need moe_intermediate_size % 64 == 0");
     if (!((bits == 4 || bits == 8) && gs == 64))
         return fail(h, APT_ERR_UNSUPPORTED, "bits=%d group=%d (need bits 4|8, group 64)", bits, gs);
     DeviceGuard g(h->cfg.device);

@@ -77,7 +77,10 @@ typedef struct apt_moe_config {
 APT_API apt_status apt_moe_config_from_json(const char *json_text, apt_moe_config *cfg);
 
 /* Create a handle: validates the config, allocates the workspace for
- * max_tokens on cfg->device.  No weights yet. */
+ * max_tokens on cfg->device.  No weights yet.  hidden_size must be a multiple
+ * of 64; moe_intermediate_size a multiple of 64, or of 8 for bf16 experts (the
+ * handle then pads the experts with zero rows / columns to the next multiple
+ * of 64, which leaves every output unchanged). */
 APT_API apt_status apt_moe_create(const apt_moe_config *cfg, apt_moe_handle **out);
 APT_API apt_status apt_moe_destroy(apt_moe_handle *h);
 

@@ -273,8 +273,9 @@ def test_golden_hf_through_cuda(oracle, case):
     g = load(case)
     gu, dn = _expert_bank(oracle, g)
     H, E, K, I, T = (int(g[k]) for k in ("H", "E", "K", "I", "T"))
-    if H % 64 or I % 64:
-        pytest.skip("shape outside the kernels' 64-multiple contract")
+    if H % 64:
+        pytest.skip("hidden size outside the kernels' 64-multiple contract")
+    # I % 64 != 0 (the unit case, I = 32) runs on zero-padded expert rows
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).to(DEV).view(torch.bfloat16)
     cfg = A.ESModelConfig(hidden_size=H, num_experts=E, top_k_experts=K, moe_intermediate_size=I,
                           moe_sparse=True, max_tokens=T)
