@@ -128,6 +128,8 @@ public:
         if (computeDtype != Dtype::bfloat16)
             throw std::runtime_error("ESRouter: the CUDA path computes in bf16");
         detail::need(projWeight, Dtype::bfloat16, 2, "ESRouter proj");
+        if (scale.dtype != Dtype::bfloat16 || perExpertScale.dtype != Dtype::bfloat16)
+            throw std::runtime_error("ESRouter: scale and per_expert_scale must be bf16");
         if (projWeight.dim(0) != E_ || projWeight.dim(1) != H_ || scale.numel() != H_ ||
             perExpertScale.numel() != E_)
             throw std::runtime_error("ESRouter: weight shapes do not match E, H");
@@ -229,6 +231,9 @@ public:
         for (const Array *a : {&gateUpS, &gateUpB, &downQ, &downS, &downB})
             if (a->on_device != dev)
                 throw std::runtime_error("ESExperts: quantised tensors must all be host or all device");
+        for (const Array *a : {&gateUpS, &gateUpB, &downS, &downB})
+            if (a->dtype != Dtype::bfloat16)
+                throw std::runtime_error("ESExperts: scales and biases must be bf16");
         create(bits, groupSize, topK, maxTokens, device);
         detail::check(apt_moe_load_experts_quant(
                           h_.get(), static_cast<const uint32_t *>(gateUpQ.data),
