@@ -9,25 +9,29 @@
 // combine) every hand-over drains the weight stream and the GEMVs run only
 // 2-3 work items per SM.  Here one CTA per SM does:
 //   1. router: CTA e computes expert e's scores for all T tokens (its proj
-//      row, the token rows and scale arrive by bulk copies); the last CTA to
-//      finish (atomic ticket) selects the top-K of every token (one warp per
-//      token), builds the dispatch and bumps a generation word the others
-//      wait on.  The counters are re-armed by that CTA, so the kernel can be
-//      replayed (CUDA graphs) without host resets.
+//      row, the token rows, scale and per_expert_scale arrive by bulk
+//      copies); an acquire-release ticket finds the last CTA, which bumps a
+//      generation word the others wait on.  Every CTA then reads the T x E
+//      scores and runs softmax, top-K and the dispatch itself in shared
+//      memory (same inputs, same arithmetic, same result in every CTA); CTA 0
+//      writes idx, w and the dispatch out for the caller.
 //   2. experts: equal-size work items, 32 gate_up rows x H (16 intermediate
-//      columns) or 128 down rows x I, both 11 x 16 KB weight stages; all
-//      gate_up items first, then all down items, spread round-robin over G
-//      CTAs with G chosen so every CTA gets the same number of items.  A
-//      producer warp streams each item's weights through a TMA ring without
-//      waiting on anything but ring slots, so a down item's weights are in
-//      flight while its expert's gate_up items finish elsewhere; a stager
-//      warp waits on the expert's gate_up completion count and copies its
-//      GeGLU rows (L2) into a double buffer; compute warps do the dot
-//      products (f32 accumulate).
-//   3. combine: each down item publishes its rows, then counts in
-//      (token, 128-row block) counters; the item that completes a block's K
-//      contributions sums bf16(w * row) in k order (f32) and stores the
-//      output slice, rounded once.
+//      columns) or 128 down rows x I, both 11 x 16 KB weight stages; every
+//      gate_up item precedes every down item in the global order, and CTAs
+//      claim items from an atomic counter (a down item only ever waits on
+//      items already claimed by running CTAs).  A producer warp streams each
+//      claimed item's weights through a TMA ring without waiting on anything
+//      but ring slots, so a down item's weights are in flight while its
+//      expert's gate_up items finish elsewhere; a stager warp waits on the
+//      expert's gate_up completion count and copies its GeGLU rows (L2) into
+//      a double buffer; eight compute warps do the dot products (f32).
+//   3. combine: a signal warp publishes each finished item (release, GPU
+//      scope); for a down item it counts into (token, 128-row block)
+//      counters, and the item that completes a block's K contributions sums
+//      bf16(w * row) in k order (f32) and stores the slice, rounded once.
+// The last CTA to finish re-arms the counters, so the kernel can be replayed
+// (CUDA graphs) without host resets.  The router hand-over needs the whole
+// grid resident: one CTA per SM, grid = SMs.
 // Every wait is bounded; on expiry the kernel records an error code in the
 // handle's error word and returns (apt_moe_sync reports APT_ERR_TIMEOUT).
 #include <cuda.h>
