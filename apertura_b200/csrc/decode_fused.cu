@@ -95,9 +95,9 @@ struct FusedArgs {
     uint16_t *yp;                       // [P, I] GeGLU rows, sorted order
     uint16_t *op;                       // [P, H] down rows, sorted order
     uint16_t *out;                      // [T, H]
-    int32_t *sync;                      // [0] ticket [1] generation [2] next work item
-                                        // [3, 3+E) gate_up done, then [T][H/128] combine
-                                        // counters
+    int32_t *sync;                      // [0] exit count [1] generation [2] next work
+                                        // item [3, 3+E) gate_up done, then [8][H/128]
+                                        // combine counts, then the router ticket
     int32_t *err;
 };
 
