@@ -10,9 +10,9 @@
 // 2-3 work items per SM.  Here one CTA per SM does:
 //   1. router: CTA e computes expert e's scores for all T tokens (its proj
 //      row, the token rows, scale and per_expert_scale arrive by bulk
-//      copies); an acquire-release ticket finds the last CTA, which bumps a
-//      generation word the others wait on.  Every CTA then reads the T x E
-//      scores and runs softmax, top-K and the dispatch itself in shared
+//      copies), stores them and adds one to a count (release); every CTA
+//      waits for the count to reach E (acquire), reads the T x E scores and
+//      runs softmax, top-K and the dispatch itself in shared
 //      memory (same inputs, same arithmetic, same result in every CTA); CTA 0
 //      writes idx, w and the dispatch out for the caller.
 //   2. experts: equal-size work items, 32 gate_up rows x H (16 intermediate
@@ -29,9 +29,10 @@
 //      scope); for a down item it counts into (token, 128-row block)
 //      counters, and the item that completes a block's K contributions sums
 //      bf16(w * row) in k order (f32) and stores the slice, rounded once.
-// The last CTA to finish re-arms the counters, so the kernel can be replayed
-// (CUDA graphs) without host resets.  The router hand-over needs the whole
-// grid resident: one CTA per SM, grid = SMs.
+// Counters come in two sets used by calls of even and odd count; each call
+// zeroes the set the previous call used, so the kernel can be replayed (CUDA
+// graphs) without host resets or a reset step at its end.  The router
+// hand-over needs the whole grid resident: one CTA per SM, grid = SMs.
 // Every wait is bounded; on expiry the kernel records an error code in the
 // handle's error word and returns (apt_moe_sync reports APT_ERR_TIMEOUT).
 #include <cuda.h>
@@ -64,13 +65,21 @@ constexpr int kGuCols = 16;            // intermediate columns per gate_up item
 constexpr int kDnRows = 128;           // hidden rows per down item
 constexpr int kQ = 8;                  // claimed-item queue between the producer and the rest
 constexpr long long kWait = 4000000000LL;
+constexpr int kMaxGrid = 256;          // per-CTA call counters in the sync words
 // dynamic shared memory cap: 227 KB per CTA less the kernel's static arrays
 constexpr int kMaxDynSmem = 214 * 1024;
 
 // Phase timestamps (%globaltimer, one thread per CTA) for tuning builds
 // compiled with -DAPT_FUSED_TRACE; absent from the library build.
 #ifdef APT_FUSED_TRACE
-__device__ unsigned long long g_ftrace[1024][8];
+__device__ unsigned long long g_ftrace[1024][16];
+__device__ unsigned long long g_itrace[1024][16][8];
+#define FT_ITEM(slot, j, v)                                                \
+    do {                                                                   \
+        unsigned long long t_;                                             \
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));             \
+        if ((j) < 16) { g_itrace[blockIdx.x][j][slot] = t_; if (slot == 0) g_itrace[blockIdx.x][j][3] = (v); } \
+    } while (0)
 #define FT_STAMP(i)                                                        \
     do {                                                                   \
         unsigned long long t_;                                             \
@@ -78,10 +87,24 @@ __device__ unsigned long long g_ftrace[1024][8];
         g_ftrace[blockIdx.x][i] = t_;                                      \
     } while (0)
 #else
+#define FT_ITEM(slot, j, v) \
+    do {                    \
+    } while (0)
 #define FT_STAMP(i) \
     do {            \
     } while (0)
 #endif
+
+// Sync words (int32, zeroed once when the handle is created):
+//   [0, kMaxGrid)  per-CTA call count: CTA b increments word b at the start of
+//                  every call; all CTAs run in every call, so all agree on it
+//   two counter sets of set_words() each, used by calls of even / odd count:
+//                  [0] next work item, [1] CTAs whose scores are published,
+//                  [2, 2+E) gate_up items done per active expert, then
+//                  [kMaxT][H/128] combine counts; a call zeroes the other
+//                  parity's set, which the previous call used, for the next
+//                  call (no reset step at the end of a call)
+__host__ __device__ constexpr int set_words(int E, int H) { return 2 + E + kMaxT * (H / kDnRows); }
 
 struct FusedArgs {
     const uint16_t *xr, *xe;            // router input, expert input [T, H]
@@ -95,10 +118,9 @@ struct FusedArgs {
     uint16_t *yp;                       // [P, I] GeGLU rows, sorted order
     uint16_t *op;                       // [P, H] down rows, sorted order
     uint16_t *out;                      // [T, H]
-    int32_t *sync;                      // [0] exit count [1] generation [2] next work
-                                        // item [3, 3+E) gate_up done, then [8][H/128]
-                                        // combine counts, then the router ticket
+    int32_t *sync;                      // see the sync-word layout above set_words()
     int32_t *err;
+    const uint16_t *dn;                 // [E, H, I] down weights (base of tmDN)
 };
 
 __device__ __forceinline__ void record_error(int32_t *err, int code, int where) {
@@ -170,6 +192,7 @@ __device__ bool gateup_item(const uint8_t *ring, uint64_t *full, uint64_t *empty
             return false;
         }
         const uint8_t *st = ring + s * kStageBytes;
+#ifndef APT_FUSED_NOCOMPUTE
         float wf[4][8];
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
@@ -184,6 +207,9 @@ __device__ bool gateup_item(const uint8_t *ring, uint64_t *full, uint64_t *empty
 #pragma unroll
             for (int r = 0; r < 4; ++r) acc[r][t] += dot8(wf[r], xf);
         }
+#else
+        acc[0][0] += st[lane];
+#endif
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
@@ -220,6 +246,12 @@ __device__ bool down_item(const uint8_t *ring, uint64_t *full, uint64_t *empty,
             return false;
         }
         const uint8_t *st = ring + s * kStageBytes;
+#ifdef APT_FUSED_NOCOMPUTE
+        acc[0][0] += st[lane];
+        if (0) {
+#else
+        {
+#endif
         float wf[4][8];
 #pragma unroll
         for (int r = 0; r < 4; ++r)
@@ -230,6 +262,7 @@ __device__ bool down_item(const uint8_t *ring, uint64_t *full, uint64_t *empty,
             unpack8(*reinterpret_cast<const uint4 *>(ys + t * a.I + kc * 64 + c * 8), yf);
 #pragma unroll
             for (int r = 0; r < 4; ++r) acc[r][t] += dot8(wf[r], yf);
+        }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
@@ -294,7 +327,8 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
     uint64_t *yfull = bars + 2 * S, *yempty = yfull + 2, *xbar = yempty + 2;
     __shared__ float s_r[kMaxT];
     __shared__ float s_part[kThreads / 32][kMaxT];
-    __shared__ int s_U, s_skip, s_last, s_gen0;
+    __shared__ int s_U, s_skip;
+    __shared__ uint32_t s_epoch;
     __shared__ int s_idx[kMaxPairs];
     __shared__ int s_ecnt[kEpMaxExperts], s_eoff[kEpMaxExperts + 1];
     __shared__ int s_act[kMaxPairs], s_n[kMaxPairs], s_off[kMaxPairs];
@@ -319,13 +353,8 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
     uint16_t *sc_s = p_s + H;
     uint16_t *pes_s = sc_s + H;
     float *s_all = reinterpret_cast<float *>(pes_s + ((E + 7) / 8) * 8);
-    int32_t *exit_ctr = a.sync;
-    int32_t *gen = a.sync + 1;
-    int32_t *ticket = a.sync + 3 + E + kMaxT * (H / kDnRows);
-    int32_t *work = a.sync + 2;
-    int32_t *gu_done = a.sync + 3;
-    int32_t *cmb = a.sync + 3 + E;
     const int NDN = H / kDnRows;
+    const int SW = set_words(E, H);
 
     // ---- 1. router: CTA e computes expert e's scores for all T tokens
     if (tid == 0) FT_STAMP(0);
@@ -346,7 +375,8 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
         fence_barrier_init();
         s_idone = 0;
         s_skip = 0;
-        s_gen0 = *reinterpret_cast<volatile int32_t *>(gen);  // before the ticket
+        s_epoch = (uint32_t)a.sync[blockIdx.x] + 1u;  // this call's count
+        a.sync[blockIdx.x] = (int32_t)s_epoch;
         const uint32_t row = (uint32_t)H * 2;
         uint32_t bytes = (uint32_t)T * row + (uint32_t)E * 2;
         if (!same_x) bytes += (uint32_t)T * row;
@@ -363,6 +393,16 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
         tma_prefetch(&tmDN);
     }
     __syncthreads();
+    const uint32_t epoch = s_epoch;
+    int32_t *set = a.sync + kMaxGrid + (epoch & 1u) * SW;
+    int32_t *work = set;
+    int32_t *scnt = set + 1;
+    int32_t *gu_done = set + 2;
+    int32_t *cmb = set + 2 + E;
+    {  // the other parity's counters, used by the previous call, for the next one
+        int32_t *other = a.sync + kMaxGrid + ((epoch & 1u) ^ 1u) * SW;
+        for (int i = blockIdx.x * kThreads + tid; i < SW; i += gridDim.x * kThreads) other[i] = 0;
+    }
     if (!mbar_wait(xbar, 0, kWait) && tid == 0) {
         record_error(a.err, 70, blockIdx.x);
         s_skip = 1;
@@ -412,17 +452,13 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
         }
     }
     if (tid == 0) FT_STAMP(2);
-    // ---- ticket: the last CTA to finish its scores bumps the generation
+    // ---- hand-over: each scoring CTA adds one to the count (release, after
+    // its scores); every CTA waits until all E have (acquire), then reads them
     __syncthreads();
     if (tid == 0) {
-        const int prev = atom_add_acqrel_gpu(ticket, 1);  // publishes this CTA's scores
-        s_last = prev == (int)gridDim.x - 1;
-        if (s_last) {
-            *ticket = 0;
-            red_add_release_gpu(gen, 1);  // releases every CTA
-        }
+        if (has_e) red_add_release_gpu(scnt, 1);
         const long long t0 = clock64();
-        while (ld_acquire_gpu(gen) == s_gen0) {
+        while (ld_acquire_gpu(scnt) < E) {
             if (clock64() - t0 > kWait) {
                 record_error(a.err, 73, blockIdx.x);
                 s_skip = 1;
@@ -467,12 +503,16 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
             }
         }
     }
-    if (tid == 0) FT_STAMP(7);
-    for (int e = tid; e < E; e += kThreads) s_ecnt[e] = 0;
+    if (tid == 0) FT_STAMP(8);
     __syncthreads();
-    for (int p = tid; p < P; p += kThreads) atomicAdd(&s_ecnt[s_idx[p]], 1);
-    __syncthreads();
-    if (warp == 0) {  // exclusive scan of the counts (E <= 256: 8 per lane) and the active list
+    // ---- warp 0 builds the dispatch: counts, offsets, active list, stable order
+    if (warp == 0) {
+        for (int e = lane; e < E; e += 32) s_ecnt[e] = 0;
+        __syncwarp();
+        for (int p = lane; p < P; p += 32) atomicAdd(&s_ecnt[s_idx[p]], 1);
+        __syncwarp();
+        if (tid == 0) FT_STAMP(9);
+        // exclusive scan of the counts (E <= 256: 8 per lane) and the active list
         int loc[8], sum = 0;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -503,6 +543,7 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
             s_eoff[E] = run;
             if (blockIdx.x == 0) a.d.offsets[E] = run;
         }
+        __syncwarp();  // s_eoff complete
         int base = 0;
         for (int c0 = 0; c0 < E; c0 += 32) {
             const int e = c0 + lane;
@@ -522,22 +563,23 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
             s_U = base;
             if (blockIdx.x == 0) *a.d.n_active = base;
         }
-    }
-    __syncthreads();
-    for (int p = tid; p < P; p += kThreads) {  // stable order within each expert
-        const int e = s_idx[p];
-        int rank = 0;
-        for (int q = 0; q < p; ++q) rank += s_idx[q] == e;
-        const int pos = s_eoff[e] + rank;
-        s_inv[p] = pos;
-        s_tok[s_slot[e]][rank] = p / K;
-        if (blockIdx.x == 0) {
-            a.d.perm[pos] = p;
-            a.d.inv[p] = pos;
+        __syncwarp();
+        if (tid == 0) FT_STAMP(10);
+        for (int p = lane; p < P; p += 32) {  // stable order within each expert
+            const int e = s_idx[p];
+            int rank = 0;
+            for (int q = 0; q < p; ++q) rank += s_idx[q] == e;
+            const int pos = s_eoff[e] + rank;
+            s_inv[p] = pos;
+            s_tok[s_slot[e]][rank] = p / K;
+            if (blockIdx.x == 0) {
+                a.d.perm[pos] = p;
+                a.d.inv[p] = pos;
+            }
         }
     }
-    const int U = s_U;
     __syncthreads();  // the router's staging in the ring is dead from here on
+    const int U = s_U;
     if (tid == 0) FT_STAMP(4);
 
     // ---- 2. expert items
@@ -556,6 +598,7 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
                 return;
             }
             s_q[slot] = i;
+            FT_ITEM(0, qi, i + 1);
             mbar_arrive(&s_qfull[slot]);
             ++qi;
             if (i < 0) break;
@@ -582,9 +625,14 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
                     tma_load_2d(dst, &tmGU, &full[s], kc * 256, r0);
                     tma_load_2d(dst + kStageBytes / 2, &tmGU, &full[s], kc * 256, r0 + I);
                 } else {
+#ifdef APT_FUSED_DN1D
+                    bulk_load(dst, a.dn + (size_t)r0 * I + (size_t)kc * (kStageBytes / 2), kStageBytes, &full[s]);
+#else
                     tma_load_2d(dst, &tmDN, &full[s], kc * 64, r0);
+#endif
                 }
             }
+            FT_ITEM(6, qi - 1, 0);
         }
     };
     int qi = 0;
@@ -614,6 +662,7 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
                     }
                     __nanosleep(32);
                 }
+                FT_ITEM(5, qi - 1, 0);
             }
             __syncwarp();
             const int b = ub & 1;
@@ -649,6 +698,7 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
                 }
             }
             __syncwarp();
+            if (lane == 0) FT_ITEM(2, j, 0);
             if (i < Ngu) {
                 if (lane == 0) red_add_release_gpu(gu_done + i / NGU, 1);
                 continue;
@@ -704,6 +754,7 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
                 if (lane == 0) record_error(a.err, 77, i);
                 return;
             }
+            if (tid == 0) FT_ITEM(4, qi - 1, 0);
             uint16_t *odst = a.op + (size_t)s_off[u] * H + hb * kDnRows;
             if (!run_down<NTMAX, S>(ring, full, empty, ys + (size_t)b * NTMAX * I, s_n[u], a, g,
                                     warp, lane, odst))
@@ -714,6 +765,7 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
         }
         __syncwarp();  // the warp's stores of this item, then one release
         if (lane == 0) red_add_release_cta_shared(&s_idone, 1);
+        if (tid == 0) FT_ITEM(1, qi - 1, 0);
     }
     if (tid == 0) FT_STAMP(5);
     };
@@ -728,18 +780,10 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
             compute();
         }
     }
-    // ---- re-arm the counters for the next call: the last CTA to get here
+#ifdef APT_FUSED_TRACE
     __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        if (atomicAdd(exit_ctr, 1) == (int)gridDim.x - 1) {
-            __threadfence();
-            *work = 0;
-            for (int e = 0; e < E; ++e) gu_done[e] = 0;
-            for (int i = 0; i < T * NDN; ++i) cmb[i] = 0;
-            *exit_ctr = 0;
-        }
-    }
+    if (tid == 0) FT_STAMP(7);
+#endif
 }
 
 template <int NTMAX>
@@ -796,12 +840,13 @@ bool decode_fused_supported(int T, int H, int I, int E, int K, bool same_x) {
     const size_t router = (same_x ? 0 : (size_t)T * H * 2) + (size_t)H * 4 +
                           (size_t)(E + 7) / 8 * 16 + (size_t)T * E * 4;
     return T * K <= kMaxPairs && K <= 32 && E <= kEpMaxExperts && E % 8 == 0 &&
-           E <= grid_sms(current_device()) && router <= (size_t)S * kStageBytes &&
+           E <= grid_sms(current_device()) && grid_sms(current_device()) <= kMaxGrid &&
+           router <= (size_t)S * kStageBytes &&
            H % 256 == 0 && H % kDnRows == 0 && I % 64 == 0 && I % kGuCols == 0 &&
            fused_smem_T(T, H, I) <= kMaxDynSmem && encode_tiled_fn() != nullptr;
 }
 
-size_t decode_fused_sync_words(int E, int H) { return 4 + (size_t)E + (size_t)kMaxT * (H / kDnRows); }
+size_t decode_fused_sync_words(int E, int H) { return kMaxGrid + 2 * (size_t)set_words(E, H); }
 
 cudaError_t launch_decode_fused(const uint16_t *xr, const uint16_t *xe, const uint16_t *proj,
                                 const uint16_t *scale, const uint16_t *pes, int T, int H, int E,
@@ -814,7 +859,7 @@ cudaError_t launch_decode_fused(const uint16_t *xr, const uint16_t *xe, const ui
         !bf16_map_2d(&dn, wt.dn, I, (uint64_t)E * H, 64, kDnRows, false))
         return cudaErrorInvalidValue;
     FusedArgs a{xr, xe, scale, pes, proj, T, H, E, K, I, eps, (float)(1.0 / sqrt((double)H)),
-                scores, idx, w, d, yp, op, out, sync, err};
+                scores, idx, w, d, yp, op, out, sync, err, wt.dn};
     // the largest per-expert token count is at most T
     const int nt = T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8;
     cudaError_t e = nt == 1   ? launch_fused_nt<1>(gu, dn, a, s)
@@ -830,5 +875,8 @@ cudaError_t launch_decode_fused(const uint16_t *xr, const uint16_t *xe, const ui
 #ifdef APT_FUSED_TRACE
 extern "C" int apt_fused_trace_read(unsigned long long *host) {
     return (int)cudaMemcpyFromSymbol(host, apt::g_ftrace, sizeof(apt::g_ftrace));
+}
+extern "C" int apt_fused_itrace_read(unsigned long long *host) {
+    return (int)cudaMemcpyFromSymbol(host, apt::g_itrace, sizeof(apt::g_itrace));
 }
 #endif
