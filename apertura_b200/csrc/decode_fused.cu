@@ -330,7 +330,7 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
     __shared__ int s_U, s_skip;
     __shared__ uint32_t s_epoch;
     __shared__ int s_idx[kMaxPairs];
-    __shared__ int s_ecnt[kEpMaxExperts], s_eoff[kEpMaxExperts + 1];
+    __shared__ int s_rank[kMaxPairs], s_lt[kMaxPairs], s_cnt[kMaxPairs];
     __shared__ int s_act[kMaxPairs], s_n[kMaxPairs], s_off[kMaxPairs];
     __shared__ int s_tok[kMaxPairs][kMaxT];
     __shared__ int s_idone;
@@ -473,27 +473,26 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
     // ---- every CTA selects the top-K and builds the dispatch itself, in
     // shared memory (same inputs and arithmetic, so the same result in every
     // CTA); CTA 0 also writes idx, w and the dispatch out for the caller.
+    // Selection: one warp per token (select_core: softmax, top-K in
+    // descending probability with lower id on ties, k-order sum), then the
+    // routing weights p_k / sum * per_expert_scale.
     for (int t = warp; t < T; t += kThreads / 32) {
         int e;
         float sel_p, sum;
+        const float *pt = s_all + t * E;
         if (E <= 128) {
             float p[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int ee = lane + 32 * j;
-                p[j] = ee < E ? s_all[t * E + ee] : -INFINITY;
-            }
+            for (int j = 0; j < 4; ++j) p[j] = lane + 32 * j < E ? pt[lane + 32 * j] : -INFINITY;
             select_core<4>(p, E, K, lane, e, sel_p, sum);
         } else {
             float p[kMaxPerLane];
 #pragma unroll
-            for (int j = 0; j < kMaxPerLane; ++j) {
-                const int ee = lane + 32 * j;
-                p[j] = ee < E ? s_all[t * E + ee] : -INFINITY;
-            }
+            for (int j = 0; j < kMaxPerLane; ++j) p[j] = lane + 32 * j < E ? pt[lane + 32 * j] : -INFINITY;
             select_core<kMaxPerLane>(p, E, K, lane, e, sel_p, sum);
         }
         if (lane < K) {
+            if ((unsigned)e >= (unsigned)E) e = 0;  // all-NaN scores: stay in range
             const uint16_t wb = f2bf(__fmul_rn(__fdiv_rn(sel_p, sum), bf2f(pes_s[e])));
             s_idx[t * K + lane] = e;
             s_wsel[t * K + lane] = bf2f(wb);
@@ -503,81 +502,61 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
             }
         }
     }
-    if (tid == 0) FT_STAMP(8);
     __syncthreads();
-    // ---- warp 0 builds the dispatch: counts, offsets, active list, stable order
-    if (warp == 0) {
-        for (int e = lane; e < E; e += 32) s_ecnt[e] = 0;
-        __syncwarp();
-        for (int p = lane; p < P; p += 32) atomicAdd(&s_ecnt[s_idx[p]], 1);
-        __syncwarp();
-        if (tid == 0) FT_STAMP(9);
-        // exclusive scan of the counts (E <= 256: 8 per lane) and the active list
-        int loc[8], sum = 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int e = lane * 8 + j;
-            loc[j] = e < E ? s_ecnt[e] : 0;
-            sum += loc[j];
+    if (tid == 0) FT_STAMP(8);
+    // dispatch position: pairs sorted by expert, stable (pair order inside an
+    // expert); the expert's group offset, size and this pair's rank in it
+    if (tid < P) {
+        const int e = s_idx[tid];
+        int lt = 0, before = 0, n = 0;
+        for (int j = 0; j < P; ++j) {
+            const int ej = s_idx[j];
+            lt += ej < e;
+            n += ej == e;
+            before += (ej == e) & (j < tid);
         }
-        int incl = sum;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int v = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += v;
-        }
-        int run = incl - sum;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int e = lane * 8 + j;
-            if (e < E) {
-                s_eoff[e] = run;
-                if (blockIdx.x == 0) {
-                    a.d.counts[e] = loc[j];
-                    a.d.offsets[e] = run;
-                }
-            }
-            run += loc[j];
-        }
-        if (lane == 31) {
-            s_eoff[E] = run;
-            if (blockIdx.x == 0) a.d.offsets[E] = run;
-        }
-        __syncwarp();  // s_eoff complete
-        int base = 0;
-        for (int c0 = 0; c0 < E; c0 += 32) {
-            const int e = c0 + lane;
-            const bool has = e < E && s_ecnt[e] > 0;
-            const unsigned m = __ballot_sync(0xffffffffu, has);
-            if (has) {
-                const int u = base + __popc(m & ((1u << lane) - 1u));
-                s_slot[e] = u;
-                s_act[u] = e;
-                s_n[u] = s_ecnt[e];
-                s_off[u] = s_eoff[e];
-                if (blockIdx.x == 0) a.d.active[u] = e;
-            }
-            base += __popc(m);
-        }
-        if (lane == 0) {
-            s_U = base;
-            if (blockIdx.x == 0) *a.d.n_active = base;
-        }
-        __syncwarp();
-        if (tid == 0) FT_STAMP(10);
-        for (int p = lane; p < P; p += 32) {  // stable order within each expert
-            const int e = s_idx[p];
-            int rank = 0;
-            for (int q = 0; q < p; ++q) rank += s_idx[q] == e;
-            const int pos = s_eoff[e] + rank;
-            s_inv[p] = pos;
-            s_tok[s_slot[e]][rank] = p / K;
-            if (blockIdx.x == 0) {
-                a.d.perm[pos] = p;
-                a.d.inv[p] = pos;
-            }
+        s_inv[tid] = lt + before;
+        s_rank[tid] = before;
+        s_lt[tid] = lt;
+        s_cnt[tid] = n;
+        if (blockIdx.x == 0) {
+            a.d.perm[lt + before] = tid;
+            a.d.inv[tid] = lt + before;
         }
     }
+    // active experts (ascending id): the first pair of each expert takes slot
+    // #{first pairs of smaller experts}
+    const int nact = __syncthreads_count(tid < P && s_rank[tid] == 0);
+    if (tid == 0) FT_STAMP(9);
+    if (tid < P && s_rank[tid] == 0) {
+        const int e = s_idx[tid];
+        int u = 0;
+        for (int j = 0; j < P; ++j) u += (s_rank[j] == 0) & (s_idx[j] < e);
+        s_slot[e] = u;
+        s_act[u] = e;
+        s_n[u] = s_cnt[tid];
+        s_off[u] = s_lt[tid];
+        if (blockIdx.x == 0) a.d.active[u] = e;
+    }
+    if (blockIdx.x == 0) {  // the dispatch's per-expert counts and offsets
+        for (int e = tid; e < E; e += kThreads) {
+            int lt = 0, n = 0;
+            for (int j = 0; j < P; ++j) {
+                lt += s_idx[j] < e;
+                n += s_idx[j] == e;
+            }
+            a.d.counts[e] = n;
+            a.d.offsets[e] = lt;
+        }
+        if (tid == 0) {
+            a.d.offsets[E] = P;
+            *a.d.n_active = nact;
+        }
+    }
+    if (tid == 0) s_U = nact;
+    __syncthreads();
+    if (tid == 0) FT_STAMP(10);
+    if (tid < P) s_tok[s_slot[s_idx[tid]]][s_rank[tid]] = tid / K;
     __syncthreads();  // the router's staging in the ring is dead from here on
     const int U = s_U;
     if (tid == 0) FT_STAMP(4);

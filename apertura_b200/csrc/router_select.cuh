@@ -28,10 +28,11 @@ __device__ __forceinline__ float fkey_inv(unsigned k) {
     return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
-// NP = scores per lane (E <= 32 NP); E <= 128 scans 4 slots per lane per round.
+// Softmax of one token's scores in place, by one warp: p[j] (expert
+// lane + 32 j) becomes exp(s - max) / sum, rounded as the f32 ops round;
+// slots past E become -1 (never selected).
 template <int NP>
-__device__ __forceinline__ void select_core(float (&p)[NP], int E, int K, int lane,
-                                            int &sel_e, float &sel_p, float &sum) {
+__device__ __forceinline__ void softmax_core(float (&p)[NP], int E, int lane) {
     float m = -INFINITY;
 #pragma unroll
     for (int j = 0; j < NP; ++j) m = fmaxf(m, p[j]);
@@ -49,6 +50,13 @@ __device__ __forceinline__ void select_core(float (&p)[NP], int E, int K, int la
         const int e = lane + 32 * j;
         p[j] = (e < E) ? __fdiv_rn(p[j], den) : -1.f;  // -1: never selected
     }
+}
+
+// NP = scores per lane (E <= 32 NP); E <= 128 scans 4 slots per lane per round.
+template <int NP>
+__device__ __forceinline__ void select_core(float (&p)[NP], int E, int K, int lane,
+                                            int &sel_e, float &sel_p, float &sum) {
+    softmax_core<NP>(p, E, lane);
     sum = 0.f;
     sel_p = 0.f;
     sel_e = -1;
