@@ -359,7 +359,7 @@ extern "C" apt_status apt_moe_create(const apt_moe_config *cfg, apt_moe_handle *
     ALLOC(xin, (size_t)h->Tm * H);
     ALLOC(xout, (size_t)h->Tm * H);
     ALLOC(xn, (size_t)h->Tm * H);
-    ALLOC(fsync, decode_fused_sync_words(E, H));
+    ALLOC(fsync, decode_fused_sync_words(E, H, h->cfg.moe_intermediate_size));
 #undef ALLOC
     if (e1 == cudaSuccess) e1 = router_init();
     if (e1 == cudaSuccess) e1 = gemv_init();
@@ -367,7 +367,7 @@ extern "C" apt_status apt_moe_create(const apt_moe_config *cfg, apt_moe_handle *
     if (e1 == cudaSuccess) e1 = gemv_tma_init();
     if (e1 == cudaSuccess) e1 = decode_fused_init();
     if (e1 == cudaSuccess)
-        e1 = cudaMemset(h->fsync, 0, sizeof(int32_t) * decode_fused_sync_words(E, H));
+        e1 = cudaMemset(h->fsync, 0, sizeof(int32_t) * decode_fused_sync_words(E, H, h->cfg.moe_intermediate_size));
     if (e1 == cudaSuccess) e1 = cudaMemset(h->errflag, 0, 16);
     if (e1 == cudaSuccess) e1 = cudaMemset(h->done, 0, 16 * sizeof(int32_t));
     for (int i = 0; i < APT_STAGE_COUNT && e1 == cudaSuccess; ++i)
@@ -895,8 +895,8 @@ apt_status forward_impl(apt_moe_handle *h, const uint16_t *x_router, const uint1
         STAGE(h, APT_STAGE_GATE_UP, s,
               launch_decode_fused(x_router, x_experts, h->proj, h->scale, h->pes, T, H, E, K,
                                   h->cfg.moe_intermediate_size, h->cfg.rms_norm_eps, h->scores,
-                                  idx, w, h->disp(), weights_for(h, false), h->yp, h->op, out,
-                                  h->fsync, h->errflag, s, &h->launches));
+                                  idx, w, h->disp(), weights_for(h, false), out, h->fsync,
+                                  h->errflag, s, &h->launches));
         return APT_OK;
     }
     if (h->cfg.moe_sparse && router_dispatch_fusable(T, H, E, K)) {

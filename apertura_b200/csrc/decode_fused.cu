@@ -22,17 +22,22 @@
 //      items already claimed by running CTAs).  A producer warp streams each
 //      claimed item's weights through a TMA ring without waiting on anything
 //      but ring slots, so a down item's weights are in flight while its
-//      expert's gate_up items finish elsewhere; a stager warp waits on the
-//      expert's gate_up completion count and copies its GeGLU rows (L2) into
-//      a double buffer; eight compute warps do the dot products (f32).
-//   3. combine: a signal warp publishes each finished item (release, GPU
-//      scope); for a down item it counts into (token, 128-row block)
-//      counters, and the item that completes a block's K contributions sums
-//      bf16(w * row) in k order (f32) and stores the slice, rounded once.
-// Counters come in two sets used by calls of even and odd count; each call
-// zeroes the set the previous call used, so the kernel can be replayed (CUDA
-// graphs) without host resets or a reset step at its end.  The router
-// hand-over needs the whole grid resident: one CTA per SM, grid = SMs.
+//      expert's gate_up items finish elsewhere; eight compute warps do the
+//      dot products (f32).  Hand-overs between CTAs carry no flags: GeGLU
+//      and down rows are stored as 64-bit words tagged with the call's count
+//      (two bf16 values + the count), and a reader polls the words
+//      themselves, so readiness and value arrive in one load.  A stager warp
+//      loads a down item's GeGLU rows this way into a double buffer.
+//   3. combine: the down item (u, hb) of each token's last expert in claim
+//      order -- whose other experts' down items were all claimed before it
+//      -- has its signal warp read the token's K tagged down rows of row
+//      block hb, sum bf16(w * row) in k order (f32) and store the slice,
+//      rounded once.
+// The two counters (next work item, scores published) come in two sets used
+// by calls of even and odd count; each call zeroes the set the previous call
+// used, so the kernel can be replayed (CUDA graphs) without host resets or a
+// reset step at its end.  The router hand-over needs the whole grid
+// resident: one CTA per SM, grid = SMs.
 // Every wait is bounded; on expiry the kernel records an error code in the
 // handle's error word and returns (apt_moe_sync reports APT_ERR_TIMEOUT).
 #include <cuda.h>
@@ -98,13 +103,17 @@ __device__ unsigned long long g_itrace[1024][16][8];
 // Sync words (int32, zeroed once when the handle is created):
 //   [0, kMaxGrid)  per-CTA call count: CTA b increments word b at the start of
 //                  every call; all CTAs run in every call, so all agree on it
-//   two counter sets of set_words() each, used by calls of even / odd count:
-//                  [0] next work item, [1] CTAs whose scores are published,
-//                  [2, 2+E) gate_up items done per active expert, then
-//                  [kMaxT][H/128] combine counts; a call zeroes the other
-//                  parity's set, which the previous call used, for the next
-//                  call (no reset step at the end of a call)
-__host__ __device__ constexpr int set_words(int E, int H) { return 2 + E + kMaxT * (H / kDnRows); }
+//   two counter sets, used by calls of even / odd count: [0] next work item,
+//                  [1] CTAs whose scores are published; a call zeroes the
+//                  other parity's set, which the previous call used, for the
+//                  next call (no reset step at the end of a call)
+//   tagged rows    from word kTagWord (8-byte aligned), u64 each: the call
+//                  count in the high half, two bf16 values in the low half;
+//                  GeGLU rows [kMaxPairs][I/2], then down rows [kMaxPairs][H/2].
+//                  A reader polls a word until it carries this call's count:
+//                  the value and its readiness arrive in one load.
+constexpr int kSetWords = 2;
+constexpr int kTagWord = kMaxGrid + 2 * kSetWords;
 
 struct FusedArgs {
     const uint16_t *xr, *xe;            // router input, expert input [T, H]
@@ -115,12 +124,11 @@ struct FusedArgs {
     int32_t *idx;                       // [T, K]
     uint16_t *w;                        // [T, K]
     Dispatch d;
-    uint16_t *yp;                       // [P, I] GeGLU rows, sorted order
-    uint16_t *op;                       // [P, H] down rows, sorted order
+    unsigned long long *yq;             // [kMaxPairs][I/2] GeGLU rows, sorted order, tagged
+    unsigned long long *oq;             // [kMaxPairs][H/2] down rows, sorted order, tagged
     uint16_t *out;                      // [T, H]
     int32_t *sync;                      // see the sync-word layout above set_words()
     int32_t *err;
-    const uint16_t *dn;                 // [E, H, I] down weights (base of tmDN)
 };
 
 __device__ __forceinline__ void record_error(int32_t *err, int code, int where) {
@@ -133,10 +141,46 @@ __device__ __forceinline__ int ld_acquire_gpu(const int32_t *p) {
     return v;
 }
 
-__device__ __forceinline__ int atom_add_acqrel_gpu(int32_t *p, int v) {
-    int old;
-    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-    return old;
+__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_relaxed_gpu_v2u64(unsigned long long *p, unsigned long long v0,
+                                                     unsigned long long v1) {
+    asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(v0), "l"(v1)
+                 : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Load NW tagged words per lane (p[q], q < n) and wait (bounded) until every
+// word of the warp carries call count `epoch`: each retry reloads all the
+// words not yet current at once, so a retry costs one round trip.
+template <int NW>
+__device__ __forceinline__ void tagged_load(unsigned long long (&x)[NW],
+                                            const unsigned long long *const (&p)[NW], int n,
+                                            uint32_t epoch, int32_t *err, int code, int where) {
+#pragma unroll
+    for (int q = 0; q < NW; ++q) x[q] = q < n ? ld_relaxed_gpu_u64(p[q]) : 0ull;
+    const long long t0 = clock64();
+    for (;;) {
+        bool ok = true;
+#pragma unroll
+        for (int q = 0; q < NW; ++q) ok &= q >= n || (uint32_t)(x[q] >> 32) == epoch;
+        if (__all_sync(0xffffffffu, ok)) return;
+        if (clock64() - t0 > kWait) {
+            record_error(err, code, where);
+            return;
+        }
+        __nanosleep(64);
+#pragma unroll
+        for (int q = 0; q < NW; ++q)
+            if (q < n && (uint32_t)(x[q] >> 32) != epoch) x[q] = ld_relaxed_gpu_u64(p[q]);
+    }
 }
 
 __device__ __forceinline__ void red_add_release_gpu(int32_t *p, int v) {
@@ -175,7 +219,8 @@ __device__ __forceinline__ float pick(const float (&acc)[R][NT], int r, int t) {
 template <int NT, int S>
 __device__ bool gateup_item(const uint8_t *ring, uint64_t *full, uint64_t *empty,
                             const uint16_t *xs, const int *toks, int nt, const FusedArgs &a,
-                            int &g, int w, int lane, uint16_t *ydst) {
+                            int &g, int w, int lane, unsigned long long *ydst,
+                            unsigned long long tag) {
     const int NK = a.H / 256;
     int toff[NT];
 #pragma unroll
@@ -192,7 +237,6 @@ __device__ bool gateup_item(const uint8_t *ring, uint64_t *full, uint64_t *empty
             return false;
         }
         const uint8_t *st = ring + s * kStageBytes;
-#ifndef APT_FUSED_NOCOMPUTE
         float wf[4][8];
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
@@ -207,9 +251,6 @@ __device__ bool gateup_item(const uint8_t *ring, uint64_t *full, uint64_t *empty
 #pragma unroll
             for (int r = 0; r < 4; ++r) acc[r][t] += dot8(wf[r], xf);
         }
-#else
-        acc[0][0] += st[lane];
-#endif
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
@@ -220,7 +261,7 @@ __device__ bool gateup_item(const uint8_t *ring, uint64_t *full, uint64_t *empty
     if (lane < nt) {
         const float y0 = geglu_bf16(rbf(pick<NT, 4>(acc, 0, lane)), rbf(pick<NT, 4>(acc, 2, lane)));
         const float y1 = geglu_bf16(rbf(pick<NT, 4>(acc, 1, lane)), rbf(pick<NT, 4>(acc, 3, lane)));
-        *reinterpret_cast<uint32_t *>(ydst + (size_t)lane * a.I + 2 * w) = pack_bf2(y0, y1);
+        st_relaxed_gpu_u64(ydst + (size_t)lane * (a.I / 2) + w, tag | pack_bf2(y0, y1));
     }
     return true;
 }
@@ -230,7 +271,7 @@ __device__ bool gateup_item(const uint8_t *ring, uint64_t *full, uint64_t *empty
 template <int NT, int S>
 __device__ bool down_item(const uint8_t *ring, uint64_t *full, uint64_t *empty,
                           const uint16_t *ys, int nt, const FusedArgs &a, int &g, int w, int lane,
-                          uint16_t *odst) {
+                          unsigned long long *odst, unsigned long long tag) {
     const int NK = a.I / 64;
     const int gq = lane >> 3, c = lane & 7;
     const int rbase = 16 * w + 4 * gq;
@@ -246,12 +287,6 @@ __device__ bool down_item(const uint8_t *ring, uint64_t *full, uint64_t *empty,
             return false;
         }
         const uint8_t *st = ring + s * kStageBytes;
-#ifdef APT_FUSED_NOCOMPUTE
-        acc[0][0] += st[lane];
-        if (0) {
-#else
-        {
-#endif
         float wf[4][8];
 #pragma unroll
         for (int r = 0; r < 4; ++r)
@@ -262,7 +297,6 @@ __device__ bool down_item(const uint8_t *ring, uint64_t *full, uint64_t *empty,
             unpack8(*reinterpret_cast<const uint4 *>(ys + t * a.I + kc * 64 + c * 8), yf);
 #pragma unroll
             for (int r = 0; r < 4; ++r) acc[r][t] += dot8(wf[r], yf);
-        }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
@@ -277,38 +311,38 @@ __device__ bool down_item(const uint8_t *ring, uint64_t *full, uint64_t *empty,
             v += __shfl_xor_sync(0xffffffffu, v, 4);
             acc[r][t] = v;
         }
-    if (c < nt) {
-        uint2 v;
-        v.x = pack_bf2(pick<NT, 4>(acc, 0, c), pick<NT, 4>(acc, 1, c));
-        v.y = pack_bf2(pick<NT, 4>(acc, 2, c), pick<NT, 4>(acc, 3, c));
-        *reinterpret_cast<uint2 *>(odst + (size_t)c * a.H + rbase) = v;
-    }
+    if (c < nt)
+        st_relaxed_gpu_v2u64(odst + (size_t)c * (a.H / 2) + rbase / 2,
+                             tag | pack_bf2(pick<NT, 4>(acc, 0, c), pick<NT, 4>(acc, 1, c)),
+                             tag | pack_bf2(pick<NT, 4>(acc, 2, c), pick<NT, 4>(acc, 3, c)));
     return true;
 }
 
 template <int NTMAX, int S>
 __device__ bool run_gateup(const uint8_t *ring, uint64_t *full, uint64_t *empty,
                            const uint16_t *xs, const int *toks, int nt, const FusedArgs &a,
-                           int &g, int w, int lane, uint16_t *ydst) {
-    if (nt == 1) return gateup_item<1, S>(ring, full, empty, xs, toks, nt, a, g, w, lane, ydst);
+                           int &g, int w, int lane, unsigned long long *ydst,
+                           unsigned long long tag) {
+    if (nt == 1) return gateup_item<1, S>(ring, full, empty, xs, toks, nt, a, g, w, lane, ydst, tag);
     if constexpr (NTMAX >= 2)
-        if (nt == 2) return gateup_item<2, S>(ring, full, empty, xs, toks, nt, a, g, w, lane, ydst);
+        if (nt == 2) return gateup_item<2, S>(ring, full, empty, xs, toks, nt, a, g, w, lane, ydst, tag);
     if constexpr (NTMAX >= 4)
-        if (nt <= 4) return gateup_item<4, S>(ring, full, empty, xs, toks, nt, a, g, w, lane, ydst);
+        if (nt <= 4) return gateup_item<4, S>(ring, full, empty, xs, toks, nt, a, g, w, lane, ydst, tag);
     if constexpr (NTMAX >= 8)
-        return gateup_item<8, S>(ring, full, empty, xs, toks, nt, a, g, w, lane, ydst);
+        return gateup_item<8, S>(ring, full, empty, xs, toks, nt, a, g, w, lane, ydst, tag);
     return false;
 }
 
 template <int NTMAX, int S>
 __device__ bool run_down(const uint8_t *ring, uint64_t *full, uint64_t *empty, const uint16_t *ys,
-                         int nt, const FusedArgs &a, int &g, int w, int lane, uint16_t *odst) {
-    if (nt == 1) return down_item<1, S>(ring, full, empty, ys, nt, a, g, w, lane, odst);
+                         int nt, const FusedArgs &a, int &g, int w, int lane,
+                         unsigned long long *odst, unsigned long long tag) {
+    if (nt == 1) return down_item<1, S>(ring, full, empty, ys, nt, a, g, w, lane, odst, tag);
     if constexpr (NTMAX >= 2)
-        if (nt == 2) return down_item<2, S>(ring, full, empty, ys, nt, a, g, w, lane, odst);
+        if (nt == 2) return down_item<2, S>(ring, full, empty, ys, nt, a, g, w, lane, odst, tag);
     if constexpr (NTMAX >= 4)
-        if (nt <= 4) return down_item<4, S>(ring, full, empty, ys, nt, a, g, w, lane, odst);
-    if constexpr (NTMAX >= 8) return down_item<8, S>(ring, full, empty, ys, nt, a, g, w, lane, odst);
+        if (nt <= 4) return down_item<4, S>(ring, full, empty, ys, nt, a, g, w, lane, odst, tag);
+    if constexpr (NTMAX >= 8) return down_item<8, S>(ring, full, empty, ys, nt, a, g, w, lane, odst, tag);
     return false;
 }
 
@@ -339,6 +373,7 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
     __shared__ int s_inv[kMaxPairs];
     __shared__ float s_wsel[kMaxPairs];
     __shared__ int s_slot[kEpMaxExperts];
+    __shared__ int s_ulast[kMaxT];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int T = a.T, H = a.H, E = a.E, K = a.K, I = a.I;
@@ -354,7 +389,7 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
     uint16_t *pes_s = sc_s + H;
     float *s_all = reinterpret_cast<float *>(pes_s + ((E + 7) / 8) * 8);
     const int NDN = H / kDnRows;
-    const int SW = set_words(E, H);
+    const int SW = kSetWords;
 
     // ---- 1. router: CTA e computes expert e's scores for all T tokens
     if (tid == 0) FT_STAMP(0);
@@ -397,8 +432,7 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
     int32_t *set = a.sync + kMaxGrid + (epoch & 1u) * SW;
     int32_t *work = set;
     int32_t *scnt = set + 1;
-    int32_t *gu_done = set + 2;
-    int32_t *cmb = set + 2 + E;
+    const unsigned long long tag = (unsigned long long)epoch << 32;
     {  // the other parity's counters, used by the previous call, for the next one
         int32_t *other = a.sync + kMaxGrid + ((epoch & 1u) ^ 1u) * SW;
         for (int i = blockIdx.x * kThreads + tid; i < SW; i += gridDim.x * kThreads) other[i] = 0;
@@ -557,6 +591,11 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
     __syncthreads();
     if (tid == 0) FT_STAMP(10);
     if (tid < P) s_tok[s_slot[s_idx[tid]]][s_rank[tid]] = tid / K;
+    if (tid < T) {  // each token's last expert in claim order (highest active slot)
+        int ul = 0;
+        for (int k = 0; k < K; ++k) ul = max(ul, s_slot[s_idx[tid * K + k]]);
+        s_ulast[tid] = ul;
+    }
     __syncthreads();  // the router's staging in the ring is dead from here on
     const int U = s_U;
     if (tid == 0) FT_STAMP(4);
@@ -604,11 +643,7 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
                     tma_load_2d(dst, &tmGU, &full[s], kc * 256, r0);
                     tma_load_2d(dst + kStageBytes / 2, &tmGU, &full[s], kc * 256, r0 + I);
                 } else {
-#ifdef APT_FUSED_DN1D
-                    bulk_load(dst, a.dn + (size_t)r0 * I + (size_t)kc * (kStageBytes / 2), kStageBytes, &full[s]);
-#else
                     tma_load_2d(dst, &tmDN, &full[s], kc * 64, r0);
-#endif
                 }
             }
             FT_ITEM(6, qi - 1, 0);
@@ -628,45 +663,53 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
         return i;
     };
     auto stager = [&]() {
+        // a down item's GeGLU rows: poll the tagged words (up to kYB loads in
+        // flight per lane) until every one carries this call's count, then
+        // hand the rows to the compute warps through a double buffer
+        constexpr int kYB = 12;
         int ub = 0;
         for (int i = next(); i >= 0; i = next()) {
             if (i < Ngu) continue;
             const int u = (i - Ngu) / NDN;
-            if (lane == 0) {
-                const long long t0 = clock64();
-                while (ld_acquire_gpu(gu_done + u) < NGU) {
-                    if (clock64() - t0 > kWait) {
-                        record_error(a.err, 75, u);
-                        break;
-                    }
-                    __nanosleep(32);
-                }
-                FT_ITEM(5, qi - 1, 0);
-            }
-            __syncwarp();
             const int b = ub & 1;
             if (!mbar_wait(&yempty[b], ((ub >> 1) & 1) ^ 1, kWait)) {
                 if (lane == 0) record_error(a.err, 76, i);
                 return;
             }
-            const int nv = s_n[u] * I / 8;
-            const uint4 *src = reinterpret_cast<const uint4 *>(a.yp + (size_t)s_off[u] * I);
-            uint4 *dst = reinterpret_cast<uint4 *>(ys + (size_t)b * NTMAX * I);
-            for (int v = lane; v < nv; v += 32) dst[v] = __ldcg(src + v);
+            const int nw = s_n[u] * (I / 2);
+            const unsigned long long *src = a.yq + (size_t)s_off[u] * (I / 2);
+            uint32_t *dst = reinterpret_cast<uint32_t *>(ys + (size_t)b * NTMAX * I);
+            for (int v0 = 0; v0 < nw; v0 += 32 * kYB) {
+                unsigned long long x[kYB];
+                const unsigned long long *ptr[kYB];
+                int n = 0;
+#pragma unroll
+                for (int q = 0; q < kYB; ++q) {
+                    const int v = v0 + q * 32 + lane;
+                    ptr[q] = src + (v < nw ? v : 0);
+                    n += v < nw;
+                }
+                tagged_load<kYB>(x, ptr, n, epoch, a.err, 75, u);
+#pragma unroll
+                for (int q = 0; q < kYB; ++q)
+                    if (q < n) dst[v0 + q * 32 + lane] = (uint32_t)x[q];
+            }
+            if (lane == 0) FT_ITEM(5, qi - 1, 0);
             __syncwarp();
             if (lane == 0) mbar_arrive(&yfull[b]);
             ++ub;
         }
     };
     auto signal = [&]() {
-        // Global signalling off the compute warps' path: after each item the
-        // four compute warps bump s_idone (release, CTA scope); this warp then
-        // publishes a gate_up item to its expert's count, or counts a down
-        // item into the (token, row block) combine counters and, for every
-        // block the item completes, sums bf16(w * row) in k order (f32) over
-        // the block's K rows and stores the output slice, rounded once.
+        // The combine, off the compute warps' path: the down item (u, hb) of
+        // each token's last expert in claim order (the highest active slot;
+        // its other experts' down items were claimed before it) sums
+        // bf16(w * row) in k order (f32) over the token's K down rows of row
+        // block hb and stores the output slice, rounded once.  The rows are
+        // read as tagged words; those of other CTAs are almost always ready.
         int j = 0;
         for (int i = next(); i >= 0; i = next(), ++j) {
+            if (i < Ngu) continue;
             {  // every lane acquires the compute warps' stores of this item
                 const long long t0 = clock64();
                 while (ld_acquire_cta_shared(&s_idone) < kCW * (j + 1)) {
@@ -678,42 +721,42 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
             }
             __syncwarp();
             if (lane == 0) FT_ITEM(2, j, 0);
-            if (i < Ngu) {
-                if (lane == 0) red_add_release_gpu(gu_done + i / NGU, 1);
-                continue;
-            }
             const int jj = i - Ngu, u = jj / NDN, hb = jj - u * NDN;
             const int n = s_n[u];
-            int t = -1;
-            if (lane < n) {
-                t = s_tok[u][lane];
-                if (atom_add_acqrel_gpu(cmb + t * NDN + hb, 1) != K - 1) t = -1;
-            }
-            unsigned fin = __ballot_sync(0xffffffffu, t >= 0);
-            if (fin) __threadfence();
+            unsigned fin = __ballot_sync(0xffffffffu, lane < n && s_ulast[s_tok[u][lane < n ? lane : 0]] == u);
             while (fin) {
                 const int r = __ffs(fin) - 1;
                 fin &= fin - 1;
-                const int tt = __shfl_sync(0xffffffffu, t, r);
-                if (lane < kDnRows / 8) {
-                    const int h0 = hb * kDnRows + lane * 8;
-                    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                    for (int k = 0; k < K; ++k) {
-                        const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(
-                            a.op + (size_t)s_inv[tt * K + k] * H + h0));
-                        float f[8];
-                        unpack8(v, f);
-                        const float wk = s_wsel[tt * K + k];
+                const int tt = s_tok[u][r];
+                const int w0 = hb * (kDnRows / 2) + lane * 2;  // 4 hidden columns per lane
+                float acc[4] = {0, 0, 0, 0};
+                for (int k0 = 0; k0 < K; k0 += 8) {
+                    unsigned long long x[16];
+                    const unsigned long long *ptr[16];
+                    const int nk = min(8, K - k0);
 #pragma unroll
-                        for (int q = 0; q < 8; ++q) acc[q] = __fadd_rn(acc[q], rbf(__fmul_rn(wk, f[q])));
+                    for (int q = 0; q < 8; ++q) {
+                        const unsigned long long *src =
+                            a.oq + (size_t)s_inv[tt * K + k0 + (q < nk ? q : 0)] * (H / 2) + w0;
+                        ptr[2 * q] = src;
+                        ptr[2 * q + 1] = src + 1;
                     }
-                    uint4 o;
-                    o.x = pack_bf2(acc[0], acc[1]);
-                    o.y = pack_bf2(acc[2], acc[3]);
-                    o.z = pack_bf2(acc[4], acc[5]);
-                    o.w = pack_bf2(acc[6], acc[7]);
-                    *reinterpret_cast<uint4 *>(a.out + (size_t)tt * H + h0) = o;
+                    tagged_load<16>(x, ptr, 2 * nk, epoch, a.err, 81, tt);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        if (q >= nk) continue;
+                        const uint32_t lo = (uint32_t)x[2 * q], hi = (uint32_t)x[2 * q + 1];
+                        const float f[4] = {bf2f((uint16_t)lo), bf2f((uint16_t)(lo >> 16)),
+                                            bf2f((uint16_t)hi), bf2f((uint16_t)(hi >> 16))};
+                        const float wk = s_wsel[tt * K + k0 + q];
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) acc[c] = __fadd_rn(acc[c], rbf(__fmul_rn(wk, f[c])));
+                    }
                 }
+                uint2 o;
+                o.x = pack_bf2(acc[0], acc[1]);
+                o.y = pack_bf2(acc[2], acc[3]);
+                *reinterpret_cast<uint2 *>(a.out + (size_t)tt * H + 2 * w0) = o;
             }
         }
         if (lane == 0) FT_STAMP(6);
@@ -723,8 +766,9 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
     for (int i = next(); i >= 0; i = next()) {
         if (i < Ngu) {
             const int u = i / NGU, blk = i - u * NGU;
-            uint16_t *ydst = a.yp + (size_t)s_off[u] * I + blk * kGuCols;  // + 4 w inside
-            if (!run_gateup<NTMAX, S>(ring, full, empty, xs, s_tok[u], s_n[u], a, g, warp, lane, ydst))
+            unsigned long long *ydst = a.yq + (size_t)s_off[u] * (I / 2) + blk * (kGuCols / 2);
+            if (!run_gateup<NTMAX, S>(ring, full, empty, xs, s_tok[u], s_n[u], a, g, warp, lane,
+                                      ydst, tag))
                 return;
         } else {
             const int jj = i - Ngu, u = jj / NDN, hb = jj - u * NDN;
@@ -734,9 +778,9 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
                 return;
             }
             if (tid == 0) FT_ITEM(4, qi - 1, 0);
-            uint16_t *odst = a.op + (size_t)s_off[u] * H + hb * kDnRows;
+            unsigned long long *odst = a.oq + (size_t)s_off[u] * (H / 2) + hb * (kDnRows / 2);
             if (!run_down<NTMAX, S>(ring, full, empty, ys + (size_t)b * NTMAX * I, s_n[u], a, g,
-                                    warp, lane, odst))
+                                    warp, lane, odst, tag))
                 return;
             __syncwarp();
             if (lane == 0) mbar_arrive(&yempty[b]);
@@ -825,20 +869,24 @@ bool decode_fused_supported(int T, int H, int I, int E, int K, bool same_x) {
            fused_smem_T(T, H, I) <= kMaxDynSmem && encode_tiled_fn() != nullptr;
 }
 
-size_t decode_fused_sync_words(int E, int H) { return kMaxGrid + 2 * (size_t)set_words(E, H); }
+size_t decode_fused_sync_words(int E, int H, int I) {
+    (void)E;
+    return kTagWord + 2 * (size_t)kMaxPairs * (size_t)(I + H) / 2;
+}
 
 cudaError_t launch_decode_fused(const uint16_t *xr, const uint16_t *xe, const uint16_t *proj,
                                 const uint16_t *scale, const uint16_t *pes, int T, int H, int E,
                                 int K, int I, float eps, float *scores, int32_t *idx, uint16_t *w,
-                                const Dispatch &d, const ExpertWeights &wt, uint16_t *yp,
-                                uint16_t *op, uint16_t *out, int32_t *sync, int32_t *err,
-                                cudaStream_t s, int *launches) {
+                                const Dispatch &d, const ExpertWeights &wt, uint16_t *out,
+                                int32_t *sync, int32_t *err, cudaStream_t s, int *launches) {
+    unsigned long long *yq = reinterpret_cast<unsigned long long *>(sync + kTagWord);
+    unsigned long long *oq = yq + (size_t)kMaxPairs * (I / 2);
     CUtensorMap gu, dn;
     if (!bf16_map_2d(&gu, wt.gu, H, (uint64_t)E * 2 * I, 256, kGuCols, false) ||
         !bf16_map_2d(&dn, wt.dn, I, (uint64_t)E * H, 64, kDnRows, false))
         return cudaErrorInvalidValue;
     FusedArgs a{xr, xe, scale, pes, proj, T, H, E, K, I, eps, (float)(1.0 / sqrt((double)H)),
-                scores, idx, w, d, yp, op, out, sync, err, wt.dn};
+                scores, idx, w, d, yq, oq, out, sync, err};
     // the largest per-expert token count is at most T
     const int nt = T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8;
     cudaError_t e = nt == 1   ? launch_fused_nt<1>(gu, dn, a, s)

@@ -225,17 +225,17 @@ cudaError_t launch_ep_combine(const EpP2PArgs &a, const uint16_t *w, int T, int 
                               int grid, cudaStream_t s);
 // ---- the whole decode block in one persistent kernel (decode_fused.cu):
 // router, dispatch, gate_up, down and combine for T <= 8, bf16 experts.
-// sync: decode_fused_sync_words(E, H) int32, zero at the first call (the
-// kernel re-arms it).
+// sync: decode_fused_sync_words(E, H, I) int32 (counters and the tagged
+// GeGLU / down rows), zeroed once before the first call; the kernel keeps it
+// consistent from call to call itself.
 cudaError_t decode_fused_init();
 bool decode_fused_supported(int T, int H, int I, int E, int K, bool same_x);
-size_t decode_fused_sync_words(int E, int H);
+size_t decode_fused_sync_words(int E, int H, int I);
 cudaError_t launch_decode_fused(const uint16_t *xr, const uint16_t *xe, const uint16_t *proj,
                                 const uint16_t *scale, const uint16_t *pes, int T, int H, int E,
                                 int K, int I, float eps, float *scores, int32_t *idx, uint16_t *w,
-                                const Dispatch &d, const ExpertWeights &wt, uint16_t *yp,
-                                uint16_t *op, uint16_t *out, int32_t *sync, int32_t *err,
-                                cudaStream_t s, int *launches);
+                                const Dispatch &d, const ExpertWeights &wt, uint16_t *out,
+                                int32_t *sync, int32_t *err, cudaStream_t s, int *launches);
 
 // The dispatch (counts, offsets, perm, inv) of the last routing call on h.
 Dispatch handle_dispatch(apt_moe_handle *h);
