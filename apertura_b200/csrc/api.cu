@@ -888,14 +888,16 @@ apt_status forward_impl(apt_moe_handle *h, const uint16_t *x_router, const uint1
         apt_moe_handle *h;
         ~ClearPost() { h->cur_tail = CombineTail{}; }
     } clear_post{h};
-    if (h->cfg.moe_sparse && h->fused_decode && !pre_w && !tail && h->qbits == 0 && h->gu &&
-        T <= h->gemv_max_tokens &&
-        decode_fused_supported(T, H, h->cfg.moe_intermediate_size, E, K, x_router == x_experts)) {
+    const bool fq = h->qbits > 0;
+    if (h->cfg.moe_sparse && h->fused_decode && !pre_w && !tail &&
+        (fq ? h->gu_q && h->gu_sb && h->dn_sb : h->gu != nullptr) && T <= h->gemv_max_tokens &&
+        decode_fused_supported(T, H, h->cfg.moe_intermediate_size, E, K, x_router == x_experts,
+                               h->qbits, h->qgs)) {
         // decode: the whole block (router .. combine) in one persistent kernel
         STAGE(h, APT_STAGE_GATE_UP, s,
               launch_decode_fused(x_router, x_experts, h->proj, h->scale, h->pes, T, H, E, K,
                                   h->cfg.moe_intermediate_size, h->cfg.rms_norm_eps, h->scores,
-                                  idx, w, h->disp(), weights_for(h, false), out, h->fsync,
+                                  idx, w, h->disp(), weights_for(h, fq), out, h->fsync,
                                   h->errflag, s, &h->launches));
         return APT_OK;
     }

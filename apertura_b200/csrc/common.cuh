@@ -30,6 +30,18 @@ __device__ __forceinline__ void unpack8(const uint4 &v, float *f) {
     f[6] = bf_lo(v.w); f[7] = bf_hi(v.w);
 }
 
+// Packed unsigned q -> f32 without the int-to-float unit: OR-ing q into the
+// mantissa of 2^23 gives exactly 2^23 + q, and subtracting 2^23 leaves q.
+template <int BITS>
+__device__ __forceinline__ void unpack_q8(const uint32_t *w, float (&q)[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        q[i] = __fsub_rn(__uint_as_float(((w[i * BITS / 32] >> ((i * BITS) & 31)) &
+                                          ((1u << BITS) - 1u)) |
+                                         0x4B000000u),
+                         8388608.0f);
+}
+
 // Streaming 16-byte global load that does not allocate in L1 (weights are
 // read once per launch).
 __device__ __forceinline__ uint4 ldg_stream(const void *p) {

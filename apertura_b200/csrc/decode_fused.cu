@@ -62,8 +62,23 @@ constexpr int kThreads = (kCW + 3) * 32;
 constexpr int kStageBytes = 16384;
 // ring depth by the call's largest per-expert token count: the smaller the
 // staged token rows, the more 16 KB weight stages fit (bytes in flight per SM)
-template <int NTMAX>
-constexpr int stages_for() { return NTMAX <= 2 ? 12 : NTMAX <= 4 ? 10 : 8; }
+// Quantised experts (BITS = 4 or 8, MLX affine, 64-element groups): the same
+// items, with packed codes streamed in stages of 32 gate_up rows x 256 or 128
+// down rows x 64 columns (1 KB x BITS either way), and each item's (scale,
+// bias) pairs in a ring of kSB slots.
+template <int BITS>
+constexpr int stage_bytes() { return BITS ? 1024 * BITS : kStageBytes; }
+template <int NTMAX, int BITS = 0>
+constexpr int stages_for() {
+    return BITS == 0 ? (NTMAX <= 2 ? 12 : NTMAX <= 4 ? 10 : 8)
+                     : (NTMAX <= 4 ? 144 * 1024 : 112 * 1024) / stage_bytes<BITS>();
+}
+constexpr int kSB = 4;  // (scale, bias) slots: items in flight between the producer and the rest
+// words of one (scale, bias) slot: 32 gate_up rows x gp(H) or 128 down rows x gp(I)
+__host__ __device__ inline int sb_slot_words(int H, int I) {
+    const int gu = 32 * (((H / 64) + 3) / 4 * 4), dn = 128 * (((I / 64) + 3) / 4 * 4);
+    return ((gu > dn ? gu : dn) + 31) / 32 * 32;
+}
 constexpr int kMaxT = 8;
 constexpr int kMaxPairs = 64;          // T * K
 constexpr int kGuCols = 16;            // intermediate columns per gate_up item
@@ -346,19 +361,193 @@ __device__ bool run_down(const uint8_t *ring, uint64_t *full, uint64_t *empty, c
     return false;
 }
 
-template <int NTMAX>
+// Quantised gate_up item: the rows and lanes of gateup_item; a lane's 8
+// codes of a row lie in one 64-element group, so its contribution is
+// s * sum(q x) + b * sum(x) in f32, with (s, b) from the item's slot `sbs`
+// ([32 rows][gp] (scale | bias << 16) words).
+template <int NT, int S, int BITS>
+__device__ bool gateup_item_q(const uint8_t *ring, uint64_t *full, uint64_t *empty,
+                              const uint16_t *xs, const uint32_t *sbs, int gp, const int *toks,
+                              int nt, const FusedArgs &a, int &g, int w, int lane,
+                              unsigned long long *ydst, unsigned long long tag) {
+    constexpr int SBY = stage_bytes<BITS>();
+    constexpr int RW = 256 * BITS / 32;  // words per row per stage
+    constexpr int LW = BITS / 4;         // words per lane per row
+    const int NK = a.H / 256;
+    int toff[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) toff[t] = (t < nt ? toks[t] : toks[0]) * a.H + lane * 8;
+    float acc[4][NT];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[r][t] = 0.f;
+    for (int kc = 0; kc < NK; ++kc, ++g) {
+        const int s = g % S;
+        if (!mbar_wait(&full[s], (g / S) & 1, kWait)) {
+            record_error(a.err, 71, kc);
+            return false;
+        }
+        const uint32_t *st = reinterpret_cast<const uint32_t *>(ring + s * SBY);
+        const int grp = kc * 4 + (lane >> 3);
+        float qf[4][8], sr[4], br[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int row = (q < 2 ? 0 : kGuCols) + 2 * w + (q & 1);
+            uint32_t wd[LW];
+#pragma unroll
+            for (int k = 0; k < LW; ++k) wd[k] = st[row * RW + lane * LW + k];
+            unpack_q8<BITS>(wd, qf[q]);
+            const uint32_t pv = sbs[row * gp + grp];
+            sr[q] = bf_lo(pv);
+            br[q] = bf_hi(pv);
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            float xf[8];
+            unpack8(*reinterpret_cast<const uint4 *>(xs + toff[t] + kc * 256), xf);
+            float xsum = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) xsum += xf[i];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) acc[r][t] += fmaf(sr[r], dot8(qf[r], xf), br[r] * xsum);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[r][t] = warp_sum(acc[r][t]);
+    if (lane < nt) {
+        const float y0 = geglu_bf16(rbf(pick<NT, 4>(acc, 0, lane)), rbf(pick<NT, 4>(acc, 2, lane)));
+        const float y1 = geglu_bf16(rbf(pick<NT, 4>(acc, 1, lane)), rbf(pick<NT, 4>(acc, 3, lane)));
+        st_relaxed_gpu_u64(ydst + (size_t)lane * (a.I / 2) + w, tag | pack_bf2(y0, y1));
+    }
+    return true;
+}
+
+// Quantised down item: the rows and lanes of down_item; a stage is one
+// 64-element group of the 128 rows.
+template <int NT, int S, int BITS>
+__device__ bool down_item_q(const uint8_t *ring, uint64_t *full, uint64_t *empty,
+                            const uint16_t *ys, const uint32_t *sbs, int gp, int nt,
+                            const FusedArgs &a, int &g, int w, int lane, unsigned long long *odst,
+                            unsigned long long tag) {
+    constexpr int SBY = stage_bytes<BITS>();
+    constexpr int RW = 64 * BITS / 32;
+    constexpr int LW = BITS / 4;
+    const int NK = a.I / 64;
+    const int gq = lane >> 3, c = lane & 7;
+    const int rbase = 16 * w + 4 * gq;
+    float acc[4][NT];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[r][t] = 0.f;
+    for (int kc = 0; kc < NK; ++kc, ++g) {
+        const int s = g % S;
+        if (!mbar_wait(&full[s], (g / S) & 1, kWait)) {
+            record_error(a.err, 72, kc);
+            return false;
+        }
+        const uint32_t *st = reinterpret_cast<const uint32_t *>(ring + s * SBY);
+        float qf[4][8], sr[4], br[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            uint32_t wd[LW];
+#pragma unroll
+            for (int k = 0; k < LW; ++k) wd[k] = st[(rbase + r) * RW + c * LW + k];
+            unpack_q8<BITS>(wd, qf[r]);
+            const uint32_t pv = sbs[(rbase + r) * gp + kc];
+            sr[r] = bf_lo(pv);
+            br[r] = bf_hi(pv);
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            float yf[8];
+            unpack8(*reinterpret_cast<const uint4 *>(ys + t * a.I + kc * 64 + c * 8), yf);
+            float ysum = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ysum += yf[i];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) acc[r][t] += fmaf(sr[r], dot8(qf[r], yf), br[r] * ysum);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            float v = acc[r][t];
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            acc[r][t] = v;
+        }
+    if (c < nt)
+        st_relaxed_gpu_v2u64(odst + (size_t)c * (a.H / 2) + rbase / 2,
+                             tag | pack_bf2(pick<NT, 4>(acc, 0, c), pick<NT, 4>(acc, 1, c)),
+                             tag | pack_bf2(pick<NT, 4>(acc, 2, c), pick<NT, 4>(acc, 3, c)));
+    return true;
+}
+
+template <int NTMAX, int S, int BITS>
+__device__ bool run_gateup_q(const uint8_t *ring, uint64_t *full, uint64_t *empty,
+                             const uint16_t *xs, const uint32_t *sbs, int gp, const int *toks,
+                             int nt, const FusedArgs &a, int &g, int w, int lane,
+                             unsigned long long *ydst, unsigned long long tag) {
+    if (nt == 1)
+        return gateup_item_q<1, S, BITS>(ring, full, empty, xs, sbs, gp, toks, nt, a, g, w, lane, ydst, tag);
+    if constexpr (NTMAX >= 2)
+        if (nt == 2)
+            return gateup_item_q<2, S, BITS>(ring, full, empty, xs, sbs, gp, toks, nt, a, g, w, lane, ydst, tag);
+    if constexpr (NTMAX >= 4)
+        if (nt <= 4)
+            return gateup_item_q<4, S, BITS>(ring, full, empty, xs, sbs, gp, toks, nt, a, g, w, lane, ydst, tag);
+    if constexpr (NTMAX >= 8)
+        return gateup_item_q<8, S, BITS>(ring, full, empty, xs, sbs, gp, toks, nt, a, g, w, lane, ydst, tag);
+    return false;
+}
+
+template <int NTMAX, int S, int BITS>
+__device__ bool run_down_q(const uint8_t *ring, uint64_t *full, uint64_t *empty, const uint16_t *ys,
+                           const uint32_t *sbs, int gp, int nt, const FusedArgs &a, int &g, int w,
+                           int lane, unsigned long long *odst, unsigned long long tag) {
+    if (nt == 1) return down_item_q<1, S, BITS>(ring, full, empty, ys, sbs, gp, nt, a, g, w, lane, odst, tag);
+    if constexpr (NTMAX >= 2)
+        if (nt == 2)
+            return down_item_q<2, S, BITS>(ring, full, empty, ys, sbs, gp, nt, a, g, w, lane, odst, tag);
+    if constexpr (NTMAX >= 4)
+        if (nt <= 4)
+            return down_item_q<4, S, BITS>(ring, full, empty, ys, sbs, gp, nt, a, g, w, lane, odst, tag);
+    if constexpr (NTMAX >= 8)
+        return down_item_q<8, S, BITS>(ring, full, empty, ys, sbs, gp, nt, a, g, w, lane, odst, tag);
+    return false;
+}
+
+template <int NTMAX, int BITS>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
-                    const __grid_constant__ CUtensorMap tmDN, FusedArgs a) {
-    constexpr int S = stages_for<NTMAX>();
+                    const __grid_constant__ CUtensorMap tmDN,
+                    const __grid_constant__ CUtensorMap tmSG,
+                    const __grid_constant__ CUtensorMap tmSD, FusedArgs a) {
+    constexpr int S = stages_for<NTMAX, BITS>();
+    constexpr int SBY = stage_bytes<BITS>();
     extern __shared__ uint8_t smem_raw[];
     uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~uintptr_t(1023));
-    uint16_t *xs = reinterpret_cast<uint16_t *>(ring + S * kStageBytes);  // [T][H]
-    uint16_t *ys = xs + (size_t)a.T * a.H;                                       // [2][NTMAX][I]
-    uint64_t *bars = reinterpret_cast<uint64_t *>(ys + 2 * NTMAX * a.I);
+    uint16_t *xs = reinterpret_cast<uint16_t *>(ring + S * SBY);  // [T][H]
+    uint16_t *ys = xs + (size_t)a.T * a.H;                         // [2][NTMAX][I]
+    // quantised experts: kSB (scale, bias) slots, 128-byte aligned
+    uint32_t *sbq = reinterpret_cast<uint32_t *>(ys + 2 * NTMAX * a.I);
+    const int slotw = sb_slot_words(a.H, a.I);
+    const int gpH = ((a.H / 64) + 3) / 4 * 4, gpI = ((a.I / 64) + 3) / 4 * 4;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sbq + (BITS ? kSB * slotw : 0));
     uint64_t *full = bars, *empty = bars + S;
     uint64_t *yfull = bars + 2 * S, *yempty = yfull + 2, *xbar = yempty + 2;
+    uint64_t *sbfull = xbar + 1, *sbempty = sbfull + kSB;
     __shared__ float s_r[kMaxT];
     __shared__ float s_part[kThreads / 32][kMaxT];
     __shared__ int s_U, s_skip;
@@ -403,6 +592,11 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
             mbar_init(&yempty[b], kCW);
         }
         mbar_init(xbar, 1);
+        if (BITS)
+            for (int q = 0; q < kSB; ++q) {
+                mbar_init(&sbfull[q], 1);
+                mbar_init(&sbempty[q], kCW);
+            }
         for (int q = 0; q < kQ; ++q) {
             mbar_init(&s_qfull[q], 1);
             mbar_init(&s_qempty[q], kCW + 2);  // compute warps, stager, signal warp
@@ -604,7 +798,7 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
     const int NGU = I / kGuCols;
     const int Ngu = U * NGU, N = U * (NGU + NDN);
     auto producer = [&]() {
-        int g = 0, qi = 0;
+        int g = 0, qi = 0, it = 0;
         for (;;) {
             // claim the next item (global order: every gate_up item before any
             // down item, so a down item only waits on items already claimed)
@@ -631,19 +825,38 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
                 r0 = s_act[u] * H + hb * kDnRows;
                 nk = I / 64;
             }
+            if constexpr (BITS > 0) {  // the item's (scale, bias) pairs
+                const int sl = it % kSB;
+                if (!mbar_wait(&sbempty[sl], ((it / kSB) & 1) ^ 1, kWait)) {
+                    record_error(a.err, 82, i);
+                    return;
+                }
+                uint32_t *dsb = sbq + sl * slotw;
+                if (gu) {
+                    mbar_arrive_expect_tx(&sbfull[sl], 2u * 16 * gpH * 4);
+                    tma_load_2d(dsb, &tmSG, &sbfull[sl], 0, r0);
+                    tma_load_2d(dsb + 16 * gpH, &tmSG, &sbfull[sl], 0, r0 + I);
+                } else {
+                    mbar_arrive_expect_tx(&sbfull[sl], (uint32_t)kDnRows * gpI * 4);
+                    tma_load_2d(dsb, &tmSD, &sbfull[sl], 0, r0);
+                }
+                ++it;
+            }
             for (int kc = 0; kc < nk; ++kc, ++g) {
                 const int s = g % S;
                 if (!mbar_wait(&empty[s], ((g / S) & 1) ^ 1, kWait)) {
                     record_error(a.err, 74, i);
                     return;
                 }
-                mbar_arrive_expect_tx(&full[s], kStageBytes);
-                uint8_t *dst = ring + s * kStageBytes;
+                mbar_arrive_expect_tx(&full[s], SBY);
+                uint8_t *dst = ring + s * SBY;
+                // coordinates in elements: bf16 values, or u32 words of codes
+                constexpr int GU_X = BITS ? 256 * BITS / 32 : 256, DN_X = BITS ? 64 * BITS / 32 : 64;
                 if (gu) {
-                    tma_load_2d(dst, &tmGU, &full[s], kc * 256, r0);
-                    tma_load_2d(dst + kStageBytes / 2, &tmGU, &full[s], kc * 256, r0 + I);
+                    tma_load_2d(dst, &tmGU, &full[s], kc * GU_X, r0);
+                    tma_load_2d(dst + SBY / 2, &tmGU, &full[s], kc * GU_X, r0 + I);
                 } else {
-                    tma_load_2d(dst, &tmDN, &full[s], kc * 64, r0);
+                    tma_load_2d(dst, &tmDN, &full[s], kc * DN_X, r0);
                 }
             }
             FT_ITEM(6, qi - 1, 0);
@@ -762,14 +975,30 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
         if (lane == 0) FT_STAMP(6);
     };
     auto compute = [&]() {
-    int g = 0, ub = 0;
+    int g = 0, ub = 0, it = 0;
     for (int i = next(); i >= 0; i = next()) {
+        const uint32_t *sbs = nullptr;
+        int sl = 0;
+        if constexpr (BITS > 0) {  // the item's (scale, bias) pairs
+            sl = it % kSB;
+            if (!mbar_wait(&sbfull[sl], (it / kSB) & 1, kWait)) {
+                if (lane == 0) record_error(a.err, 83, i);
+                return;
+            }
+            sbs = sbq + sl * slotw;
+            ++it;
+        }
         if (i < Ngu) {
             const int u = i / NGU, blk = i - u * NGU;
             unsigned long long *ydst = a.yq + (size_t)s_off[u] * (I / 2) + blk * (kGuCols / 2);
-            if (!run_gateup<NTMAX, S>(ring, full, empty, xs, s_tok[u], s_n[u], a, g, warp, lane,
-                                      ydst, tag))
-                return;
+            bool ok;
+            if constexpr (BITS > 0)
+                ok = run_gateup_q<NTMAX, S, BITS>(ring, full, empty, xs, sbs, gpH, s_tok[u], s_n[u],
+                                                  a, g, warp, lane, ydst, tag);
+            else
+                ok = run_gateup<NTMAX, S>(ring, full, empty, xs, s_tok[u], s_n[u], a, g, warp,
+                                          lane, ydst, tag);
+            if (!ok) return;
         } else {
             const int jj = i - Ngu, u = jj / NDN, hb = jj - u * NDN;
             const int b = ub & 1;
@@ -779,15 +1008,23 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
             }
             if (tid == 0) FT_ITEM(4, qi - 1, 0);
             unsigned long long *odst = a.oq + (size_t)s_off[u] * (H / 2) + hb * (kDnRows / 2);
-            if (!run_down<NTMAX, S>(ring, full, empty, ys + (size_t)b * NTMAX * I, s_n[u], a, g,
-                                    warp, lane, odst, tag))
-                return;
+            bool ok;
+            if constexpr (BITS > 0)
+                ok = run_down_q<NTMAX, S, BITS>(ring, full, empty, ys + (size_t)b * NTMAX * I, sbs,
+                                                gpI, s_n[u], a, g, warp, lane, odst, tag);
+            else
+                ok = run_down<NTMAX, S>(ring, full, empty, ys + (size_t)b * NTMAX * I, s_n[u], a, g,
+                                        warp, lane, odst, tag);
+            if (!ok) return;
             __syncwarp();
             if (lane == 0) mbar_arrive(&yempty[b]);
             ++ub;
         }
         __syncwarp();  // the warp's stores of this item, then one release
-        if (lane == 0) red_add_release_cta_shared(&s_idone, 1);
+        if (lane == 0) {
+            red_add_release_cta_shared(&s_idone, 1);
+            if (BITS) mbar_arrive(&sbempty[sl]);
+        }
         if (tid == 0) FT_ITEM(1, qi - 1, 0);
     }
     if (tid == 0) FT_STAMP(5);
@@ -809,64 +1046,87 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
 #endif
 }
 
-template <int NTMAX>
+template <int NTMAX, int BITS>
 size_t fused_smem(int T, int H, int I) {
-    constexpr int S = stages_for<NTMAX>();
-    return 1024 + (size_t)S * kStageBytes + (size_t)T * H * 2 + 2 * (size_t)NTMAX * I * 2 +
-           8 * (2 * S + 5) + 64;
+    constexpr int S = stages_for<NTMAX, BITS>();
+    return 1024 + (size_t)S * stage_bytes<BITS>() + (size_t)T * H * 2 +
+           2 * (size_t)NTMAX * I * 2 + (BITS ? (size_t)kSB * sb_slot_words(H, I) * 4 : 0) +
+           8 * (2 * S + 5 + 2 * kSB) + 64;
 }
 
-template <int NTMAX>
+template <int NTMAX, int BITS>
 cudaError_t fused_attr() {
-    return cudaFuncSetAttribute(decode_fused_kernel<NTMAX>,
+    return cudaFuncSetAttribute(decode_fused_kernel<NTMAX, BITS>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
 }
 
-template <int NTMAX>
-cudaError_t launch_fused_nt(const CUtensorMap &gu, const CUtensorMap &dn, const FusedArgs &a,
-                            cudaStream_t s) {
+template <int NTMAX, int BITS>
+cudaError_t launch_fused_nt(const CUtensorMap (&m)[4], const FusedArgs &a, cudaStream_t s) {
     const int dev = current_device();
-    static int occ_cache[64][4] = {};
-    const int slot = NTMAX == 1 ? 0 : NTMAX == 2 ? 1 : NTMAX == 4 ? 2 : 3;
+    static int occ_cache[64][12] = {};
+    const int slot = (NTMAX == 1 ? 0 : NTMAX == 2 ? 1 : NTMAX == 4 ? 2 : 3) + 4 * (BITS / 4);
     int &occ = occ_cache[dev & 63][slot];
     if (!occ) {
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_fused_kernel<NTMAX>, kThreads,
-                                                      fused_smem<NTMAX>(NTMAX, a.H, a.I));
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_fused_kernel<NTMAX, BITS>,
+                                                      kThreads,
+                                                      fused_smem<NTMAX, BITS>(NTMAX, a.H, a.I));
         if (occ < 1) return cudaErrorInvalidConfiguration;
     }
-    // every CTA waits on the router's last CTA: the grid must be resident at
-    // once, one CTA per SM
+    // every CTA waits on the scores of the CTAs < E: the grid must be
+    // resident at once, one CTA per SM
     const int grid = grid_sms(dev);
     if (grid < a.E) return cudaErrorInvalidConfiguration;
-    return launch_ex(decode_fused_kernel<NTMAX>, dim3(grid), dim3(kThreads),
-                     fused_smem<NTMAX>(a.T, a.H, a.I), s, false, gu, dn, a);
+    return launch_ex(decode_fused_kernel<NTMAX, BITS>, dim3(grid), dim3(kThreads),
+                     fused_smem<NTMAX, BITS>(a.T, a.H, a.I), s, false, m[0], m[1], m[2], m[3], a);
 }
 
+template <int BITS>
 size_t fused_smem_T(int T, int H, int I) {
-    return T <= 1 ? fused_smem<1>(T, H, I) : T <= 2 ? fused_smem<2>(T, H, I)
-         : T <= 4 ? fused_smem<4>(T, H, I) : fused_smem<8>(T, H, I);
+    return T <= 1 ? fused_smem<1, BITS>(T, H, I) : T <= 2 ? fused_smem<2, BITS>(T, H, I)
+         : T <= 4 ? fused_smem<4, BITS>(T, H, I) : fused_smem<8, BITS>(T, H, I);
+}
+
+template <int BITS>
+int stages_T(int T) {
+    return T <= 2 ? stages_for<2, BITS>() : T <= 4 ? stages_for<4, BITS>() : stages_for<8, BITS>();
+}
+
+template <int BITS>
+cudaError_t launch_bits(const CUtensorMap (&m)[4], const FusedArgs &a, cudaStream_t s) {
+    // the largest per-expert token count is at most T
+    const int T = a.T;
+    return T <= 1   ? launch_fused_nt<1, BITS>(m, a, s)
+           : T <= 2 ? launch_fused_nt<2, BITS>(m, a, s)
+           : T <= 4 ? launch_fused_nt<4, BITS>(m, a, s)
+                    : launch_fused_nt<8, BITS>(m, a, s);
 }
 
 }  // namespace
 
 cudaError_t decode_fused_init() {
     cudaError_t e;
-    if ((e = fused_attr<1>()) || (e = fused_attr<2>()) || (e = fused_attr<4>()) ||
-        (e = fused_attr<8>()))
+    if ((e = fused_attr<1, 0>()) || (e = fused_attr<2, 0>()) || (e = fused_attr<4, 0>()) ||
+        (e = fused_attr<8, 0>()) || (e = fused_attr<1, 4>()) || (e = fused_attr<2, 4>()) ||
+        (e = fused_attr<4, 4>()) || (e = fused_attr<8, 4>()) || (e = fused_attr<1, 8>()) ||
+        (e = fused_attr<2, 8>()) || (e = fused_attr<4, 8>()) || (e = fused_attr<8, 8>()))
         return e;
     return cudaSuccess;
 }
 
-bool decode_fused_supported(int T, int H, int I, int E, int K, bool same_x) {
+bool decode_fused_supported(int T, int H, int I, int E, int K, bool same_x, int bits, int gs) {
     if (T < 1 || T > kMaxT) return false;
-    const int S = T <= 2 ? stages_for<2>() : T <= 4 ? stages_for<4>() : stages_for<8>();
+    if (bits != 0 && !((bits == 4 || bits == 8) && gs == 64)) return false;
+    const size_t ring = bits == 0   ? (size_t)stages_T<0>(T) * stage_bytes<0>()
+                        : bits == 4 ? (size_t)stages_T<4>(T) * stage_bytes<4>()
+                                    : (size_t)stages_T<8>(T) * stage_bytes<8>();
+    const size_t smem = bits == 0 ? fused_smem_T<0>(T, H, I)
+                        : bits == 4 ? fused_smem_T<4>(T, H, I) : fused_smem_T<8>(T, H, I);
     const size_t router = (same_x ? 0 : (size_t)T * H * 2) + (size_t)H * 4 +
                           (size_t)(E + 7) / 8 * 16 + (size_t)T * E * 4;
     return T * K <= kMaxPairs && K <= 32 && E <= kEpMaxExperts && E % 8 == 0 &&
            E <= grid_sms(current_device()) && grid_sms(current_device()) <= kMaxGrid &&
-           router <= (size_t)S * kStageBytes &&
-           H % 256 == 0 && H % kDnRows == 0 && I % 64 == 0 && I % kGuCols == 0 &&
-           fused_smem_T(T, H, I) <= kMaxDynSmem && encode_tiled_fn() != nullptr;
+           router <= ring && H % 256 == 0 && H % kDnRows == 0 && I % 64 == 0 &&
+           I % kGuCols == 0 && smem <= kMaxDynSmem && encode_tiled_fn() != nullptr;
 }
 
 size_t decode_fused_sync_words(int E, int H, int I) {
@@ -881,18 +1141,31 @@ cudaError_t launch_decode_fused(const uint16_t *xr, const uint16_t *xe, const ui
                                 int32_t *sync, int32_t *err, cudaStream_t s, int *launches) {
     unsigned long long *yq = reinterpret_cast<unsigned long long *>(sync + kTagWord);
     unsigned long long *oq = yq + (size_t)kMaxPairs * (I / 2);
-    CUtensorMap gu, dn;
-    if (!bf16_map_2d(&gu, wt.gu, H, (uint64_t)E * 2 * I, 256, kGuCols, false) ||
-        !bf16_map_2d(&dn, wt.dn, I, (uint64_t)E * H, 64, kDnRows, false))
-        return cudaErrorInvalidValue;
+    CUtensorMap m[4];
+    const int bits = wt.bits;
+    if (bits == 0) {
+        if (!bf16_map_2d(&m[0], wt.gu, H, (uint64_t)E * 2 * I, 256, kGuCols, false) ||
+            !bf16_map_2d(&m[1], wt.dn, I, (uint64_t)E * H, 64, kDnRows, false))
+            return cudaErrorInvalidValue;
+        m[2] = m[0];  // unused
+        m[3] = m[1];
+    } else {
+        // packed codes [rows][len * bits / 32] u32 and (scale, bias) words
+        // [rows][gp], gp = groups rounded up to 4
+        const int gpH = ((H / 64) + 3) / 4 * 4, gpI = ((I / 64) + 3) / 4 * 4;
+        if (!map_2d(&m[0], wt.gu_q, (uint64_t)H * bits / 32, (uint64_t)E * 2 * I, 256 * bits / 32,
+                    kGuCols, false, true) ||
+            !map_2d(&m[1], wt.dn_q, (uint64_t)I * bits / 32, (uint64_t)E * H, 64 * bits / 32,
+                    kDnRows, false, true) ||
+            !map_2d(&m[2], wt.gu_sb, gpH, (uint64_t)E * 2 * I, gpH, kGuCols, false, true) ||
+            !map_2d(&m[3], wt.dn_sb, gpI, (uint64_t)E * H, gpI, kDnRows, false, true))
+            return cudaErrorInvalidValue;
+    }
     FusedArgs a{xr, xe, scale, pes, proj, T, H, E, K, I, eps, (float)(1.0 / sqrt((double)H)),
                 scores, idx, w, d, yq, oq, out, sync, err};
-    // the largest per-expert token count is at most T
-    const int nt = T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8;
-    cudaError_t e = nt == 1   ? launch_fused_nt<1>(gu, dn, a, s)
-                    : nt == 2 ? launch_fused_nt<2>(gu, dn, a, s)
-                    : nt == 4 ? launch_fused_nt<4>(gu, dn, a, s)
-                              : launch_fused_nt<8>(gu, dn, a, s);
+    const cudaError_t e = bits == 0   ? launch_bits<0>(m, a, s)
+                          : bits == 4 ? launch_bits<4>(m, a, s)
+                                      : launch_bits<8>(m, a, s);
     if (launches) ++*launches;
     return e;
 }

@@ -53,18 +53,6 @@ __device__ __forceinline__ void record_error(int32_t *err, int code, int where) 
     if (atomicCAS(err, 0, code) == 0) err[1] = where;
 }
 
-// Packed unsigned q -> f32 without the int-to-float unit: OR-ing q into the
-// mantissa of 2^23 gives exactly 2^23 + q, and subtracting 2^23 leaves q.
-template <int BITS>
-__device__ __forceinline__ void unpack_q8(const uint32_t *w, float (&q)[8]) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-        q[i] = __fsub_rn(__uint_as_float(((w[i * BITS / 32] >> ((i * BITS) & 31)) &
-                                          ((1u << BITS) - 1u)) |
-                                         0x4B000000u),
-                         8388608.0f);
-}
-
 template <int NT, int R>
 __device__ __forceinline__ float pick(const float (&acc)[R][NT], int r, int t) {
     float v = 0.f;

@@ -65,48 +65,55 @@ inline EncodeTiledFn encode_tiled_fn() {
     return fn;
 }
 
-// 2-D bf16 row-major [rows, inner] tensor, box {box_inner, box_rows}.  Returns
-// false if the driver entry point is missing or encoding fails.  Results are
-// cached by all their parameters (a small direct-mapped cache).
-inline bool bf16_map_2d(CUtensorMap *out, const void *base, uint64_t inner, uint64_t rows,
-                        uint32_t box_inner, uint32_t box_rows, bool swizzle128) {
+// 2-D row-major [rows, inner] tensor of 2-byte (bf16) or 4-byte (u32)
+// elements, box {box_inner, box_rows}.  Returns false if the driver entry
+// point is missing or encoding fails.  Results are cached by all their
+// parameters (a small direct-mapped cache).
+inline bool map_2d(CUtensorMap *out, const void *base, uint64_t inner, uint64_t rows,
+                   uint32_t box_inner, uint32_t box_rows, bool swizzle128, bool u32) {
     struct Entry {
         const void *base;
         uint64_t inner, rows;
         uint32_t bi, br;
-        bool sw;
+        bool sw, u32;
         bool valid;
         CUtensorMap map;
     };
     static Entry cache[64];
     static std::mutex mu;
     const uint64_t key = (reinterpret_cast<uintptr_t>(base) >> 8) ^ (inner * 31) ^ (rows * 131) ^
-                         (box_inner * 7) ^ (box_rows * 13) ^ (swizzle128 ? 1 : 0);
+                         (box_inner * 7) ^ (box_rows * 13) ^ (swizzle128 ? 1 : 0) ^ (u32 ? 2 : 0);
     Entry &slot = cache[key % 64];
     {
         std::lock_guard<std::mutex> lock(mu);
         if (slot.valid && slot.base == base && slot.inner == inner && slot.rows == rows &&
-            slot.bi == box_inner && slot.br == box_rows && slot.sw == swizzle128) {
+            slot.bi == box_inner && slot.br == box_rows && slot.sw == swizzle128 && slot.u32 == u32) {
             *out = slot.map;
             return true;
         }
     }
     EncodeTiledFn fn = encode_tiled_fn();
     if (!fn) return false;
+    const uint64_t esize = u32 ? 4 : 2;
     cuuint64_t dims[2] = {inner, rows};
-    cuuint64_t strides[1] = {inner * 2};
+    cuuint64_t strides[1] = {inner * esize};
     cuuint32_t box[2] = {box_inner, box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUtensorMap m;
-    if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box,
-           estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+    if (fn(&m, u32 ? CU_TENSOR_MAP_DATA_TYPE_UINT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+           const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
            swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return false;
     std::lock_guard<std::mutex> lock(mu);
-    slot = Entry{base, inner, rows, box_inner, box_rows, swizzle128, true, m};
+    slot = Entry{base, inner, rows, box_inner, box_rows, swizzle128, u32, true, m};
     *out = m;
     return true;
+}
+
+inline bool bf16_map_2d(CUtensorMap *out, const void *base, uint64_t inner, uint64_t rows,
+                        uint32_t box_inner, uint32_t box_rows, bool swizzle128) {
+    return map_2d(out, base, inner, rows, box_inner, box_rows, swizzle128, false);
 }
 
 // ---------------------------------------------------------------- launches

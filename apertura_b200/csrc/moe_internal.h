@@ -224,12 +224,13 @@ cudaError_t launch_ep_done(const EpP2PArgs &a, cudaStream_t s);
 cudaError_t launch_ep_combine(const EpP2PArgs &a, const uint16_t *w, int T, int K, uint16_t *out,
                               int grid, cudaStream_t s);
 // ---- the whole decode block in one persistent kernel (decode_fused.cu):
-// router, dispatch, gate_up, down and combine for T <= 8, bf16 experts.
+// router, dispatch, gate_up, down and combine for T <= 8; bf16 experts, or
+// 4/8-bit MLX affine experts with 64-element groups (wt.bits, wt.gs).
 // sync: decode_fused_sync_words(E, H, I) int32 (counters and the tagged
 // GeGLU / down rows), zeroed once before the first call; the kernel keeps it
 // consistent from call to call itself.
 cudaError_t decode_fused_init();
-bool decode_fused_supported(int T, int H, int I, int E, int K, bool same_x);
+bool decode_fused_supported(int T, int H, int I, int E, int K, bool same_x, int bits, int gs);
 size_t decode_fused_sync_words(int E, int H, int I);
 cudaError_t launch_decode_fused(const uint16_t *xr, const uint16_t *xe, const uint16_t *proj,
                                 const uint16_t *scale, const uint16_t *pes, int T, int H, int E,

@@ -100,3 +100,58 @@ def test_fused_decode_host_graph_replay():
         ref_out = blk.forward(xh.to(DEV))
         torch.cuda.synchronize()
         assert torch.equal(oh.view(torch.int16), ref_out.cpu().view(torch.int16))
+
+
+def _quant_block(oracle, d, T, bits):
+    gq = oracle.quantize_affine(_np(d["gate_up"]), 64, bits)
+    dq = oracle.quantize_affine(_np(d["down"]), 64, bits)
+
+    def dev(a):
+        a = np.ascontiguousarray(a)
+        if a.dtype == np.uint16:
+            return torch.from_numpy(a.view(np.int16)).to(DEV).view(torch.bfloat16)
+        return torch.from_numpy(a.view(np.int32)).to(DEV)
+
+    cfg = A.ESModelConfig(hidden_size=d["H"], num_experts=d["E"], top_k_experts=d["K"],
+                          moe_intermediate_size=d["I"], moe_sparse=True, max_tokens=T)
+    q = dict(gu_q=dev(gq[0]), gu_s=dev(gq[1]), gu_b=dev(gq[2]), dn_q=dev(dq[0]),
+             dn_s=dev(dq[1]), dn_b=dev(dq[2]), bits=bits, group_size=64)
+    return A.MoEBlock(cfg, d["proj"], d["scale"], d["pes"], quantized=q), gq, dq
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("T", [1, 3, 8])
+def test_fused_decode_quant_vs_oracle(oracle, bits, T):
+    """MLX affine experts (gather_qmm, ESExperts.mm:50-57) through the one-kernel
+    block: repeated calls against the oracle on the same packed weights."""
+    d = block_inputs(2 * T, seed=700 + T + bits, device=DEV)
+    blk, gq, dq = _quant_block(oracle, d, T, bits)
+    for call in range(2):
+        x = d["x"][call * T:(call + 1) * T].contiguous()
+        out, tk = blk.forward(x, return_routing=True)
+        torch.cuda.synchronize()
+        blk.handle.sync()
+        assert blk.handle.last_launches() == 1
+        ref = oracle.experts_sparse_q(_np(x), *gq, *dq, bits, 64, tk.idx.cpu().numpy(),
+                                      _np(tk.w), d["I"])
+        got, refv = bf16_to_f32(_np(out)), bf16_to_f32(ref)
+        ok, ma, cos = block_close(got, refv)
+        assert ok and ma <= TIGHT_REL * np.abs(refv).max(), (call, ma, cos)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_fused_decode_quant_matches_chain(oracle, bits):
+    T = 4
+    d = block_inputs(T, seed=910 + bits, device=DEV)
+    blk, _, _ = _quant_block(oracle, d, T, bits)
+    a, ta = blk.forward(d["x"], return_routing=True)
+    a = a.clone()
+    blk.handle.set_fused_decode(False)
+    b, tb = blk.forward(d["x"], return_routing=True)
+    torch.cuda.synchronize()
+    assert blk.handle.last_launches() > 1
+    blk.handle.set_fused_decode(True)
+    same = torch.all(ta.idx == tb.idx, dim=1).cpu().numpy()
+    assert same.mean() >= 0.75
+    fa, fb = bf16_to_f32(_np(a))[same], bf16_to_f32(_np(b))[same]
+    assert np.abs(fa - fb).max() <= TIGHT_REL * np.abs(fb).max()
