@@ -68,11 +68,23 @@ constexpr int kStageBytes = 16384;
 // bias) pairs in a ring of kSB slots.
 template <int BITS>
 constexpr int stage_bytes() { return BITS ? 1024 * BITS : kStageBytes; }
+// ring stages (4-bit: the most whole-item slots; their number depends on H, I)
 template <int NTMAX, int BITS = 0>
 constexpr int stages_for() {
     return BITS == 0 ? (NTMAX <= 2 ? 12 : NTMAX <= 4 ? 10 : 8)
-                     : (NTMAX <= 4 ? 144 * 1024 : 112 * 1024) / stage_bytes<BITS>();
+           : BITS == 4 ? 4
+                       : (NTMAX <= 4 ? 144 * 1024 : 112 * 1024) / stage_bytes<BITS>();
 }
+template <int NTMAX, int BITS>
+constexpr int ring_bytes() {
+    return BITS == 4 ? (NTMAX <= 4 ? 150 : 100) * 1024 : stages_for<NTMAX, BITS>() * stage_bytes<BITS>();
+}
+// 4-bit experts run their multiplies on mma.sync (codes become bf16 128 + q,
+// exact; tokens are the n = 8 dimension).  Extra shared memory: the gate_up
+// partial sums of the eight compute warps [8][32 rows][8 tokens], per-token
+// sums of x over 32-column blocks [T][H/32], and per-token sums of the staged
+// GeGLU rows over 64-element groups [2][NTMAX][I/64].
+constexpr int kRedFloats = kCW * 32 * 8;
 constexpr int kSB = 4;  // (scale, bias) slots: items in flight between the producer and the rest
 // words of one (scale, bias) slot: 32 gate_up rows x gp(H) or 128 down rows x gp(I)
 __host__ __device__ inline int sb_slot_words(int H, int I) {
@@ -144,6 +156,7 @@ struct FusedArgs {
     uint16_t *out;                      // [T, H]
     int32_t *sync;                      // see the sync-word layout above set_words()
     int32_t *err;
+    const uint32_t *gq, *dq, *gsb, *dsb;  // 4-bit: packed codes and (scale, bias) rows
 };
 
 __device__ __forceinline__ void record_error(int32_t *err, int code, int where) {
@@ -493,6 +506,187 @@ __device__ bool down_item_q(const uint8_t *ring, uint64_t *full, uint64_t *empty
     return true;
 }
 
+// 4-bit gate_up item on mma.sync: warp w multiplies columns 32w..32w+31 of
+// every 256-column stage for all 32 rows (two 16-row tiles: gate, up) with the
+// item's tokens (n = token slot, x rows from the staged token rows), then adds
+// the affine terms of that 64-element group: s * D + (b - 128 s) * sum(x).
+// The eight warps' partial sums meet in `red`; warps 0-1 reduce them (in warp
+// order), apply GeGLU and store the tagged GeGLU words.  The hand-offs use
+// mbarriers with bounded waits: redfull (all 8 warps wrote), redfree (the
+// reduction has read `red`).
+// 4-bit items arrive whole: one ring slot holds an item's packed rows (gate_up:
+// 16 gate + 16 up rows of H/8 words; down: 128 rows of I/8 words), copied as
+// contiguous runs by 1-D bulk copies, followed by its (scale, bias) rows.
+__host__ __device__ inline int q4_code_words(int H, int I) {
+    const int gu = 32 * (H / 8), dn = kDnRows * (I / 8);
+    return gu > dn ? gu : dn;
+}
+__host__ __device__ inline size_t q4_slot_bytes(int H, int I) {
+    return ((size_t)q4_code_words(H, I) + sb_slot_words(H, I)) * 4;
+}
+
+// 4-bit gate_up item on mma.sync: warp w multiplies columns 32w..32w+31 of
+// every 256-column block for all 32 rows (two 16-row tiles: gate, up) with the
+// item's tokens (n = token slot, x rows from the staged token rows), then adds
+// the affine terms of that 64-element group: s * D + (b - 128 s) * sum(x).
+// The eight warps' partial sums meet in `red`; warps 0-1 reduce them (in warp
+// order), apply GeGLU and store the tagged GeGLU words.  The hand-offs use
+// mbarriers with bounded waits: redfull (all 8 warps wrote), redfree (the
+// reduction has read `red`).
+__device__ bool gateup_item_q4(const uint32_t *codes, const uint32_t *sbs, int gp,
+                               const uint16_t *xs, const float *xsum32, const int *toks, int nt,
+                               float *red, uint64_t *redfull, uint64_t *redfree, int &gi,
+                               const FusedArgs &a, int w, int lane, unsigned long long *ydst,
+                               unsigned long long tag) {
+    const int NK = a.H / 256, HB = a.H / 32, RW = a.H / 8;
+    const int gid = lane >> 2, t = lane & 3;
+    const uint16_t *xrow = xs + (size_t)(gid < nt ? toks[gid] : toks[0]) * a.H;
+    const int n0 = 2 * t, n1 = 2 * t + 1;
+    const float *xs0 = xsum32 + (size_t)(n0 < nt ? toks[n0] : toks[0]) * HB;
+    const float *xs1 = xsum32 + (size_t)(n1 < nt ? toks[n1] : toks[0]) * HB;
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    for (int kc = 0; kc < NK; ++kc) {
+        float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        // the warp's 32 columns of each row in one 16-byte load (4 words)
+        uint4 v[2][2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            v[h][0] = *reinterpret_cast<const uint4 *>(codes + (h * 16 + gid) * RW + kc * 32 + 4 * w);
+            v[h][1] = *reinterpret_cast<const uint4 *>(codes + (h * 16 + gid + 8) * RW + kc * 32 + 4 * w);
+        }
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+            const int k0 = kc * 256 + 32 * w + 16 * c;  // column within the row
+            uint32_t b0 = 0u, b1 = 0u;
+            if (gid < nt) {
+                b0 = *reinterpret_cast<const uint32_t *>(xrow + k0 + 2 * t);
+                b1 = *reinterpret_cast<const uint32_t *>(xrow + k0 + 2 * t + 8);
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                uint32_t af[4];
+                q4_pair(c ? v[h][0].z : v[h][0].x, c ? v[h][0].w : v[h][0].y, t, af[0], af[2]);
+                q4_pair(c ? v[h][1].z : v[h][1].x, c ? v[h][1].w : v[h][1].y, t, af[1], af[3]);
+                mma_bf16_16816(d[h], af, b0, b1);
+            }
+        }
+        const int grp = kc * 4 + (w >> 1);
+        const float x0 = n0 < nt ? xs0[kc * 8 + w] : 0.f;
+        const float x1 = n1 < nt ? xs1[kc * 8 + w] : 0.f;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t p0 = sbs[(h * 16 + gid) * gp + grp];
+            const uint32_t p1 = sbs[(h * 16 + gid + 8) * gp + grp];
+            const float s0 = bf_lo(p0), c0 = fmaf(-128.f, s0, bf_hi(p0));
+            const float s1 = bf_lo(p1), c1 = fmaf(-128.f, s1, bf_hi(p1));
+            acc[h][0] += fmaf(s0, d[h][0], c0 * x0);
+            acc[h][1] += fmaf(s0, d[h][1], c0 * x1);
+            acc[h][2] += fmaf(s1, d[h][2], c1 * x0);
+            acc[h][3] += fmaf(s1, d[h][3], c1 * x1);
+        }
+    }
+    // partial sums -> red[w][row][token], once the previous item's reduction has read red
+    if (gi > 0 && !mbar_wait(redfree, (gi - 1) & 1, kWait)) {
+        record_error(a.err, 84, gi);
+        return false;
+    }
+    float *rw = red + w * 256;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        rw[(h * 16 + gid) * 8 + n0] = acc[h][0];
+        rw[(h * 16 + gid) * 8 + n1] = acc[h][1];
+        rw[(h * 16 + gid + 8) * 8 + n0] = acc[h][2];
+        rw[(h * 16 + gid + 8) * 8 + n1] = acc[h][3];
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(redfull);
+    if (w < 2) {
+        if (!mbar_wait(redfull, gi & 1, kWait)) {
+            record_error(a.err, 85, gi);
+            return false;
+        }
+        const int tid = w * 32 + lane, jp = tid >> 3, n = tid & 7;  // column pair, token
+        if (n < nt) {
+            float v[4] = {0.f, 0.f, 0.f, 0.f};  // gate 2jp, 2jp+1, up 2jp, 2jp+1
+#pragma unroll
+            for (int q = 0; q < kCW; ++q) {
+                const float *rq = red + q * 256;
+                v[0] += rq[(2 * jp) * 8 + n];
+                v[1] += rq[(2 * jp + 1) * 8 + n];
+                v[2] += rq[(16 + 2 * jp) * 8 + n];
+                v[3] += rq[(16 + 2 * jp + 1) * 8 + n];
+            }
+            const float y0 = geglu_bf16(rbf(v[0]), rbf(v[2]));
+            const float y1 = geglu_bf16(rbf(v[1]), rbf(v[3]));
+            st_relaxed_gpu_u64(ydst + (size_t)n * (a.I / 2) + jp, tag | pack_bf2(y0, y1));
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(redfree);
+    }
+    ++gi;
+    return true;
+}
+
+// 4-bit down item on mma.sync: warp w owns rows 16w..16w+15 of the item's 128
+// and all columns, one 64-element group per step: s * D + (b - 128 s) * sum(y).
+__device__ void down_item_q4(const uint32_t *codes, const uint32_t *sbs, int gp,
+                             const uint16_t *ys, const float *ysum, int nt, const FusedArgs &a,
+                             int w, int lane, unsigned long long *odst, unsigned long long tag) {
+    const int NK = a.I / 64, RW = a.I / 8;
+    const int gid = lane >> 2, t = lane & 3;
+    const int n0 = 2 * t, n1 = 2 * t + 1;
+    const uint16_t *yrow = ys + (size_t)(gid < nt ? gid : 0) * a.I;
+    const uint32_t *row0 = codes + (16 * w + gid) * RW, *row1 = row0 + 8 * RW;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int kc = 0; kc < NK; ++kc) {
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        // the group's 64 columns of both rows: two 16-byte loads each
+        const uint4 r0a = *reinterpret_cast<const uint4 *>(row0 + kc * 8);
+        const uint4 r0b = *reinterpret_cast<const uint4 *>(row0 + kc * 8 + 4);
+        const uint4 r1a = *reinterpret_cast<const uint4 *>(row1 + kc * 8);
+        const uint4 r1b = *reinterpret_cast<const uint4 *>(row1 + kc * 8 + 4);
+        const uint32_t w0[8] = {r0a.x, r0a.y, r0a.z, r0a.w, r0b.x, r0b.y, r0b.z, r0b.w};
+        const uint32_t w1[8] = {r1a.x, r1a.y, r1a.z, r1a.w, r1b.x, r1b.y, r1b.z, r1b.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            uint32_t b0 = 0u, b1 = 0u;
+            if (gid < nt) {
+                b0 = *reinterpret_cast<const uint32_t *>(yrow + kc * 64 + 16 * c + 2 * t);
+                b1 = *reinterpret_cast<const uint32_t *>(yrow + kc * 64 + 16 * c + 2 * t + 8);
+            }
+            uint32_t af[4];
+            q4_pair(w0[2 * c], w0[2 * c + 1], t, af[0], af[2]);
+            q4_pair(w1[2 * c], w1[2 * c + 1], t, af[1], af[3]);
+            mma_bf16_16816(d, af, b0, b1);
+        }
+        const float y0 = n0 < nt ? ysum[n0 * NK + kc] : 0.f;
+        const float y1 = n1 < nt ? ysum[n1 * NK + kc] : 0.f;
+        const uint32_t p0 = sbs[(16 * w + gid) * gp + kc];
+        const uint32_t p1 = sbs[(16 * w + gid + 8) * gp + kc];
+        const float s0 = bf_lo(p0), c0 = fmaf(-128.f, s0, bf_hi(p0));
+        const float s1 = bf_lo(p1), c1 = fmaf(-128.f, s1, bf_hi(p1));
+        acc[0] += fmaf(s0, d[0], c0 * y0);
+        acc[1] += fmaf(s0, d[1], c0 * y1);
+        acc[2] += fmaf(s1, d[2], c1 * y0);
+        acc[3] += fmaf(s1, d[3], c1 * y1);
+    }
+    // rows (16w + gid, +1) pair up across lanes gid, gid + 1 (lane + 4)
+    float p[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) p[i] = __shfl_down_sync(0xffffffffu, acc[i], 4);
+    if ((gid & 1) == 0) {
+        const int r = 16 * w + gid;
+        if (n0 < nt) {
+            st_relaxed_gpu_u64(odst + (size_t)n0 * (a.H / 2) + r / 2, tag | pack_bf2(acc[0], p[0]));
+            st_relaxed_gpu_u64(odst + (size_t)n0 * (a.H / 2) + (r + 8) / 2, tag | pack_bf2(acc[2], p[2]));
+        }
+        if (n1 < nt) {
+            st_relaxed_gpu_u64(odst + (size_t)n1 * (a.H / 2) + r / 2, tag | pack_bf2(acc[1], p[1]));
+            st_relaxed_gpu_u64(odst + (size_t)n1 * (a.H / 2) + (r + 8) / 2, tag | pack_bf2(acc[3], p[3]));
+        }
+    }
+}
+
 template <int NTMAX, int S, int BITS>
 __device__ bool run_gateup_q(const uint8_t *ring, uint64_t *full, uint64_t *empty,
                              const uint16_t *xs, const uint32_t *sbs, int gp, const int *toks,
@@ -538,16 +732,26 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
     extern __shared__ uint8_t smem_raw[];
     uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~uintptr_t(1023));
-    uint16_t *xs = reinterpret_cast<uint16_t *>(ring + S * SBY);  // [T][H]
-    uint16_t *ys = xs + (size_t)a.T * a.H;                         // [2][NTMAX][I]
-    // quantised experts: kSB (scale, bias) slots, 128-byte aligned
+    uint16_t *xs = reinterpret_cast<uint16_t *>(ring + ring_bytes<NTMAX, BITS>());  // [T][H]
+    uint16_t *ys = xs + (size_t)a.T * a.H;                                           // [2][NTMAX][I]
+    // 8-bit experts: kSB (scale, bias) slots, 128-byte aligned
     uint32_t *sbq = reinterpret_cast<uint32_t *>(ys + 2 * NTMAX * a.I);
     const int slotw = sb_slot_words(a.H, a.I);
+    // 4-bit experts: whole-item slots in the ring
+    const size_t q4slot = (q4_slot_bytes(a.H, a.I) + 127) & ~size_t(127);
+    const int ns = BITS == 4 ? (int)(ring_bytes<NTMAX, BITS>() / q4slot) : S;
     const int gpH = ((a.H / 64) + 3) / 4 * 4, gpI = ((a.I / 64) + 3) / 4 * 4;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sbq + (BITS ? kSB * slotw : 0));
+    // 4-bit: gate_up partial sums, x sums per 32 columns, GeGLU-row sums per group
+    float *red = reinterpret_cast<float *>(sbq + (BITS == 8 ? kSB * slotw : 0));
+    float *xsum32 = red + (BITS == 4 ? kRedFloats : 0);
+    float *ysum = xsum32 + (BITS == 4 ? a.T * (a.H / 32) : 0);
+    const int GI = a.I / 64;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(
+        (reinterpret_cast<uintptr_t>(ysum + (BITS == 4 ? 2 * NTMAX * GI : 0)) + 7) & ~uintptr_t(7));
     uint64_t *full = bars, *empty = bars + S;
     uint64_t *yfull = bars + 2 * S, *yempty = yfull + 2, *xbar = yempty + 2;
     uint64_t *sbfull = xbar + 1, *sbempty = sbfull + kSB;
+    uint64_t *redfull = sbempty + kSB, *redfree = redfull + 1;
     __shared__ float s_r[kMaxT];
     __shared__ float s_part[kThreads / 32][kMaxT];
     __shared__ int s_U, s_skip;
@@ -597,6 +801,10 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
                 mbar_init(&sbfull[q], 1);
                 mbar_init(&sbempty[q], kCW);
             }
+        if (BITS == 4) {
+            mbar_init(redfull, kCW);
+            mbar_init(redfree, 2);
+        }
         for (int q = 0; q < kQ; ++q) {
             mbar_init(&s_qfull[q], 1);
             mbar_init(&s_qempty[q], kCW + 2);  // compute warps, stager, signal warp
@@ -636,6 +844,21 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
         s_skip = 1;
     }
     if (tid == 0) FT_STAMP(1);
+    if constexpr (BITS == 4) {  // sums of each token's x over 32-column blocks
+        const int HB = H / 32;
+        for (int i = tid; i < T * HB; i += kThreads) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(xs + (size_t)(i / HB) * H + (i % HB) * 32);
+            float sum = 0.f;
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                float f[8];
+                unpack8(src[v], f);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) sum += f[j];
+            }
+            xsum32[i] = sum;
+        }
+    }
     if (has_e) {
         for (int t = warp; t < T; t += kThreads / 32) {
             float ss = 0.f;
@@ -825,6 +1048,30 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
                 r0 = s_act[u] * H + hb * kDnRows;
                 nk = I / 64;
             }
+            if constexpr (BITS == 4) {  // the whole item into one slot: 2-4 bulk copies
+                const int sl = it % ns;
+                if (!mbar_wait(&empty[sl], ((it / ns) & 1) ^ 1, kWait)) {
+                    record_error(a.err, 74, i);
+                    return;
+                }
+                uint32_t *dc = reinterpret_cast<uint32_t *>(ring + sl * q4slot);
+                uint32_t *ds = dc + q4_code_words(H, I);
+                const uint32_t rwH = (uint32_t)H / 8, rwI = (uint32_t)I / 8;
+                if (gu) {
+                    mbar_arrive_expect_tx(&full[sl], 2u * 16 * (rwH + gpH) * 4);
+                    bulk_load(dc, a.gq + (size_t)r0 * rwH, 16 * rwH * 4, &full[sl]);
+                    bulk_load(dc + 16 * rwH, a.gq + (size_t)(r0 + I) * rwH, 16 * rwH * 4, &full[sl]);
+                    bulk_load(ds, a.gsb + (size_t)r0 * gpH, 16u * gpH * 4, &full[sl]);
+                    bulk_load(ds + 16 * gpH, a.gsb + (size_t)(r0 + I) * gpH, 16u * gpH * 4, &full[sl]);
+                } else {
+                    mbar_arrive_expect_tx(&full[sl], (uint32_t)kDnRows * (rwI + gpI) * 4);
+                    bulk_load(dc, a.dq + (size_t)r0 * rwI, kDnRows * rwI * 4, &full[sl]);
+                    bulk_load(ds, a.dsb + (size_t)r0 * gpI, (uint32_t)kDnRows * gpI * 4, &full[sl]);
+                }
+                ++it;
+                FT_ITEM(6, qi - 1, 0);
+                continue;
+            }
             if constexpr (BITS > 0) {  // the item's (scale, bias) pairs
                 const int sl = it % kSB;
                 if (!mbar_wait(&sbempty[sl], ((it / kSB) & 1) ^ 1, kWait)) {
@@ -907,6 +1154,23 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
                 for (int q = 0; q < kYB; ++q)
                     if (q < n) dst[v0 + q * 32 + lane] = (uint32_t)x[q];
             }
+            if constexpr (BITS == 4) {  // sums of each staged row over 64-element groups
+                __syncwarp();
+                const uint16_t *yb = ys + (size_t)b * NTMAX * I;
+                float *sb = ysum + b * NTMAX * GI;
+                for (int k = lane; k < s_n[u] * GI; k += 32) {
+                    const uint4 *src = reinterpret_cast<const uint4 *>(yb + (size_t)(k / GI) * I + (k % GI) * 64);
+                    float sum = 0.f;
+#pragma unroll
+                    for (int v = 0; v < 8; ++v) {
+                        float f[8];
+                        unpack8(src[v], f);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) sum += f[j];
+                    }
+                    sb[k] = sum;
+                }
+            }
             if (lane == 0) FT_ITEM(5, qi - 1, 0);
             __syncwarp();
             if (lane == 0) mbar_arrive(&yfull[b]);
@@ -975,11 +1239,20 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
         if (lane == 0) FT_STAMP(6);
     };
     auto compute = [&]() {
-    int g = 0, ub = 0, it = 0;
+    int g = 0, ub = 0, it = 0, gi = 0;
     for (int i = next(); i >= 0; i = next()) {
-        const uint32_t *sbs = nullptr;
+        const uint32_t *sbs = nullptr, *codes = nullptr;
         int sl = 0;
-        if constexpr (BITS > 0) {  // the item's (scale, bias) pairs
+        if constexpr (BITS == 4) {  // the item's slot: codes, then (scale, bias) rows
+            sl = it % ns;
+            if (!mbar_wait(&full[sl], (it / ns) & 1, kWait)) {
+                if (lane == 0) record_error(a.err, 83, i);
+                return;
+            }
+            codes = reinterpret_cast<const uint32_t *>(ring + sl * q4slot);
+            sbs = codes + q4_code_words(H, I);
+            ++it;
+        } else if constexpr (BITS > 0) {  // the item's (scale, bias) pairs
             sl = it % kSB;
             if (!mbar_wait(&sbfull[sl], (it / kSB) & 1, kWait)) {
                 if (lane == 0) record_error(a.err, 83, i);
@@ -992,7 +1265,10 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
             const int u = i / NGU, blk = i - u * NGU;
             unsigned long long *ydst = a.yq + (size_t)s_off[u] * (I / 2) + blk * (kGuCols / 2);
             bool ok;
-            if constexpr (BITS > 0)
+            if constexpr (BITS == 4)
+                ok = gateup_item_q4(codes, sbs, gpH, xs, xsum32, s_tok[u], s_n[u], red, redfull,
+                                    redfree, gi, a, warp, lane, ydst, tag);
+            else if constexpr (BITS > 0)
                 ok = run_gateup_q<NTMAX, S, BITS>(ring, full, empty, xs, sbs, gpH, s_tok[u], s_n[u],
                                                   a, g, warp, lane, ydst, tag);
             else
@@ -1009,7 +1285,12 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
             if (tid == 0) FT_ITEM(4, qi - 1, 0);
             unsigned long long *odst = a.oq + (size_t)s_off[u] * (H / 2) + hb * (kDnRows / 2);
             bool ok;
-            if constexpr (BITS > 0)
+            if constexpr (BITS == 4) {
+                down_item_q4(codes, sbs, gpI, ys + (size_t)b * NTMAX * I, ysum + b * NTMAX * GI,
+                             s_n[u], a, warp, lane, odst, tag);
+                ok = true;
+            }
+            else if constexpr (BITS > 0)
                 ok = run_down_q<NTMAX, S, BITS>(ring, full, empty, ys + (size_t)b * NTMAX * I, sbs,
                                                 gpI, s_n[u], a, g, warp, lane, odst, tag);
             else
@@ -1023,7 +1304,8 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
         __syncwarp();  // the warp's stores of this item, then one release
         if (lane == 0) {
             red_add_release_cta_shared(&s_idone, 1);
-            if (BITS) mbar_arrive(&sbempty[sl]);
+            if (BITS == 4) mbar_arrive(&empty[sl]);
+            else if (BITS) mbar_arrive(&sbempty[sl]);
         }
         if (tid == 0) FT_ITEM(1, qi - 1, 0);
     }
@@ -1049,9 +1331,11 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
 template <int NTMAX, int BITS>
 size_t fused_smem(int T, int H, int I) {
     constexpr int S = stages_for<NTMAX, BITS>();
-    return 1024 + (size_t)S * stage_bytes<BITS>() + (size_t)T * H * 2 +
-           2 * (size_t)NTMAX * I * 2 + (BITS ? (size_t)kSB * sb_slot_words(H, I) * 4 : 0) +
-           8 * (2 * S + 5 + 2 * kSB) + 64;
+    return 1024 + (size_t)ring_bytes<NTMAX, BITS>() + (size_t)T * H * 2 +
+           2 * (size_t)NTMAX * I * 2 + (BITS == 8 ? (size_t)kSB * sb_slot_words(H, I) * 4 : 0) +
+           (BITS == 4 ? 4 * ((size_t)kRedFloats + (size_t)T * (H / 32) + 2 * (size_t)NTMAX * (I / 64)) + 8
+                      : 0) +
+           8 * (2 * S + 5 + 2 * kSB + 2) + 64;
 }
 
 template <int NTMAX, int BITS>
@@ -1087,8 +1371,8 @@ size_t fused_smem_T(int T, int H, int I) {
 }
 
 template <int BITS>
-int stages_T(int T) {
-    return T <= 2 ? stages_for<2, BITS>() : T <= 4 ? stages_for<4, BITS>() : stages_for<8, BITS>();
+size_t ring_T(int T) {
+    return T <= 2 ? ring_bytes<2, BITS>() : T <= 4 ? ring_bytes<4, BITS>() : ring_bytes<8, BITS>();
 }
 
 template <int BITS>
@@ -1116,9 +1400,9 @@ cudaError_t decode_fused_init() {
 bool decode_fused_supported(int T, int H, int I, int E, int K, bool same_x, int bits, int gs) {
     if (T < 1 || T > kMaxT) return false;
     if (bits != 0 && !((bits == 4 || bits == 8) && gs == 64)) return false;
-    const size_t ring = bits == 0   ? (size_t)stages_T<0>(T) * stage_bytes<0>()
-                        : bits == 4 ? (size_t)stages_T<4>(T) * stage_bytes<4>()
-                                    : (size_t)stages_T<8>(T) * stage_bytes<8>();
+    const size_t ring = bits == 0 ? ring_T<0>(T) : bits == 4 ? ring_T<4>(T) : ring_T<8>(T);
+    // 4-bit: at least two whole-item slots (one in use, one filling)
+    if (bits == 4 && ring / ((q4_slot_bytes(H, I) + 127) & ~size_t(127)) < 2) return false;
     const size_t smem = bits == 0 ? fused_smem_T<0>(T, H, I)
                         : bits == 4 ? fused_smem_T<4>(T, H, I) : fused_smem_T<8>(T, H, I);
     const size_t router = (same_x ? 0 : (size_t)T * H * 2) + (size_t)H * 4 +
@@ -1162,7 +1446,8 @@ cudaError_t launch_decode_fused(const uint16_t *xr, const uint16_t *xe, const ui
             return cudaErrorInvalidValue;
     }
     FusedArgs a{xr, xe, scale, pes, proj, T, H, E, K, I, eps, (float)(1.0 / sqrt((double)H)),
-                scores, idx, w, d, yq, oq, out, sync, err};
+                scores, idx, w, d, yq, oq, out, sync, err,
+                wt.gu_q, wt.dn_q, wt.gu_sb, wt.dn_sb};
     const cudaError_t e = bits == 0   ? launch_bits<0>(m, a, s)
                           : bits == 4 ? launch_bits<4>(m, a, s)
                                       : launch_bits<8>(m, a, s);

@@ -228,25 +228,6 @@ __device__ __forceinline__ bool down_pass_q(const uint8_t *ring, uint64_t *full,
 // the work and the operands are built in registers; a tcgen05 MMA would need
 // them written to shared memory first.)
 
-__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4],
-                                               uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-        "{%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// The A fragment of one 16x16 tile (rows g and g + 8, k = 2t, 2t+1, 2t+8,
-// 2t+9 of the tile) from the two packed words (k 0..7, k 8..15) of each row.
-__device__ __forceinline__ void q4_pair(uint32_t w0, uint32_t w1, int t, uint32_t &lo,
-                                        uint32_t &hi) {
-    // byte t of w0 (codes k=2t, 2t+1) and byte t of w1 (k=2t+8, 2t+9)
-    const uint32_t x = __byte_perm(w0, w1, (uint32_t)(t | ((4 + t) << 4))) & 0xFFFFu;
-    lo = ((x | (x << 12)) & 0x000F000Fu) | 0x43004300u;         // (128+q0, 128+q1)
-    hi = (((x >> 8) | (x << 4)) & 0x000F000Fu) | 0x43004300u;  // (128+q8, 128+q9)
-}
-
 // gate_up, 32 rows (16 gate + 16 up) x one 256-wide stage per pass step;
 // warp w takes the stage's group w (k = 64w .. 64w+63) for both row halves.
 // Partial sums meet in shared memory at the end of the item.
