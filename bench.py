@@ -687,6 +687,39 @@ def run_prefill_only(args):
     return 0
 
 
+def run_decode_only(args):
+    """One decode forward at T tokens (bf16, or MLX affine --bits), repeated
+    warmup + steps times with the L2 flushed before each: the case the ncu
+    captures of decode_fused_kernel use (every forward is one launch)."""
+    import torch
+    import apertura_b200 as A
+    from apertura_b200 import build as B
+    from apertura_b200.synthetic import block_inputs, expert_bank
+    B.build()
+    dev = torch.device("cuda", 0)
+    gu, dn = expert_bank(E, H, I, 0, dev)
+    T = args.decode_only
+    d = block_inputs(T, seed=11, device=dev, with_experts=False)
+    cfg = A.ESModelConfig(moe_sparse=True, quant_bits=args.bits, max_tokens=T)
+    blk = A.MoEBlock(cfg, d["proj"], d["scale"], d["pes"], gu, dn)
+    flush = torch.ones(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ms = 0.0
+    for i in range(args.warmup + args.steps):
+        flush.sum()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        blk.forward(d["x"])
+        b.record(stream)
+        b.synchronize()
+        if i >= args.warmup:
+            ms += a.elapsed_time(b) / args.steps
+    blk.handle.sync()
+    print(json.dumps({"decode_only": {"T": T, "bits": args.bits, "ms": ms,
+                                      "launches": blk.handle.last_launches()}}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -705,6 +738,10 @@ def main():
                     help="largest T that uses the GEMV expert kernels (default: library's)")
     ap.add_argument("--prefill-only", type=int, default=0, metavar="T",
                     help="only run the prefill config at T tokens (profiling case)")
+    ap.add_argument("--decode-only", type=int, default=0, metavar="T",
+                    help="only repeat one decode forward at T tokens (profiling case)")
+    ap.add_argument("--bits", type=int, default=0, choices=[0, 4, 8],
+                    help="with --decode-only: MLX affine expert bits (0: bf16)")
     ap.add_argument("--traffic", type=float, default=None,
                     help="dram bytes per gate_up launch from an ncu capture (reported as is)")
     args = ap.parse_args()
@@ -712,6 +749,8 @@ def main():
         args.warmup = 3
     if args.prefill_only:
         return run_prefill_only(args)
+    if args.decode_only:
+        return run_decode_only(args)
     return run_reference(args) if args.impl == "reference" else run_ours(args)
 
 
