@@ -77,6 +77,9 @@ struct apt_moe_handle {
 
     // router
     uint16_t *proj = nullptr, *scale = nullptr, *pes = nullptr;
+    // (scale * H^-1/2 * proj) as a two-term bf16 split [E, 2H], folded at load
+    // for the tensor-core router (T > 64)
+    uint16_t *projw = nullptr;
     // experts, bf16 (kept when quantised from bf16 so the dense path works)
     uint16_t *gu = nullptr, *dn = nullptr;
     // per-call bf16 expansion of the touched quantised experts for the
@@ -92,15 +95,17 @@ struct apt_moe_handle {
 
     // workspace
     int Tm = 0, Pcap = 0;
-    float *scores = nullptr;
+    float *scores = nullptr;     // [Tm, E] (tensor-core router: two planes [2][T][E])
     int32_t *idx_i = nullptr;
     uint16_t *w_i = nullptr;
     int32_t *counts = nullptr, *offsets = nullptr, *perm = nullptr, *inv = nullptr;
     int32_t *active = nullptr, *n_active = nullptr, *errflag = nullptr;
     int32_t *done = nullptr;    // fused decode router's completion counter (self-resetting)
     int32_t *fsync = nullptr;   // one-kernel decode block's counters (self re-arming)
-    uint16_t *hsplit = nullptr; // tensor-core router input [Tm, 2H]
-    int32_t *rt_cnt = nullptr;  // its single-group {count, offset, end}
+    // router rows x of the current call when h->scores holds the tensor-core
+    // router's raw x . (scale * H^-1/2 * proj) (router_select applies the RMS
+    // factor); nullptr when the scores are final
+    const uint16_t *rs_x = nullptr;
     uint16_t *xp = nullptr, *yp = nullptr, *op = nullptr;
     uint16_t *Wd = nullptr;     // dense routing matrix [Tm,E]
     int32_t *idx2 = nullptr;    // dense pair lists [Pcap]
@@ -211,7 +216,7 @@ std::vector<void **> weight_fields(apt_moe_handle *h) {
             reinterpret_cast<void **>(&h->dn_q),  reinterpret_cast<void **>(&h->gu_s),
             reinterpret_cast<void **>(&h->gu_b),  reinterpret_cast<void **>(&h->dn_s),
             reinterpret_cast<void **>(&h->dn_b),  reinterpret_cast<void **>(&h->gu_sb),
-            reinterpret_cast<void **>(&h->dn_sb)};
+            reinterpret_cast<void **>(&h->dn_sb), reinterpret_cast<void **>(&h->projw)};
 }
 
 void drop_graphs(apt_moe_handle *h) {
@@ -337,7 +342,7 @@ extern "C" apt_status apt_moe_create(const apt_moe_config *cfg, apt_moe_handle *
     h->Pcap = h->Tm * K;
     cudaError_t e1 = cudaSuccess;
 #define ALLOC(p, n) if (e1 == cudaSuccess) e1 = dalloc(&h->p, (size_t)(n))
-    ALLOC(scores, (size_t)h->Tm * E);
+    ALLOC(scores, 2 * (size_t)h->Tm * E);  // two partial planes on the tensor-core router
     ALLOC(idx_i, h->Pcap);
     ALLOC(w_i, h->Pcap);
     ALLOC(counts, E);
@@ -348,8 +353,6 @@ extern "C" apt_status apt_moe_create(const apt_moe_config *cfg, apt_moe_handle *
     ALLOC(n_active, 1);
     ALLOC(errflag, 4);
     ALLOC(done, 16);
-    ALLOC(hsplit, (size_t)h->Tm * 2 * H);
-    ALLOC(rt_cnt, 4);
     ALLOC(xp, (size_t)h->Pcap * H);
     ALLOC(yp, (size_t)h->Pcap * I);
     ALLOC(op, (size_t)h->Pcap * H);
@@ -391,7 +394,7 @@ extern "C" apt_status apt_moe_destroy(apt_moe_handle *h) {
     }
     void *ptrs[] = {h->proj, h->scale, h->pes, h->gu, h->dn, h->gu_q, h->dn_q, h->gu_s, h->gu_b,
                     h->dn_s, h->dn_b, h->scores, h->idx_i, h->w_i, h->counts, h->offsets,
-                    h->perm, h->inv, h->active, h->n_active, h->errflag, h->done, h->hsplit, h->rt_cnt, h->xp, h->yp, h->op,
+                    h->perm, h->inv, h->active, h->n_active, h->errflag, h->done, h->projw, h->xp, h->yp, h->op,
                     h->Wd, h->idx2, h->w2, h->xin, h->xout, h->dq_gu, h->dq_dn, h->gu_sb, h->dn_sb, h->xn, h->fsync};
     for (void *p : ptrs) dfree(p);
     drop_graphs(h);
@@ -551,11 +554,14 @@ extern "C" apt_status apt_moe_load_router(apt_moe_handle *h, const uint16_t *pro
         CUDA_TRY(h, dalloc(&h->proj, (size_t)E * H));
         CUDA_TRY(h, dalloc(&h->scale, (size_t)H));
         CUDA_TRY(h, dalloc(&h->pes, (size_t)E));
+        CUDA_TRY(h, dalloc(&h->projw, (size_t)E * 2 * H));
     }
     apt_status st;
     if ((st = copy_in(h, h->proj, proj, sizeof(uint16_t) * E * H, on_device))) return st;
     if ((st = copy_in(h, h->scale, scale, sizeof(uint16_t) * H, on_device))) return st;
     if ((st = copy_in(h, h->pes, pes, sizeof(uint16_t) * E, on_device))) return st;
+    CUDA_TRY(h, launch_router_fold_split(h->proj, h->scale, H, E, h->projw, 0));
+    CUDA_TRY(h, cudaDeviceSynchronize());
     return APT_OK;
 }
 
@@ -667,24 +673,22 @@ apt_status check_T(apt_moe_handle *h, int T) {
     return APT_OK;
 }
 
-// Router scores [T,E] f32 into h->scores: tensor-core split GEMM for
-// prefill-sized T, f32 SIMT kernels otherwise.
+// Router scores [T,E] f32 into h->scores: tensor-core GEMM on the folded
+// weights for prefill-sized T (raw scores; h->rs_x = x tells router_select to
+// apply the RMS factor), f32 SIMT kernels otherwise (final scores).
 apt_status router_scores(apt_moe_handle *h, const uint16_t *x, int T, cudaStream_t s,
                          const uint16_t *pre_w = nullptr) {
     const int H = h->cfg.hidden_size, E = h->cfg.num_experts;
-    if (T > 64 && E % 64 == 0 && gemm_supported(H, h->cfg.moe_intermediate_size)) {
-        STAGE(h, APT_STAGE_ROUTER_SCORES, s,
-              launch_router_norm_split(x, h->scale, T, H, h->cfg.rms_norm_eps, h->hsplit,
-                                       h->rt_cnt, s, &h->launches, pre_w,
-                                       pre_w ? h->xn : nullptr));
-        STAGE(h, APT_STAGE_ROUTER_SCORES, s,
-              launch_gemm_router(h->hsplit, h->proj, h->rt_cnt, T, H, E, h->scores, h->errflag, s,
-                                 &h->launches));
-        return APT_OK;
-    }
     if (pre_w)
         STAGE(h, APT_STAGE_ROUTER_SCORES, s,
               launch_rmsnorm(x, pre_w, T, H, h->cfg.rms_norm_eps, h->xn, s, &h->launches));
+    if (T > 64 && E % 64 == 0 && gemm_supported(H, h->cfg.moe_intermediate_size)) {
+        STAGE(h, APT_STAGE_ROUTER_SCORES, s,
+              launch_gemm_router(x, h->projw, T, H, E, h->scores, h->errflag, s, &h->launches));
+        h->rs_x = x;
+        return APT_OK;
+    }
+    h->rs_x = nullptr;
     STAGE(h, APT_STAGE_ROUTER_SCORES, s,
           launch_router_scores(x, h->proj, h->scale, T, H, E, h->cfg.rms_norm_eps, h->scores, s,
                                &h->launches));
@@ -817,7 +821,8 @@ extern "C" apt_status apt_moe_route(apt_moe_handle *h, const uint16_t *x, int T,
     (void)H;
     if (apt_status st = router_scores(h, x, T, s)) return st;
     STAGE(h, APT_STAGE_ROUTER_SELECT, s, launch_router_select(h->scores, h->pes, T, E, K, idx, w, nullptr, s,
-                                     &h->launches));
+                                     &h->launches, nullptr, nullptr, h->rs_x, H,
+                                     h->cfg.rms_norm_eps));
     return APT_OK;
 }
 
@@ -920,7 +925,8 @@ apt_status forward_impl(apt_moe_handle *h, const uint16_t *x_router, const uint1
         // per-expert scan of the dispatch kernel
         STAGE(h, APT_STAGE_ROUTER_SELECT, s,
               launch_router_select(h->scores, h->pes, T, E, K, idx, w, h->counts, s,
-                                   &h->launches, h->idx2));
+                                   &h->launches, h->idx2, nullptr, h->rs_x, H,
+                                   h->cfg.rms_norm_eps));
         STAGE(h, APT_STAGE_DISPATCH, s,
               launch_place(idx, h->idx2, T * K, E, h->disp(), s, &h->launches));
         const bool quant = h->qbits > 0;
@@ -930,7 +936,8 @@ apt_status forward_impl(apt_moe_handle *h, const uint16_t *x_router, const uint1
     }
     // dense (reference default): routeWeights then ESExperts::forward
     STAGE(h, APT_STAGE_ROUTER_SELECT, s, launch_router_select(h->scores, h->pes, T, E, K, idx, w, nullptr, s,
-                                     &h->launches));
+                                     &h->launches, nullptr, nullptr, h->rs_x, H,
+                                     h->cfg.rms_norm_eps));
     STAGE(h, APT_STAGE_ROUTER_SELECT, s, launch_scatter_dense(idx, w, T, E, K, h->Wd, s, &h->launches));
     return experts_dense(h, x_experts, h->Wd, T, out, s);
 }
@@ -1014,7 +1021,8 @@ extern "C" apt_status apt_moe_ep_dispatch(apt_moe_handle *h, const uint16_t *x, 
         CUDA_TRY(h, cudaMemsetAsync(h->counts, 0, sizeof(int32_t) * E, s));
         STAGE(h, APT_STAGE_ROUTER_SELECT, s,
               launch_router_select(h->scores, h->pes, T, E, K, idx, w, h->counts, s,
-                                   &h->launches, h->idx2));
+                                   &h->launches, h->idx2, nullptr, h->rs_x, H,
+                                   h->cfg.rms_norm_eps));
         STAGE(h, APT_STAGE_DISPATCH, s, launch_place(idx, h->idx2, T * K, E, d, s, &h->launches));
     }
     STAGE(h, APT_STAGE_GATHER, s,

@@ -122,11 +122,15 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         tma_prefetch(&tmB);
     }
     pdl_wait();  // dispatch / gather / gate_up output this kernel reads is complete
+    // EPI_F32 (router scores) has one group of gk = T rows at offset 0 and no
+    // count arrays
+    auto grp_cnt = [&](int e) { return EPI == EPI_F32 ? gk : counts[e]; };
+    auto grp_off = [&](int e) { return EPI == EPI_F32 ? 0 : offsets[e]; };
     if (warp == 0 && lane == 0) {
         int acc = 0;
         for (int e = 0; e < E; ++e) {
             mtp[e] = acc;
-            acc += (counts[e] + kBM - 1) / kBM;
+            acc += (grp_cnt(e) + kBM - 1) / kBM;
         }
         mtp[E] = acc;
     }
@@ -139,9 +143,13 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     pdl_trigger();
-    // EPI_F32 (router scores): one "expert", N = H outputs, and the B operand
-    // (proj [H, I]) is reused for every I-wide slice of the K = 2*I split input.
-    const int NT = GU ? (I + BN2 - 1) / BN2 : H / BN;
+    // EPI_F32 (router scores): one "expert", N = H outputs, K = I; the B
+    // operand is the folded two-term weights [H, 2*I], and the n-tiles run
+    // over (term, column block): term 0 multiplies the token rows by the
+    // first I-wide half of B, term 1 by the second, each into its own score
+    // plane, so that twice as many CTAs share the T / 128 m-tiles.
+    const int NCB = H / BN;  // column blocks (EPI_F32)
+    const int NT = GU ? (I + BN2 - 1) / BN2 : EPI == EPI_F32 ? 2 * NCB : H / BN;
     const int tiles = mtp[E] * NT;
     const int KB = Kdim / kBK;
     // gate_up: the last n-tile covers TW = I - (NT-1)*BN2 columns; when that is
@@ -202,7 +210,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
                 int e, mloc, nt;
                 decode_tile(t, NT, mtp, E, e, mloc, nt);
-                const int row0 = offsets[e] + mloc * kBM;
+                const int row0 = grp_off(e) + mloc * kBM;
                 const bool tail = GU && nt == NT - 1 && TW < BN2;
                 const int wrows = tail ? TW : BN2;
                 const CUtensorMap *mb = tail ? &tmC : &tmB;
@@ -226,7 +234,8 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                         tma_load_2d(sB + s * B_BYTES + wrows * kBK * 2, mb, &full[s], kb * kBK,
                                     gate_row + I);
                     } else if (EPI == EPI_F32) {
-                        tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], (kb * kBK) % I, nt * BN);
+                        tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], kb * kBK + (nt / NCB) * I,
+                                    (nt % NCB) * BN);
                     } else {
                         const int ew = g2e ? g2e[e] : e;
                         tma_load_2d(sB + s * B_BYTES, &tmB, &full[s], kb * kBK, ew * H + nt * BN);
@@ -274,8 +283,8 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
             int e, mloc, nt;
             decode_tile(t, NT, mtp, E, e, mloc, nt);
-            const int nvalid = counts[e] - mloc * kBM;
-            const int row = offsets[e] + mloc * kBM + r;
+            const int nvalid = grp_cnt(e) - mloc * kBM;
+            const int row = grp_off(e) + mloc * kBM + r;
             const int buf = i & 1;
             const uint32_t use = i >> 1;
             if (!mbar_wait(&tfull[buf], use & 1, kWaitLimit)) {
@@ -290,7 +299,9 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 epilogue_geglu(taddr, w, w, r < nvalid,
                                out + (size_t)row * out_ld + nt * BN2);
             } else if constexpr (EPI == EPI_F32) {
-                float *dst = reinterpret_cast<float *>(out) + (size_t)row * out_ld + nt * BN;
+                // plane nt / NCB of [2][gk = T][out_ld]
+                float *dst = reinterpret_cast<float *>(out) + (size_t)(nt / NCB) * gk * out_ld +
+                             (size_t)row * out_ld + (nt % NCB) * BN;
 #pragma unroll 1
                 for (int c = 0; c < BN / 8; ++c) {
                     uint32_t a[8];
@@ -364,6 +375,7 @@ constexpr int kGuStages = 5, kDnStages = 4, kRtStages = 6;
 cudaError_t gemm_init() {
     cudaError_t e;
     if ((e = set_attr<EPI_F32, 64, 0, kRtStages>())) return e;
+    if ((e = set_attr<EPI_F32, 128, 0, kRtStages>())) return e;
     if ((e = set_attr<EPI_GATEUP, 176, 88, kGuStages>())) return e;
     if ((e = set_attr<EPI_GATEUP, 256, 128, kDnStages>())) return e;
     if ((e = set_attr<EPI_GATEUP, 128, 64, kGuStages>())) return e;
@@ -520,20 +532,26 @@ cudaError_t launch_gemm_down(const uint16_t *yp, const Dispatch &d, const Expert
 
 namespace apt {
 
-// Router scores on the tensor cores: scores [T,E] f32 = hs [T, 2H] . [proj|proj]^T
-// where hs = (h1 | h2) is the two-term bf16 split of the f32 router input.
-cudaError_t launch_gemm_router(const uint16_t *hs, const uint16_t *proj, const int32_t *cnt_off,
-                               int T, int H, int E, float *scores, int32_t *err, cudaStream_t s,
-                               int *launches) {
+// Router scores on the tensor cores, before the per-token RMS factor, as two
+// planes scores[term] [T,E] f32 = x [T, H] . w_term^T, where (w1 | w2)
+// [E, 2H] is the two-term bf16 split of (scale * H^-1/2) * proj folded at
+// load; x is bf16, the products are exact and accumulate in f32, so
+// plane 0 + plane 1 matches the f32 dot product to ~2^-17 relative per term.
+cudaError_t launch_gemm_router(const uint16_t *x, const uint16_t *projw, int T, int H, int E,
+                               float *scores, int32_t *err, cudaStream_t s, int *launches) {
+    const int bn = E % 128 == 0 ? 128 : 64;
     CUtensorMap a, b;
-    if (!make_map(&a, hs, 2 * (uint64_t)H, T, kBM) || !make_map(&b, proj, H, E, 64))
+    if (!make_map(&a, x, H, T, kBM) || !make_map(&b, projw, 2 * (uint64_t)H, E, bn))
         return cudaErrorInvalidValue;
     Dispatch d{};
-    d.counts = const_cast<int32_t *>(cnt_off);
-    d.offsets = const_cast<int32_t *>(cnt_off + 1);
-    cudaError_t e = launch<EPI_F32, 64, 0, kRtStages>(a, b, d, 1, 2 * H, H, E,
-                                                     reinterpret_cast<uint16_t *>(scores), E, err,
-                                                     s);
+    float *o = scores;
+    cudaError_t e =
+        bn == 128 ? launch<EPI_F32, 128, 0, kRtStages>(a, b, d, 1, H, H, E,
+                                                       reinterpret_cast<uint16_t *>(o), E, err, s,
+                                                       nullptr, nullptr, nullptr, T)
+                  : launch<EPI_F32, 64, 0, kRtStages>(a, b, d, 1, H, H, E,
+                                                      reinterpret_cast<uint16_t *>(o), E, err, s,
+                                                      nullptr, nullptr, nullptr, T);
     if (launches) ++*launches;
     return e;
 }

@@ -36,7 +36,8 @@ cudaError_t launch_router_scores(const uint16_t *x, const uint16_t *proj, const 
 cudaError_t launch_router_select(const float *scores, const uint16_t *pes, int T, int E, int K,
                                  int32_t *idx, uint16_t *w, int32_t *counts, cudaStream_t s,
                                  int *launches, int32_t *rank = nullptr,
-                                 const int32_t *err = nullptr);
+                                 const int32_t *err = nullptr, const uint16_t *x = nullptr,
+                                 int H = 0, float eps = 0.f);
 // Decode-sized fused router + dispatch (one launch): writes idx/w and the full
 // Dispatch.  `done` is a zero-initialised device counter the kernel resets.
 bool router_dispatch_fusable(int T, int H, int E, int K);
@@ -46,13 +47,12 @@ cudaError_t launch_router_dispatch(const uint16_t *x, const uint16_t *proj, cons
                                    int32_t *done, cudaStream_t s, int *launches,
                                    const uint16_t *pre_w = nullptr, uint16_t *xn = nullptr,
                                    int32_t *err = nullptr);
-// Tensor-core router path: two-term bf16 split of the f32 router input, then
-// an f32-output tcgen05 GEMM against proj (gemm_sm100.cu).
-// pre_w/xn (optional): also write xn = RMSNorm(x) * pre_w (pre_ff_ln_2)
-cudaError_t launch_router_norm_split(const uint16_t *x, const uint16_t *scale, int T, int H,
-                                     float eps, uint16_t *hs, int32_t *cnt_off, cudaStream_t s,
-                                     int *launches, const uint16_t *pre_w = nullptr,
-                                     uint16_t *xn = nullptr);
+// Tensor-core router path: (scale * H^-1/2 * proj) folded at load into a
+// two-term bf16 split [E, 2H]; the f32-output tcgen05 GEMM reads the token
+// rows directly (gemm_sm100.cu) and router_select applies the RMS factor
+// (launch_router_select with x).
+cudaError_t launch_router_fold_split(const uint16_t *proj, const uint16_t *scale, int H, int E,
+                                     uint16_t *pw, cudaStream_t s);
 // out = RMSNorm(x) * w (ESRMSNorm.mm:14-28), one warp per row
 // idx[i] = 0, w[i] = bf16 1.0 for i < n: every row to the single "expert"
 // of a dense GeGLU MLP handle
@@ -60,9 +60,8 @@ cudaError_t launch_fill_mlp_routing(int32_t *idx, uint16_t *w, int n, cudaStream
                                     int *launches);
 cudaError_t launch_rmsnorm(const uint16_t *x, const uint16_t *w, int T, int H, float eps,
                           uint16_t *out, cudaStream_t s, int *launches);
-cudaError_t launch_gemm_router(const uint16_t *hs, const uint16_t *proj, const int32_t *cnt_off,
-                               int T, int H, int E, float *scores, int32_t *err, cudaStream_t s,
-                               int *launches);
+cudaError_t launch_gemm_router(const uint16_t *x, const uint16_t *projw, int T, int H, int E,
+                               float *scores, int32_t *err, cudaStream_t s, int *launches);
 // dense routeWeights scatter: W [T,E] = 0 except W[t, idx[t,k]] = w[t,k]
 cudaError_t launch_scatter_dense(const int32_t *idx, const uint16_t *w, int T, int E, int K,
                                  uint16_t *W, cudaStream_t s, int *launches);

@@ -275,12 +275,23 @@ __device__ __forceinline__ void load_scores(const float *__restrict__ sr, int E,
     }
 }
 
+// sr2 (optional): a second partial-score row added to sr's; rs: per-token
+// factor applied to the (summed) scores -- the RMS factor when the scores
+// were computed from the un-normalised token row.
 template <int NP>
 __device__ __forceinline__ void select_token(const float *__restrict__ sr,
                                              const uint16_t *__restrict__ pes, int E, int K,
-                                             int lane, int &sel_e_out, float &wk_out) {
+                                             int lane, int &sel_e_out, float &wk_out,
+                                             const float *__restrict__ sr2 = nullptr,
+                                             float rs = 1.f) {
     float p[NP];
     load_scores<NP>(sr, E, lane, p);
+    if (sr2) {
+        float p2[NP];
+        load_scores<NP>(sr2, E, lane, p2);
+#pragma unroll
+        for (int j = 0; j < NP; ++j) p[j] = __fmul_rn(__fadd_rn(p[j], p2[j]), rs);
+    }
     int sel_e;
     float sel_p, sum;
     select_core<NP>(p, E, K, lane, sel_e, sel_p, sum);
@@ -304,12 +315,29 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
 router_select(const float *__restrict__ scores, const uint16_t *__restrict__ pes, int T, int E,
               int K, int32_t *__restrict__ idx, uint16_t *__restrict__ w,
               int32_t *__restrict__ counts, int32_t *__restrict__ rank,
-              const int32_t *__restrict__ err) {
+              const int32_t *__restrict__ err, const uint16_t *__restrict__ xr, int H,
+              float eps) {
     __shared__ int s_cnt[kMaxPerLane * 32];
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
     pdl_trigger();
     pdl_wait();
+    // xr: the scores are two planes [2][T][E] of partial x . (scale * H^-1/2
+    // * proj) of the raw token rows; they are summed and the RMS factor
+    // r = 1 / sqrt(mean(x^2) + eps) of ESRouter.mm:18-20 is applied here
+    float rs = 1.f;
+    if (xr && warp < T) {
+        const uint16_t *row = xr + (size_t)warp * H;
+        float ss = 0.f;
+        for (int i = lane * 8; i < H; i += 256) {
+            float f[8];
+            unpack8(*reinterpret_cast<const uint4 *>(row + i), f);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+        }
+        ss = warp_sum(ss);
+        rs = 1.0f / sqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / (float)H), eps));
+    }
     int e = -1, local = 0;
     float wk = 0.f;
     if (err && __ldcg(err) != 0) {  // the scores of this call never arrived: mark it invalid
@@ -320,7 +348,8 @@ router_select(const float *__restrict__ scores, const uint16_t *__restrict__ pes
         return;
     }
     if (warp < T) {
-        select_token<NP>(scores + (size_t)warp * E, pes, E, K, lane, e, wk);
+        select_token<NP>(scores + (size_t)warp * E, pes, E, K, lane, e, wk,
+                         xr ? scores + ((size_t)T + warp) * E : nullptr, rs);
         if (lane < K) {
             idx[(size_t)warp * K + lane] = e;
             w[(size_t)warp * K + lane] = f2bf(wk);
@@ -480,98 +509,21 @@ router_dispatch_small(const uint16_t *__restrict__ x, const uint16_t *__restrict
     RT_STAMP(6);
 }
 
-// Router input for the tensor-core score GEMM: h = ((x*r)*scale)*H^-1/2 in
-// f32 (the reference's rounding points), written as a two-term bf16 split
-// hs[t] = (h1 | h2), h1 = bf16(h), h2 = bf16(h - h1), so that
-// h1.p + h2.p reproduces h.p to ~2^-17 relative per term with exact bf16
-// products and f32 accumulation.  One warp per token.  Thread 0 of block 0
-// writes the single-group counts/offsets {T, 0, T} the GEMM scheduler reads.
-__global__ void router_norm_split(const uint16_t *__restrict__ x,
-                                  const uint16_t *__restrict__ scale, int T, int H, float eps,
-                                  float root, uint16_t *__restrict__ hs,
-                                  int32_t *__restrict__ cnt_off,
-                                  const uint16_t *__restrict__ pre_w, uint16_t *__restrict__ xn) {
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
-        cnt_off[0] = T;
-        cnt_off[1] = 0;
-        cnt_off[2] = T;
-    }
-    if (warp >= T) return;
-    const uint16_t *xr = x + (size_t)warp * H;
-    // the row stays in registers (all of its loads in flight at once) when
-    // H <= 32 * 8 * kNormVec; longer rows are read twice
-    constexpr int kNormVec = 12;
-    const int nv = (H + 255) / 256;
-    const bool in_regs = nv <= kNormVec;
-    uint4 xv[kNormVec];
-    float ss = 0.f;
-    if (in_regs) {
-#pragma unroll
-        for (int q = 0; q < kNormVec; ++q) {
-            const int i = lane * 8 + q * 256;
-            if (q < nv && i < H) xv[q] = *reinterpret_cast<const uint4 *>(xr + i);
-        }
-#pragma unroll
-        for (int q = 0; q < kNormVec; ++q) {
-            const int i = lane * 8 + q * 256;
-            if (q < nv && i < H) {
-                float f[8];
-                unpack8(xv[q], f);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
-            }
-        }
-    } else {
-        for (int i = lane * 8; i < H; i += 256) {
-            float f[8];
-            unpack8(*reinterpret_cast<const uint4 *>(xr + i), f);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
-        }
-    }
-    ss = warp_sum(ss);
-    const float r = 1.0f / sqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / (float)H), eps));
-    uint16_t *d1 = hs + (size_t)warp * 2 * H;
-    uint16_t *d2 = d1 + H;
-    auto emit = [&](int i, const uint4 &xq) {
-        float f[8], sf[8];
-        unpack8(xq, f);
-        unpack8(*reinterpret_cast<const uint4 *>(scale + i), sf);
-        float h1[8], h2[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float h = router_h(f[j], r, sf[j], root);
-            h1[j] = rbf(h);
-            h2[j] = rbf(__fsub_rn(h, h1[j]));
-        }
-        uint4 v1, v2;
-        v1.x = pack_bf2(h1[0], h1[1]); v1.y = pack_bf2(h1[2], h1[3]);
-        v1.z = pack_bf2(h1[4], h1[5]); v1.w = pack_bf2(h1[6], h1[7]);
-        v2.x = pack_bf2(h2[0], h2[1]); v2.y = pack_bf2(h2[2], h2[3]);
-        v2.z = pack_bf2(h2[4], h2[5]); v2.w = pack_bf2(h2[6], h2[7]);
-        *reinterpret_cast<uint4 *>(d1 + i) = v1;
-        *reinterpret_cast<uint4 *>(d2 + i) = v2;
-        if (xn) {  // pre_ff_ln_2(x1): the same r times the norm weight
-            float wf[8], o[8];
-            unpack8(*reinterpret_cast<const uint4 *>(pre_w + i), wf);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) o[j] = __fmul_rn(__fmul_rn(f[j], r), wf[j]);
-            uint4 v;
-            v.x = pack_bf2(o[0], o[1]); v.y = pack_bf2(o[2], o[3]);
-            v.z = pack_bf2(o[4], o[5]); v.w = pack_bf2(o[6], o[7]);
-            *reinterpret_cast<uint4 *>(xn + (size_t)warp * H + i) = v;
-        }
-    };
-    if (in_regs) {
-#pragma unroll
-        for (int q = 0; q < kNormVec; ++q) {
-            const int i = lane * 8 + q * 256;
-            if (q < nv && i < H) emit(i, xv[q]);
-        }
-    } else {
-        for (int i = lane * 8; i < H; i += 256) emit(i, *reinterpret_cast<const uint4 *>(xr + i));
-    }
+// Router weights for the tensor-core score GEMM, folded once at load:
+// w = (scale[h] * H^-1/2) * proj[e, h] in f32, stored as the two-term bf16
+// split pw[e] = (w1 | w2) [E, 2H], w1 = bf16(w), w2 = bf16(w - w1), so that
+// x . w1 + x . w2 reproduces x . w to ~2^-17 relative per term (x is bf16,
+// the products are exact, the accumulation f32).
+__global__ void router_fold_split(const uint16_t *__restrict__ proj,
+                                  const uint16_t *__restrict__ scale, int H, int E, float root,
+                                  uint16_t *__restrict__ pw) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)E * H) return;
+    const size_t e = i / H, c = i - e * H;
+    const float wv = __fmul_rn(__fmul_rn(bf2f(scale[c]), root), bf2f(proj[i]));
+    const float w1 = rbf(wv);
+    pw[e * 2 * H + c] = f2bf(w1);
+    pw[e * 2 * H + H + c] = f2bf(__fsub_rn(wv, w1));
 }
 
 // Standalone RMSNorm with weight (ESRMSNorm.mm:14-28), one warp per row.
@@ -694,24 +646,23 @@ cudaError_t launch_rmsnorm(const uint16_t *x, const uint16_t *w, int T, int H, f
     return err;
 }
 
-cudaError_t launch_router_norm_split(const uint16_t *x, const uint16_t *scale, int T, int H,
-                                     float eps, uint16_t *hs, int32_t *cnt_off, cudaStream_t s,
-                                     int *launches, const uint16_t *pre_w, uint16_t *xn) {
+cudaError_t launch_router_fold_split(const uint16_t *proj, const uint16_t *scale, int H, int E,
+                                     uint16_t *pw, cudaStream_t s) {
     const float root = (float)(1.0 / sqrt((double)H));
-    const int wpb = 8;
-    router_norm_split<<<(T + wpb - 1) / wpb, wpb * 32, 0, s>>>(x, scale, T, H, eps, root, hs,
-                                                               cnt_off, pre_w, xn);
-    if (launches) ++*launches;
+    const size_t n = (size_t)E * H;
+    router_fold_split<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(proj, scale, H, E, root, pw);
     return cudaGetLastError();
 }
 
 cudaError_t launch_router_select(const float *scores, const uint16_t *pes, int T, int E, int K,
                                  int32_t *idx, uint16_t *w, int32_t *counts, cudaStream_t s,
-                                 int *launches, int32_t *rank, const int32_t *err) {
+                                 int *launches, int32_t *rank, const int32_t *err,
+                                 const uint16_t *x, int H, float eps) {
     dim3 grid((T + kSelectWarps - 1) / kSelectWarps);
     cudaError_t r = launch_ex(E <= 128 ? router_select<4> : router_select<kMaxPerLane>, grid,
                               dim3(kSelectWarps * 32), 0, s, true,
-                              (const float *)scores, pes, T, E, K, idx, w, counts, rank, err);
+                              (const float *)scores, pes, T, E, K, idx, w, counts, rank, err,
+                              x, H, eps);
     if (launches) ++*launches;
     return r;
 }

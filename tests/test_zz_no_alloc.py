@@ -62,14 +62,19 @@ def test_noalloc_matches_route_and_oracle_twice(oracle, T, H):
         idx, w = _noalloc(d, x, H)
         torch.cuda.synchronize()
         got = idx.cpu().numpy()
-        # against the handle path: the same score and selection kernels
-        np.testing.assert_array_equal(got, ref.idx.cpu().numpy())
-        a, b = _wf(w), _wf(ref.w)
-        assert np.all(np.abs(a - b) <= np.abs(b) * W_REL + 1e-9)
-        # against the oracle: bit-exact indices except one-bf16-ulp ties
         idx_o, w_o, aux = oracle.route_topk(to_numpy_bits(x), to_numpy_bits(d["proj"]),
                                             to_numpy_bits(d["scale"]), to_numpy_bits(d["pes"]), K,
                                             return_scores=True)
+        # against the handle path (above T = 64 its scores come from the
+        # tensor-core router, another f32 summation order): bit-exact indices
+        # except one-bf16-ulp ties of the oracle's scores
+        ref_idx = ref.idx.cpu().numpy()
+        bad, exempt = router_index_check(got, ref_idx, aux["scores"])
+        assert bad == 0, f"{bad} non-tie mismatches vs apt_moe_route (exempt {exempt})"
+        eq = np.all(got == ref_idx, axis=1)
+        a, b = _wf(w), _wf(ref.w)
+        assert np.all(np.abs(a[eq] - b[eq]) <= np.abs(b[eq]) * W_REL + 1e-9)
+        # against the oracle: bit-exact indices except one-bf16-ulp ties
         bad, exempt = router_index_check(got, idx_o, aux["scores"])
         assert bad == 0, f"{bad} non-tie index mismatches (exempt {exempt} of {T})"
         same = np.all(got == idx_o, axis=1)
