@@ -23,7 +23,7 @@ EXPORTED = [
     "apt_moe_experts_dense", "apt_moe_forward", "apt_moe_layer_forward", "apt_moe_decoder_ff", "apt_moe_mlp_forward", "apt_moe_decoder_ff_full", "apt_moe_forward_host", "apt_moe_forward_host_async", "apt_moe_ep_dispatch",
     "apt_moe_ep_combine", "apt_moe_experts_grouped", "apt_moe_sync",
     "apt_moe_last_counts", "apt_moe_last_launches", "apt_moe_set_gemv_max_tokens",
-    "apt_moe_set_sm_limit", "apt_moe_set_fused_decode",
+    "apt_moe_set_sm_limit", "apt_moe_set_fused_decode", "apt_moe_set_q4_gemm",
     "apt_moe_set_timing", "apt_moe_stage_times", "apt_moe_route_noalloc",
     "apt_moe_nccl_unique_id", "apt_moe_create_ep", "apt_moe_ep_destroy", "apt_moe_ep_last_error",
     "apt_moe_ep_load_router", "apt_moe_ep_load_experts_bf16", "apt_moe_ep_forward",
@@ -99,6 +99,7 @@ def lib():
         "apt_moe_last_launches": ([hp], i32),
         "apt_moe_set_gemv_max_tokens": ([hp, i32], i32),
         "apt_moe_set_fused_decode": ([hp, i32], i32),
+        "apt_moe_set_q4_gemm": ([hp, i32], i32),
         "apt_moe_set_sm_limit": ([hp, i32], i32),
         "apt_moe_set_timing": ([hp, i32], i32),
         "apt_moe_stage_times": ([hp, P], i32),

@@ -49,6 +49,7 @@ struct apt_moe_handle {
     int sm_limit = 0;      // cap on SMs for persistent grids (0: all)
     bool gemv_tma = true;  // TMA-streamed bf16 GEMV (else the register-prefetch GEMV)
     bool fused_decode = true;  // whole decode block in one kernel (decode_fused.cu)
+    bool q4_gemm = true;       // 4-bit experts: dequantise B tiles inside the tcgen05 GEMMs
     // moe_intermediate_size as given when it is not a multiple of 64: the
     // handle then runs I rounded up to 64, the extra gate / up rows and down
     // columns zero (GeGLU of a zero row is exactly 0, and a zero column adds
@@ -470,6 +471,13 @@ extern "C" apt_status apt_moe_set_fused_decode(apt_moe_handle *h, int on) {
     return APT_OK;
 }
 
+extern "C" apt_status apt_moe_set_q4_gemm(apt_moe_handle *h, int on) {
+    if (!h || on < 0 || on > 1) return APT_ERR_INVALID;
+    drop_graphs(h);
+    h->q4_gemm = on != 0;
+    return APT_OK;
+}
+
 extern "C" apt_status apt_moe_set_timing(apt_moe_handle *h, int enable) {
     if (!h) return APT_ERR_INVALID;
     drop_graphs(h);
@@ -708,7 +716,10 @@ apt_status run_experts(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
     ExpertWeights ew = weights_for(h, quant);
     const int max_rows = T;  // an expert appears at most once per token
     const bool gemm = T > h->gemv_max_tokens && gemm_supported(H, I);
-    if (gemm && quant) {
+    // 4-bit experts: the GEMMs dequantise their B tiles in shared memory
+    const bool q4 = gemm && quant && h->qbits == 4 && h->qgs == 64 && h->q4_gemm &&
+                    gemm_q4_supported(H, I);
+    if (gemm && quant && !q4) {
         // The bf16 GEMM on the dequantised experts (w = scale*q + bias, rounded
         // to bf16 as MLX's dequantise does).  Every call expands the experts
         // it touches (the dispatch's active list) into a scratch bank laid out
@@ -732,12 +743,19 @@ apt_status run_experts(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
         const int rows_cap = P < h->Pcap ? P : h->Pcap;
         // Few rows per expert: A rows gathered inside the GEMM (tile::gather4);
         // prefill-sized groups: one gather pass, then full-tile TMA copies.
-        const bool gather_in_gemm = rows_cap <= kGatherInGemmRows;
+        const bool gather_in_gemm = rows_cap <= kGatherInGemmRows && !q4;
         if (!gather_in_gemm)
             STAGE(h, APT_STAGE_GATHER, s,
                   launch_gather_rows(x, H, Kp, E, d, rows_cap, h->xp, s, &h->launches, idx, T,
                                      h->errflag));
-        if (gather_in_gemm)
+        if (q4) {
+            STAGE(h, APT_STAGE_GATE_UP, s,
+                  launch_gemm_gateup_q4(h->xp, d, ew, rows_cap, H, I, E, h->yp, h->errflag, s,
+                                        &h->launches));
+            STAGE(h, APT_STAGE_DOWN, s,
+                  launch_gemm_down_q4(h->yp, d, ew, rows_cap, H, I, E, h->op, h->errflag, s,
+                                      &h->launches));
+        } else if (gather_in_gemm)
             STAGE(h, APT_STAGE_GATE_UP, s,
                   launch_gemm_gateup_gather(x, T, Kp, d, ew, rows_cap, H, I, E, h->yp,
                                             h->errflag, s, &h->launches));
@@ -745,9 +763,10 @@ apt_status run_experts(apt_moe_handle *h, const uint16_t *x, const int32_t *idx,
             STAGE(h, APT_STAGE_GATE_UP, s,
                   launch_gemm_gateup(h->xp, d, ew, rows_cap, H, I, E, h->yp, h->errflag, s,
                                      &h->launches));
-        STAGE(h, APT_STAGE_DOWN, s,
-              launch_gemm_down(h->yp, d, ew, rows_cap, H, I, E, h->op, h->errflag, s,
-                               &h->launches, max_rows));
+        if (!q4)
+            STAGE(h, APT_STAGE_DOWN, s,
+                  launch_gemm_down(h->yp, d, ew, rows_cap, H, I, E, h->op, h->errflag, s,
+                                   &h->launches, max_rows));
     } else if (quant && h->gemv_tma && gemv_tma_q_supported(H, I, h->qbits)) {
         STAGE(h, APT_STAGE_GATE_UP, s,
               launch_gemv_tma_q_gateup(x, Kp, d, ew, H, I, E, max_rows, h->yp, h->errflag, s,

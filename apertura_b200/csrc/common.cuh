@@ -18,8 +18,11 @@ __device__ __forceinline__ uint16_t f2bf(float f) {
     return __bfloat16_as_ushort(__float2bfloat16_rn(f));
 }
 __device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
+// Two round-to-nearest-even conversions (lo in the low half) as one paired
+// conversion instruction.
 __device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
-    return (uint32_t)f2bf(lo) | ((uint32_t)f2bf(hi) << 16);
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&v);
 }
 
 // Unpack 8 bf16 held in a uint4 into f32.

@@ -45,6 +45,10 @@ constexpr int kAccStride = 256;          // TMEM columns between the two accumul
 constexpr long long kWaitLimit = 4000000000LL;  // cycles (~2 s) before giving up
 constexpr int kMaxExperts = 256;
 constexpr int kStageC = 4 * 2 * 4096;    // down: 2 x 4 KB store boxes per epilogue warp
+// QB = 4 (MLX affine 4-bit experts, 64-element groups): eight more warps
+// dequantise each stage's packed codes into the bf16 B tile
+constexpr int kDqThreads = 256;
+constexpr int kBRing = 2;  // dequantised B tiles in flight (QB)
 
 // EPI_GATEUP_G: gate_up whose A rows are gathered from the token rows by the
 // TMA (tile::gather4, 4 rows per copy) through the dispatch permutation, so no
@@ -83,28 +87,51 @@ __device__ __forceinline__ void decode_tile(int t, int NT, const int *mtp, int E
 // groups (at most 64 rows per expert), which frees shared memory for more
 // weight stages in flight.  The M = 128 MMA then reads rows 64..127 from
 // whatever follows the stage (never stored rows: D rows are independent).
-template <int EPI, int BN, int BN2, int STAGES, int AROWS = 128>
-__global__ void __launch_bounds__(kThreads, 1)
+//
+// QB = 4: the expert weights are MLX affine 4-bit codes (ESExperts.mm:51,56
+// gather_qmm, 64-element groups).  The producer streams a stage's codes
+// (BN rows x 8 words, tmB / tmC) and its rows' (scale | bias << 16) words
+// (a 4-group box, tmS / tmSt) next to the A tile, through the STAGES-deep
+// ring; warps 6..13 turn them into the bf16 B tile w = bf16(scale * q + bias)
+// -- the rounding of MLX's dequantise and of dequant_active_kernel -- written
+// in the 128-byte-swizzled layout a TMA copy would produce into a separate
+// kBRing-deep ring of B tiles, then fence.proxy.async and arrive on bfull.
+// The MMA thread waits on full (A) and bfull (B) and commits to empty (the A /
+// code stage: its codes were consumed before B was complete) and to bempty
+// (the B tile), which the dequantising warps wait on before rewriting it.
+template <int EPI, int BN, int BN2, int STAGES, int AROWS = 128, int QB = 0>
+__global__ void __launch_bounds__(QB ? kThreads + kDqThreads : kThreads, 1)
 moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const int32_t *__restrict__ counts, const int32_t *__restrict__ offsets, int E,
                 int Kdim, int I, int H, uint16_t *__restrict__ out, int out_ld,
                 int32_t *__restrict__ err, const int32_t *__restrict__ g2e,
-                const int32_t *__restrict__ gperm, int gk, int a_rows) {
+                const int32_t *__restrict__ gperm, int gk, int a_rows,
+                const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmSt) {
     constexpr bool GU = (EPI == EPI_GATEUP || EPI == EPI_GATEUP_G);
     constexpr int A_BYTES = AROWS * kBK * 2, B_BYTES = Smem<BN>::B_BYTES;
+    constexpr int Q_BYTES = QB ? BN * kBK * QB / 8 : 0;  // packed codes of a stage
+    constexpr int S_BYTES = QB ? BN * 16 : 0;            // 4 (scale, bias) words per row
     constexpr bool STAGE_C = (EPI == EPI_DOWN && AROWS == kBM);  // TMA-store epilogue
     constexpr uint32_t IDESC = idesc_bf16_f32(kBM, BN);
+    static_assert(QB == 0 || (QB == 4 && (EPI == EPI_GATEUP || EPI == EPI_DOWN) && AROWS == kBM &&
+                              BN <= kDqThreads),
+                  "quantised B: 4-bit, tiled A, one dequantising thread per B row");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~uintptr_t(1023));
+    constexpr int BSTAGES = QB ? kBRing : STAGES;  // B tiles: own ring when dequantised
     uint8_t *sA = smem;
     uint8_t *sB = smem + STAGES * A_BYTES;
-    uint8_t *sC = sB + STAGES * B_BYTES;  // down: per-epilogue-warp store staging
-    uint64_t *full = reinterpret_cast<uint64_t *>(sC + (STAGE_C ? kStageC : 0));
+    uint8_t *sC = sB + BSTAGES * B_BYTES;  // down: per-epilogue-warp store staging
+    uint8_t *sQ = sC + (STAGE_C ? kStageC : 0);
+    uint8_t *sS = sQ + STAGES * Q_BYTES;
+    uint64_t *full = reinterpret_cast<uint64_t *>(sS + STAGES * S_BYTES);
     uint64_t *empty = full + STAGES;
     uint64_t *tfull = empty + STAGES;
     uint64_t *tempty = tfull + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+    uint64_t *bfull = tempty + 2;          // QB: B tile dequantised
+    uint64_t *bempty = bfull + kBRing;     // QB: B tile read by the MMAs
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bempty + (QB ? kBRing : 0));
     int *mtp = reinterpret_cast<int *>(tmem_slot + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -117,9 +144,15 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             mbar_init(&tfull[b], 1);
             mbar_init(&tempty[b], 128);
         }
+        if (QB)
+            for (int b = 0; b < kBRing; ++b) {
+                mbar_init(&bfull[b], kDqThreads);
+                mbar_init(&bempty[b], 1);
+            }
         fence_barrier_init();
         tma_prefetch(&tmA);
         tma_prefetch(&tmB);
+        if (QB) tma_prefetch(&tmS);
     }
     pdl_wait();  // dispatch / gather / gate_up output this kernel reads is complete
     // EPI_F32 (router scores) has one group of gk = T rows at offset 0 and no
@@ -223,10 +256,30 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     }
                     // a_rows: A box height (decode-sized groups stage fewer rows;
                     // the rest of the stage is never stored)
+                    const int brows = GU ? 2 * wrows : BN;
                     mbar_arrive_expect_tx(&full[s], a_rows * kBK * 2 +
-                                                        (GU ? 2 * wrows * kBK * 2 : B_BYTES));
+                                                        (QB ? brows * (kBK * QB / 8 + 16)
+                                                            : GU ? 2 * wrows * kBK * 2 : B_BYTES));
                     tma_load_2d(sA + s * A_BYTES, &tmA, &full[s], kb * kBK, row0);
-                    if (EPI == EPI_GATEUP) {
+                    if constexpr (QB != 0) {
+                        // codes: kBK * QB / 32 words of each B row; (scale, bias):
+                        // the 4-word (16-byte) box holding group kb
+                        const int ew = g2e ? g2e[e] : e;
+                        const int cx = kb * (kBK * QB / 32), sx = kb & ~3;
+                        if (GU) {
+                            const int gate_row = ew * 2 * I + nt * BN2;
+                            const CUtensorMap *ms = tail ? &tmSt : &tmS;
+                            tma_load_2d(sQ + s * Q_BYTES, mb, &full[s], cx, gate_row);
+                            tma_load_2d(sQ + s * Q_BYTES + wrows * (kBK * QB / 8), mb, &full[s],
+                                        cx, gate_row + I);
+                            tma_load_2d(sS + s * S_BYTES, ms, &full[s], sx, gate_row);
+                            tma_load_2d(sS + s * S_BYTES + wrows * 16, ms, &full[s], sx,
+                                        gate_row + I);
+                        } else {
+                            tma_load_2d(sQ + s * Q_BYTES, &tmB, &full[s], cx, ew * H + nt * BN);
+                            tma_load_2d(sS + s * S_BYTES, &tmS, &full[s], sx, ew * H + nt * BN);
+                        }
+                    } else if (EPI == EPI_GATEUP) {
                         // g2e: row group -> expert (grouped entry point); else identity
                         const int ew = g2e ? g2e[e] : e;
                         const int gate_row = ew * 2 * I + nt * BN2;
@@ -260,20 +313,82 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 for (int kb = 0; kb < KB; ++kb, ++g) {
                     const int s = g % STAGES;
                     const uint32_t ph = (g / STAGES) & 1;
-                    if (!mbar_wait(&full[s], ph, kWaitLimit)) {
+                    const int bs = QB ? g % kBRing : s;
+                    if (!mbar_wait(&full[s], ph, kWaitLimit) ||
+                        (QB && !mbar_wait(&bfull[bs], (g / kBRing) & 1, kWaitLimit))) {
                         record_error(err, 3, t);
                         goto done;
                     }
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(sA + s * A_BYTES);
-                    const uint32_t b0 = smem_u32(sB + s * B_BYTES);
+                    const uint32_t b0 = smem_u32(sB + bs * B_BYTES);
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; ++kk)
                         mma_bf16(d, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32),
                                  idesc, (kb | kk) != 0);
                     mma_commit(&empty[s]);  // frees the stage once these MMAs finish
+                    if (QB) mma_commit(&bempty[bs]);
                 }
                 mma_commit(&tfull[buf]);    // accumulator ready for the epilogue
+            }
+        }
+    } else if (QB && warp >= kThreads / 32) {
+        // dequantising warps: thread r owns B row r of every stage
+        const int r = threadIdx.x - kThreads;
+        int g = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+            const int nt = t % NT;
+            const bool tail = GU && nt == NT - 1 && TW < BN2;
+            const int brows = GU ? 2 * (tail ? TW : BN2) : BN;
+            for (int kb = 0; kb < KB; ++kb, ++g) {
+                const int s = g % STAGES;
+                const uint32_t ph = (g / STAGES) & 1;
+                const int bs = g % kBRing;
+                if (!mbar_wait(&full[s], ph, kWaitLimit) ||
+                    !mbar_wait(&bempty[bs], ((g / kBRing) & 1) ^ 1, kWaitLimit)) {
+                    record_error(err, 5, t);
+                    goto done;
+                }
+                if (r < brows) {
+                    // the two 16-byte halves of the row in an order that
+                    // spreads a warp's loads over all banks
+                    const uint4 *qr = reinterpret_cast<const uint4 *>(sQ + s * Q_BYTES + r * 32);
+                    const int h0 = (r >> 2) & 1;
+                    const uint4 qa = qr[h0], qb = qr[h0 ^ 1];
+                    const uint4 q0 = h0 ? qb : qa, q1 = h0 ? qa : qb;
+                    const uint32_t sbw = *reinterpret_cast<const uint32_t *>(
+                        sS + s * S_BYTES + r * 16 + (kb & 3) * 4);
+                    const float2 sc2 = make_float2(bf_lo(sbw), bf_lo(sbw));
+                    const float2 bi2 = make_float2(bf_hi(sbw), bf_hi(sbw));
+                    const float2 m23 = make_float2(-8388608.f, -8388608.f);
+                    const uint32_t wds[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+                    uint8_t *dst = sB + bs * B_BYTES + r * 128;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        // 16-byte chunk c = elements 8c..8c+7 = code word c:
+                        // element 2i is byte i of the low nibbles, 2i+1 of the
+                        // high ones; a byte permute puts each under the
+                        // exponent of 2^23 (exactly 2^23 + q as an f32)
+                        const uint32_t lo = wds[c] & 0x0F0F0F0Fu, hi = (wds[c] >> 4) & 0x0F0F0F0Fu;
+                        uint32_t o[4];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            // packed f32x2 arithmetic: (2^23 + q) - 2^23 = q
+                            // exactly, then fma(scale, q, bias) per lane
+                            const uint32_t sel = (uint32_t)i | 0x7440u;
+                            const float2 q = __fadd2_rn(
+                                make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, sel)),
+                                            __uint_as_float(__byte_perm(hi, 0x4B000000u, sel))),
+                                m23);
+                            const float2 f = __ffma2_rn(sc2, q, bi2);
+                            o[i] = pack_bf2(f.x, f.y);
+                        }
+                        *reinterpret_cast<uint4 *>(dst + ((c ^ (r & 7)) << 4)) =
+                            make_uint4(o[0], o[1], o[2], o[3]);
+                    }
+                }
+                fence_proxy_async();  // generic-proxy stores -> the tensor core's reads
+                mbar_arrive(&bfull[bs]);
             }
         }
     } else {
@@ -341,34 +456,44 @@ bool make_map(CUtensorMap *m, const void *base, uint64_t inner, uint64_t rows, u
     return bf16_map_2d(m, base, inner, rows, kBK, box_rows, true);
 }
 
-template <int EPI, int BN, int BN2, int STAGES, int AROWS = 128>
+template <int EPI, int BN, int BN2, int STAGES, int AROWS = 128, int QB = 0>
 constexpr size_t smem_bytes() {
-    return 1024 + (size_t)STAGES * (AROWS * kBK * 2 + Smem<BN>::B_BYTES) +
-           ((EPI == EPI_DOWN && AROWS == kBM) ? kStageC : 0) + 8 * (2 * STAGES + 4) + 16 +
-           4 * (kMaxExperts + 1);
+    return 1024 +
+           (size_t)STAGES * (AROWS * kBK * 2 + (QB ? BN * kBK * QB / 8 + BN * 16
+                                                   : Smem<BN>::B_BYTES)) +
+           (QB ? (size_t)kBRing * Smem<BN>::B_BYTES : 0) +
+           ((EPI == EPI_DOWN && AROWS == kBM) ? kStageC : 0) +
+           8 * (2 * STAGES + 4 + (QB ? 2 * kBRing : 0)) + 16 + 4 * (kMaxExperts + 1);
 }
 
-template <int EPI, int BN, int BN2, int STAGES, int AROWS = 128>
+template <int EPI, int BN, int BN2, int STAGES, int AROWS = 128, int QB = 0>
 cudaError_t set_attr() {
-    static_assert(smem_bytes<EPI, BN, BN2, STAGES, AROWS>() <= 232448, "shared memory");
-    return cudaFuncSetAttribute(moe_gemm_kernel<EPI, BN, BN2, STAGES, AROWS>,
+    static_assert(smem_bytes<EPI, BN, BN2, STAGES, AROWS, QB>() <= 232448, "shared memory");
+    return cudaFuncSetAttribute(moe_gemm_kernel<EPI, BN, BN2, STAGES, AROWS, QB>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)smem_bytes<EPI, BN, BN2, STAGES, AROWS>());
+                                (int)smem_bytes<EPI, BN, BN2, STAGES, AROWS, QB>());
 }
 
-template <int EPI, int BN, int BN2, int STAGES, int AROWS = 128>
+// sq / sqt (QB only): the (scale, bias) word maps of the full and the narrow
+// last gate_up tile.
+template <int EPI, int BN, int BN2, int STAGES, int AROWS = 128, int QB = 0>
 cudaError_t launch(const CUtensorMap &a, const CUtensorMap &b, const Dispatch &d, int E, int Kdim,
                    int I, int H, uint16_t *out, int out_ld, int32_t *err, cudaStream_t s,
                    const int32_t *g2e = nullptr, const CUtensorMap *c = nullptr,
-                   const int32_t *gperm = nullptr, int gk = 1, int a_rows = kBM) {
+                   const int32_t *gperm = nullptr, int gk = 1, int a_rows = kBM,
+                   const CUtensorMap *sq = nullptr, const CUtensorMap *sqt = nullptr) {
     const int sms = grid_sms(current_device());
-    return launch_ex(moe_gemm_kernel<EPI, BN, BN2, STAGES, AROWS>, dim3(sms), dim3(kThreads),
-                     smem_bytes<EPI, BN, BN2, STAGES, AROWS>(), s, true, a, b, c ? *c : a, d.counts,
-                     d.offsets, E, Kdim, I, H, out, out_ld, err, g2e, gperm, gk, a_rows);
+    return launch_ex(moe_gemm_kernel<EPI, BN, BN2, STAGES, AROWS, QB>, dim3(sms),
+                     dim3(QB ? kThreads + kDqThreads : kThreads),
+                     smem_bytes<EPI, BN, BN2, STAGES, AROWS, QB>(), s, true, a, b, c ? *c : a,
+                     d.counts, d.offsets, E, Kdim, I, H, out, out_ld, err, g2e, gperm, gk, a_rows,
+                     sq ? *sq : a, sqt ? *sqt : (sq ? *sq : a));
 }
 
 // gate_up tile: BN2 gate + BN2 up rows; down tile: BN rows of W_down.
 constexpr int kGuStages = 5, kDnStages = 4, kRtStages = 6;
+// QB: A + codes + (scale, bias) stages of 28 KB, plus two 32 KB B tiles
+constexpr int kQ4GuStages = 5, kQ4DnStages = 4;
 
 }  // namespace
 
@@ -385,6 +510,8 @@ cudaError_t gemm_init() {
     if ((e = set_attr<EPI_GATEUP_G, 256, 128, kDnStages>())) return e;
     if ((e = set_attr<EPI_GATEUP_G, 128, 64, kGuStages>())) return e;
     if ((e = set_attr<EPI_DOWN, 256, 0, kDnStages>())) return e;
+    if ((e = set_attr<EPI_GATEUP, 256, 128, kQ4GuStages, kBM, 4>())) return e;
+    if ((e = set_attr<EPI_DOWN, 256, 0, kQ4DnStages, kBM, 4>())) return e;
     return set_attr<EPI_DOWN, 128, 0, kDnStages>();
 }
 
@@ -497,6 +624,50 @@ cudaError_t launch_gemm_down_grouped(const uint16_t *yp, const Dispatch &d, cons
     cudaError_t e = (bn == 256)
         ? launch<EPI_DOWN, 256, 0, kDnStages>(a, b, d, G, I, I, H, out, H, err, s, g2e, &c)
         : launch<EPI_DOWN, 128, 0, kDnStages>(a, b, d, G, I, I, H, out, H, err, s, g2e, &c);
+    if (launches) ++*launches;
+    return e;
+}
+
+// 4-bit MLX affine experts (64-element groups) on the tensor cores: the
+// gate_up / down GEMMs with the B tiles dequantised in shared memory from the
+// packed codes and the interleaved (scale, bias) words (QB = 4 above); no
+// bf16 copy of the weights is made.
+bool gemm_q4_supported(int H, int I) {
+    return gemm_supported(H, I) && H % 256 == 0 && I % 64 == 0 && I >= 128;
+}
+
+cudaError_t launch_gemm_gateup_q4(const uint16_t *xp, const Dispatch &d, const ExpertWeights &w,
+                                  int rows_cap, int H, int I, int E, uint16_t *yp, int32_t *err,
+                                  cudaStream_t s, int *launches) {
+    if (E > kMaxExperts || w.bits != 4 || !w.gu_q || !w.gu_sb) return cudaErrorInvalidValue;
+    const int bn2 = 128, tw = I % bn2 ? I % bn2 : bn2;
+    const uint64_t rows = (uint64_t)E * 2 * I;
+    CUtensorMap a, b, c, sq, sqt;
+    if (!make_map(&a, xp, H, rows_cap, kBM) ||
+        !map_2d(&b, w.gu_q, H / 8, rows, 8, bn2, false, true) ||
+        !map_2d(&c, w.gu_q, H / 8, rows, 8, tw, false, true) ||
+        !map_2d(&sq, w.gu_sb, sb_row_words(H), rows, 4, bn2, false, true) ||
+        !map_2d(&sqt, w.gu_sb, sb_row_words(H), rows, 4, tw, false, true))
+        return cudaErrorInvalidValue;
+    cudaError_t e = launch<EPI_GATEUP, 256, 128, kQ4GuStages, kBM, 4>(
+        a, b, d, E, H, I, H, yp, I, err, s, nullptr, &c, nullptr, 1, kBM, &sq, &sqt);
+    if (launches) ++*launches;
+    return e;
+}
+
+cudaError_t launch_gemm_down_q4(const uint16_t *yp, const Dispatch &d, const ExpertWeights &w,
+                                int rows_cap, int H, int I, int E, uint16_t *op, int32_t *err,
+                                cudaStream_t s, int *launches) {
+    if (E > kMaxExperts || w.bits != 4 || !w.dn_q || !w.dn_sb) return cudaErrorInvalidValue;
+    const uint64_t rows = (uint64_t)E * H;
+    CUtensorMap a, b, c, sq;
+    if (!make_map(&a, yp, I, rows_cap, kBM) ||
+        !map_2d(&b, w.dn_q, I / 8, rows, 8, 256, false, true) ||
+        !map_2d(&sq, w.dn_sb, sb_row_words(I), rows, 4, 256, false, true) ||
+        !bf16_map_2d(&c, op, H, rows_cap, 64, 32, true))
+        return cudaErrorInvalidValue;
+    cudaError_t e = launch<EPI_DOWN, 256, 0, kQ4DnStages, kBM, 4>(
+        a, b, d, E, I, I, H, op, H, err, s, nullptr, &c, nullptr, 1, kBM, &sq, nullptr);
     if (launches) ++*launches;
     return e;
 }

@@ -184,6 +184,15 @@ cudaError_t launch_selftest_wait(long long limit_cycles, int32_t *err, cudaStrea
 // Interleaved (scale, bias) pairs of `rows` rows of g groups each, rows padded
 // to sb_row_words(g * 64) words (zeros), for the quantised TMA GEMV.
 inline int sb_row_words(int len) { return ((len / 64) + 3) / 4 * 4; }
+// 4-bit experts on the tensor cores, B tiles dequantised in shared memory
+// (gemm_sm100.cu); A rows tiled (the expert-sorted copy xp / yp).
+bool gemm_q4_supported(int H, int I);
+cudaError_t launch_gemm_gateup_q4(const uint16_t *xp, const Dispatch &d, const ExpertWeights &w,
+                                  int rows_cap, int H, int I, int E, uint16_t *yp, int32_t *err,
+                                  cudaStream_t s, int *launches);
+cudaError_t launch_gemm_down_q4(const uint16_t *yp, const Dispatch &d, const ExpertWeights &w,
+                                int rows_cap, int H, int I, int E, uint16_t *op, int32_t *err,
+                                cudaStream_t s, int *launches);
 cudaError_t launch_interleave_sb(const uint16_t *sc, const uint16_t *bi, int64_t rows, int g,
                                  uint32_t *out, cudaStream_t s);
 // bf16 copy of the active experts' quantised rows (prefill path)

@@ -147,6 +147,11 @@ class Handle:
         """Decode (T <= 8) as one persistent kernel (default) or the kernel chain."""
         self.check(lib().apt_moe_set_fused_decode(self.h, int(bool(on))))
 
+    def set_q4_gemm(self, on: bool):
+        """4-bit experts above decode sizes: dequantise B tiles inside the
+        tensor-core GEMMs (default) or expand the touched experts to bf16 first."""
+        self.check(lib().apt_moe_set_q4_gemm(self.h, int(bool(on))))
+
     def last_counts(self) -> torch.Tensor:
         out = torch.zeros(self.cfg.num_experts, dtype=torch.int32)
         self.check(lib().apt_moe_last_counts(self.h, ctypes.c_void_p(out.data_ptr())))

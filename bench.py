@@ -601,15 +601,26 @@ def run_quant(dev, peaks, flush, bits=4, Ts=(1, 4096), steps=5):
         out, tk = blk.forward(d["x"], return_routing=True)
         U = n_unique(tk.idx)
         stream = torch.cuda.current_stream(dev)
-        ms = 0.0
-        for _ in range(steps):
-            flush.sum()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
+
+        def timed():
+            ms = 0.0
+            for _ in range(steps):
+                flush.sum()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                blk.forward(d["x"])
+                b.record(stream)
+                b.synchronize()
+                ms += a.elapsed_time(b) / steps
+            return ms
+
+        ms = timed()
+        ms_expand = None
+        if T > 64 and bits == 4:  # the other tensor-core form, for comparison
+            blk.handle.set_q4_gemm(False)
             blk.forward(d["x"])
-            b.record(stream)
-            b.synchronize()
-            ms += a.elapsed_time(b) / steps
+            ms_expand = timed()
+            blk.handle.set_q4_gemm(True)
         qbytes = U * ((2 * I * H + H * I) * bits // 8 + (2 * I * H + H * I) // 64 * 4)
         res[str(T)] = {"ms": ms, "tokens_per_s": T / (ms / 1e3), "U": U,
                        "expert_bytes": qbytes,
@@ -626,7 +637,11 @@ def run_quant(dev, peaks, flush, bits=4, Ts=(1, 4096), steps=5):
                 block_tflops=flops / (ms / 1e3) / 1e12,
                 block_tc_frac=flops / (ms / 1e3) / 1e12 / peaks["tc"],
                 expert_kernels_tflops=flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None,
-                stages_ms=st, kernel="dequant_active_kernel (touched experts, every call) + bf16 moe_gemm_kernel")
+                stages_ms=st,
+                kernel=("moe_gemm_kernel QB=4: B tiles dequantised in shared memory"
+                        if bits == 4 else
+                        "dequant_active_kernel (touched experts, every call) + bf16 moe_gemm_kernel"),
+                ms_expansion_path=ms_expand)
         del blk
     return {"bits": bits, "group": 64, **res}
 

@@ -323,6 +323,17 @@ APT_API apt_status apt_moe_set_gemv_max_tokens(apt_moe_handle *h, int t);
 APT_API apt_status apt_moe_set_fused_decode(apt_moe_handle *h, int on);
 
 /*
+ * Tensor-core form of 4-bit (group 64) experts above the decode sizes
+ * (gather_qmm, aptransformer/ESExperts.mm:51,56): 1 (default) = the grouped
+ * GEMMs dequantise each B tile in shared memory from the packed codes and
+ * (scale, bias) pairs; 0 = every call first expands the experts it touches
+ * to a bf16 scratch bank and runs the bf16 GEMMs on it.  Both feed the tensor
+ * cores the same bf16 values w = bf16(scale * q + bias), so the outputs are
+ * bitwise equal.  8-bit experts always use the expansion.
+ */
+APT_API apt_status apt_moe_set_q4_gemm(apt_moe_handle *h, int on);
+
+/*
  * Cap on the SMs this handle's persistent kernels fill (0 = all, the
  * default).  Leaves room for kernels that must run beside them, e.g. NCCL's
  * all-to-all while the replicated experts of an expert-parallel step run.

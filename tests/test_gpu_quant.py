@@ -142,3 +142,35 @@ def test_quant4_prefill_T4096_zipf_vs_oracle(oracle):
     got, refv = bf16_to_f32(_np(out))[rows], bf16_to_f32(ref)
     ok, ma, cos = block_close(got, refv)
     assert ok and ma <= TIGHT_REL * np.abs(refv).max(), (ma, cos)
+
+
+@pytest.mark.parametrize("shape,T,routing", [((2816, 128, 8, 704), 16, "uniform"),
+                                             ((2816, 128, 8, 704), 300, "zipf"),
+                                             ((2816, 128, 8, 704), 4096, "zipf"),
+                                             ((256, 32, 8, 128), 64, "uniform")])
+def test_quant4_gemm_equals_expansion(shape, T, routing):
+    """4-bit experts on the tensor cores: the GEMMs that dequantise each B tile
+    in shared memory (apt_moe_set_q4_gemm 1) must give the same bits as
+    expanding the touched experts to a bf16 bank first (0) -- both feed the
+    tensor cores w = bf16(scale * q + bias) -- and the same bits on a repeat
+    call.  Covers the narrow last gate_up tile (I = 704) and I = 128 (none)."""
+    from oracle import oracle as O
+    H, E, K, I = shape
+    d = block_inputs(T, seed=400 + T, device=DEV, routing=routing, H=H, E=E, K=K, I=I)
+    gq = O.quantize_affine(_np(d["gate_up"]), 64, 4)
+    dq = O.quantize_affine(_np(d["down"]), 64, 4)
+    cfg = A.ESModelConfig(hidden_size=H, num_experts=E, top_k_experts=K, moe_intermediate_size=I,
+                          moe_sparse=True, max_tokens=T)
+    q = dict(gu_q=_dev(gq[0]), gu_s=_dev(gq[1]), gu_b=_dev(gq[2]), dn_q=_dev(dq[0]),
+             dn_s=_dev(dq[1]), dn_b=_dev(dq[2]), bits=4, group_size=64)
+    blk = A.MoEBlock(cfg, d["proj"], d["scale"], d["pes"], quantized=q)
+    outs = []
+    for on in (1, 1, 0):
+        blk.handle.set_q4_gemm(on)
+        outs.append(blk.forward(d["x"]))
+        torch.cuda.synchronize()
+        blk.handle.sync()
+    assert torch.isfinite(outs[0].float()).all()
+    assert torch.equal(outs[0], outs[1]), "dequantising GEMM not deterministic"
+    diff = (outs[0].float() - outs[2].float()).abs().max().item()
+    assert torch.equal(outs[0], outs[2]), f"dequantising GEMM != expansion path (max {diff})"
