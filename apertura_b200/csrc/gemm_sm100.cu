@@ -48,7 +48,25 @@ constexpr int kStageC = 4 * 2 * 4096;    // down: 2 x 4 KB store boxes per epilo
 // QB = 4 (MLX affine 4-bit experts, 64-element groups): eight more warps
 // dequantise each stage's packed codes into the bf16 B tile
 constexpr int kDqThreads = 256;
-constexpr int kBRing = 2;  // dequantised B tiles in flight (QB)
+constexpr int kBRing = 3;  // dequantised B tiles in flight (QB)
+
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z),
+                 "r"(w)
+                 : "memory");
+}
 
 // EPI_GATEUP_G: gate_up whose A rows are gathered from the token rows by the
 // TMA (tile::gather4, 4 rows per copy) through the dispatch permutation, so no
@@ -352,17 +370,16 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 if (r < brows) {
                     // the two 16-byte halves of the row in an order that
                     // spreads a warp's loads over all banks
-                    const uint4 *qr = reinterpret_cast<const uint4 *>(sQ + s * Q_BYTES + r * 32);
+                    const uint32_t qr = smem_u32(sQ + s * Q_BYTES + r * 32);
                     const int h0 = (r >> 2) & 1;
-                    const uint4 qa = qr[h0], qb = qr[h0 ^ 1];
+                    const uint4 qa = lds128(qr + 16 * h0), qb = lds128(qr + 16 * (h0 ^ 1));
                     const uint4 q0 = h0 ? qb : qa, q1 = h0 ? qa : qb;
-                    const uint32_t sbw = *reinterpret_cast<const uint32_t *>(
-                        sS + s * S_BYTES + r * 16 + (kb & 3) * 4);
+                    const uint32_t sbw = lds32(smem_u32(sS + s * S_BYTES + r * 16 + (kb & 3) * 4));
                     const float2 sc2 = make_float2(bf_lo(sbw), bf_lo(sbw));
                     const float2 bi2 = make_float2(bf_hi(sbw), bf_hi(sbw));
                     const float2 m23 = make_float2(-8388608.f, -8388608.f);
                     const uint32_t wds[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-                    uint8_t *dst = sB + bs * B_BYTES + r * 128;
+                    const uint32_t dst = smem_u32(sB + bs * B_BYTES + r * 128);
 #pragma unroll
                     for (int c = 0; c < 8; ++c) {
                         // 16-byte chunk c = elements 8c..8c+7 = code word c:
@@ -383,8 +400,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                             const float2 f = __ffma2_rn(sc2, q, bi2);
                             o[i] = pack_bf2(f.x, f.y);
                         }
-                        *reinterpret_cast<uint4 *>(dst + ((c ^ (r & 7)) << 4)) =
-                            make_uint4(o[0], o[1], o[2], o[3]);
+                        sts128(dst + ((c ^ (r & 7)) << 4), o[0], o[1], o[2], o[3]);
                     }
                 }
                 fence_proxy_async();  // generic-proxy stores -> the tensor core's reads
@@ -492,8 +508,8 @@ cudaError_t launch(const CUtensorMap &a, const CUtensorMap &b, const Dispatch &d
 
 // gate_up tile: BN2 gate + BN2 up rows; down tile: BN rows of W_down.
 constexpr int kGuStages = 5, kDnStages = 4, kRtStages = 6;
-// QB: A + codes + (scale, bias) stages of 28 KB, plus two 32 KB B tiles
-constexpr int kQ4GuStages = 5, kQ4DnStages = 4;
+// QB: A + codes + (scale, bias) stages of 28 KB, plus kBRing 32 KB B tiles
+constexpr int kQ4GuStages = 4, kQ4DnStages = 3;
 
 }  // namespace
 
