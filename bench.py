@@ -682,7 +682,8 @@ def run_prefill(blk, dev, peaks, flush, T=8192, steps=3):
 
 
 def run_prefill_only(args):
-    """Prefill config alone at T tokens (the small case the ncu captures use)."""
+    """Prefill config alone at T tokens (the small case the ncu captures use);
+    --bits 4/8 quantises the experts at load (MLX affine, group 64)."""
     import torch
     import apertura_b200 as A
     from apertura_b200 import build as B
@@ -694,7 +695,7 @@ def run_prefill_only(args):
     ones_h = torch.ones(H, dtype=torch.bfloat16, device=dev)
     ones_e = torch.ones(E, dtype=torch.bfloat16, device=dev)
     proj = torch.zeros(E, H, dtype=torch.bfloat16, device=dev)
-    cfg = A.ESModelConfig(moe_sparse=True, max_tokens=T)
+    cfg = A.ESModelConfig(moe_sparse=True, quant_bits=args.bits, max_tokens=T)
     blk = A.MoEBlock(cfg, proj, ones_h, ones_e, gate_up, down)
     flush = torch.ones(256 << 20, dtype=torch.uint8, device=dev)
     res = run_prefill(blk, dev, load_peaks(), flush, T=T, steps=args.steps)
@@ -756,7 +757,7 @@ def main():
     ap.add_argument("--decode-only", type=int, default=0, metavar="T",
                     help="only repeat one decode forward at T tokens (profiling case)")
     ap.add_argument("--bits", type=int, default=0, choices=[0, 4, 8],
-                    help="with --decode-only: MLX affine expert bits (0: bf16)")
+                    help="with --decode-only / --prefill-only: MLX affine expert bits (0: bf16)")
     ap.add_argument("--traffic", type=float, default=None,
                     help="dram bytes per gate_up launch from an ncu capture (reported as is)")
     args = ap.parse_args()
