@@ -327,7 +327,15 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 tc_fence_after();
                 const uint32_t d = tmem_base + buf * kAccStride;
                 const bool tail = GU && t % NT == NT - 1 && TW < BN2;
-                const uint32_t idesc = tail ? idesc_bf16_f32(kBM, 2 * TW) : IDESC;
+                // a gate_up m-tile with at most 64 rows (an expert group's
+                // last, or a decode-sized group) runs M = 64 MMAs: half the
+                // tensor work (down tiles keep M = 128 and their TMA-store
+                // epilogue, which matters more for their short K loop)
+                int e_, mloc_, nt_;
+                decode_tile(t, NT, mtp, E, e_, mloc_, nt_);
+                const int mrows = (GU && grp_cnt(e_) - mloc_ * kBM <= 64) ? 64 : kBM;
+                const uint32_t idesc = tail ? idesc_bf16_f32(mrows, 2 * TW)
+                                            : (mrows == kBM ? IDESC : idesc_bf16_f32(64, BN));
                 for (int kb = 0; kb < KB; ++kb, ++g) {
                     const int s = g % STAGES;
                     const uint32_t ph = (g / STAGES) & 1;
@@ -409,12 +417,17 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         }
     } else {
         const int q = warp & 3;             // TMEM lane quarter this warp may read
-        const int r = q * 32 + lane;        // accumulator row of this thread
         int i = 0, bufsel = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
             int e, mloc, nt;
             decode_tile(t, NT, mtp, E, e, mloc, nt);
             const int nvalid = grp_cnt(e) - mloc * kBM;
+            // accumulator row of this thread: lane q*32 + lane holds row
+            // q*32 + lane of an M = 128 tile, and row q*16 + lane (lanes < 16)
+            // of an M = 64 tile
+            const bool m64 = GU && nvalid <= 64;
+            const int r = m64 ? q * 16 + lane : q * 32 + lane;
+            const bool rvalid = r < nvalid && (!m64 || lane < 16);
             const int row = grp_off(e) + mloc * kBM + r;
             const int buf = i & 1;
             const uint32_t use = i >> 1;
@@ -427,8 +440,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             if constexpr (GU) {
                 // a narrow last tile holds g in columns [0, TW), u in [TW, 2*TW)
                 const int w = min(BN2, I - nt * BN2);
-                epilogue_geglu(taddr, w, w, r < nvalid,
-                               out + (size_t)row * out_ld + nt * BN2);
+                epilogue_geglu(taddr, w, w, rvalid, out + (size_t)row * out_ld + nt * BN2);
             } else if constexpr (EPI == EPI_F32) {
                 // plane nt / NCB of [2][gk = T][out_ld]
                 float *dst = reinterpret_cast<float *>(out) + (size_t)(nt / NCB) * gk * out_ld +
@@ -446,11 +458,11 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                                             __uint_as_float(a[6]), __uint_as_float(a[7]));
                     }
                 }
-            } else if (STAGE_C && q * 32 + 32 <= nvalid) {
+            } else if (STAGE_C && !m64 && q * 32 + 32 <= nvalid) {
                 epilogue_bf16_tma<BN>(taddr, sC + q * 8192, bufsel, &tmC, nt * BN, row - lane,
                                       lane);
-            } else if (q * 32 < nvalid) {
-                epilogue_bf16<BN>(taddr, r < nvalid, out + (size_t)row * out_ld + nt * BN);
+            } else if ((m64 ? q * 16 : q * 32) < nvalid) {
+                epilogue_bf16<BN>(taddr, rvalid, out + (size_t)row * out_ld + nt * BN);
             }
             tc_fence_before();
             mbar_arrive(&tempty[buf]);
