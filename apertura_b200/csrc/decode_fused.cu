@@ -730,8 +730,7 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
     constexpr int S = stages_for<NTMAX, BITS>();
     constexpr int SBY = stage_bytes<BITS>();
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                                ~uintptr_t(1023));
+    uint8_t *ring = smem_align(smem_raw, 1024);
     uint16_t *xs = reinterpret_cast<uint16_t *>(ring + ring_bytes<NTMAX, BITS>());  // [T][H]
     uint16_t *ys = xs + (size_t)a.T * a.H;                                           // [2][NTMAX][I]
     // 8-bit experts: kSB (scale, bias) slots, 128-byte aligned
@@ -747,7 +746,7 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
     float *ysum = xsum32 + (BITS == 4 ? a.T * (a.H / 32) : 0);
     const int GI = a.I / 64;
     uint64_t *bars = reinterpret_cast<uint64_t *>(
-        (reinterpret_cast<uintptr_t>(ysum + (BITS == 4 ? 2 * NTMAX * GI : 0)) + 7) & ~uintptr_t(7));
+        smem_align(reinterpret_cast<uint8_t *>(ysum + (BITS == 4 ? 2 * NTMAX * GI : 0)), 8));
     uint64_t *full = bars, *empty = bars + S;
     uint64_t *yfull = bars + 2 * S, *yempty = yfull + 2, *xbar = yempty + 2;
     uint64_t *sbfull = xbar + 1, *sbempty = sbfull + kSB;

@@ -494,7 +494,7 @@ combine_bulk_kernel(CombineBulkArgs a, CombineTail tail) {
     uint32_t *s_w = reinterpret_cast<uint32_t *>(s_moe + (post ? H : 0));  // [S][K] w as bf16x2
     uint32_t *s_mask = s_w + S * K;                                           // [S] routed slots
     uint64_t *fullb = reinterpret_cast<uint64_t *>(
-        (reinterpret_cast<uintptr_t>(s_mask + S) + 7) & ~uintptr_t(7));
+        smem_align(reinterpret_cast<uint8_t *>(s_mask + S), 8));
     uint64_t *emptyb = fullb + S;
     __shared__ float2 s_red[32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

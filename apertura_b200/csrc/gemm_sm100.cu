@@ -135,8 +135,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                               BN <= kDqThreads),
                   "quantised B: 4-bit, tiled A, one dequantising thread per B row");
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                                ~uintptr_t(1023));
+    uint8_t *smem = smem_align(smem_raw, 1024);
     constexpr int BSTAGES = QB ? kBRing : STAGES;  // B tiles: own ring when dequantised
     uint8_t *sA = smem;
     uint8_t *sB = smem + STAGES * A_BYTES;

@@ -197,8 +197,7 @@ __global__ void __launch_bounds__(kThreads)
 gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, Args a) {
     using S = Shape<EPI>;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                                ~uintptr_t(1023));
+    uint8_t *ring = smem_align(smem_raw, 1024);
     const int LEN = (EPI == GATEUP) ? a.H : a.I;
     // token rows per unit (item x token pass), double-buffered, fetched by the
     // producer with 1-D bulk copies ahead of the compute warps

@@ -377,21 +377,19 @@ gemv_tma_q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
                   QArgs a) {
     using S = QShape<EPI, BITS>;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                                ~uintptr_t(1023));
+    uint8_t *ring = smem_align(smem_raw, 1024);
     const int LEN = (EPI == GATEUP) ? a.H : a.I;
     const int Gp = a.gp;
     // per unit (item x token pass), double-buffered: token rows, (scale, bias)
     uint16_t *xs0 = reinterpret_cast<uint16_t *>(ring + S::STAGES * S::STAGE_BYTES);
     uint32_t *sb0 = reinterpret_cast<uint32_t *>(
-        (reinterpret_cast<uintptr_t>(xs0 + 2 * NTMAX * LEN) + 127) & ~uintptr_t(127));
+        smem_align(reinterpret_cast<uint8_t *>(xs0 + 2 * NTMAX * LEN), 128));
     // MMA variant: per-unit sums of x over each group, and gate_up's
     // cross-warp partial sums
     float *xsum = reinterpret_cast<float *>(sb0 + 2 * S::ROWS * Gp);
     float *red = xsum + (MMA ? NTMAX * Gp : 0);
-    uint64_t *full = reinterpret_cast<uint64_t *>(
-        (reinterpret_cast<uintptr_t>(red + (MMA && EPI == GATEUP ? kComputeWarps * 256 : 0)) + 7) &
-        ~uintptr_t(7));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem_align(
+        reinterpret_cast<uint8_t *>(red + (MMA && EPI == GATEUP ? kComputeWarps * 256 : 0)), 8));
     uint64_t *empty = full + S::STAGES;
     uint64_t *ufull = empty + S::STAGES;
     uint64_t *uempty = ufull + 2;

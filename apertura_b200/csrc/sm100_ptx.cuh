@@ -16,6 +16,16 @@ __device__ __forceinline__ uint32_t smem_u32(const void *p) {
 
 // ---------------------------------------------------------------- mbarrier
 
+// p moved up to the next multiple of `align` (a power of two) bytes of its
+// shared-window address, by pointer arithmetic on the shared-memory array.
+// (Aligning through an integer round trip would leave a generic pointer, and
+// every access through it a generic load or store instead of a shared one.)
+template <typename T>
+__device__ __forceinline__ T *smem_align(T *p, uint32_t align) {
+    const uint32_t a = smem_u32(p);
+    return reinterpret_cast<T *>(reinterpret_cast<uint8_t *>(p) + (((a + align - 1) & ~(align - 1)) - a));
+}
+
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
                  : "memory");
