@@ -90,6 +90,10 @@ struct apt_moe_handle {
     uint32_t *gu_q = nullptr, *dn_q = nullptr;
     uint16_t *gu_s = nullptr, *gu_b = nullptr, *dn_s = nullptr, *dn_b = nullptr;
     uint32_t *gu_sb = nullptr, *dn_sb = nullptr;  // (scale, bias) pairs, per-row contiguous
+    // 4-bit codes re-ordered for the one-kernel decode block's mma.sync
+    // fragments (repack_q4_decode_kernel); the MLX-format gu_q / dn_q stay the
+    // source of every other path
+    uint32_t *gu_qd = nullptr, *dn_qd = nullptr;
     int qbits = 0, qgs = 64;
     // set when the weights above are shared with other handles (read-only then)
     std::shared_ptr<WeightOwner> wowner;
@@ -181,6 +185,8 @@ ExpertWeights weights_for(const apt_moe_handle *h, bool quant) {
         w.dn_b = h->dn_b;
         w.gu_sb = h->gu_sb;
         w.dn_sb = h->dn_sb;
+        w.gu_qd = h->gu_qd;
+        w.dn_qd = h->dn_qd;
         w.bits = h->qbits;
         w.gs = h->qgs;
     }
@@ -217,7 +223,8 @@ std::vector<void **> weight_fields(apt_moe_handle *h) {
             reinterpret_cast<void **>(&h->dn_q),  reinterpret_cast<void **>(&h->gu_s),
             reinterpret_cast<void **>(&h->gu_b),  reinterpret_cast<void **>(&h->dn_s),
             reinterpret_cast<void **>(&h->dn_b),  reinterpret_cast<void **>(&h->gu_sb),
-            reinterpret_cast<void **>(&h->dn_sb), reinterpret_cast<void **>(&h->projw)};
+            reinterpret_cast<void **>(&h->dn_sb), reinterpret_cast<void **>(&h->projw),
+            reinterpret_cast<void **>(&h->gu_qd), reinterpret_cast<void **>(&h->dn_qd)};
 }
 
 void drop_graphs(apt_moe_handle *h) {
@@ -396,7 +403,7 @@ extern "C" apt_status apt_moe_destroy(apt_moe_handle *h) {
     void *ptrs[] = {h->proj, h->scale, h->pes, h->gu, h->dn, h->gu_q, h->dn_q, h->gu_s, h->gu_b,
                     h->dn_s, h->dn_b, h->scores, h->idx_i, h->w_i, h->counts, h->offsets,
                     h->perm, h->inv, h->active, h->n_active, h->errflag, h->done, h->projw, h->xp, h->yp, h->op,
-                    h->Wd, h->idx2, h->w2, h->xin, h->xout, h->dq_gu, h->dq_dn, h->gu_sb, h->dn_sb, h->xn, h->fsync};
+                    h->Wd, h->idx2, h->w2, h->xin, h->xout, h->dq_gu, h->dq_dn, h->gu_sb, h->dn_sb, h->xn, h->fsync, h->gu_qd, h->dn_qd};
     for (void *p : ptrs) dfree(p);
     drop_graphs(h);
     if (h->gstream) cudaStreamDestroy(h->gstream);
@@ -544,6 +551,16 @@ apt_status build_sb(apt_moe_handle *h) {
     CUDA_TRY(h, dalloc(&h->dn_sb, dn_rows * sb_row_words((int)I)));
     CUDA_TRY(h, launch_interleave_sb(h->gu_s, h->gu_b, (int64_t)gu_rows, (int)H / 64, h->gu_sb, 0));
     CUDA_TRY(h, launch_interleave_sb(h->dn_s, h->dn_b, (int64_t)dn_rows, (int)I / 64, h->dn_sb, 0));
+    dfree(h->gu_qd);
+    dfree(h->dn_qd);
+    h->gu_qd = h->dn_qd = nullptr;
+    if (h->qbits == 4 && h->qgs == 64 && H % 256 == 0 && H % 128 == 0 && I % 64 == 0) {
+        // the decode block's fragment-ordered copy of the codes (same size as gu_q / dn_q)
+        CUDA_TRY(h, dalloc(&h->gu_qd, gu_rows * H / 8));
+        CUDA_TRY(h, dalloc(&h->dn_qd, dn_rows * I / 8));
+        CUDA_TRY(h, launch_repack_q4_decode(h->gu_q, h->dn_q, (int)E, (int)H, (int)I, h->gu_qd,
+                                            h->dn_qd, 0));
+    }
     CUDA_TRY(h, cudaDeviceSynchronize());
     return APT_OK;
 }
@@ -914,7 +931,9 @@ apt_status forward_impl(apt_moe_handle *h, const uint16_t *x_router, const uint1
     } clear_post{h};
     const bool fq = h->qbits > 0;
     if (h->cfg.moe_sparse && h->fused_decode && !pre_w && !tail &&
-        (fq ? h->gu_q && h->gu_sb && h->dn_sb : h->gu != nullptr) && T <= h->gemv_max_tokens &&
+        (fq ? h->gu_q && h->gu_sb && h->dn_sb && (h->qbits != 4 || h->gu_qd)
+            : h->gu != nullptr) &&
+        T <= h->gemv_max_tokens &&
         decode_fused_supported(T, H, h->cfg.moe_intermediate_size, E, K, x_router == x_experts,
                                h->qbits, h->qgs)) {
         // decode: the whole block (router .. combine) in one persistent kernel

@@ -156,7 +156,7 @@ struct FusedArgs {
     uint16_t *out;                      // [T, H]
     int32_t *sync;                      // see the sync-word layout above set_words()
     int32_t *err;
-    const uint32_t *gq, *dq, *gsb, *dsb;  // 4-bit: packed codes and (scale, bias) rows
+    const uint32_t *gq, *dq, *gsb, *dsb;  // 4-bit: fragment-ordered codes, (scale, bias) rows
 };
 
 __device__ __forceinline__ void record_error(int32_t *err, int code, int where) {
@@ -517,6 +517,12 @@ __device__ bool down_item_q(const uint8_t *ring, uint64_t *full, uint64_t *empty
 // 4-bit items arrive whole: one ring slot holds an item's packed rows (gate_up:
 // 16 gate + 16 up rows of H/8 words; down: 128 rows of I/8 words), copied as
 // contiguous runs by 1-D bulk copies, followed by its (scale, bias) rows.
+// One bf16 fragment pair (128 + q, 128 + q') from a fragment-ordered code
+// word (repack_q4_decode_kernel, quant.cu): pair p sits at bits 4p and 16 + 4p.
+__device__ __forceinline__ uint32_t q4_frag(uint32_t w, int p) {
+    return ((w >> (4 * p)) & 0x000F000Fu) | 0x43004300u;
+}
+
 __host__ __device__ inline int q4_code_words(int H, int I) {
     const int gu = 32 * (H / 8), dn = kDnRows * (I / 8);
     return gu > dn ? gu : dn;
@@ -545,15 +551,12 @@ __device__ bool gateup_item_q4(const uint32_t *codes, const uint32_t *sbs, int g
     const float *xs0 = xsum32 + (size_t)(n0 < nt ? toks[n0] : toks[0]) * HB;
     const float *xs1 = xsum32 + (size_t)(n1 < nt ? toks[n1] : toks[0]) * HB;
     float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    (void)RW;
     for (int kc = 0; kc < NK; ++kc) {
         float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-        // the warp's 32 columns of each row in one 16-byte load (4 words)
-        uint4 v[2][2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            v[h][0] = *reinterpret_cast<const uint4 *>(codes + (h * 16 + gid) * RW + kc * 32 + 4 * w);
-            v[h][1] = *reinterpret_cast<const uint4 *>(codes + (h * 16 + gid + 8) * RW + kc * 32 + 4 * w);
-        }
+        // this lane's codes of the step, fragment-ordered: gate rows g, g + 8,
+        // up rows g, g + 8 (one conflict-free 16-byte load)
+        const uint4 q = *reinterpret_cast<const uint4 *>(codes + ((kc * 8 + w) * 32 + lane) * 4);
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
             const int k0 = kc * 256 + 32 * w + 16 * c;  // column within the row
@@ -564,9 +567,9 @@ __device__ bool gateup_item_q4(const uint32_t *codes, const uint32_t *sbs, int g
             }
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                uint32_t af[4];
-                q4_pair(c ? v[h][0].z : v[h][0].x, c ? v[h][0].w : v[h][0].y, t, af[0], af[2]);
-                q4_pair(c ? v[h][1].z : v[h][1].x, c ? v[h][1].w : v[h][1].y, t, af[1], af[3]);
+                const uint32_t wa = h ? q.z : q.x, wb = h ? q.w : q.y;
+                const uint32_t af[4] = {q4_frag(wa, 2 * c), q4_frag(wb, 2 * c),
+                                        q4_frag(wa, 2 * c + 1), q4_frag(wb, 2 * c + 1)};
                 mma_bf16_16816(d[h], af, b0, b1);
             }
         }
@@ -636,17 +639,13 @@ __device__ void down_item_q4(const uint32_t *codes, const uint32_t *sbs, int gp,
     const int gid = lane >> 2, t = lane & 3;
     const int n0 = 2 * t, n1 = 2 * t + 1;
     const uint16_t *yrow = ys + (size_t)(gid < nt ? gid : 0) * a.I;
-    const uint32_t *row0 = codes + (16 * w + gid) * RW, *row1 = row0 + 8 * RW;
+    (void)RW;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int kc = 0; kc < NK; ++kc) {
         float d[4] = {0.f, 0.f, 0.f, 0.f};
-        // the group's 64 columns of both rows: two 16-byte loads each
-        const uint4 r0a = *reinterpret_cast<const uint4 *>(row0 + kc * 8);
-        const uint4 r0b = *reinterpret_cast<const uint4 *>(row0 + kc * 8 + 4);
-        const uint4 r1a = *reinterpret_cast<const uint4 *>(row1 + kc * 8);
-        const uint4 r1b = *reinterpret_cast<const uint4 *>(row1 + kc * 8 + 4);
-        const uint32_t w0[8] = {r0a.x, r0a.y, r0a.z, r0a.w, r0b.x, r0b.y, r0b.z, r0b.w};
-        const uint32_t w1[8] = {r1a.x, r1a.y, r1a.z, r1a.w, r1b.x, r1b.y, r1b.z, r1b.w};
+        // this lane's codes of the group, fragment-ordered: rows g, g + 8 of
+        // the first 32 columns, then of the second (one 16-byte load)
+        const uint4 q = *reinterpret_cast<const uint4 *>(codes + ((kc * 8 + w) * 32 + lane) * 4);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             uint32_t b0 = 0u, b1 = 0u;
@@ -654,9 +653,10 @@ __device__ void down_item_q4(const uint32_t *codes, const uint32_t *sbs, int gp,
                 b0 = *reinterpret_cast<const uint32_t *>(yrow + kc * 64 + 16 * c + 2 * t);
                 b1 = *reinterpret_cast<const uint32_t *>(yrow + kc * 64 + 16 * c + 2 * t + 8);
             }
-            uint32_t af[4];
-            q4_pair(w0[2 * c], w0[2 * c + 1], t, af[0], af[2]);
-            q4_pair(w1[2 * c], w1[2 * c + 1], t, af[1], af[3]);
+            const uint32_t wa = (c >> 1) ? q.z : q.x, wb = (c >> 1) ? q.w : q.y;
+            const int p = 2 * (c & 1);
+            const uint32_t af[4] = {q4_frag(wa, p), q4_frag(wb, p), q4_frag(wa, p + 1),
+                                    q4_frag(wb, p + 1)};
             mma_bf16_16816(d, af, b0, b1);
         }
         const float y0 = n0 < nt ? ysum[n0 * NK + kc] : 0.f;
@@ -1057,14 +1057,19 @@ decode_fused_kernel(const __grid_constant__ CUtensorMap tmGU,
                 uint32_t *ds = dc + q4_code_words(H, I);
                 const uint32_t rwH = (uint32_t)H / 8, rwI = (uint32_t)I / 8;
                 if (gu) {
+                    // codes: the item's fragment-ordered block (32 rows x H/8 words)
+                    const int u = i / NGU, blk = i - u * NGU;
+                    const size_t item = (size_t)s_act[u] * NGU + blk;
                     mbar_arrive_expect_tx(&full[sl], 2u * 16 * (rwH + gpH) * 4);
-                    bulk_load(dc, a.gq + (size_t)r0 * rwH, 16 * rwH * 4, &full[sl]);
-                    bulk_load(dc + 16 * rwH, a.gq + (size_t)(r0 + I) * rwH, 16 * rwH * 4, &full[sl]);
+                    bulk_load(dc, a.gq + item * 32 * rwH, 32 * rwH * 4, &full[sl]);
                     bulk_load(ds, a.gsb + (size_t)r0 * gpH, 16u * gpH * 4, &full[sl]);
                     bulk_load(ds + 16 * gpH, a.gsb + (size_t)(r0 + I) * gpH, 16u * gpH * 4, &full[sl]);
                 } else {
+                    // codes: the item's fragment-ordered block (128 rows x I/8 words)
+                    const int j = i - Ngu, u = j / NDN, hb = j - u * NDN;
+                    const size_t item = (size_t)s_act[u] * NDN + hb;
                     mbar_arrive_expect_tx(&full[sl], (uint32_t)kDnRows * (rwI + gpI) * 4);
-                    bulk_load(dc, a.dq + (size_t)r0 * rwI, kDnRows * rwI * 4, &full[sl]);
+                    bulk_load(dc, a.dq + item * kDnRows * rwI, kDnRows * rwI * 4, &full[sl]);
                     bulk_load(ds, a.dsb + (size_t)r0 * gpI, (uint32_t)kDnRows * gpI * 4, &full[sl]);
                 }
                 ++it;
@@ -1446,7 +1451,8 @@ cudaError_t launch_decode_fused(const uint16_t *xr, const uint16_t *xe, const ui
     }
     FusedArgs a{xr, xe, scale, pes, proj, T, H, E, K, I, eps, (float)(1.0 / sqrt((double)H)),
                 scores, idx, w, d, yq, oq, out, sync, err,
-                wt.gu_q, wt.dn_q, wt.gu_sb, wt.dn_sb};
+                bits == 4 ? wt.gu_qd : wt.gu_q, bits == 4 ? wt.dn_qd : wt.dn_q, wt.gu_sb,
+                wt.dn_sb};
     const cudaError_t e = bits == 0   ? launch_bits<0>(m, a, s)
                           : bits == 4 ? launch_bits<4>(m, a, s)
                                       : launch_bits<8>(m, a, s);

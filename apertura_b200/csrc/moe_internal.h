@@ -113,6 +113,7 @@ struct ExpertWeights {
     const uint32_t *gu_q, *dn_q;            // packed
     const uint16_t *gu_s, *gu_b, *dn_s, *dn_b;
     const uint32_t *gu_sb, *dn_sb;          // interleaved (scale, bias) pairs
+    const uint32_t *gu_qd, *dn_qd;          // 4-bit codes in the decode block's fragment order
     int bits, gs;
 };
 // max_rows_per_expert bounds counts[e] for this call (T for top-k routing).
@@ -196,6 +197,11 @@ cudaError_t launch_gemm_down_q4(const uint16_t *yp, const Dispatch &d, const Exp
 cudaError_t launch_interleave_sb(const uint16_t *sc, const uint16_t *bi, int64_t rows, int g,
                                  uint32_t *out, cudaStream_t s);
 // bf16 copy of the active experts' quantised rows (prefill path)
+// 4-bit codes re-ordered for the one-kernel decode block (quant.cu):
+// gate_up items of 16 intermediate columns (32 rows x H) and down items of
+// 128 rows x I, each one contiguous block in its mma.sync fragment order.
+cudaError_t launch_repack_q4_decode(const uint32_t *gu_q, const uint32_t *dn_q, int E, int H, int I,
+                                    uint32_t *gu_qd, uint32_t *dn_qd, cudaStream_t s);
 cudaError_t launch_dequant_active(const uint32_t *q, const uint16_t *sc, const uint16_t *bi,
                                   int rows, int cols, int bits, const Dispatch &d, int E,
                                   uint16_t *out, cudaStream_t s, int *launches);

@@ -106,6 +106,58 @@ dequant_active_kernel(const uint32_t *__restrict__ q, const uint16_t *__restrict
     }
 }
 
+// 4-bit codes of one MLX row-major bank (low nibble first) in the order the
+// one-kernel decode block's mma.sync m16n8k16 A fragments read them
+// (decode_fused.cu).  An item is one contiguous block of words
+// [k-step][warp 0..7][lane 0..31][4]; lane (g, t) = (lane >> 2, lane & 3)
+// finds in each of its 4 words the codes of one row at
+// k = base + 2t + 8p and base + 2t + 8p + 1 for p = 0..3, at bits 4p and
+// 16 + 4p, so that ((word >> 4p) & 0x000F000F) | 0x43004300 is its bf16
+// fragment pair (128 + q, 128 + q') -- the same values the MLX layout gives.
+//   gate_up item (expert e, 16-column block b, H/256 k-steps of 256 columns):
+//     warp w covers columns 256 kc + 32 w; words (gate row g, gate row g + 8,
+//     up row g, up row g + 8) of the block; base = 256 kc + 32 w.
+//   down item (expert e, 128-row block hb, I/64 k-steps of one 64-column
+//     group): warp w covers rows 16 w .. 16 w + 15; words (row 16w + g, base
+//     64 kc), (row 16w + g + 8, same), (row 16w + g, base 64 kc + 32),
+//     (row 16w + g + 8, same).
+__global__ void repack_q4_decode_kernel(const uint32_t *__restrict__ q, int E, int H, int I,
+                                        int down, uint32_t *__restrict__ out) {
+    const int cols = down ? I : H;
+    const int64_t item_words = down ? 16LL * I : 4LL * H;
+    const int per_expert = down ? H / 128 : I / 16;
+    const int64_t total = (int64_t)E * per_expert * item_words;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t item = idx / item_words;
+        const int within = (int)(idx - item * item_words);
+        const int kc = within >> 10, w = (within >> 7) & 7, lane = (within >> 2) & 31, j = within & 3;
+        const int g = lane >> 2, t = lane & 3;
+        const int e = (int)(item / per_expert), b = (int)(item - (int64_t)e * per_expert);
+        int64_t row;
+        int base;
+        if (!down) {
+            const int h = j >> 1, rs = j & 1;
+            row = (int64_t)e * 2 * I + (h ? I : 0) + b * 16 + g + 8 * rs;
+            base = 256 * kc + 32 * w;
+        } else {
+            const int rs = j & 1, ch = j >> 1;
+            row = (int64_t)e * H + b * 128 + 16 * w + g + 8 * rs;
+            base = 64 * kc + 32 * ch;
+        }
+        const uint32_t *qr = q + row * (cols / 8);
+        uint32_t word = 0;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            const int k = base + 2 * t + 8 * p;
+            const uint32_t c0 = (qr[k >> 3] >> (4 * (k & 7))) & 15u;
+            const uint32_t c1 = (qr[(k + 1) >> 3] >> (4 * ((k + 1) & 7))) & 15u;
+            word |= (c0 << (4 * p)) | (c1 << (16 + 4 * p));
+        }
+        out[idx] = word;
+    }
+}
+
 // Repack scales/biases [rows, groups] x2 into one [rows, groups] uint32 array
 // of (scale | bias << 16) pairs: a row's pairs are contiguous (groups*4 bytes),
 // so a kernel stages a block of rows with plain 16-byte loads.
@@ -128,6 +180,15 @@ __global__ void interleave_sb_kernel(const uint16_t *__restrict__ sc,
 cudaError_t launch_interleave_sb(const uint16_t *sc, const uint16_t *bi, int64_t rows, int g,
                                  uint32_t *out, cudaStream_t s) {
     interleave_sb_kernel<<<1024, 256, 0, s>>>(sc, bi, rows, g, sb_row_words(g * 64), out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_repack_q4_decode(const uint32_t *gu_q, const uint32_t *dn_q, int E, int H, int I,
+                                    uint32_t *gu_qd, uint32_t *dn_qd, cudaStream_t s) {
+    repack_q4_decode_kernel<<<2048, 256, 0, s>>>(gu_q, E, H, I, 0, gu_qd);
+    cudaError_t e = cudaGetLastError();
+    if (e) return e;
+    repack_q4_decode_kernel<<<2048, 256, 0, s>>>(dn_q, E, H, I, 1, dn_qd);
     return cudaGetLastError();
 }
 
